@@ -1,0 +1,177 @@
+"""fp32 numpy restatement of the letter-family decoder forward + option readout.
+
+TEST INFRASTRUCTURE ONLY (see `oracle/__init__.py`).
+
+Reference path: `GraphRunner._eager_readout` (`executor/torch_exec.py:255-261`):
+    hs = model.model(input_ids=ids, use_cache=False[, attention_mask]).last_hidden_state
+    logits = hs[slot_batch, slot_idx].float() @ head_w.T
+with `head_w = model.get_output_embeddings().weight[letter_ids].float()`
+(`executor/torch_exec.py:2383-2386`), the model in fp32 on CPU
+(`executor/torch_exec.py:2352`).  The per-layer math is HF transformers'
+Qwen3 (`Qwen3RMSNorm`, q/k RMSNorm, `rotate_half` RoPE, SDPA causal GQA,
+SiLU-gated MLP) and Gemma (`(1 + w)` RMSNorm, sqrt(d) embedding scale,
+tanh-GELU gated MLP, tied head).  Right padding is never attended by a causal
+model, so each row is computed over its `real_len` tokens only.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from verdict_b200.synth import SyntheticCheckpoint, synthetic_label_ids
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, plus_one: bool) -> np.ndarray:
+    """Qwen3RMSNorm: w * (x * rsqrt(mean(x^2) + eps)); GemmaRMSNorm: (1 + w) * (...)."""
+    var = np.mean(np.square(x, dtype=np.float32), axis=-1, keepdims=True, dtype=np.float32)
+    y = x * (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
+    g = (np.float32(1.0) + w) if plus_one else w
+    return (y * g).astype(np.float32)
+
+
+def rope_tables(positions: np.ndarray, head_dim: int, theta: float):
+    """cos/sin of the default RoPE: inv_freq = 1 / theta^(2i/hd), emb = cat(freqs, freqs)."""
+    exps = np.arange(0, head_dim, 2, dtype=np.int64).astype(np.float32) / np.float32(head_dim)
+    inv_freq = (np.float32(1.0) / np.power(np.float32(theta), exps)).astype(np.float32)
+    freqs = positions.astype(np.float32)[:, None] * inv_freq[None, :]
+    emb = np.concatenate([freqs, freqs], axis=-1)
+    return np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """x * cos + rotate_half(x) * sin with rotate_half(x) = cat(-x2, x1); x is [n, h, hd]."""
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    return (x * cos[:, None, :] + rot * sin[:, None, :]).astype(np.float32)
+
+
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool) -> np.ndarray:
+    """softmax(q k^T / sqrt(hd) [+ causal mask]) v with GQA head sharing; q [n,hq,hd], k/v [n,hkv,hd]."""
+    n, hq, hd = q.shape
+    hkv = k.shape[1]
+    group = hq // hkv
+    scale = np.float32(hd ** -0.5)
+    out = np.empty_like(q)
+    mask = np.triu(np.ones((n, n), dtype=bool), 1) if causal else None
+    for h in range(hq):
+        s = (q[:, h, :] @ k[:, h // group, :].T) * scale
+        if mask is not None:
+            s = np.where(mask, np.float32(-np.inf), s)
+        s = s - s.max(axis=-1, keepdims=True)
+        p = np.exp(s, dtype=np.float32)
+        p /= p.sum(axis=-1, keepdims=True)
+        out[:, h, :] = p @ v[:, h // group, :]
+    return out
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    c = np.float32(np.sqrt(2.0 / np.pi))
+    return (np.float32(0.5) * x * (np.float32(1.0) + np.tanh(c * (x + np.float32(0.044715) * x * x * x)))).astype(np.float32)
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+class DecoderOracle:
+    """Holds the synthetic checkpoint (host, fp32 copies of the bf16 weights)."""
+
+    def __init__(self, spec: dict, layers: int | None = None):
+        self.spec = spec
+        self.ckpt = SyntheticCheckpoint(spec)
+        self.n_layers = spec["layers"] if layers is None else layers
+        self.label_ids = synthetic_label_ids(spec)
+        self._layers = {}
+        self.final_norm = self.ckpt.get("model.norm.weight")
+        self.head_w = self.ckpt.get(self.ckpt.head_name(), rows=self.label_ids)
+
+    def layer(self, i: int) -> dict:
+        if i not in self._layers:
+            p = f"model.layers.{i}."
+            names = ["input_layernorm.weight", "self_attn.q_proj.weight", "self_attn.k_proj.weight",
+                     "self_attn.v_proj.weight", "self_attn.o_proj.weight",
+                     "post_attention_layernorm.weight", "mlp.gate_proj.weight",
+                     "mlp.up_proj.weight", "mlp.down_proj.weight"]
+            if self.spec["qk_norm"]:
+                names += ["self_attn.q_norm.weight", "self_attn.k_norm.weight"]
+            if self.spec["qkv_bias"]:
+                names += ["self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias"]
+            self._layers[i] = {n: self.ckpt.get(p + n) for n in names}
+        return self._layers[i]
+
+    def embed(self, ids: np.ndarray) -> np.ndarray:
+        uniq, inv = np.unique(ids, return_inverse=True)
+        rows = self.ckpt.get("model.embed_tokens.weight", rows=uniq)
+        h = rows[inv].astype(np.float32)
+        if self.spec["embed_scale"]:
+            h = h * np.float32(self.spec["hidden"] ** 0.5)
+        return h
+
+    def layer_forward(self, i: int, h: np.ndarray, cos, sin) -> np.ndarray:
+        s = self.spec
+        w = self.layer(i)
+        hd, nq, nkv = s["head_dim"], s["heads"], s["kv_heads"]
+        n = h.shape[0]
+        x = rmsnorm(h, w["input_layernorm.weight"], s["rms_eps"], s["norm_plus_one"])
+        q = x @ w["self_attn.q_proj.weight"].T
+        k = x @ w["self_attn.k_proj.weight"].T
+        v = x @ w["self_attn.v_proj.weight"].T
+        if s["qkv_bias"]:
+            q = q + w["self_attn.q_proj.bias"]
+            k = k + w["self_attn.k_proj.bias"]
+            v = v + w["self_attn.v_proj.bias"]
+        q = q.reshape(n, nq, hd)
+        k = k.reshape(n, nkv, hd)
+        v = v.reshape(n, nkv, hd)
+        if s["qk_norm"]:
+            q = rmsnorm(q, w["self_attn.q_norm.weight"], s["rms_eps"], s["norm_plus_one"])
+            k = rmsnorm(k, w["self_attn.k_norm.weight"], s["rms_eps"], s["norm_plus_one"])
+        q = apply_rope(q, cos, sin)
+        k = apply_rope(k, cos, sin)
+        a = attention(q, k, v, causal=True).reshape(n, nq * hd)
+        h = h + a @ w["self_attn.o_proj.weight"].T
+        x = rmsnorm(h, w["post_attention_layernorm.weight"], s["rms_eps"], s["norm_plus_one"])
+        g = x @ w["mlp.gate_proj.weight"].T
+        u = x @ w["mlp.up_proj.weight"].T
+        act = silu(g) if s["act"] == "silu" else gelu_tanh(g)
+        h = h + (act * u) @ w["mlp.down_proj.weight"].T
+        return h.astype(np.float32)
+
+    def hidden(self, ids: np.ndarray) -> np.ndarray:
+        """Final-norm hidden states of one sequence, [n, d] fp32."""
+        ids = np.asarray(ids, dtype=np.int64)
+        n = ids.shape[0]
+        cos, sin = rope_tables(np.arange(n), self.spec["head_dim"], self.spec["rope_theta"])
+        h = self.embed(ids)
+        for i in range(self.n_layers):
+            h = self.layer_forward(i, h, cos, sin)
+        return rmsnorm(h, self.final_norm, self.spec["rms_eps"], self.spec["norm_plus_one"])
+
+    def readout(self, ids: np.ndarray, slot: int) -> np.ndarray:
+        """Label-row logits at one slot: hs[slot] @ head_w.T, width = #labels."""
+        hs = self.hidden(ids)
+        return (hs[slot] @ self.head_w.T).astype(np.float32)
+
+    def infer(self, batch) -> np.ndarray:
+        """Raw label logits [b, width] for a `CollatedBatch` (slot = marker_pos[i*k])."""
+        out = np.empty((batch.b, len(self.label_ids)), dtype=np.float32)
+        for i, row in enumerate(batch.rows):
+            ids = batch.input_ids[i * batch.l:i * batch.l + row.real_len]
+            out[i] = self.readout(ids, int(batch.marker_pos[i * batch.k]))
+        return out
+
+
+def option_logprobs(logits: np.ndarray, nopts) -> np.ndarray:
+    """log_softmax over the first nopts[i] columns, -1e4 elsewhere (what `vd_infer` returns).
+
+    Softmax is shift-invariant, so this carries the same information the
+    reference's Rust side computes with `finish_rows` (columns >= nopts set to
+    -1e4, `src/torch_engine.rs:97-114`) and `softmax(logits / t)`
+    (`src/calibration.rs:248-253`)."""
+    logits = np.asarray(logits, dtype=np.float64)
+    out = np.full(logits.shape, -1e4, dtype=np.float64)
+    for i, k in enumerate(nopts):
+        z = logits[i, :int(k)]
+        m = z.max()
+        out[i, :int(k)] = z - m - np.log(np.exp(z - m).sum())
+    return out
