@@ -1,0 +1,394 @@
+"""Decision-forward throughput on B200: decisions/s for OneJev-9B-shaped text decisions.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: torchrun --nproc-per-node N ... bench.py --gpus N ...)
+
+A step is one forward + option readout of one batch of `--batch` (64) seeded
+synthetic decisions of the OneJev-9B-shaped workload (prompt lengths
+clip(lognormal(6, 0.7), 32, 4096), 2-8 options, slot = last token, ids
+U[3, 152064)); every step uses a different batch.  One full-weight replica per
+GPU, each rank runs its own shard of decisions: no collective on the data path
+("scaling": "weak"); ranks meet only at the barriers and the max-over-ranks
+timing reduction.
+
+Printed JSON (rank 0, one line):
+  value  decisions/s over all ranks, inputs already resident in HBM, device time
+         (CUDA events on the executor's stream), max over ranks
+  e2e    the same through the public C ABI `vd_infer` with pinned host buffers:
+         each step copies the padded batch to the device and the logits back
+  roofline  the gate/up projection GEMM (tcgen05, the largest kernel): its
+         algorithmic FLOPs per launch / its mean launch time from events around
+         each launch, against the measured sustained bf16 peak
+  cpu_baseline  the CPU oracle (fp32 numpy restatement of the reference's CPU
+         executor path) on a bounded sample, on this host's cores
+--impl reference runs that CPU implementation as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "decisions/sec (9B text, 1/2/4/8 B200); p99 latency; GEMM tensor-pipe % of peak"
+UNIT = "decisions/s"
+WORKLOAD = ("OneJev-9B-shaped text decisions: 40 layers, d=4096, 32/8 heads hd=128, SwiGLU 12288, "
+            "vocab 152064, causal varlen prefill + option log-softmax; lengths clip(lognormal(6,0.7),32,4096), "
+            "2-8 options")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM traffic of one gate/up GEMM launch from an ncu capture (profiles/gemm_gateup_onejev9b.md),
+# scaled per launch to the bench's token count; None until captured.
+GATEUP_TRAFFIC_BYTES_PER_TOKEN = None
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.path = f"/tmp/vd_clocks_{os.getpid()}.csv"
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(gpu_index)], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_batches(rank, n_batches, per_batch, vocab, seed):
+    from verdict_b200.batch import Layout, collate, decoder_rows
+    out = []
+    for j in range(n_batches):
+        rng = np.random.default_rng([seed, rank, j])
+        rows = decoder_rows(rng, per_batch, vocab, lengths="lognormal-9b")
+        out.append(collate(rows, Layout(pad_id=0)))
+    return out
+
+
+def cpu_baseline_sample(spec, batch, layers_timed):
+    """Time the oracle (fp32 numpy) on one decision through `layers_timed` of the
+    model's layers and scale to the full depth; returns (decisions/s, sample text)."""
+    from oracle.decoder import DecoderOracle, rmsnorm, rope_tables
+    orc = DecoderOracle(spec, layers=layers_timed)
+    n = int(batch.rows[0].real_len)
+    ids = batch.input_ids[:n]
+    for i in range(layers_timed):
+        orc.layer(i)  # generate weights outside the timed region
+    t0 = time.perf_counter()
+    cos, sin = rope_tables(np.arange(n), spec["head_dim"], spec["rope_theta"])
+    h = orc.embed(ids)
+    t1 = time.perf_counter()
+    for i in range(layers_timed):
+        h = orc.layer_forward(i, h, cos, sin)
+    t2 = time.perf_counter()
+    hs = rmsnorm(h[-1:], orc.final_norm, spec["rms_eps"], spec["norm_plus_one"])
+    _ = hs @ orc.head_w[: int(batch.nopts[0])].T
+    t3 = time.perf_counter()
+    per_decision = (t1 - t0) + (t2 - t1) * spec["layers"] / layers_timed + (t3 - t2)
+    sample = (f"1 decision of {n} tokens; {layers_timed} of {spec['layers']} layers timed and scaled "
+              f"to full depth (embed + readout timed once)")
+    return 1.0 / per_decision, sample, per_decision
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the CPU path of the reference executor (fp32), as the
+    oracle port, on this host's cores; rank 0 only."""
+    if rank != 0:
+        return
+    import torch  # noqa: F401  (thread settings only)
+    from verdict_b200 import spec as specs
+    from verdict_b200.synth import with_labels
+    spec = with_labels(specs.preset("onejev-9b"))
+    batches = make_batches(0, args.warmup + args.steps, 1, spec["vocab"], args.seed)
+    times = []
+    for j, b in enumerate(batches):
+        _, _, per = cpu_baseline_sample(spec, b, args.ref_layers)
+        if j >= args.warmup:
+            times.append(per)
+    mean = float(np.mean(times))
+    value = 1.0 / mean
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "model": "onejev-9b", "decisions_per_step": 1,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"per step 1 decision; {args.ref_layers} of 40 layers timed and scaled"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="decisions per step (concurrency)")
+    ap.add_argument("--layers", type=int, default=None, help="override depth (default: full 40)")
+    ap.add_argument("--seed", type=int, default=20261201)
+    ap.add_argument("--ref-layers", type=int, default=2, help="layers timed per CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    from verdict_b200 import spec as specs
+    from verdict_b200.engine import B200Engine
+    from verdict_b200.synth import with_labels
+
+    over = {} if args.layers is None else {"layers": args.layers}
+    spec = with_labels(specs.preset("onejev-9b", **over))
+    n_batches = args.warmup + args.steps
+    batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed)
+    max_tokens = max(int(b.real_len().sum()) for b in batches)
+    eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
+                     max_seq=4096)
+    width = eng.width
+    stream_ptr = eng.stream()
+    stream = torch.cuda.ExternalStream(stream_ptr)
+
+    # Device-resident inputs for every step.
+    dev = []
+    for b in batches:
+        d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(f"cuda:{local}") for k, v in dict(
+            input_ids=b.input_ids, marker_pos=b.marker_pos, marker_mask=b.marker_mask.astype(np.uint8),
+            nopts=b.nopts, qtype=b.qtype).items()}
+        dev.append(d)
+    out = torch.empty(args.batch, width, device=f"cuda:{local}", dtype=torch.float32)
+
+    def step_dev(j):
+        b = batches[j]
+        eng.infer_device(b.b, b.l, b.k, {k: v.data_ptr() for k, v in dev[j].items()}, b.real_len(),
+                         out.data_ptr(), width)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Warm-up.
+    for j in range(args.warmup):
+        step_dev(j)
+    eng.sync()
+    barrier()
+
+    # Timed region: device-resident inputs.
+    clocks = Clocks(local)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    launches = 0
+    with torch.cuda.stream(stream):
+        evs[0].record(stream)
+        for i in range(args.steps):
+            step_dev(args.warmup + i)
+            evs[i + 1].record(stream)
+    eng.sync()
+    launches = eng.last_stats()["launches"] * args.steps
+    barrier()
+    clk = clocks.stop()
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = max_over_ranks(evs[0].elapsed_time(evs[-1]))
+    p99_ms = max_over_ranks(float(np.percentile(step_ms, 99)))
+    decisions = args.batch * args.steps * world
+    value = decisions / (total_ms / 1e3)
+    tokens_per_step = float(np.mean([b.real_len().sum() for b in batches[args.warmup:]]))
+
+    # Per-kernel timing pass (events around each launch), for the roofline.
+    eng.lib.vd_set_profiling(eng.h, 1)
+    kern = {}
+    prof_steps = min(3, args.steps)
+    acc_ms = np.zeros(8)
+    acc_fl = np.zeros(8)
+    acc_n = np.zeros(8)
+    for i in range(prof_steps):
+        b = batches[args.warmup + i]
+        eng.infer_device(b.b, b.l, b.k, {k: v.data_ptr() for k, v in dev[args.warmup + i].items()}, b.real_len(),
+                         out.data_ptr(), width, sync=True)
+        st = eng.last_stats()
+        acc_ms += np.array(st["kernel_ms"][:])
+        acc_fl += np.array(st["kernel_flops"][:])
+        acc_n += np.array(st["kernel_launches"][:])
+    eng.lib.vd_set_profiling(eng.h, 0)
+    from verdict_b200._abi import KERNEL_CLASSES
+    for c, name in enumerate(KERNEL_CLASSES):
+        if acc_n[c] > 0:
+            kern[name] = {"ms_per_step": acc_ms[c] / prof_steps, "launches_per_step": acc_n[c] / prof_steps,
+                          "tflops": (acc_fl[c] / (acc_ms[c] / 1e3) / 1e12) if acc_ms[c] > 0 and acc_fl[c] > 0
+                          else None}
+    gu = 2  # VD_K_GATEUP
+    gu_launch_ms = acc_ms[gu] / acc_n[gu]
+    gu_flops = acc_fl[gu] / acc_n[gu]
+    pk, pk_kind = peaks()
+    peak = pk["bf16_tflops_sustained"]
+    achieved = gu_flops / (gu_launch_ms / 1e3) / 1e12
+    gemm_ms = acc_ms[:4].sum() / prof_steps
+    gemm_tf = acc_fl[:4].sum() / (acc_ms[:4].sum() / 1e3) / 1e12
+    roofline = {
+        "kernel": "gemm_tcgen05_kernel<256,gated> (gate/up projection)",
+        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+        "peak_source": f"{pk_kind} bf16_tflops_sustained",
+        "traffic": (GATEUP_TRAFFIC_BYTES_PER_TOKEN * tokens_per_step) if GATEUP_TRAFFIC_BYTES_PER_TOKEN else None,
+        "flops_per_launch": gu_flops, "launch_ms": gu_launch_ms,
+        "all_gemms": {"tflops": gemm_tf, "frac": gemm_tf / peak, "ms_per_step": gemm_ms},
+    }
+
+    # End to end through the C ABI with pinned host buffers.
+    e2e = None
+    if not args.no_e2e:
+        host = []
+        for b in batches:
+            pinned = {}
+            for k, v in dict(ids=b.input_ids, mpos=b.marker_pos, mmask=b.marker_mask.astype(np.uint8),
+                             nopts=b.nopts, qtype=b.qtype).items():
+                t = torch.from_numpy(np.ascontiguousarray(v)).pin_memory()
+                pinned[k] = t
+            host.append(pinned)
+        out_h = torch.empty(args.batch, width, dtype=torch.float32).pin_memory()
+
+        def step_host(j):
+            b, p = batches[j], host[j]
+            from verdict_b200._abi import VdBatch, VD_MEM_HOST
+            import ctypes
+            st = VdBatch()
+            st.b, st.l, st.k, st.memory = b.b, b.l, b.k, VD_MEM_HOST
+            st.input_ids = ctypes.c_void_p(p["ids"].data_ptr())
+            st.marker_pos = ctypes.c_void_p(p["mpos"].data_ptr())
+            st.marker_mask = ctypes.c_void_p(p["mmask"].data_ptr())
+            st.nopts = ctypes.c_void_p(p["nopts"].data_ptr())
+            st.qtype = ctypes.c_void_p(p["qtype"].data_ptr())
+            rl = b.real_len()
+            st.real_len = ctypes.c_void_p(rl.ctypes.data)
+            err = ctypes.create_string_buffer(512)
+            rc = eng.lib.vd_infer(eng.h, ctypes.byref(st), ctypes.c_void_p(out_h.data_ptr()), width, err, 512)
+            if rc != 0:
+                raise RuntimeError(err.value.decode())
+            return int(b.input_ids.nbytes + b.marker_pos.nbytes + b.b * b.k + b.nopts.nbytes + b.qtype.nbytes), \
+                int(b.b * width * 4)
+
+        for j in range(args.warmup):
+            step_host(j)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        h2d = d2h = 0
+        for i in range(args.steps):
+            bi, bo = step_host(args.warmup + i)
+            h2d += bi
+            d2h += bo
+        e1.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": decisions / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+               "d2h_bytes_per_step": d2h // args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, _ = cpu_baseline_sample(spec, batches[0], args.ref_layers)
+        cpu = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; random-init weights generated on device)",
+            "config": {"workload": WORKLOAD, "model": "onejev-9b", "layers": spec["layers"],
+                       "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
+                       "parallelism": f"replicas x{world} (one full-weight replica per GPU, no collectives)",
+                       "l2": "no flush: each step streams 15.4 GB of weights and ~0.5 GB of activations, "
+                             "far above the 126 MB L2"},
+            "e2e": e2e, "gpu_launches": int(launches), "clocks": clk, "roofline": roofline,
+            "kernels": kern, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,233 @@
+"""The whole decision forward on the GPU, through the C ABI, against the oracle.
+
+Bar (per the decision-model contract): token ids and slot / marker positions
+are consumed bit-exactly (checked by construction: the same CollatedBatch goes
+to both sides, and chunking / batching changes nothing, bit for bit);
+per-option log-probs within LOGPROB_TOL = 2e-2 absolute of the fp32 reference;
+the chosen option identical wherever the reference's top-2 margin exceeds 2e-2.
+Encoder scorer logits: within ENC_TOL absolute (the reference's own export
+check allows 1e-3 relative to max(1, |ref|), convert/compare.py:9-25).
+"""
+
+import glob
+import json
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle.decoder import DecoderOracle, option_logprobs  # noqa: E402
+from oracle.encoder import EncoderOracle  # noqa: E402
+from verdict_b200 import spec as specs  # noqa: E402
+from verdict_b200.batch import CollatedBatch, Layout, RowMeta, collate, decoder_rows, encoder_rows  # noqa: E402
+from verdict_b200.engine import B200Engine, EngineError  # noqa: E402
+from verdict_b200.synth import with_labels  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+LOGPROB_TOL = 2e-2
+MARGIN = 2e-2
+ENC_TOL = 2e-3
+
+
+def load_fixture(path):
+    z = np.load(path)
+    spec = json.loads(str(z["spec"]))
+    b, l, k = int(z["b"]), int(z["l"]), int(z["k"])
+    rows = [RowMeta(int(n), 1, 0) for n in z["real_len"]]
+    nopts = z["nopts"] if "nopts" in z.files else np.zeros(0, np.int64)
+    batch = CollatedBatch(z["input_ids"], z["attention_mask"], z["marker_pos"], z["marker_mask"], z["qtype"],
+                          nopts, b, l, k, rows)
+    return spec, batch, z["logits"]
+
+
+def engine_logprobs(engine, batch):
+    rows = engine.infer(batch)
+    return np.array([r.logits for r in rows], dtype=np.float64)
+
+
+def assert_decoder_parity(got_lp, ref_logits, nopts, tol=LOGPROB_TOL):
+    ref_lp = option_logprobs(ref_logits, nopts)
+    for i, k in enumerate(nopts):
+        k = int(k)
+        d = np.abs(got_lp[i, :k] - ref_lp[i, :k]).max()
+        assert d <= tol, f"row {i}: max |log-prob diff| {d:.3e} > {tol}"
+        assert np.all(got_lp[i, k:] == -1e4), f"row {i}: columns >= nopts must be -1e4"
+        top = np.sort(ref_lp[i, :k])[::-1]
+        if k >= 2 and top[0] - top[1] > MARGIN:
+            assert int(np.argmax(got_lp[i, :k])) == int(np.argmax(ref_lp[i, :k])), f"row {i}: choice differs"
+
+
+DECODER_FIXTURES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz")) if "_marker_" not in p)
+ENCODER_FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*_marker_*.npz")))
+
+
+@pytest.mark.parametrize("path", DECODER_FIXTURES, ids=os.path.basename)
+def test_decoder_golden(path):
+    spec, batch, ref_logits = load_fixture(path)
+    eng = B200Engine(spec, max_tokens=4096, max_rows=64, max_seq=2048)
+    try:
+        got = engine_logprobs(eng, batch)
+        assert got.shape == (batch.b, len(spec["label_ids"]))
+        assert_decoder_parity(got, ref_logits, batch.nopts)
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("path", DECODER_FIXTURES[:1], ids=os.path.basename)
+def test_decoder_golden_raw_logits(path):
+    spec, batch, ref_logits = load_fixture(path)
+    eng = B200Engine(spec, max_tokens=4096, max_rows=64, max_seq=2048, output="logits")
+    try:
+        got = engine_logprobs(eng, batch)
+        for i, k in enumerate(batch.nopts):
+            assert np.abs(got[i, :k] - ref_logits[i, :k]).max() <= LOGPROB_TOL
+            assert np.all(got[i, k:] == -1e4)
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("path", ENCODER_FIXTURES, ids=os.path.basename)
+def test_encoder_golden(path):
+    spec, batch, ref = load_fixture(path)
+    eng = B200Engine(spec, max_tokens=4096, max_rows=64, max_seq=512)
+    try:
+        got = engine_logprobs(eng, batch)
+        live = ref > -1e4
+        assert np.all(got[~live] == -1e4)
+        d = np.abs(got[live] - ref[live]).max()
+        assert d <= ENC_TOL, f"max |logit diff| {d:.3e}"
+    finally:
+        eng.close()
+
+
+def decoder_case(preset, layers, n_rows, seed, max_len, **over):
+    spec = with_labels(specs.preset(preset, layers=layers, seed=seed, **over))
+    rng = np.random.default_rng(seed)
+    kind = {"onejev-9b": "lognormal-9b", "decider-2b": "uniform-2b", "onejev-27b": "uniform-27b"}[preset]
+    rows = decoder_rows(rng, n_rows, spec["vocab"], lengths=kind)
+    for r in rows:
+        n = min(len(r.ids), max_len)
+        r.ids, r.markers = r.ids[:n], [n - 1]
+    return spec, collate(rows, Layout(pad_id=0))
+
+
+@pytest.mark.parametrize("preset,layers,n_rows,max_len", [
+    ("onejev-9b", 2, 6, 700),
+    ("decider-2b", 2, 4, 600),
+    ("onejev-27b", 1, 2, 800),
+])
+def test_decoder_shapes_vs_oracle(preset, layers, n_rows, max_len):
+    spec, batch = decoder_case(preset, layers, n_rows, seed=31, max_len=max_len)
+    ref = DecoderOracle(spec).infer(batch)
+    eng = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096)
+    try:
+        got = engine_logprobs(eng, batch)
+        assert_decoder_parity(got, ref, batch.nopts)
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("preset,lengths", [("laya-bert", "uniform-bert"), ("laya-xlmr", "lognormal-xlmr")])
+def test_encoder_full_depth_vs_oracle(preset, lengths):
+    spec = specs.preset(preset, seed=41)
+    rng = np.random.default_rng(41)
+    cls_id, sep_id = (101, 102) if preset == "laya-bert" else (0, 2)
+    rows = encoder_rows(rng, 8, spec["vocab"], lengths=lengths, cls_id=cls_id, sep_id=sep_id, id_low=5,
+                        max_len=spec["max_pos"] - 2)
+    batch = collate(rows, Layout(pad_id=spec["pad_id"]))
+    batch.qtype[:] = rng.integers(0, 3, size=batch.b)
+    ref = EncoderOracle(spec).infer(batch)
+    eng = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=512)
+    try:
+        got = engine_logprobs(eng, batch)
+        live = ref > -1e4
+        assert np.all(got[~live] == -1e4)
+        scale = max(1.0, float(np.abs(ref[live]).max()))
+        d = np.abs(got[live] - ref[live]).max() / scale
+        assert d <= ENC_TOL, f"max relative deviation {d:.3e}"
+    finally:
+        eng.close()
+
+
+def test_chunking_and_batching_are_bit_exact():
+    """Rows are independent: splitting a batch by rows (small workspace) or
+    running rows alone gives the same bits as one packed forward."""
+    spec, batch = decoder_case("onejev-9b", 2, 5, seed=7, max_len=900)
+    big = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096)
+    small = B200Engine(spec, max_tokens=1024, max_rows=2, max_seq=1024)
+    try:
+        a = engine_logprobs(big, batch)
+        b = engine_logprobs(small, batch)
+        assert small.last_stats()["chunks"] >= 3
+        np.testing.assert_array_equal(a, b)
+    finally:
+        big.close()
+        small.close()
+
+
+def test_edge_lengths_vs_oracle():
+    spec = with_labels(specs.preset("onejev-9b", layers=1, seed=5, hidden=1024, heads=8, kv_heads=2,
+                                    ffn=2048, vocab=4096))
+    rng = np.random.default_rng(5)
+    lens = [1, 2, 63, 64, 65, 127, 128, 129, 1500]
+    rows = decoder_rows(rng, len(lens), spec["vocab"], lengths="fixed:4", min_opts=1, max_opts=1)
+    for r, n, k in zip(rows, lens, [1, 2, 3, 4, 5, 6, 7, 8, 256]):
+        r.ids = rng.integers(3, spec["vocab"], size=n).tolist()
+        r.markers, r.nopts = [n - 1], [k]
+    batch = collate(rows, Layout(pad_id=0))
+    ref = DecoderOracle(spec).infer(batch)
+    eng = B200Engine(spec, max_tokens=4096, max_rows=64, max_seq=2048)
+    try:
+        got = engine_logprobs(eng, batch)
+        assert_decoder_parity(got, ref, batch.nopts)
+        assert got[0, 0] == 0.0  # one option: log-prob 0
+    finally:
+        eng.close()
+
+
+def test_bad_inputs_fail_the_batch_not_the_engine():
+    spec, batch = decoder_case("onejev-9b", 1, 2, seed=3, max_len=64, hidden=512, heads=4, kv_heads=2,
+                               ffn=1024, vocab=2048)
+    eng = B200Engine(spec, max_tokens=1024, max_rows=8, max_seq=512)
+    try:
+        bad = CollatedBatch(batch.input_ids.copy(), batch.attention_mask, batch.marker_pos, batch.marker_mask,
+                            batch.qtype, batch.nopts, batch.b, batch.l, batch.k, batch.rows)
+        bad.input_ids[0] = spec["vocab"] + 5
+        with pytest.raises(EngineError, match="token id"):
+            eng.infer(bad)
+        assert eng.health()
+        two = CollatedBatch(batch.input_ids, batch.attention_mask, np.zeros(2 * batch.b, np.int64),
+                            np.ones(2 * batch.b, bool), batch.qtype, batch.nopts, batch.b, batch.l, 2, batch.rows)
+        with pytest.raises(EngineError, match="exactly one slot per row"):
+            eng.infer(two)
+        nomark = CollatedBatch(batch.input_ids, batch.attention_mask, batch.marker_pos,
+                               np.zeros(batch.b, bool), batch.qtype, batch.nopts, batch.b, batch.l, 1, batch.rows)
+        with pytest.raises(EngineError, match="has no slot marker"):
+            eng.infer(nomark)
+        ok = engine_logprobs(eng, batch)
+        assert ok.shape[0] == batch.b and eng.health()
+        st = eng.last_stats()
+        assert st["rows"] == batch.b and st["launches"] > 0 and st["tokens"] == int(batch.real_len().sum())
+    finally:
+        eng.close()
+
+
+def test_device_resident_path_matches_host_path():
+    spec, batch = decoder_case("onejev-9b", 1, 3, seed=9, max_len=300, hidden=1024, heads=8, kv_heads=2,
+                               ffn=2048, vocab=4096)
+    eng = B200Engine(spec, max_tokens=2048, max_rows=8, max_seq=1024)
+    try:
+        host = engine_logprobs(eng, batch)
+        dev = {name: torch.from_numpy(np.ascontiguousarray(a)).cuda() for name, a in dict(
+            input_ids=batch.input_ids, marker_pos=batch.marker_pos,
+            marker_mask=batch.marker_mask.astype(np.uint8), nopts=batch.nopts, qtype=batch.qtype).items()}
+        out = torch.empty(batch.b, eng.width, device="cuda", dtype=torch.float32)
+        eng.infer_device(batch.b, batch.l, batch.k, {k: v.data_ptr() for k, v in dev.items()}, batch.real_len(),
+                         out.data_ptr(), eng.width, sync=True)
+        np.testing.assert_array_equal(out.cpu().numpy().astype(np.float64), host)
+    finally:
+        eng.close()

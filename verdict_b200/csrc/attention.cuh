@@ -1,0 +1,242 @@
+// Varlen (packed, ragged) multi-head attention for the prefill-only decision
+// forward: causal for the decoders, bidirectional for the marker-head encoders,
+// with grouped K/V heads (GQA / MQA).
+//
+// Input is the fused projection output qkv[T, ld] (bf16): head h of Q at column
+// q_col0 + h*HD, its K/V head (h / group) at k_col0 / v_col0 + (h/group)*HD.
+// Output attn[T, ld_out] at column h*HD.  Sequences are given by cu_seqlens; a
+// CTA processes one 64-row query tile of one sequence for one query head, as
+// listed in a host-built tile table (longest causal work first).
+//
+// This is the warp-level (ldmatrix + mma.sync m16n8k16) flash-attention
+// formulation: Q tile in smem, double-buffered K/V tiles via cp.async with a
+// 16-byte XOR swizzle, online softmax in registers (exp2 with the 1/sqrt(d)
+// scale folded in), fp32 accumulation.
+#pragma once
+
+#include "common.cuh"
+
+namespace vd {
+
+struct AttnTile {
+  int seq_start;  // first token of the sequence in the packed batch
+  int seq_len;
+  int q_start;    // first query row of this tile inside the sequence
+  int pad;
+};
+
+struct AttnParams {
+  const __nv_bfloat16* qkv;
+  int ld_qkv;
+  int q_col0, k_col0, v_col0;
+  __nv_bfloat16* out;
+  int ld_out;
+  const AttnTile* tiles;
+  int group;          // query heads per K/V head
+  float scale_log2;   // softmax scale * log2(e)
+};
+
+template <int HD>
+struct AttnConfig {
+  static constexpr int BM = 64, BN = 64, THREADS = 128;
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int KV_BYTES = BN * HD * 2;
+  static constexpr int SMEM_BYTES = Q_BYTES + 4 * KV_BYTES;  // Q, K[2], V[2]
+};
+
+// Byte offset of 16-byte chunk c of row r in a [rows][HD] bf16 tile.
+template <int HD>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return static_cast<uint32_t>(r * HD * 2 + ((c ^ (r & 7)) << 4));
+}
+
+template <int HD>
+__device__ __forceinline__ void load_tile_async(uint32_t s_base, const __nv_bfloat16* g, int ld, int row0,
+                                                int rows_valid, int tid) {
+  constexpr int CH = HD / 8;  // 16-byte chunks per row
+  constexpr int TOTAL = 64 * CH;
+#pragma unroll
+  for (int i = tid; i < TOTAL; i += 128) {
+    const int r = i / CH, c = i % CH;
+    const bool ok = r < rows_valid;
+    const __nv_bfloat16* src = g + static_cast<size_t>(row0 + (ok ? r : 0)) * ld + c * 8;
+    cp_async16(s_base + swz<HD>(r, c), src, ok);
+  }
+}
+
+template <int HD, bool CAUSAL>
+__global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
+  using Cfg = AttnConfig<HD>;
+  constexpr int NB = Cfg::BN / 8;   // n-blocks of S per warp (8)
+  constexpr int ND = HD / 8;        // n-blocks of O per warp
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK0 = sQ + Cfg::Q_BYTES;
+  const uint32_t sV0 = sK0 + 2 * Cfg::KV_BYTES;
+
+  const AttnTile tile = p.tiles[blockIdx.x];
+  const int head = blockIdx.y;
+  const int kvh = head / p.group;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const __nv_bfloat16* gq = p.qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.q_col0 + head * HD;
+  const __nv_bfloat16* gk = p.qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.k_col0 + kvh * HD;
+  const __nv_bfloat16* gv = p.qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.v_col0 + kvh * HD;
+
+  const int q_rows = min(Cfg::BM, tile.seq_len - tile.q_start);
+  int kv_end = tile.seq_len;
+  if (CAUSAL) kv_end = min(tile.seq_len, tile.q_start + Cfg::BM);
+  const int n_kv = (kv_end + Cfg::BN - 1) / Cfg::BN;
+
+  load_tile_async<HD>(sQ, gq, p.ld_qkv, tile.q_start, q_rows, tid);
+  load_tile_async<HD>(sK0, gk, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
+  load_tile_async<HD>(sV0, gv, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
+  cp_async_commit();
+
+  float o[ND][4];
+#pragma unroll
+  for (int i = 0; i < ND; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.0f, 0.0f};
+
+  const int q_row_a = tile.q_start + warp * 16 + (lane >> 2);  // rows of c0/c1; c2/c3 are +8
+
+  for (int j = 0; j < n_kv; ++j) {
+    const int buf = j & 1;
+    if (j + 1 < n_kv) {
+      const int kv0n = (j + 1) * Cfg::BN;
+      const uint32_t nb = (buf ^ 1) * Cfg::KV_BYTES;
+      load_tile_async<HD>(sK0 + nb, gk, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
+      load_tile_async<HD>(sV0 + nb, gv, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+
+    const uint32_t sK = sK0 + buf * Cfg::KV_BYTES;
+    const uint32_t sV = sV0 + buf * Cfg::KV_BYTES;
+    const int kv0 = j * Cfg::BN;
+
+    // S = Q K^T for this warp's 16 query rows x 64 keys.
+    float s[NB][4];
+#pragma unroll
+    for (int i = 0; i < NB; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t a[4];
+      {
+        const int r = warp * 16 + (lane & 15);
+        const int c = ks * 2 + (lane >> 4);
+        ldmatrix_x4(sQ + swz<HD>(r, c), a[0], a[1], a[2], a[3]);
+      }
+#pragma unroll
+      for (int nb2 = 0; nb2 < NB / 2; ++nb2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = ks * 2 + ((lane >> 3) & 1);
+        ldmatrix_x4(sK + swz<HD>(r, c), b0, b1, b2, b3);
+        mma_bf16_16816(s[2 * nb2], a, b0, b1);
+        mma_bf16_16816(s[2 * nb2 + 1], a, b2, b3);
+      }
+    }
+
+    // Mask keys past the sequence end and (causal) past the query row.
+    const bool need_mask = (kv0 + Cfg::BN > tile.seq_len) || (CAUSAL && kv0 + Cfg::BN > tile.q_start);
+    if (need_mask) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kv = kv0 + nb * 8 + ((lane & 3) << 1) + (e & 1);
+          const int qr = q_row_a + ((e >> 1) << 3);
+          bool dead = kv >= tile.seq_len;
+          if (CAUSAL) dead = dead || kv > qr;
+          if (dead) s[nb][e] = -INFINITY;
+        }
+      }
+    }
+
+    // Online softmax (rows r and r+8 of the warp tile; a quad of lanes shares a row).
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      mx[0] = fmaxf(mx[0], fmaxf(s[nb][0], s[nb][1]));
+      mx[1] = fmaxf(mx[1], fmaxf(s[nb][2], s[nb][3]));
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    }
+    float alpha[2], base[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float m_new = fmaxf(m_run[h], mx[h] * p.scale_log2);
+      base[h] = (m_new == -INFINITY) ? 0.0f : m_new;
+      alpha[h] = exp2f(m_run[h] - base[h]);
+      m_run[h] = m_new;
+    }
+    float rs[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      s[nb][0] = exp2f(s[nb][0] * p.scale_log2 - base[0]);
+      s[nb][1] = exp2f(s[nb][1] * p.scale_log2 - base[0]);
+      s[nb][2] = exp2f(s[nb][2] * p.scale_log2 - base[1]);
+      s[nb][3] = exp2f(s[nb][3] * p.scale_log2 - base[1]);
+      rs[0] += s[nb][0] + s[nb][1];
+      rs[1] += s[nb][2] + s[nb][3];
+    }
+    l_run[0] = l_run[0] * alpha[0] + rs[0];
+    l_run[1] = l_run[1] * alpha[1] + rs[1];
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd) {
+      o[nd][0] *= alpha[0];
+      o[nd][1] *= alpha[0];
+      o[nd][2] *= alpha[1];
+      o[nd][3] *= alpha[1];
+    }
+
+    // O += P V.
+#pragma unroll
+    for (int ks = 0; ks < Cfg::BN / 16; ++ks) {
+      uint32_t a[4];
+      a[0] = pack_bf16x2(s[2 * ks][0], s[2 * ks][1]);
+      a[1] = pack_bf16x2(s[2 * ks][2], s[2 * ks][3]);
+      a[2] = pack_bf16x2(s[2 * ks + 1][0], s[2 * ks + 1][1]);
+      a[3] = pack_bf16x2(s[2 * ks + 1][2], s[2 * ks + 1][3]);
+#pragma unroll
+      for (int nd2 = 0; nd2 < ND / 2; ++nd2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int c = nd2 * 2 + (lane >> 4);
+        ldmatrix_x4_trans(sV + swz<HD>(r, c), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * nd2], a, b0, b1);
+        mma_bf16_16816(o[2 * nd2 + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+
+  // Normalise and store rows inside the sequence.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+  const float inv0 = l_run[0] > 0.0f ? 1.0f / l_run[0] : 0.0f;
+  const float inv1 = l_run[1] > 0.0f ? 1.0f / l_run[1] : 0.0f;
+  const int r0 = warp * 16 + (lane >> 2);
+  __nv_bfloat16* out0 = p.out + static_cast<size_t>(tile.seq_start + tile.q_start + r0) * p.ld_out + head * HD;
+  __nv_bfloat16* out1 = out0 + static_cast<size_t>(8) * p.ld_out;
+  const bool ok0 = r0 < q_rows, ok1 = r0 + 8 < q_rows;
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) {
+    const int col = nd * 8 + ((lane & 3) << 1);
+    if (ok0) *reinterpret_cast<uint32_t*>(out0 + col) = pack_bf16x2(o[nd][0] * inv0, o[nd][1] * inv0);
+    if (ok1) *reinterpret_cast<uint32_t*>(out1 + col) = pack_bf16x2(o[nd][2] * inv1, o[nd][3] * inv1);
+  }
+}
+
+}  // namespace vd

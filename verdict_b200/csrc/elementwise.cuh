@@ -1,0 +1,320 @@
+// HBM-bound kernels around the GEMMs: batch packing, embedding gather, row
+// norms, and the option / marker scoring at the end of the forward.
+#pragma once
+
+#include "common.cuh"
+
+namespace vd {
+
+constexpr float kSentinel = -1e4f;  // masked option / marker slots (src/torch_engine.rs:97-114)
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (threadIdx.x < NT / 32) ? red[threadIdx.x] : 0.0f;
+  if (warp == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red[NT / 32] = t;
+  }
+  __syncthreads();
+  const float r = red[NT / 32];
+  __syncthreads();
+  return r;
+}
+
+// Right-padded [b, l] int64 ids -> packed int32 tokens, in-sequence positions and
+// sequence index per token.  Token ids outside [0, vocab) are reported and
+// replaced by 0 so no gather reads outside the table.
+__global__ void pack_tokens_kernel(const int64_t* __restrict__ ids, int64_t l, const int* __restrict__ cu, int b,
+                                   int vocab, int pos_offset, int* __restrict__ tokens, int* __restrict__ positions,
+                                   int* __restrict__ seq_id, int* err) {
+  const int row = blockIdx.y;
+  if (row >= b) return;
+  const int start = cu[row], len = cu[row + 1] - start;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < len; j += gridDim.x * blockDim.x) {
+    int64_t id = ids[static_cast<int64_t>(row) * l + j];
+    if (id < 0 || id >= vocab) {
+      record_error(err, kErrTokenRange);
+      id = 0;
+    }
+    tokens[start + j] = static_cast<int>(id);
+    positions[start + j] = j + pos_offset;
+    seq_id[start + j] = row;
+  }
+}
+
+// h[t, :] = emb[tokens[t], :] * scale (bf16 table -> fp32 residual stream).
+__global__ void embed_kernel(const int* __restrict__ tokens, int T, const __nv_bfloat16* __restrict__ emb, int d,
+                             float scale, float* __restrict__ h) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const uint4* src = reinterpret_cast<const uint4*>(emb + static_cast<size_t>(tokens[t]) * d);
+  float4* dst = reinterpret_cast<float4*>(h + static_cast<size_t>(t) * d);
+  for (int i = threadIdx.x; i < d / 8; i += blockDim.x) {
+    const uint4 v = __ldg(src + i);
+    const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), e = unpack_bf16x2(v.w);
+    dst[2 * i] = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
+    dst[2 * i + 1] = make_float4(c.x * scale, c.y * scale, e.x * scale, e.y * scale);
+  }
+}
+
+// RMSNorm of fp32 rows -> bf16: out = bf16(x * rsqrt(mean(x^2) + eps) * g),
+// g = w or (1 + w).
+template <int NT>
+__global__ void __launch_bounds__(NT) rmsnorm_kernel(const float* __restrict__ x, int d, const float* __restrict__ w,
+                                                     int plus_one, float eps, __nv_bfloat16* __restrict__ out,
+                                                     int rows) {
+  __shared__ float red[NT / 32 + 1];
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * d);
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < d / 4; i += NT) {
+    const float4 v = xr[i];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = block_sum<NT>(ss, red);
+  const float rstd = rsqrtf(ss / static_cast<float>(d) + eps);
+  const float add = plus_one ? 1.0f : 0.0f;
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * d);
+  const float4* wv = reinterpret_cast<const float4*>(w);
+  for (int i = threadIdx.x; i < d / 4; i += NT) {
+    const float4 v = xr[i];
+    const float4 g = __ldg(wv + i);
+    uint2 pk;
+    pk.x = pack_bf16x2(v.x * rstd * (g.x + add), v.y * rstd * (g.y + add));
+    pk.y = pack_bf16x2(v.z * rstd * (g.z + add), v.w * rstd * (g.w + add));
+    o[i] = pk;
+  }
+}
+
+// LayerNorm of fp32 rows: y = (x - mean) / sqrt(var + eps) * w + b.  Writes the
+// fp32 result back in place when `inplace` and always a bf16 copy to `out`.
+// With `src_rows` it gathers row src_rows[r] of x (no in-place write then) and
+// writes fp32 rows to out_f.
+template <int NT>
+__global__ void __launch_bounds__(NT)
+    layernorm_kernel(float* __restrict__ x, int d, const float* __restrict__ w, const float* __restrict__ bvec,
+                     float eps, int inplace, __nv_bfloat16* __restrict__ out, int rows) {
+  __shared__ float red[NT / 32 + 1];
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(r) * d);
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < d / 4; i += NT) {
+    const float4 v = xr[i];
+    s += v.x + v.y + v.z + v.w;
+  }
+  const float mean = block_sum<NT>(s, red) / static_cast<float>(d);
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < d / 4; i += NT) {
+    const float4 v = xr[i];
+    const float a = v.x - mean, b = v.y - mean, c = v.z - mean, e = v.w - mean;
+    ss += a * a + b * b + c * c + e * e;
+  }
+  const float rstd = rsqrtf(block_sum<NT>(ss, red) / static_cast<float>(d) + eps);
+  const float4* wv = reinterpret_cast<const float4*>(w);
+  const float4* bv = reinterpret_cast<const float4*>(bvec);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * d);
+  for (int i = threadIdx.x; i < d / 4; i += NT) {
+    float4 v = xr[i];
+    const float4 g = __ldg(wv + i), bb = __ldg(bv + i);
+    v.x = (v.x - mean) * rstd * g.x + bb.x;
+    v.y = (v.y - mean) * rstd * g.y + bb.y;
+    v.z = (v.z - mean) * rstd * g.z + bb.z;
+    v.w = (v.w - mean) * rstd * g.w + bb.w;
+    if (inplace) xr[i] = v;
+    uint2 pk;
+    pk.x = pack_bf16x2(v.x, v.y);
+    pk.y = pack_bf16x2(v.z, v.w);
+    o[i] = pk;
+  }
+}
+
+// Encoder embeddings: h = LN(word[tok] + pos[p] + type[0]); fp32 h and bf16 copy.
+template <int NT>
+__global__ void __launch_bounds__(NT)
+    embed_ln_kernel(const int* __restrict__ tokens, const int* __restrict__ positions, int T,
+                    const __nv_bfloat16* __restrict__ word, const __nv_bfloat16* __restrict__ pos_emb,
+                    const __nv_bfloat16* __restrict__ type0, int d, const float* __restrict__ w,
+                    const float* __restrict__ bvec, float eps, float* __restrict__ h,
+                    __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const __nv_bfloat16* a = word + static_cast<size_t>(tokens[t]) * d;
+  const __nv_bfloat16* p = pos_emb + static_cast<size_t>(positions[t]) * d;
+  float* hr = h + static_cast<size_t>(t) * d;
+  for (int i = threadIdx.x; i < d; i += NT)
+    hr[i] = __bfloat162float(a[i]) + __bfloat162float(p[i]) + __bfloat162float(type0[i]);
+  __syncthreads();
+  // Reuse the LayerNorm body on this single row.
+  __shared__ float red[NT / 32 + 1];
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < d; i += NT) s += hr[i];
+  const float mean = block_sum<NT>(s, red) / static_cast<float>(d);
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < d; i += NT) {
+    const float c = hr[i] - mean;
+    ss += c * c;
+  }
+  const float rstd = rsqrtf(block_sum<NT>(ss, red) / static_cast<float>(d) + eps);
+  for (int i = threadIdx.x; i < d; i += NT) {
+    const float v = (hr[i] - mean) * rstd * w[i] + bvec[i];
+    hr[i] = v;
+    out[static_cast<size_t>(t) * d + i] = __float2bfloat16_rn(v);
+  }
+}
+
+// h[t, :] += table[qtype[seq_id[t]], :] (the decision head's question-type embedding).
+__global__ void add_type_kernel(float* __restrict__ h, int T, int d, const int* __restrict__ seq_id,
+                                const int64_t* __restrict__ qtype, const __nv_bfloat16* __restrict__ table,
+                                int n_types, int* err) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  int64_t q = qtype ? qtype[seq_id[t]] : 0;
+  if (q < 0 || q >= n_types) {
+    record_error(err, kErrTokenRange);
+    q = 0;
+  }
+  const __nv_bfloat16* e = table + static_cast<size_t>(q) * d;
+  float* hr = h + static_cast<size_t>(t) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] += __bfloat162float(e[i]);
+}
+
+// Decoder readout, one CTA per row: final RMSNorm of the slot token's hidden
+// state, dot products with the first n option-label rows of the LM head (fp32,
+// as `hs[slot].float() @ head_w.T`), then either the log-softmax restricted to
+// the n options or the raw logits; columns >= n are -1e4.
+template <int NT>
+__global__ void __launch_bounds__(NT)
+    readout_kernel(const float* __restrict__ h, int d, const int* __restrict__ cu,
+                   const int64_t* __restrict__ marker_pos, int k, const int64_t* __restrict__ nopts,
+                   const float* __restrict__ norm_w, int plus_one, float eps, const float* __restrict__ head,
+                   int n_labels, float* __restrict__ out, int width, int logprobs, int* err) {
+  extern __shared__ float sm[];
+  float* xs = sm;                 // [d]
+  float* lg = sm + d;             // [n_labels]
+  __shared__ float red[NT / 32 + 1];
+  const int i = blockIdx.x;
+  const int start = cu[i], len = cu[i + 1] - start;
+  const int64_t slot = marker_pos[static_cast<int64_t>(i) * k];
+  int n = nopts ? static_cast<int>(nopts[i]) : n_labels;
+  n = max(0, min(n, min(n_labels, width)));
+  float* orow = out + static_cast<size_t>(i) * width;
+  if (slot < 0 || slot >= len) {
+    if (threadIdx.x == 0) record_error(err, kErrSlotRange);
+    for (int j = threadIdx.x; j < width; j += NT) orow[j] = kSentinel;
+    return;
+  }
+  const float* x = h + static_cast<size_t>(start + slot) * d;
+  float ss = 0.0f;
+  for (int j = threadIdx.x; j < d; j += NT) {
+    const float v = x[j];
+    xs[j] = v;
+    ss += v * v;
+  }
+  const float rstd = rsqrtf(block_sum<NT>(ss, red) / static_cast<float>(d) + eps);
+  const float add = plus_one ? 1.0f : 0.0f;
+  for (int j = threadIdx.x; j < d; j += NT) xs[j] = xs[j] * rstd * (norm_w[j] + add);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int o = warp; o < n; o += NT / 32) {
+    const float* hr = head + static_cast<size_t>(o) * d;
+    float acc = 0.0f;
+    for (int j = lane * 4; j < d; j += 128) {
+      const float4 a = *reinterpret_cast<const float4*>(xs + j);
+      const float4 b = __ldg(reinterpret_cast<const float4*>(hr + j));
+      acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+    if (lane == 0) lg[o] = acc;
+  }
+  __syncthreads();
+  float shift = 0.0f;
+  if (logprobs && n > 0) {
+    if (threadIdx.x < 32) {
+      float m = -INFINITY;
+      for (int j = lane; j < n; j += 32) m = fmaxf(m, lg[j]);
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+      float e = 0.0f;
+      for (int j = lane; j < n; j += 32) e += expf(lg[j] - m);
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) e += __shfl_xor_sync(0xffffffffu, e, s);
+      if (lane == 0) red[0] = m + logf(e);
+    }
+    __syncthreads();
+    shift = red[0];
+  }
+  for (int j = threadIdx.x; j < width; j += NT) orow[j] = j < n ? lg[j] - shift : kSentinel;
+}
+
+// Encoder markers: flat token index of every (row, slot) pair, clamped like
+// `marker_pos.clamp(min=0)`; a live marker outside its row is an input error.
+__global__ void marker_index_kernel(const int* __restrict__ cu, const int64_t* __restrict__ marker_pos,
+                                    const uint8_t* __restrict__ marker_mask, int b, int k, int* __restrict__ idx,
+                                    int* err) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= b * k) return;
+  const int i = q / k;
+  const int start = cu[i], len = cu[i + 1] - start;
+  int64_t p = marker_pos[q];
+  const bool live = marker_mask[q] != 0;
+  if (live && (p < 0 || p >= len)) record_error(err, kErrSlotRange);
+  p = p < 0 ? 0 : (p >= len ? len - 1 : p);
+  idx[q] = start + static_cast<int>(p);
+}
+
+// Gather + LayerNorm of marker rows -> bf16 scorer input.
+template <int NT>
+__global__ void __launch_bounds__(NT)
+    gather_layernorm_kernel(const float* __restrict__ h, const int* __restrict__ idx, int n, int d,
+                            const float* __restrict__ w, const float* __restrict__ bvec, float eps,
+                            __nv_bfloat16* __restrict__ out) {
+  __shared__ float red[NT / 32 + 1];
+  const int r = blockIdx.x;
+  if (r >= n) return;
+  const float* x = h + static_cast<size_t>(idx[r]) * d;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < d; i += NT) s += x[i];
+  const float mean = block_sum<NT>(s, red) / static_cast<float>(d);
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < d; i += NT) {
+    const float c = x[i] - mean;
+    ss += c * c;
+  }
+  const float rstd = rsqrtf(block_sum<NT>(ss, red) / static_cast<float>(d) + eps);
+  for (int i = threadIdx.x; i < d; i += NT)
+    out[static_cast<size_t>(r) * d + i] = __float2bfloat16_rn((x[i] - mean) * rstd * w[i] + bvec[i]);
+}
+
+// Final scorer projection Linear(d, 1) on the GELU'd rows, then the marker mask:
+// out[i, j] = y[i*k + j] . w + b for live markers, -1e4 otherwise; columns
+// j >= k of a wider output are -1e4.
+__global__ void marker_score_kernel(const __nv_bfloat16* __restrict__ y, int d, const float* __restrict__ w,
+                                    const float* __restrict__ bias, const uint8_t* __restrict__ marker_mask, int b,
+                                    int k, float* __restrict__ out, int width) {
+  const int i = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int j = warp; j < width; j += nw) {
+    float acc = 0.0f;
+    if (j < k && marker_mask[i * k + j]) {
+      const __nv_bfloat16* yr = y + static_cast<size_t>(i * k + j) * d;
+      for (int c = lane; c < d; c += 32) acc += __bfloat162float(yr[c]) * w[c];
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+      acc += bias[0];
+    } else {
+      acc = kSentinel;
+    }
+    if (lane == 0) out[static_cast<size_t>(i) * width + j] = acc;
+  }
+}
+
+}  // namespace vd

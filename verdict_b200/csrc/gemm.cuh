@@ -1,0 +1,415 @@
+// Persistent tcgen05 GEMM for sm_100a: C[M, N] = A[M, K] * W[N, K]^T, bf16 in,
+// fp32 accumulate in tensor memory, with the layer's elementwise work fused
+// into the epilogue.
+//
+// CTA layout (192 threads, one CTA per SM):
+//   warp 0      : TMA producer (one elected lane) - A and W tiles, 128-byte swizzle
+//   warp 1      : TMEM allocator + MMA issuer (one lane issues tcgen05.mma)
+//   warps 2..5  : epilogue - each warp drains the 32 TMEM lanes it may access
+//                 (lanes 32*(warp%4) .. +31), one accumulator row per thread.
+// Tiles are BM=128 x BN (128 or 256) x BK=64; a STAGES-deep smem ring feeds the
+// MMA warp, and two TMEM accumulators (2*BN columns) let the epilogue of tile i
+// overlap the MMAs of tile i+1.  Tiles are visited in groups of 16 M-tiles so the
+// ~148 tiles in flight share A row-blocks and W column-blocks in L2.
+//
+// Epilogues:
+//   kEpiStore     : out_bf16 = act(acc + bias)
+//   kEpiResidual  : out_f32 += acc + bias                (residual stream in fp32)
+//   kEpiGated     : out_bf16[:, n/2 + j] = act(acc[:, j]) * acc[:, BN/2 + j]
+//                   (W rows are interleaved at load time in blocks of BN/2: gate, up)
+//   kEpiQKRope    : per attention head of the tile: optional bias, optional
+//                   q/k RMSNorm over the head, rotary embedding for q and k
+//                   heads; v heads are stored as they are.
+#pragma once
+
+#include "common.cuh"
+
+namespace vd {
+
+enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiGated = 2, kEpiQKRope = 3 };
+enum ActKind : int { kActNone = 0, kActGeluErf = 1, kActGeluTanh = 2, kActRelu = 3, kActSilu = 4 };
+
+struct EpiParams {
+  void* out;              // bf16 (store / gated / qkrope) or fp32 (residual)
+  int ld_out;             // row stride of out, elements
+  const float* bias;      // [N] or null
+  int act;                // ActKind
+  // kEpiQKRope
+  const float* q_norm;    // [head_dim] gains (null: no q/k norm)
+  const float* k_norm;
+  int q_cols, k_cols;     // heads*head_dim, kv_heads*head_dim
+  int head_dim;
+  int plus_one;           // gain applied as (1 + w)
+  float eps;
+  const int* positions;   // [M] token position inside its sequence
+  const float2* rope;     // [max_pos][head_dim/2] (cos, sin)
+};
+
+struct GemmShape {
+  int M, N, K;
+};
+
+__device__ __forceinline__ float apply_act(float x, int act) {
+  switch (act) {
+    case kActGeluErf: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    case kActGeluTanh: {
+      const float c = 0.7978845608028654f;  // sqrt(2/pi)
+      return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+    }
+    case kActRelu: return fmaxf(x, 0.0f);
+    case kActSilu: return x / (1.0f + expf(-x));
+    default: return x;
+  }
+}
+
+__device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    d[q] = w;
+  }
+}
+
+__device__ __forceinline__ void add_bias32(float (&v)[32], const float* bias, int col) {
+  if (bias == nullptr) return;
+  const float4* b = reinterpret_cast<const float4*>(bias + col);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float4 t = __ldg(b + q);
+    v[q * 4 + 0] += t.x;
+    v[q * 4 + 1] += t.y;
+    v[q * 4 + 2] += t.z;
+    v[q * 4 + 3] += t.w;
+  }
+}
+
+// One head of kEpiQKRope: columns [col0, col0 + hd) of row `row`, TMEM at tbase.
+template <int HD>
+__device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_ok, int col0, const EpiParams& p,
+                                              const float* gain) {
+  constexpr int HALF = HD / 2;
+  constexpr int CHUNKS = HALF / 32;
+  float rstd = 1.0f;
+  if (gain != nullptr) {
+    float ss = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < HD / 32; ++c) {
+      float v[32];
+      tmem_load_f32x32(tbase + c * 32, v);
+      add_bias32(v, p.bias, col0 + c * 32);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
+    }
+    rstd = rsqrtf(ss / static_cast<float>(HD) + p.eps);
+  }
+  const int pos = row_ok ? __ldg(p.positions + row) : 0;
+  const float2* rope = p.rope + static_cast<size_t>(pos) * HALF;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out;
+#pragma unroll 1
+  for (int c = 0; c < CHUNKS; ++c) {
+    float x1[32], x2[32];
+    tmem_load_f32x32(tbase + c * 32, x1);
+    tmem_load_f32x32(tbase + HALF + c * 32, x2);
+    add_bias32(x1, p.bias, col0 + c * 32);
+    add_bias32(x2, p.bias, col0 + HALF + c * 32);
+    if (gain != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float g1 = __ldg(gain + c * 32 + j), g2 = __ldg(gain + HALF + c * 32 + j);
+        if (p.plus_one) {
+          g1 += 1.0f;
+          g2 += 1.0f;
+        }
+        x1[j] = x1[j] * rstd * g1;
+        x2[j] = x2[j] * rstd * g2;
+      }
+    }
+    if (row_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float2 cs = __ldg(rope + c * 32 + j);
+        const float a = x1[j], b = x2[j];
+        x1[j] = a * cs.x - b * cs.y;
+        x2[j] = b * cs.x + a * cs.y;
+      }
+      store_bf16x32(out + col0 + c * 32, x1);
+      store_bf16x32(out + col0 + HALF + c * 32, x2);
+    }
+  }
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_ok, int n0, const EpiParams& p) {
+  if constexpr (EPI == kEpiStore) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_load_f32x32(taddr + c * 32, v);
+      add_bias32(v, p.bias, n0 + c * 32);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], p.act);
+      if (row_ok)
+        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 + c * 32, v);
+    }
+  } else if constexpr (EPI == kEpiResidual) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_load_f32x32(taddr + c * 32, v);
+      add_bias32(v, p.bias, n0 + c * 32);
+      if (row_ok) {
+        float4* h = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(row) * p.ld_out +
+                                              n0 + c * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 t = h[q];
+          t.x += v[q * 4 + 0];
+          t.y += v[q * 4 + 1];
+          t.z += v[q * 4 + 2];
+          t.w += v[q * 4 + 3];
+          h[q] = t;
+        }
+      }
+    }
+  } else if constexpr (EPI == kEpiGated) {
+    constexpr int HALF = BN / 2;
+#pragma unroll 1
+    for (int c = 0; c < HALF / 32; ++c) {
+      float g[32], u[32];
+      tmem_load_f32x32(taddr + c * 32, g);
+      tmem_load_f32x32(taddr + HALF + c * 32, u);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) g[j] = apply_act(g[j], p.act) * u[j];
+      if (row_ok)
+        store_bf16x32(
+            reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 / 2 + c * 32, g);
+    }
+  } else if constexpr (EPI == kEpiQKRope) {
+    // One or two heads per tile (head_dim 256 or 128); heads never straddle tiles.
+    if (p.head_dim == 128) {
+#pragma unroll 1
+      for (int h = 0; h < BN / 128; ++h) {
+        const int col0 = n0 + h * 128;
+        const uint32_t tb = taddr + h * 128;
+        if (col0 < p.q_cols + p.k_cols) {
+          epi_head_rope<128>(tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_load_f32x32(tb + c * 32, v);
+            add_bias32(v, p.bias, col0 + c * 32);
+            if (row_ok)
+              store_bf16x32(
+                  reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
+          }
+        }
+      }
+    } else if constexpr (BN == 256) {
+      const int col0 = n0;
+      if (col0 < p.q_cols + p.k_cols) {
+        epi_head_rope<256>(taddr, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float v[32];
+          tmem_load_f32x32(taddr + c * 32, v);
+          add_bias32(v, p.bias, col0 + c * 32);
+          if (row_ok)
+            store_bf16x32(
+                reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
+        }
+      }
+    }
+  }
+}
+
+template <int BN>
+struct GemmConfig {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 192;
+  static constexpr int GROUP_M = 16;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& m, int& n) {
+  const int group_size = group_m * num_n;
+  const int g = tile / group_size;
+  const int first_m = g * group_m;
+  const int gm = min(num_m - first_m, group_m);
+  const int local = tile - g * group_size;
+  m = first_m + local % gm;
+  n = local / gm;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmShape shape, EpiParams ep, int* err) {
+  using Cfg = GemmConfig<BN>;
+  constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&acc_full[j], 1);
+      mbar_init(&acc_empty[j], 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (shape.M + BM - 1) / BM;
+  const int num_n = shape.N / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = shape.K / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        int m, n;
+        tile_coords(tile, num_m, num_n, Cfg::GROUP_M, m, n);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * BK, m * BM);
+          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * BK, n * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: wait until the MMA warp released every stage we filled, so no TMA
+      // write can land after the CTA exits.
+      for (int i = 0; i < STAGES; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32), IDESC,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // Epilogue warps 2..5.
+    const int lane_group = warp & 3;
+    const int row_in_tile = lane_group * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      int m, n;
+      tile_coords(tile, num_m, num_n, Cfg::GROUP_M, m, n);
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
+      const int row = m * BM + row_in_tile;
+      gemm_epilogue<BN, EPI>(taddr, row, row < shape.M, n * BN, ep);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace vd

@@ -1,0 +1,64 @@
+// On-GPU generation of the synthetic checkpoints (random-init weights from a
+// seed).  Element i of a tensor is a pure function of (tensor base, i); the
+// host generator in verdict_b200/synth.py evaluates the same function, and both
+// round the same fp32 value to bf16 (ties to even), so the CUDA forward and the
+// CPU oracle read bit-identical weights.
+#pragma once
+
+#include "common.cuh"
+
+namespace vd {
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// fp32 value before bf16 rounding; every operation rounds exactly once (no FMA
+// contraction) so the host generator reproduces it bit for bit.
+__device__ __forceinline__ __nv_bfloat16 synth_bf16(uint64_t base, uint64_t i, float scale, float offset) {
+  const uint64_t z = splitmix64(base + i);
+  const float u = static_cast<float>(static_cast<uint32_t>(z >> 40)) * 5.9604644775390625e-08f;  // 2^-24
+  float v = __fmul_rn(__fsub_rn(__fmul_rn(u, 2.0f), 1.0f), scale);
+  v = __fadd_rn(v, offset);
+  return __float2bfloat16_rn(v);
+}
+
+// Rows r of a [n_rows, cols] source tensor land at destination row
+// (r / group) * dst_group_stride + (r % group) + dst_row_off of a row-major
+// [*, cols] bf16 matrix.  group = n_rows with stride 0 is a plain copy; group 128
+// with stride 256 interleaves gate/up blocks for the fused gated-MLP GEMM.
+__global__ void synth_rows_bf16_kernel(__nv_bfloat16* __restrict__ dst, int64_t n_rows, int64_t cols, uint64_t base,
+                                       float scale, float offset, int64_t group, int64_t dst_group_stride,
+                                       int64_t dst_row_off) {
+  const int64_t total = n_rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const int64_t dr = (r / group) * dst_group_stride + (r % group) + dst_row_off;
+    dst[dr * cols + c] = synth_bf16(base, static_cast<uint64_t>(i), scale, offset);
+  }
+}
+
+// A 1-D tensor as fp32 (bf16-valued), e.g. norm gains and biases.
+__global__ void synth_f32_kernel(float* __restrict__ dst, int64_t n, uint64_t base, float scale, float offset) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = __bfloat162float(synth_bf16(base, static_cast<uint64_t>(i), scale, offset));
+}
+
+// Selected rows of a [*, cols] tensor as fp32 (the option-label rows of the LM head).
+__global__ void synth_rows_gather_f32_kernel(float* __restrict__ dst, const int* __restrict__ rows, int n_rows,
+                                             int64_t cols, uint64_t base, float scale, float offset) {
+  const int64_t total = static_cast<int64_t>(n_rows) * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const uint64_t src = static_cast<uint64_t>(rows[r]) * static_cast<uint64_t>(cols) + static_cast<uint64_t>(c);
+    dst[i] = __bfloat162float(synth_bf16(base, src, scale, offset));
+  }
+}
+
+}  // namespace vd

@@ -1,0 +1,1167 @@
+// vdexec runtime: model load, workspaces, forward scheduling and the C ABI.
+//
+// One handle = one model replica pinned to one GPU (the reference never pins a
+// replica to a device, src/main.rs:60-67; here vd_open selects it).  A batch
+// arrives as the scheduler's right-padded CollatedBatch; the runtime computes the
+// ragged layout (cu_seqlens, attention tile table) on the host, packs tokens on
+// the device and runs the whole prefill forward as a fixed sequence of kernels
+// on the handle's stream:
+//   decoder: pack -> embed -> L x [RMSNorm, QKV GEMM (+q/k norm, RoPE),
+//            attention, O GEMM (+residual), RMSNorm, gate/up GEMM (+act*up),
+//            down GEMM (+residual)] -> slot readout (final norm, label rows,
+//            restricted log-softmax)
+//   encoder: pack -> embed+LN -> L x [QKV GEMM (+bias), attention, O GEMM
+//            (+bias, residual), LN, FFN GEMM (+bias, GELU), FFN GEMM (+bias,
+//            residual), LN] -> +type -> head layers (pre-LN, ReLU) -> marker
+//            gather + scorer.
+// Batches with more real tokens than the workspace holds are split by rows.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <type_traits>
+#include <vector>
+
+#include "vdexec.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "elementwise.cuh"
+#include "gemm.cuh"
+#include "json.hpp"
+#include "synth.cuh"
+
+namespace vd {
+
+using bf16 = __nv_bfloat16;
+
+struct VdError {
+  int code;
+  std::string msg;
+};
+
+[[noreturn]] static void fail(int code, const std::string& msg) { throw VdError{code, msg}; }
+
+static void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(VD_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// Model spec
+// ---------------------------------------------------------------------------
+struct ModelSpec {
+  std::string arch, style, family;
+  int hidden = 0, layers = 0, heads = 0, kv_heads = 0, head_dim = 0, ffn = 0, vocab = 0;
+  double rms_eps = 1e-6, rope_theta = 1e6, init_std = 0.02, ln_eps = 1e-12;
+  bool qk_norm = false, qkv_bias = false, tied = false, embed_scale = false, norm_plus_one = false;
+  int act = kActSilu;
+  uint64_t seed = 0;
+  std::vector<int> label_ids;
+  int max_pos = 512, type_vocab = 2, pad_id = 0, head_layers = 2;
+
+  bool decoder() const { return arch == "decoder"; }
+  int qkv_width() const { return (heads + 2 * kv_heads) * head_dim; }
+};
+
+static ModelSpec parse_spec(const Json& j) {
+  ModelSpec s;
+  s.arch = j.string_or("arch", "decoder");
+  s.style = j.string_or("style", s.arch == "decoder" ? "qwen3" : "bert");
+  s.hidden = static_cast<int>(j.integer("hidden"));
+  s.layers = static_cast<int>(j.integer("layers"));
+  s.heads = static_cast<int>(j.integer("heads"));
+  s.ffn = static_cast<int>(j.integer("ffn"));
+  s.vocab = static_cast<int>(j.integer("vocab"));
+  s.seed = static_cast<uint64_t>(j.integer_or("seed", 0));
+  s.init_std = j.number_or("init_std", 0.02);
+  if (s.decoder()) {
+    s.family = j.string_or("family", "letter_branches");
+    s.kv_heads = static_cast<int>(j.integer("kv_heads"));
+    s.head_dim = static_cast<int>(j.integer("head_dim"));
+    s.rms_eps = j.number_or("rms_eps", 1e-6);
+    s.rope_theta = j.number_or("rope_theta", 1e6);
+    s.qk_norm = j.boolean_or("qk_norm", s.style == "qwen3");
+    s.qkv_bias = j.boolean_or("qkv_bias", s.style == "qwen2");
+    s.tied = j.boolean_or("tied", false);
+    s.embed_scale = j.boolean_or("embed_scale", false);
+    s.norm_plus_one = j.boolean_or("norm_plus_one", false);
+    const std::string act = j.string_or("act", "silu");
+    if (act == "silu") s.act = kActSilu;
+    else if (act == "gelu_tanh") s.act = kActGeluTanh;
+    else fail(VD_ESPEC, "unsupported decoder activation " + act);
+    if (!j.has("label_ids") || j.at("label_ids").kind != Json::Array)
+      fail(VD_ESPEC, "decoder spec needs the option-label table \"label_ids\"");
+    for (const Json& v : j.at("label_ids").arr) s.label_ids.push_back(static_cast<int>(v.num));
+  } else {
+    s.family = j.string_or("family", "marker_head");
+    s.kv_heads = s.heads;
+    s.head_dim = s.hidden / s.heads;
+    s.max_pos = static_cast<int>(j.integer_or("max_pos", 512));
+    s.type_vocab = static_cast<int>(j.integer_or("type_vocab", 2));
+    s.pad_id = static_cast<int>(j.integer_or("pad_id", 0));
+    s.head_layers = static_cast<int>(j.integer_or("head_layers", 2));
+    s.ln_eps = j.number_or("ln_eps", 1e-12);
+  }
+  return s;
+}
+
+static void validate_spec(const ModelSpec& s) {
+  auto need = [](bool ok, const std::string& why) {
+    if (!ok) fail(VD_ESPEC, why);
+  };
+  need(s.hidden > 0 && s.hidden % 128 == 0, "hidden must be a positive multiple of 128");
+  need(s.layers > 0 && s.heads > 0, "layers and heads must be positive");
+  need(s.ffn % 128 == 0, "ffn must be a multiple of 128");
+  if (s.decoder()) {
+    need(s.style == "qwen3" || s.style == "qwen2" || s.style == "gemma", "decoder style must be qwen3/qwen2/gemma");
+    need(s.head_dim == 128 || s.head_dim == 256, "decoder head_dim must be 128 or 256");
+    need(s.kv_heads > 0 && s.heads % s.kv_heads == 0, "heads must be a multiple of kv_heads");
+    need((s.heads * s.head_dim) % 128 == 0, "heads*head_dim must be a multiple of 128");
+    need(s.head_dim == 128 || (s.heads * s.head_dim) % 256 == 0, "head_dim 256 needs 256-aligned q/k/v blocks");
+    need(!s.label_ids.empty(), "empty label table");
+    for (int id : s.label_ids) need(id >= 0 && id < s.vocab, "label id outside the vocabulary");
+  } else {
+    need(s.style == "bert" || s.style == "xlmr", "encoder style must be bert or xlmr");
+    need(s.hidden % s.heads == 0 && s.hidden / s.heads == 64, "encoder head size must be 64");
+    need(s.hidden % 64 == 0, "encoder hidden must be a multiple of 64");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Synthetic checkpoint naming (matches verdict_b200/synth.py)
+// ---------------------------------------------------------------------------
+static uint64_t fnv1a64(const std::string& s) {
+  uint64_t h = 0xCBF29CE484222325ull;
+  for (unsigned char c : s) {
+    h ^= c;
+    h *= 0x100000001B3ull;
+  }
+  return h;
+}
+static uint64_t tensor_base(uint64_t seed, const std::string& name) {
+  return fnv1a64(name) ^ (seed * 0x9E3779B97F4A7C15ull);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor maps
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) fail(VD_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return fn;
+}
+
+// Row-major [rows, cols] bf16 matrix, box = [box_rows, 64] with 128-byte swizzle.
+static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(VD_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+  return m;
+}
+
+// ---------------------------------------------------------------------------
+// Weights
+// ---------------------------------------------------------------------------
+struct Linear {
+  bf16* w = nullptr;    // [n, k]
+  float* b = nullptr;   // [n] or null
+  int n = 0, k = 0, bn = 256;
+  CUtensorMap map;
+};
+
+struct DecLayer {
+  float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  Linear qkv, o, gu, down;
+};
+
+struct EncLayer {
+  Linear qkv, o, f1, f2;
+  float *ln1_w = nullptr, *ln1_b = nullptr, *ln2_w = nullptr, *ln2_b = nullptr;
+  bool pre_norm = false;
+  int act = kActGeluErf;
+  float eps = 1e-12f;
+};
+
+struct Handle;
+
+struct Options {
+  int64_t max_tokens = 65536, max_rows = 512, max_seq = 8192, max_markers = 16384;
+  bool logprobs = true;
+};
+
+}  // namespace vd
+
+struct vd_handle {
+  std::mutex mu;
+  int device = 0;
+  vd::ModelSpec spec;
+  vd::Options opt;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  std::atomic<bool> healthy{true};
+  std::string dead_reason;
+  std::vector<void*> allocations;
+  // decoder weights
+  __nv_bfloat16* embed = nullptr;
+  float* final_norm = nullptr;
+  float* head_rows = nullptr;
+  int n_labels = 0;
+  std::vector<vd::DecLayer> dec;
+  // encoder weights
+  __nv_bfloat16 *pos_emb = nullptr, *type_emb0 = nullptr, *qtype_emb = nullptr;
+  float *emb_ln_w = nullptr, *emb_ln_b = nullptr;
+  std::vector<vd::EncLayer> enc, head;
+  float *sc_ln_w = nullptr, *sc_ln_b = nullptr, *sc_w3 = nullptr, *sc_b3 = nullptr;
+  vd::Linear sc1;
+  // workspace
+  float* h = nullptr;
+  __nv_bfloat16 *xn = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *mrow = nullptr, *mhid = nullptr;
+  int *tokens = nullptr, *positions = nullptr, *seq_id = nullptr, *cu = nullptr, *midx = nullptr, *d_err = nullptr;
+  vd::AttnTile* tiles = nullptr;
+  int64_t max_tiles = 0;
+  float2* rope = nullptr;
+  CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow;
+  // device copies of host batches
+  int64_t *in_ids = nullptr, *in_mpos = nullptr, *in_nopts = nullptr, *in_qtype = nullptr;
+  uint8_t* in_mmask = nullptr;
+  float* out_dev = nullptr;
+  int64_t out_cap = 0, cap_ids = 0, cap_markers = 0, cap_markers_mask = 0, cap_rows = 0, cap_rows_q = 0;
+  // pinned staging ring for per-chunk metadata
+  static constexpr int kSlots = 4;
+  char* pinned[kSlots] = {};
+  cudaEvent_t slot_ev[kSlots] = {};
+  int slot = 0;
+  size_t pinned_bytes = 0;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev_user = nullptr;
+  vd_stats stats{};
+  int64_t launches = 0;
+  // per-kernel event timing (vd_set_profiling)
+  bool profiling = false;
+  struct ProfRec {
+    int kind;
+    cudaEvent_t a, b;
+  };
+  std::vector<cudaEvent_t> prof_pool;
+  size_t prof_next = 0;
+  std::vector<ProfRec> prof;
+};
+
+namespace vd {
+
+template <class T>
+static T* dalloc(vd_handle* H, size_t count) {
+  void* p = nullptr;
+  if (count == 0) count = 1;
+  cudaError_t e = cudaMalloc(&p, count * sizeof(T));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    fail(VD_ENOMEM, "cudaMalloc of " + std::to_string(count * sizeof(T)) + " bytes failed: " + cudaGetErrorString(e));
+  }
+  H->allocations.push_back(p);
+  return static_cast<T*>(p);
+}
+
+static cudaEvent_t prof_event(vd_handle* H) {
+  if (H->prof_next == H->prof_pool.size()) {
+    cudaEvent_t e;
+    cuda_check(cudaEventCreate(&e), "profiling event");
+    H->prof_pool.push_back(e);
+  }
+  return H->prof_pool[H->prof_next++];
+}
+
+// Every forward kernel goes through here: counts launches and algorithmic FLOPs
+// per kernel class and, with profiling on, brackets the launch with events.
+template <class F>
+static void launch(vd_handle* H, int kind, double flops, F&& f) {
+  cudaEvent_t a = nullptr;
+  if (H->profiling) {
+    a = prof_event(H);
+    cuda_check(cudaEventRecord(a, H->stream), "profiling event");
+  }
+  f();
+  ++H->launches;
+  H->stats.kernel_launches[kind] += 1;
+  H->stats.kernel_flops[kind] += flops;
+  if (H->profiling) {
+    cudaEvent_t b = prof_event(H);
+    cuda_check(cudaEventRecord(b, H->stream), "profiling event");
+    H->prof.push_back(vd_handle::ProfRec{kind, a, b});
+  }
+}
+
+// After a synchronize: fold the recorded event pairs into per-class times.
+static void prof_collect(vd_handle* H) {
+  for (const auto& r : H->prof) {
+    float ms = 0;
+    if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) H->stats.kernel_ms[r.kind] += ms;
+  }
+  H->prof.clear();
+  H->prof_next = 0;
+}
+
+static int grid_for(int64_t n) { return static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16)); }
+
+static void synth_bf16(vd_handle* H, bf16* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
+                       float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
+  if (group == 0) group = rows;
+  synth_rows_bf16_kernel<<<grid_for(rows * cols), 256, 0, H->stream>>>(
+      dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, group, stride, off);
+}
+static void synth_f32(vd_handle* H, float* dst, const std::string& name, int64_t n, float scale, float offset) {
+  synth_f32_kernel<<<grid_for(n), 256, 0, H->stream>>>(dst, n, tensor_base(H->spec.seed, name), scale, offset);
+}
+
+static int pick_bn(int n) { return n % 256 == 0 ? 256 : 128; }
+
+static void init_linear(vd_handle* H, Linear& L, int n, int k, bool bias, int bn = 0) {
+  if (n % 128 != 0 || k % 64 != 0) fail(VD_ESPEC, "GEMM shape not tileable: N % 128 and K % 64 must be 0");
+  L.n = n;
+  L.k = k;
+  L.bn = bn ? bn : pick_bn(n);
+  L.w = dalloc<bf16>(H, static_cast<size_t>(n) * k);
+  L.b = bias ? dalloc<float>(H, n) : nullptr;
+  L.map = make_map(L.w, n, k, L.bn);
+}
+
+static void load_decoder(vd_handle* H) {
+  const ModelSpec& s = H->spec;
+  const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads, f = s.ffn;
+  const float lin = static_cast<float>(s.init_std * std::sqrt(3.0));
+  const float n_scale = 0.1f, n_off = s.norm_plus_one ? 0.0f : 1.0f;
+  H->embed = dalloc<bf16>(H, static_cast<size_t>(s.vocab) * d);
+  synth_bf16(H, H->embed, "model.embed_tokens.weight", s.vocab, d, lin, 0.0f);
+  const int qc = nq * hd, kc = nkv * hd;
+  // QKV tiles must not straddle the q / k / v column blocks.
+  int bn_qkv = 256;
+  if (hd == 128 && (qc % 256 != 0 || kc % 256 != 0)) bn_qkv = 128;
+  H->dec.resize(s.layers);
+  for (int i = 0; i < s.layers; ++i) {
+    DecLayer& L = H->dec[i];
+    const std::string p = "model.layers." + std::to_string(i) + ".";
+    L.in_norm = dalloc<float>(H, d);
+    L.post_norm = dalloc<float>(H, d);
+    synth_f32(H, L.in_norm, p + "input_layernorm.weight", d, n_scale, n_off);
+    synth_f32(H, L.post_norm, p + "post_attention_layernorm.weight", d, n_scale, n_off);
+    init_linear(H, L.qkv, s.qkv_width(), d, s.qkv_bias, bn_qkv);
+    synth_bf16(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
+    synth_bf16(H, L.qkv.w, p + "self_attn.k_proj.weight", kc, d, lin, 0.0f, kc, 0, qc);
+    synth_bf16(H, L.qkv.w, p + "self_attn.v_proj.weight", kc, d, lin, 0.0f, kc, 0, qc + kc);
+    if (s.qkv_bias) {
+      synth_f32(H, L.qkv.b, p + "self_attn.q_proj.bias", qc, lin, 0.0f);
+      synth_f32(H, L.qkv.b + qc, p + "self_attn.k_proj.bias", kc, lin, 0.0f);
+      synth_f32(H, L.qkv.b + qc + kc, p + "self_attn.v_proj.bias", kc, lin, 0.0f);
+    }
+    if (s.qk_norm) {
+      L.q_norm = dalloc<float>(H, hd);
+      L.k_norm = dalloc<float>(H, hd);
+      synth_f32(H, L.q_norm, p + "self_attn.q_norm.weight", hd, n_scale, n_off);
+      synth_f32(H, L.k_norm, p + "self_attn.k_norm.weight", hd, n_scale, n_off);
+    }
+    init_linear(H, L.o, d, qc, false);
+    synth_bf16(H, L.o.w, p + "self_attn.o_proj.weight", d, qc, lin, 0.0f);
+    init_linear(H, L.gu, 2 * f, d, false, 256);
+    synth_bf16(H, L.gu.w, p + "mlp.gate_proj.weight", f, d, lin, 0.0f, 128, 256, 0);
+    synth_bf16(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
+    init_linear(H, L.down, d, f, false);
+    synth_bf16(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
+  }
+  H->final_norm = dalloc<float>(H, d);
+  synth_f32(H, H->final_norm, "model.norm.weight", d, n_scale, n_off);
+  H->n_labels = static_cast<int>(s.label_ids.size());
+  H->head_rows = dalloc<float>(H, static_cast<size_t>(H->n_labels) * d);
+  int* rows = dalloc<int>(H, H->n_labels);
+  cuda_check(cudaMemcpyAsync(rows, s.label_ids.data(), sizeof(int) * H->n_labels, cudaMemcpyHostToDevice, H->stream),
+             "upload label ids");
+  const std::string head_name = s.tied ? "model.embed_tokens.weight" : "lm_head.weight";
+  synth_rows_gather_f32_kernel<<<grid_for(static_cast<int64_t>(H->n_labels) * d), 256, 0, H->stream>>>(
+      H->head_rows, rows, H->n_labels, d, tensor_base(s.seed, head_name), lin, 0.0f);
+  // RoPE table: cos/sin(pos * inv_freq_i), inv_freq_i = 1 / theta^(2i/hd) in fp32.
+  const int half = hd / 2;
+  std::vector<float2> tab(static_cast<size_t>(H->opt.max_seq) * half);
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i)
+    inv[i] = 1.0f / std::pow(static_cast<float>(s.rope_theta), static_cast<float>(2 * i) / static_cast<float>(hd));
+  for (int64_t pos = 0; pos < H->opt.max_seq; ++pos)
+    for (int i = 0; i < half; ++i) {
+      const float a = static_cast<float>(pos) * inv[i];
+      tab[pos * half + i] = make_float2(static_cast<float>(std::cos(static_cast<double>(a))),
+                                        static_cast<float>(std::sin(static_cast<double>(a))));
+    }
+  H->rope = dalloc<float2>(H, tab.size());
+  cuda_check(cudaMemcpy(H->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice), "upload rope");
+}
+
+static void enc_linear(vd_handle* H, Linear& L, const std::string& wname, const std::string& bname, int n, int k,
+                       float lin) {
+  init_linear(H, L, n, k, true);
+  synth_bf16(H, L.w, wname, n, k, lin, 0.0f);
+  synth_f32(H, L.b, bname, n, lin, 0.0f);
+}
+
+static void load_encoder(vd_handle* H) {
+  const ModelSpec& s = H->spec;
+  const int d = s.hidden, f = s.ffn;
+  const float lin = static_cast<float>(s.init_std * std::sqrt(3.0));
+  const float g_scale = 0.1f, g_off = 1.0f;
+  const std::string e = "encoder.embeddings.";
+  H->embed = dalloc<bf16>(H, static_cast<size_t>(s.vocab) * d);
+  synth_bf16(H, H->embed, e + "word_embeddings.weight", s.vocab, d, lin, 0.0f);
+  H->pos_emb = dalloc<bf16>(H, static_cast<size_t>(s.max_pos) * d);
+  synth_bf16(H, H->pos_emb, e + "position_embeddings.weight", s.max_pos, d, lin, 0.0f);
+  H->type_emb0 = dalloc<bf16>(H, static_cast<size_t>(s.type_vocab) * d);
+  synth_bf16(H, H->type_emb0, e + "token_type_embeddings.weight", s.type_vocab, d, lin, 0.0f);
+  H->emb_ln_w = dalloc<float>(H, d);
+  H->emb_ln_b = dalloc<float>(H, d);
+  synth_f32(H, H->emb_ln_w, e + "LayerNorm.weight", d, g_scale, g_off);
+  synth_f32(H, H->emb_ln_b, e + "LayerNorm.bias", d, lin, 0.0f);
+  H->enc.resize(s.layers);
+  for (int i = 0; i < s.layers; ++i) {
+    EncLayer& L = H->enc[i];
+    const std::string p = "encoder.encoder.layer." + std::to_string(i) + ".";
+    init_linear(H, L.qkv, 3 * d, d, true);
+    const char* parts[3] = {"query", "key", "value"};
+    for (int j = 0; j < 3; ++j) {
+      synth_bf16(H, L.qkv.w, p + "attention.self." + parts[j] + ".weight", d, d, lin, 0.0f, d, 0,
+                 static_cast<int64_t>(j) * d);
+      synth_f32(H, L.qkv.b + j * d, p + "attention.self." + parts[j] + ".bias", d, lin, 0.0f);
+    }
+    enc_linear(H, L.o, p + "attention.output.dense.weight", p + "attention.output.dense.bias", d, d, lin);
+    enc_linear(H, L.f1, p + "intermediate.dense.weight", p + "intermediate.dense.bias", f, d, lin);
+    enc_linear(H, L.f2, p + "output.dense.weight", p + "output.dense.bias", d, f, lin);
+    L.ln1_w = dalloc<float>(H, d);
+    L.ln1_b = dalloc<float>(H, d);
+    L.ln2_w = dalloc<float>(H, d);
+    L.ln2_b = dalloc<float>(H, d);
+    synth_f32(H, L.ln1_w, p + "attention.output.LayerNorm.weight", d, g_scale, g_off);
+    synth_f32(H, L.ln1_b, p + "attention.output.LayerNorm.bias", d, lin, 0.0f);
+    synth_f32(H, L.ln2_w, p + "output.LayerNorm.weight", d, g_scale, g_off);
+    synth_f32(H, L.ln2_b, p + "output.LayerNorm.bias", d, lin, 0.0f);
+    L.pre_norm = false;
+    L.act = kActGeluErf;
+    L.eps = static_cast<float>(s.ln_eps);
+  }
+  H->qtype_emb = dalloc<bf16>(H, 3 * static_cast<size_t>(d));
+  synth_bf16(H, H->qtype_emb, "type_emb.weight", 3, d, lin, 0.0f);
+  H->head.resize(s.head_layers);
+  for (int i = 0; i < s.head_layers; ++i) {
+    EncLayer& L = H->head[i];
+    const std::string p = "head.layers." + std::to_string(i) + ".";
+    enc_linear(H, L.qkv, p + "self_attn.in_proj_weight", p + "self_attn.in_proj_bias", 3 * d, d, lin);
+    enc_linear(H, L.o, p + "self_attn.out_proj.weight", p + "self_attn.out_proj.bias", d, d, lin);
+    enc_linear(H, L.f1, p + "linear1.weight", p + "linear1.bias", 4 * d, d, lin);
+    enc_linear(H, L.f2, p + "linear2.weight", p + "linear2.bias", d, 4 * d, lin);
+    L.ln1_w = dalloc<float>(H, d);
+    L.ln1_b = dalloc<float>(H, d);
+    L.ln2_w = dalloc<float>(H, d);
+    L.ln2_b = dalloc<float>(H, d);
+    synth_f32(H, L.ln1_w, p + "norm1.weight", d, g_scale, g_off);
+    synth_f32(H, L.ln1_b, p + "norm1.bias", d, lin, 0.0f);
+    synth_f32(H, L.ln2_w, p + "norm2.weight", d, g_scale, g_off);
+    synth_f32(H, L.ln2_b, p + "norm2.bias", d, lin, 0.0f);
+    L.pre_norm = true;
+    L.act = kActRelu;
+    L.eps = 1e-5f;  // nn.TransformerEncoderLayer default layer_norm_eps
+  }
+  H->sc_ln_w = dalloc<float>(H, d);
+  H->sc_ln_b = dalloc<float>(H, d);
+  synth_f32(H, H->sc_ln_w, "scorer.0.weight", d, g_scale, g_off);
+  synth_f32(H, H->sc_ln_b, "scorer.0.bias", d, lin, 0.0f);
+  enc_linear(H, H->sc1, "scorer.1.weight", "scorer.1.bias", d, d, lin);
+  H->sc_w3 = dalloc<float>(H, d);
+  H->sc_b3 = dalloc<float>(H, 1);
+  synth_f32(H, H->sc_w3, "scorer.3.weight", d, lin, 0.0f);
+  synth_f32(H, H->sc_b3, "scorer.3.bias", 1, lin, 0.0f);
+}
+
+// Device copies of host-memory batches; grown on demand (only when a batch is
+// larger than any before it).
+static void ensure_host_inputs(vd_handle* H, int64_t n_ids, int64_t n_markers, int64_t n_rows, int64_t n_out) {
+  auto grow = [&](auto*& ptr, int64_t& cap, int64_t need, size_t elem) {
+    if (need <= cap && ptr) return;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    cap = 0;
+    void* p = nullptr;
+    const int64_t n = std::max<int64_t>(need, 1);
+    const cudaError_t e = cudaMalloc(&p, static_cast<size_t>(n) * elem);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      fail(VD_ENOMEM, std::string("input staging allocation failed: ") + cudaGetErrorString(e));
+    }
+    ptr = static_cast<std::remove_reference_t<decltype(ptr)>>(p);
+    cap = n;
+  };
+  grow(H->in_ids, H->cap_ids, n_ids, sizeof(int64_t));
+  grow(H->in_mpos, H->cap_markers, n_markers, sizeof(int64_t));
+  int64_t cap_mask = H->cap_markers_mask;
+  grow(H->in_mmask, cap_mask, n_markers, sizeof(uint8_t));
+  H->cap_markers_mask = cap_mask;
+  grow(H->in_nopts, H->cap_rows, n_rows, sizeof(int64_t));
+  int64_t cap_q = H->cap_rows_q;
+  grow(H->in_qtype, cap_q, n_rows, sizeof(int64_t));
+  H->cap_rows_q = cap_q;
+  grow(H->out_dev, H->out_cap, n_out, sizeof(float));
+}
+
+static void alloc_workspace(vd_handle* H) {
+  const ModelSpec& s = H->spec;
+  const Options& o = H->opt;
+  const int64_t T = o.max_tokens;
+  const int d = s.hidden;
+  const int qkvw = s.decoder() ? s.qkv_width() : 3 * d;
+  const int attw = s.decoder() ? s.heads * s.head_dim : d;
+  const int actw = s.decoder() ? s.ffn : std::max(s.ffn, 4 * d);
+  H->h = dalloc<float>(H, T * d);
+  H->xn = dalloc<bf16>(H, T * d);
+  H->qkv = dalloc<bf16>(H, T * qkvw);
+  H->attn = dalloc<bf16>(H, T * attw);
+  H->act = dalloc<bf16>(H, T * actw);
+  H->tokens = dalloc<int>(H, T);
+  H->positions = dalloc<int>(H, T);
+  H->seq_id = dalloc<int>(H, T);
+  H->cu = dalloc<int>(H, o.max_rows + 1);
+  H->max_tiles = T / 64 + o.max_rows + 1;
+  H->tiles = dalloc<AttnTile>(H, H->max_tiles);
+  H->d_err = dalloc<int>(H, 1);
+  cuda_check(cudaMemset(H->d_err, 0, sizeof(int)), "clear error word");
+  H->map_xn = make_map(H->xn, T, d, 128);
+  H->map_attn = make_map(H->attn, T, attw, 128);
+  if (s.decoder()) {
+    H->map_act = make_map(H->act, T, s.ffn, 128);
+  } else {
+    H->map_act = make_map(H->act, T, s.ffn, 128);
+    H->map_act2 = make_map(H->act, T, 4 * d, 128);
+    H->midx = dalloc<int>(H, o.max_markers);
+    H->mrow = dalloc<bf16>(H, o.max_markers * d);
+    H->mhid = dalloc<bf16>(H, o.max_markers * d);
+    H->map_mrow = make_map(H->mrow, o.max_markers, d, 128);
+  }
+  ensure_host_inputs(H, o.max_rows * 1024, std::max(o.max_rows, o.max_markers), o.max_rows,
+                     std::max<int64_t>(o.max_rows * 256, o.max_markers));
+  H->pinned_bytes = sizeof(int) * (o.max_rows + 1) + sizeof(AttnTile) * H->max_tiles + 256;
+  for (int i = 0; i < vd_handle::kSlots; ++i) {
+    cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&H->pinned[i]), H->pinned_bytes, cudaHostAllocDefault),
+               "pinned staging");
+    cuda_check(cudaEventCreateWithFlags(&H->slot_ev[i], cudaEventDisableTiming), "event");
+  }
+  cuda_check(cudaEventCreate(&H->ev0), "event");
+  cuda_check(cudaEventCreate(&H->ev1), "event");
+  cuda_check(cudaEventCreateWithFlags(&H->ev_user, cudaEventDisableTiming), "event");
+}
+
+// ---------------------------------------------------------------------------
+// Kernel launch helpers
+// ---------------------------------------------------------------------------
+template <int BN, int EPI>
+static void set_gemm_attr() {
+  cuda_check(cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  GemmConfig<BN>::SMEM_BYTES),
+             "gemm smem attribute");
+}
+template <int HD, bool C>
+static void set_attn_attr() {
+  cuda_check(cudaFuncSetAttribute(attention_varlen_kernel<HD, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnConfig<HD>::SMEM_BYTES),
+             "attention smem attribute");
+}
+
+static void init_kernel_attrs() {
+  set_gemm_attr<256, kEpiStore>();
+  set_gemm_attr<128, kEpiStore>();
+  set_gemm_attr<256, kEpiResidual>();
+  set_gemm_attr<128, kEpiResidual>();
+  set_gemm_attr<256, kEpiGated>();
+  set_gemm_attr<256, kEpiQKRope>();
+  set_gemm_attr<128, kEpiQKRope>();
+  set_attn_attr<64, false>();
+  set_attn_attr<128, true>();
+  set_attn_attr<256, true>();
+}
+
+template <int EPI>
+static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, int M, const EpiParams& ep) {
+  if (M <= 0) return;
+  const int num_m = (M + 127) / 128;
+  const int tiles = num_m * (L.n / L.bn);
+  const int grid = std::min(tiles, H->num_sms);
+  const GemmShape shape{M, L.n, L.k};
+  const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
+  launch(H, kind, flops, [&] {
+    if (L.bn == 256) {
+      gemm_tcgen05_kernel<256, EPI>
+          <<<grid, 192, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
+    } else {
+      if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
+      else
+        gemm_tcgen05_kernel<128, EPI>
+            <<<grid, 192, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
+    }
+  });
+}
+
+static EpiParams epi(void* out, int ld, const float* bias = nullptr, int act = kActNone) {
+  EpiParams p{};
+  p.out = out;
+  p.ld_out = ld;
+  p.bias = bias;
+  p.act = act;
+  return p;
+}
+
+static EpiParams epi_params_for(void* out, int ld, const float* bias, int act) { return epi(out, ld, bias, act); }
+
+static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd, bool causal, int ld_qkv, int q0,
+                      int k0, int v0, int group, int ld_out) {
+  AttnParams p;
+  p.qkv = H->qkv;
+  p.ld_qkv = ld_qkv;
+  p.q_col0 = q0;
+  p.k_col0 = k0;
+  p.v_col0 = v0;
+  p.out = H->attn;
+  p.ld_out = ld_out;
+  p.tiles = H->tiles;
+  p.group = group;
+  p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)) * 1.4426950408889634);
+  dim3 grid(n_tiles, heads);
+  if (!((hd == 64 && !causal) || (hd == 128 && causal) || (hd == 256 && causal)))
+    fail(VD_ESPEC, "no attention kernel for this head size / mask");
+  launch(H, VD_K_ATTN, flops, [&] {
+    if (hd == 64)
+      attention_varlen_kernel<64, false><<<grid, 128, AttnConfig<64>::SMEM_BYTES, H->stream>>>(p);
+    else if (hd == 128)
+      attention_varlen_kernel<128, true><<<grid, 128, AttnConfig<128>::SMEM_BYTES, H->stream>>>(p);
+    else
+      attention_varlen_kernel<256, true><<<grid, 128, AttnConfig<256>::SMEM_BYTES, H->stream>>>(p);
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Forward of one chunk of rows (device pointers already offset to the chunk).
+// ---------------------------------------------------------------------------
+struct Chunk {
+  int nb = 0;
+  int64_t l = 0, k = 0;
+  const int64_t* ids = nullptr;      // device [nb*l]
+  const int64_t* mpos = nullptr;     // device [nb*k]
+  const uint8_t* mmask = nullptr;    // device [nb*k]
+  const int64_t* nopts = nullptr;    // device [nb] or null
+  const int64_t* qtype = nullptr;    // device [nb] or null
+  const int64_t* real_len = nullptr; // host [nb]
+  float* out = nullptr;              // device [nb*width]
+  int64_t width = 0;
+};
+
+// Host plan: cu_seqlens and the attention tile table, staged through pinned memory.
+static int plan_chunk(vd_handle* H, const Chunk& c, int& T, int& max_len, bool causal) {
+  H->slot = (H->slot + 1) % vd_handle::kSlots;
+  char* buf = H->pinned[H->slot];
+  cuda_check(cudaEventSynchronize(H->slot_ev[H->slot]), "staging slot");
+  int* cu = reinterpret_cast<int*>(buf);
+  AttnTile* tiles = reinterpret_cast<AttnTile*>(buf + ((sizeof(int) * (c.nb + 1) + 15) & ~size_t(15)));
+  cu[0] = 0;
+  max_len = 0;
+  for (int i = 0; i < c.nb; ++i) {
+    cu[i + 1] = cu[i] + static_cast<int>(c.real_len[i]);
+    max_len = std::max(max_len, static_cast<int>(c.real_len[i]));
+  }
+  T = cu[c.nb];
+  int n = 0;
+  for (int i = 0; i < c.nb; ++i) {
+    const int len = static_cast<int>(c.real_len[i]);
+    for (int q = 0; q < len; q += 64) tiles[n++] = AttnTile{cu[i], len, q, 0};
+  }
+  // Longest work first: causal tiles cost ~ q_start + 64 keys, bidirectional ~ len.
+  std::stable_sort(tiles, tiles + n, [causal](const AttnTile& a, const AttnTile& b) {
+    const int wa = causal ? std::min(a.seq_len, a.q_start + 64) : a.seq_len;
+    const int wb = causal ? std::min(b.seq_len, b.q_start + 64) : b.seq_len;
+    return wa > wb;
+  });
+  const size_t tiles_off = reinterpret_cast<char*>(tiles) - buf;
+  cuda_check(cudaMemcpyAsync(H->cu, cu, sizeof(int) * (c.nb + 1), cudaMemcpyHostToDevice, H->stream), "upload cu");
+  cuda_check(cudaMemcpyAsync(H->tiles, buf + tiles_off, sizeof(AttnTile) * n, cudaMemcpyHostToDevice, H->stream),
+             "upload tiles");
+  cuda_check(cudaEventRecord(H->slot_ev[H->slot], H->stream), "staging event");
+  return n;
+}
+
+static void pack(vd_handle* H, const Chunk& c, int max_len, int pos_offset) {
+  dim3 grid(std::max(1, std::min((max_len + 255) / 256, 64)), c.nb);
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    pack_tokens_kernel<<<grid, 256, 0, H->stream>>>(c.ids, c.l, H->cu, c.nb, H->spec.vocab, pos_offset, H->tokens,
+                                                    H->positions, H->seq_id, H->d_err);
+  });
+}
+
+static double decoder_forward(vd_handle* H, const Chunk& c) {
+  const ModelSpec& s = H->spec;
+  const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads;
+  int T = 0, max_len = 0;
+  const int n_tiles = plan_chunk(H, c, T, max_len, true);
+  pack(H, c, max_len, 0);
+  const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
+  launch(H, VD_K_OTHER, 0.0,
+         [&] { embed_kernel<<<T, 128, 0, H->stream>>>(H->tokens, T, H->embed, d, escale, H->h); });
+  const int qkvw = s.qkv_width(), qc = nq * hd, kc = nkv * hd;
+  const float eps = static_cast<float>(s.rms_eps);
+  const int pone = s.norm_plus_one ? 1 : 0;
+  double attn_pairs = 0;
+  for (int i = 0; i < c.nb; ++i) attn_pairs += 0.5 * static_cast<double>(c.real_len[i]) * (c.real_len[i] + 1);
+  const double attn_flops = 4.0 * hd * nq * attn_pairs;
+  for (int i = 0; i < s.layers; ++i) {
+    const DecLayer& L = H->dec[i];
+    launch(H, VD_K_NORM, 0.0, [&] {
+      rmsnorm_kernel<256><<<T, 256, 0, H->stream>>>(H->h, d, L.in_norm, pone, eps, H->xn, T);
+    });
+    EpiParams q = epi(H->qkv, qkvw, L.qkv.b);
+    q.q_norm = L.q_norm;
+    q.k_norm = L.k_norm;
+    q.q_cols = qc;
+    q.k_cols = kc;
+    q.head_dim = hd;
+    q.plus_one = pone;
+    q.eps = eps;
+    q.positions = H->positions;
+    q.rope = H->rope;
+    gemm<kEpiQKRope>(H, VD_K_QKV, H->map_xn, L.qkv, T, q);
+    attention(H, attn_flops, n_tiles, nq, hd, true, qkvw, 0, qc, qc + kc, nq / nkv, qc);
+    gemm<kEpiResidual>(H, VD_K_O, H->map_attn, L.o, T, epi(H->h, d));
+    launch(H, VD_K_NORM, 0.0, [&] {
+      rmsnorm_kernel<256><<<T, 256, 0, H->stream>>>(H->h, d, L.post_norm, pone, eps, H->xn, T);
+    });
+    gemm<kEpiGated>(H, VD_K_GATEUP, H->map_xn, L.gu, T, epi(H->act, s.ffn, nullptr, s.act));
+    gemm<kEpiResidual>(H, VD_K_DOWN, H->map_act, L.down, T, epi(H->h, d));
+  }
+  const size_t smem = sizeof(float) * (d + H->n_labels);
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    readout_kernel<256><<<c.nb, 256, smem, H->stream>>>(H->h, d, H->cu, c.mpos, static_cast<int>(c.k), c.nopts,
+                                                        H->final_norm, pone, eps, H->head_rows, H->n_labels, c.out,
+                                                        static_cast<int>(c.width), H->opt.logprobs ? 1 : 0, H->d_err);
+  });
+  H->stats.attn_flops += attn_flops * s.layers;
+  H->stats.gemm_flops += 2.0 * T * (static_cast<double>(d) * qkvw + static_cast<double>(qc) * d + 3.0 * d * s.ffn) *
+                         s.layers;
+  return T;
+}
+
+static void enc_layer(vd_handle* H, const EncLayer& L, int T, int n_tiles, double attn_flops) {
+  const int d = H->spec.hidden;
+  const int nh = d / 64;
+  auto ln = [&](const float* w, const float* b, int inplace) {
+    launch(H, VD_K_NORM, 0.0, [&] {
+      layernorm_kernel<256><<<T, 256, 0, H->stream>>>(H->h, d, w, b, L.eps, inplace, H->xn, T);
+    });
+  };
+  if (L.pre_norm) ln(L.ln1_w, L.ln1_b, 0);
+  gemm<kEpiStore>(H, VD_K_QKV, H->map_xn, L.qkv, T, epi(H->qkv, 3 * d, L.qkv.b));
+  attention(H, attn_flops, n_tiles, nh, 64, false, 3 * d, 0, d, 2 * d, 1, d);
+  gemm<kEpiResidual>(H, VD_K_O, H->map_attn, L.o, T, epi(H->h, d, L.o.b));
+  if (L.pre_norm) ln(L.ln2_w, L.ln2_b, 0);
+  else ln(L.ln1_w, L.ln1_b, 1);
+  const CUtensorMap& amap = (L.f1.n == H->spec.ffn) ? H->map_act : H->map_act2;
+  gemm<kEpiStore>(H, VD_K_GATEUP, H->map_xn, L.f1, T, epi(H->act, L.f1.n, L.f1.b, L.act));
+  gemm<kEpiResidual>(H, VD_K_DOWN, amap, L.f2, T, epi(H->h, d, L.f2.b));
+  if (!L.pre_norm) ln(L.ln2_w, L.ln2_b, 1);
+}
+
+static double encoder_forward(vd_handle* H, const Chunk& c) {
+  const ModelSpec& s = H->spec;
+  const int d = s.hidden;
+  int T = 0, max_len = 0;
+  const int n_tiles = plan_chunk(H, c, T, max_len, false);
+  const int pos_offset = s.style == "xlmr" ? s.pad_id + 1 : 0;
+  if (max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
+  pack(H, c, max_len, pos_offset);
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    embed_ln_kernel<256><<<T, 256, 0, H->stream>>>(H->tokens, H->positions, T, H->embed, H->pos_emb, H->type_emb0,
+                                                   d, H->emb_ln_w, H->emb_ln_b, static_cast<float>(s.ln_eps), H->h,
+                                                   H->xn);
+  });
+  double pairs = 0;
+  for (int i = 0; i < c.nb; ++i) pairs += static_cast<double>(c.real_len[i]) * c.real_len[i];
+  const double attn_flops = 4.0 * d * pairs;
+  for (const EncLayer& L : H->enc) enc_layer(H, L, T, n_tiles, attn_flops);
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    add_type_kernel<<<T, 256, 0, H->stream>>>(H->h, T, d, H->seq_id, c.qtype, H->qtype_emb, 3, H->d_err);
+  });
+  for (const EncLayer& L : H->head) enc_layer(H, L, T, n_tiles, attn_flops);
+  const int nm = static_cast<int>(c.nb * c.k);
+  if (nm > 0) {
+    launch(H, VD_K_OTHER, 0.0, [&] {
+      marker_index_kernel<<<(nm + 255) / 256, 256, 0, H->stream>>>(H->cu, c.mpos, c.mmask, c.nb,
+                                                                   static_cast<int>(c.k), H->midx, H->d_err);
+    });
+    launch(H, VD_K_NORM, 0.0, [&] {
+      gather_layernorm_kernel<256><<<nm, 256, 0, H->stream>>>(H->h, H->midx, nm, d, H->sc_ln_w, H->sc_ln_b, 1e-5f,
+                                                              H->mrow);
+    });
+    gemm<kEpiStore>(H, VD_K_OTHER, H->map_mrow, H->sc1, nm, epi(H->mhid, d, H->sc1.b, kActGeluErf));
+  }
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    marker_score_kernel<<<c.nb, 256, 0, H->stream>>>(H->mhid, d, H->sc_w3, H->sc_b3, c.mmask, c.nb,
+                                                     static_cast<int>(c.k), c.out, static_cast<int>(c.width));
+  });
+  H->stats.attn_flops += attn_flops * (s.layers + s.head_layers);
+  H->stats.gemm_flops += 2.0 * T * ((4.0 * d * d + 2.0 * d * s.ffn) * s.layers + (12.0 * d * d) * s.head_layers);
+  return T;
+}
+
+// ---------------------------------------------------------------------------
+// Batch validation and chunking
+// ---------------------------------------------------------------------------
+static void validate_batch(vd_handle* H, const vd_batch* b, int64_t width) {
+  if (!b) fail(VD_EINVAL, "null batch");
+  if (b->b < 0 || b->l < 0 || b->k < 0) fail(VD_EINVAL, "negative batch dimensions");
+  if (b->b == 0) return;
+  if (!b->input_ids || !b->real_len || !b->marker_pos) fail(VD_EINVAL, "missing input_ids / real_len / marker_pos");
+  if (b->memory != VD_MEM_HOST && b->memory != VD_MEM_DEVICE) fail(VD_EINVAL, "unknown memory kind");
+  const ModelSpec& s = H->spec;
+  if (s.decoder()) {
+    // TorchEngine::infer (src/torch_engine.rs:452-466)
+    if (b->k != 1 || !b->nopts)
+      fail(VD_EINVAL, "letter batches need exactly one slot per row (got k=" + std::to_string(b->k) +
+                          ", nopts=" + std::string(b->nopts ? std::to_string(b->b) : "0") + ")");
+    if (b->memory == VD_MEM_HOST && b->marker_mask)
+      for (int64_t i = 0; i < b->b; ++i)
+        if (!b->marker_mask[i]) fail(VD_EINVAL, "row " + std::to_string(i) + " has no slot marker");
+    if (width < 1) fail(VD_EINVAL, "output width must be positive");
+  } else {
+    if (!b->marker_mask) fail(VD_EINVAL, "marker batches need marker_mask");
+    if (width < b->k) fail(VD_EINVAL, "output width is smaller than k");
+    if (b->b * b->k > H->opt.max_markers) fail(VD_EINVAL, "too many markers for this handle (max_markers)");
+  }
+  for (int64_t i = 0; i < b->b; ++i) {
+    const int64_t n = b->real_len[i];
+    if (n < 1 || n > b->l) fail(VD_EINVAL, "row " + std::to_string(i) + " has real_len outside [1, l]");
+    if (n > H->opt.max_seq) fail(VD_EINVAL, "row " + std::to_string(i) + " is longer than max_seq");
+    if (n > H->opt.max_tokens) fail(VD_EINVAL, "row " + std::to_string(i) + " is longer than max_tokens");
+  }
+  if (b->memory == VD_MEM_HOST) {
+    if (s.decoder())
+      for (int64_t i = 0; i < b->b; ++i) {
+        const int64_t slot = b->marker_pos[i];
+        if (slot < 0 || slot >= b->real_len[i]) fail(VD_EINVAL, "row " + std::to_string(i) + " slot outside the row");
+      }
+  }
+}
+
+static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const int64_t* mpos, const uint8_t* mmask,
+                      const int64_t* nopts, const int64_t* qtype, float* out, int64_t width) {
+  H->stats = vd_stats{};
+  H->launches = 0;
+  cuda_check(cudaEventRecord(H->ev0, H->stream), "event");
+  int64_t r0 = 0, chunks = 0, tokens = 0;
+  while (r0 < b->b) {
+    int64_t r1 = r0, t = 0;
+    while (r1 < b->b && r1 - r0 < H->opt.max_rows && t + b->real_len[r1] <= H->opt.max_tokens) t += b->real_len[r1++];
+    Chunk c;
+    c.nb = static_cast<int>(r1 - r0);
+    c.l = b->l;
+    c.k = b->k;
+    c.ids = ids + r0 * b->l;
+    c.mpos = mpos + r0 * b->k;
+    c.mmask = mmask ? mmask + r0 * b->k : nullptr;
+    c.nopts = nopts ? nopts + r0 : nullptr;
+    c.qtype = qtype ? qtype + r0 : nullptr;
+    c.real_len = b->real_len + r0;
+    c.out = out + r0 * width;
+    c.width = width;
+    tokens += static_cast<int64_t>(H->spec.decoder() ? decoder_forward(H, c) : encoder_forward(H, c));
+    ++chunks;
+    r0 = r1;
+  }
+  cuda_check(cudaGetLastError(), "kernel launch");
+  cuda_check(cudaEventRecord(H->ev1, H->stream), "event");
+  H->stats.rows = b->b;
+  H->stats.tokens = tokens;
+  H->stats.chunks = chunks;
+  H->stats.launches = H->launches;
+}
+
+static void check_device_error(vd_handle* H) {
+  int e = 0;
+  cuda_check(cudaMemcpyAsync(&e, H->d_err, sizeof(int), cudaMemcpyDeviceToHost, H->stream), "read error word");
+  cuda_check(cudaStreamSynchronize(H->stream), "synchronize");
+  float ms = 0;
+  if (cudaEventElapsedTime(&ms, H->ev0, H->ev1) == cudaSuccess) H->stats.forward_ms = ms;
+  prof_collect(H);
+  if (e != 0) {
+    cuda_check(cudaMemsetAsync(H->d_err, 0, sizeof(int), H->stream), "clear error word");
+    cuda_check(cudaStreamSynchronize(H->stream), "synchronize");
+    if (e == kErrTokenRange) fail(VD_EDEVICE, "a token id or qtype is outside the model's range");
+    if (e == kErrSlotRange) fail(VD_EDEVICE, "a slot / marker position lies outside its row");
+    H->healthy = false;
+    H->dead_reason = "a kernel pipeline timed out (device error " + std::to_string(e) + ")";
+    fail(VD_ECUDA, H->dead_reason);
+  }
+}
+
+}  // namespace vd
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+using namespace vd;
+
+static void put_err(char* err, size_t errlen, const std::string& msg) {
+  if (!err || errlen == 0) return;
+  const size_t n = std::min(errlen - 1, msg.size());
+  std::memcpy(err, msg.data(), n);
+  err[n] = '\0';
+}
+
+template <class F>
+static int guarded(vd_handle* h, char* err, size_t errlen, F&& body) {
+  try {
+    body();
+    return VD_OK;
+  } catch (const VdError& e) {
+    if (e.code == VD_ECUDA && h) {
+      h->healthy = false;
+      if (h->dead_reason.empty()) h->dead_reason = e.msg;
+    }
+    put_err(err, errlen, e.msg);
+    return e.code;
+  } catch (const std::exception& e) {
+    put_err(err, errlen, e.what());
+    return VD_EINVAL;
+  }
+}
+
+extern "C" VD_API int vd_abi_version(void) { return VDEXEC_ABI_VERSION; }
+
+extern "C" VD_API int vd_open(const char* model, int device, const char* opts_json, vd_handle** out, char* err,
+                       size_t errlen) {
+  if (!out) {
+    put_err(err, errlen, "null output handle pointer");
+    return VD_EINVAL;
+  }
+  *out = nullptr;
+  vd_handle* H = new vd_handle();
+  int rc = guarded(nullptr, err, errlen, [&] {
+    if (!model) fail(VD_EINVAL, "null model");
+    std::string text(model);
+    if (text.empty() || text[0] != '{') {
+      std::ifstream f(text + "/vdexec.json");
+      if (!f) fail(VD_ESPEC, "no JSON spec given and no vdexec.json in " + text);
+      std::stringstream ss;
+      ss << f.rdbuf();
+      text = ss.str();
+    }
+    H->spec = parse_spec(parse_json(text));
+    validate_spec(H->spec);
+    if (opts_json && *opts_json) {
+      Json o = parse_json(opts_json);
+      H->opt.max_tokens = o.integer_or("max_tokens", H->opt.max_tokens);
+      H->opt.max_rows = o.integer_or("max_rows", H->opt.max_rows);
+      H->opt.max_seq = o.integer_or("max_seq", H->opt.max_seq);
+      H->opt.max_markers = o.integer_or("max_markers", H->opt.max_markers);
+      H->opt.logprobs = o.string_or("output", "logprobs") != "logits";
+    }
+    if (H->opt.max_tokens < 128 || H->opt.max_rows < 1 || H->opt.max_seq < 1)
+      fail(VD_EINVAL, "max_tokens must be >= 128 and max_rows, max_seq >= 1");
+    H->opt.max_tokens = (H->opt.max_tokens + 127) / 128 * 128;
+    H->device = device;
+    cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10) fail(VD_ECUDA, std::string("this build targets sm_100a (B200); device is ") + prop.name);
+    H->num_sms = prop.multiProcessorCount;
+    cuda_check(cudaStreamCreateWithFlags(&H->stream, cudaStreamNonBlocking), "stream");
+    init_kernel_attrs();
+    if (H->spec.decoder()) load_decoder(H);
+    else load_encoder(H);
+    alloc_workspace(H);
+    cuda_check(cudaGetLastError(), "weight generation launch");
+    cuda_check(cudaStreamSynchronize(H->stream), "weight generation");
+  });
+  if (rc != VD_OK) {
+    vd_close(H);
+    return rc;
+  }
+  *out = H;
+  return VD_OK;
+}
+
+extern "C" VD_API int vd_infer(vd_handle* h, const vd_batch* batch, float* logits_out, int64_t out_width, char* err,
+                        size_t errlen) {
+  if (!h) {
+    put_err(err, errlen, "null handle");
+    return VD_EINVAL;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (!h->healthy) {
+    put_err(err, errlen, "the executor is dead: " + h->dead_reason);
+    return VD_EDEAD;
+  }
+  return guarded(h, err, errlen, [&] {
+    cuda_check(cudaSetDevice(h->device), "cudaSetDevice");
+    validate_batch(h, batch, out_width);
+    if (batch->b == 0) return;
+    if (!logits_out) fail(VD_EINVAL, "null logits_out");
+    if (batch->memory == VD_MEM_DEVICE) {
+      run_batch(h, batch, batch->input_ids, batch->marker_pos, batch->marker_mask, batch->nopts, batch->qtype,
+                logits_out, out_width);
+      check_device_error(h);
+      return;
+    }
+    const int64_t b = batch->b, n_ids = b * batch->l, n_m = b * batch->k;
+    cudaStream_t s = h->stream;
+    cuda_check(cudaStreamSynchronize(s), "synchronize");  // staging buffers may be regrown
+    ensure_host_inputs(h, n_ids, n_m, b, b * out_width);
+    cuda_check(cudaMemcpyAsync(h->in_ids, batch->input_ids, n_ids * 8, cudaMemcpyHostToDevice, s), "upload ids");
+    cuda_check(cudaMemcpyAsync(h->in_mpos, batch->marker_pos, n_m * 8, cudaMemcpyHostToDevice, s), "upload markers");
+    if (batch->marker_mask)
+      cuda_check(cudaMemcpyAsync(h->in_mmask, batch->marker_mask, n_m, cudaMemcpyHostToDevice, s), "upload mask");
+    if (batch->nopts)
+      cuda_check(cudaMemcpyAsync(h->in_nopts, batch->nopts, b * 8, cudaMemcpyHostToDevice, s), "upload nopts");
+    if (batch->qtype)
+      cuda_check(cudaMemcpyAsync(h->in_qtype, batch->qtype, b * 8, cudaMemcpyHostToDevice, s), "upload qtype");
+    run_batch(h, batch, h->in_ids, h->in_mpos, batch->marker_mask ? h->in_mmask : nullptr,
+              batch->nopts ? h->in_nopts : nullptr, batch->qtype ? h->in_qtype : nullptr, h->out_dev, out_width);
+    cuda_check(cudaMemcpyAsync(logits_out, h->out_dev, b * out_width * sizeof(float), cudaMemcpyDeviceToHost, s),
+               "download logits");
+    check_device_error(h);
+  });
+}
+
+extern "C" VD_API int vd_infer_async(vd_handle* h, const vd_batch* batch, float* logits_out_dev, int64_t out_width,
+                              void* stream, char* err, size_t errlen) {
+  if (!h) {
+    put_err(err, errlen, "null handle");
+    return VD_EINVAL;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (!h->healthy) {
+    put_err(err, errlen, "the executor is dead: " + h->dead_reason);
+    return VD_EDEAD;
+  }
+  return guarded(h, err, errlen, [&] {
+    cuda_check(cudaSetDevice(h->device), "cudaSetDevice");
+    validate_batch(h, batch, out_width);
+    if (batch->memory != VD_MEM_DEVICE) fail(VD_EINVAL, "vd_infer_async takes device-resident batches");
+    if (batch->b == 0) return;
+    cudaStream_t user = static_cast<cudaStream_t>(stream);
+    if (user && user != h->stream) {
+      cuda_check(cudaEventRecord(h->ev_user, user), "event");
+      cuda_check(cudaStreamWaitEvent(h->stream, h->ev_user, 0), "stream wait");
+    }
+    run_batch(h, batch, batch->input_ids, batch->marker_pos, batch->marker_mask, batch->nopts, batch->qtype,
+              logits_out_dev, out_width);
+    if (user && user != h->stream) cuda_check(cudaStreamWaitEvent(user, h->ev1, 0), "stream wait");
+  });
+}
+
+extern "C" VD_API int vd_sync(vd_handle* h, char* err, size_t errlen) {
+  if (!h) {
+    put_err(err, errlen, "null handle");
+    return VD_EINVAL;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (!h->healthy) {
+    put_err(err, errlen, "the executor is dead: " + h->dead_reason);
+    return VD_EDEAD;
+  }
+  return guarded(h, err, errlen, [&] {
+    cuda_check(cudaSetDevice(h->device), "cudaSetDevice");
+    check_device_error(h);
+  });
+}
+
+extern "C" VD_API int vd_set_profiling(vd_handle* h, int on) {
+  if (!h) return VD_EINVAL;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->profiling = on != 0;
+  return VD_OK;
+}
+
+extern "C" VD_API void* vd_stream(vd_handle* h) { return h ? static_cast<void*>(h->stream) : nullptr; }
+
+extern "C" VD_API int vd_shape_buckets(vd_handle* h, int64_t* out, int64_t cap) {
+  (void)h;
+  (void)out;
+  (void)cap;
+  return 0;
+}
+
+extern "C" VD_API int vd_media_capable(vd_handle* h) {
+  (void)h;
+  return 0;
+}
+
+extern "C" VD_API int vd_health(vd_handle* h) {
+  if (!h || !h->healthy) return 0;
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (cudaSetDevice(h->device) != cudaSuccess) return 0;
+  const cudaError_t e = cudaStreamQuery(h->stream);
+  if (e != cudaSuccess && e != cudaErrorNotReady) {
+    h->healthy = false;
+    h->dead_reason = cudaGetErrorString(e);
+    return 0;
+  }
+  return 1;
+}
+
+extern "C" VD_API int64_t vd_label_width(vd_handle* h) { return h && h->spec.decoder() ? h->n_labels : 0; }
+
+extern "C" VD_API int vd_last_stats(vd_handle* h, vd_stats* out) {
+  if (!h || !out) return VD_EINVAL;
+  std::lock_guard<std::mutex> lock(h->mu);
+  *out = h->stats;
+  return VD_OK;
+}
+
+extern "C" VD_API void vd_close(vd_handle* h) {
+  if (!h) return;
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    if (cudaSetDevice(h->device) == cudaSuccess) {
+      if (h->stream) cudaStreamSynchronize(h->stream);
+      for (void* p : h->allocations) cudaFree(p);
+      for (void* p : {static_cast<void*>(h->in_ids), static_cast<void*>(h->in_mpos), static_cast<void*>(h->in_mmask),
+                      static_cast<void*>(h->in_nopts), static_cast<void*>(h->in_qtype), static_cast<void*>(h->out_dev)})
+        if (p) cudaFree(p);
+      for (int i = 0; i < vd_handle::kSlots; ++i) {
+        if (h->pinned[i]) cudaFreeHost(h->pinned[i]);
+        if (h->slot_ev[i]) cudaEventDestroy(h->slot_ev[i]);
+      }
+      if (h->ev0) cudaEventDestroy(h->ev0);
+      if (h->ev1) cudaEventDestroy(h->ev1);
+      if (h->ev_user) cudaEventDestroy(h->ev_user);
+      for (cudaEvent_t e : h->prof_pool) cudaEventDestroy(e);
+      if (h->stream) cudaStreamDestroy(h->stream);
+    }
+  }
+  delete h;
+}
+
+// Kernel-level entry points share the helpers above.
+#include "ops.cuh"
