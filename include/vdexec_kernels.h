@@ -22,10 +22,14 @@ extern "C" {
 #endif
 
 /* Epilogues of vdk_gemm. */
-#define VDK_EPI_STORE 0     /* out_bf16 = act(A W^T + bias)                                    */
-#define VDK_EPI_RESIDUAL 1  /* out_f32 += A W^T + bias                                          */
-#define VDK_EPI_GATED 2     /* out_bf16[:, j] = act(g_j) * u_j, W rows interleaved in 128-row blocks */
+#define VDK_EPI_STORE 0     /* out = act(A W^T + bias), 16-bit                                     */
+#define VDK_EPI_RESIDUAL 1  /* out_f32 += A W^T + bias                                              */
+#define VDK_EPI_GATED 2     /* out[:, j] = act(g_j) * u_j, 16-bit; W rows interleaved in 128-row blocks */
 #define VDK_EPI_QKROPE 3    /* per-head q/k RMSNorm + rotary embedding (see vdk_gemm_qkrope)   */
+
+/* 16-bit element types of A, W, qkv and 16-bit outputs. */
+#define VDK_FP16 0
+#define VDK_BF16 1
 
 /* Activations. */
 #define VDK_ACT_NONE 0
@@ -35,12 +39,13 @@ extern "C" {
 #define VDK_ACT_SILU 4
 
 /*
- * tcgen05 GEMM: A [M, K] bf16 row-major, W [N, K] bf16 row-major (nn.Linear
- * weight layout), fp32 accumulation; replaces torch.nn.functional.linear.
- * N % 128 == 0 (N % 256 == 0 for VDK_EPI_GATED), K % 64 == 0.
- * out: bf16 [M, ld_out] (store, gated) or fp32 [M, ld_out] (residual).
+ * tcgen05 GEMM: A [M, K] row-major, W [N, K] row-major (nn.Linear weight
+ * layout), both of the 16-bit type `dtype`, fp32 accumulation; replaces
+ * torch.nn.functional.linear.  N % 128 == 0 (N % 256 == 0 for
+ * VDK_EPI_GATED), K % 64 == 0.
+ * out: dtype [M, ld_out] (store, gated) or fp32 [M, ld_out] (residual).
  */
-VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int epi, int act,
+VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int dtype, int epi, int act,
                     const float* bias, void* out, int64_t ld_out, void* stream, char* err, size_t errlen);
 
 /*
@@ -51,21 +56,21 @@ VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t N, int64_t 
  * at positions[m] with base theta; the remaining columns (values) are stored as
  * they are.  Replaces q_norm(q_proj(x)) / k_norm(k_proj(x)) + apply_rotary_pos_emb.
  */
-VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, int64_t N, int64_t K, const float* bias,
+VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int dtype, const float* bias,
                            const float* q_norm, const float* k_norm, int q_cols, int k_cols, int head_dim,
                            int plus_one, float eps, const int32_t* positions, double theta, int max_pos, void* out,
                            int64_t ld_out, void* stream, char* err, size_t errlen);
 
 /*
- * Varlen attention over packed rows.  qkv [T, ld_qkv] bf16 holds query head h
+ * Varlen attention over packed rows.  qkv [T, ld_qkv] (16-bit dtype) holds query head h
  * at column q_col0 + h*head_dim and K/V head g at k_col0 / v_col0 + g*head_dim
  * (g = h / (heads / kv_heads)); cu_seqlens_host [nseq + 1] (host) delimits the
- * sequences; out [T, ld_out] bf16 at column h*head_dim.  causal = 1 for
+ * sequences; out [T, ld_out] (dtype) at column h*head_dim.  causal = 1 for
  * decoders.  Replaces F.scaled_dot_product_attention (is_causal) per sequence.
  */
 VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0, int64_t v_col0, int heads,
-                         int kv_heads, int head_dim, int causal, const int32_t* cu_seqlens_host, int64_t nseq,
-                         void* out, int64_t ld_out, void* stream, char* err, size_t errlen);
+                         int kv_heads, int head_dim, int dtype, int causal, const int32_t* cu_seqlens_host,
+                         int64_t nseq, void* out, int64_t ld_out, void* stream, char* err, size_t errlen);
 
 #ifdef __cplusplus
 }

@@ -18,7 +18,9 @@ from __future__ import annotations
 
 import numpy as np
 
-from verdict_b200.synth import SyntheticCheckpoint, synthetic_label_ids
+from verdict_b200.synth import synthetic_label_ids
+
+from .fastsynth import FastCheckpoint
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, plus_one: bool) -> np.ndarray:
@@ -74,11 +76,15 @@ def silu(x: np.ndarray) -> np.ndarray:
 
 
 class DecoderOracle:
-    """Holds the synthetic checkpoint (host, fp32 copies of the bf16 weights)."""
+    """Holds the synthetic checkpoint (host, fp32 copies of the bf16 weights).
 
-    def __init__(self, spec: dict, layers: int | None = None):
+    cache_layers=False regenerates each layer's weights when it is used and
+    drops them afterwards, so a 40-layer 9B model runs in ~2 GB of host memory."""
+
+    def __init__(self, spec: dict, layers: int | None = None, cache_layers: bool = True):
         self.spec = spec
-        self.ckpt = SyntheticCheckpoint(spec)
+        self.ckpt = FastCheckpoint(spec)
+        self.cache_layers = cache_layers
         self.n_layers = spec["layers"] if layers is None else layers
         self.label_ids = synthetic_label_ids(spec)
         self._layers = {}
@@ -96,7 +102,10 @@ class DecoderOracle:
                 names += ["self_attn.q_norm.weight", "self_attn.k_norm.weight"]
             if self.spec["qkv_bias"]:
                 names += ["self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias"]
-            self._layers[i] = {n: self.ckpt.get(p + n) for n in names}
+            w = {n: self.ckpt.get(p + n) for n in names}
+            if not self.cache_layers:
+                return w
+            self._layers[i] = w
         return self._layers[i]
 
     def embed(self, ids: np.ndarray) -> np.ndarray:
@@ -154,10 +163,33 @@ class DecoderOracle:
 
     def infer(self, batch) -> np.ndarray:
         """Raw label logits [b, width] for a `CollatedBatch` (slot = marker_pos[i*k])."""
+        if not self.cache_layers:
+            return self._infer_streaming(batch)
         out = np.empty((batch.b, len(self.label_ids)), dtype=np.float32)
         for i, row in enumerate(batch.rows):
             ids = batch.input_ids[i * batch.l:i * batch.l + row.real_len]
             out[i] = self.readout(ids, int(batch.marker_pos[i * batch.k]))
+        return out
+
+    def _infer_streaming(self, batch) -> np.ndarray:
+        """Layer-major order: each layer's weights are generated once for all rows."""
+        s = self.spec
+        hs, tabs = [], []
+        for i, row in enumerate(batch.rows):
+            ids = np.asarray(batch.input_ids[i * batch.l:i * batch.l + row.real_len], dtype=np.int64)
+            hs.append(self.embed(ids))
+            tabs.append(rope_tables(np.arange(len(ids)), s["head_dim"], s["rope_theta"]))
+        for layer in range(self.n_layers):
+            w = self.layer(layer)
+            self._layers[layer] = w
+            for i in range(len(hs)):
+                hs[i] = self.layer_forward(layer, hs[i], *tabs[i])
+            del self._layers[layer]
+        out = np.empty((batch.b, len(self.label_ids)), dtype=np.float32)
+        for i in range(len(hs)):
+            slot = int(batch.marker_pos[i * batch.k])
+            hn = rmsnorm(hs[i][slot:slot + 1], self.final_norm, s["rms_eps"], s["norm_plus_one"])
+            out[i] = (hn[0] @ self.head_w.T).astype(np.float32)
         return out
 
 

@@ -22,8 +22,8 @@ from __future__ import annotations
 import numpy as np
 from scipy.special import erf
 
-from verdict_b200.synth import SyntheticCheckpoint
 from .decoder import attention
+from .fastsynth import FastCheckpoint
 
 SENTINEL = -1e4
 
@@ -42,7 +42,7 @@ def gelu_erf(x):
 class EncoderOracle:
     def __init__(self, spec: dict):
         self.spec = spec
-        self.ckpt = SyntheticCheckpoint(spec)
+        self.ckpt = FastCheckpoint(spec)
         self.w = {}
 
     def g(self, name):

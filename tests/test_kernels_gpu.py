@@ -1,10 +1,11 @@
 """Each sm_100a kernel against a plain PyTorch fp32 reference of the same op.
 
 Kernels are called through the C ABI (include/vdexec_kernels.h) on torch-owned
-device buffers; torch computes the fp32 reference from the same bf16 inputs.
-Tolerances: bf16 outputs carry one bf16 rounding (relative 2^-8), so
-|got - ref| <= 1e-2 * |ref| + 1e-2 * rms(ref); fp32 outputs (residual
-epilogue) differ only by fp32 accumulation order: 1e-4 relative.
+device buffers, in both 16-bit element types (fp16, bf16); torch computes the
+fp32 reference from the same 16-bit inputs.
+Tolerances: 16-bit outputs carry one rounding (relative 2^-8 for bf16, 2^-11
+for fp16), so |got - ref| <= 1e-2 * |ref| + 1e-2 * rms(ref); fp32 outputs
+(residual epilogue) differ only by fp32 accumulation order: 1e-4 relative.
 """
 
 import ctypes
@@ -20,6 +21,7 @@ from verdict_b200 import _abi  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 EPI_STORE, EPI_RESIDUAL, EPI_GATED = 0, 1, 2
+DTYPES = {"fp16": (torch.float16, 0), "bf16": (torch.bfloat16, 1)}
 ACT = {"none": 0, "gelu_erf": 1, "gelu_tanh": 2, "relu": 3, "silu": 4}
 
 
@@ -49,7 +51,7 @@ def torch_act(x, act):
     return x
 
 
-def close_bf16(got, ref, rel=1e-2):
+def close16(got, ref, rel=1e-2):
     got = got.float()
     rms = ref.pow(2).mean().sqrt().item()
     err = (got - ref).abs()
@@ -58,49 +60,52 @@ def close_bf16(got, ref, rel=1e-2):
     assert bad == 0, f"{bad} of {ref.numel()} outside tolerance; max err {err.max().item():.3e} (rms {rms:.3e})"
 
 
-def rand_bf16(*shape, scale=1.0, gen=None):
-    return (torch.randn(*shape, generator=gen, device="cuda") * scale).to(torch.bfloat16)
+def rand16(dt, *shape, scale=1.0, gen=None):
+    return (torch.randn(*shape, generator=gen, device="cuda") * scale).to(DTYPES[dt][0])
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (100, 384, 256), (128, 256, 4096), (300, 1024, 512),
                                    (1000, 768, 768), (4097, 4096, 4096)])
 @pytest.mark.parametrize("act", ["none", "gelu_erf"])
-def test_gemm_store(M, N, K, act):
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_gemm_store(M, N, K, act, dt):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
-    A = rand_bf16(M, K, gen=g)
-    W = rand_bf16(N, K, scale=K ** -0.5, gen=g)
+    A = rand16(dt, M, K, gen=g)
+    W = rand16(dt, N, K, scale=K ** -0.5, gen=g)
     bias = torch.randn(N, generator=g, device="cuda") * 0.1
-    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    run(lib().vdk_gemm, P(A), P(W), M, N, K, EPI_STORE, ACT[act], P(bias), P(out), N)
+    out = torch.empty(M, N, device="cuda", dtype=DTYPES[dt][0])
+    run(lib().vdk_gemm, P(A), P(W), M, N, K, DTYPES[dt][1], EPI_STORE, ACT[act], P(bias), P(out), N)
     ref = torch_act(A.float() @ W.float().T + bias, act)
-    close_bf16(out, ref)
+    close16(out, ref)
 
 
 @pytest.mark.parametrize("M,N,K", [(5, 256, 128), (257, 512, 1024), (2048, 4096, 12288)])
-def test_gemm_residual(M, N, K):
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_gemm_residual(M, N, K, dt):
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
-    A = rand_bf16(M, K, gen=g)
-    W = rand_bf16(N, K, scale=K ** -0.5, gen=g)
+    A = rand16(dt, M, K, gen=g)
+    W = rand16(dt, N, K, scale=K ** -0.5, gen=g)
     h0 = torch.randn(M, N, generator=g, device="cuda")
     h = h0.clone()
-    run(lib().vdk_gemm, P(A), P(W), M, N, K, EPI_RESIDUAL, 0, None, P(h), N)
+    run(lib().vdk_gemm, P(A), P(W), M, N, K, DTYPES[dt][1], EPI_RESIDUAL, 0, None, P(h), N)
     ref = h0 + A.float() @ W.float().T
     torch.testing.assert_close(h, ref, rtol=1e-4, atol=1e-4)
 
 
 @pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
 @pytest.mark.parametrize("M,F,K", [(3, 128, 256), (600, 1024, 512), (1500, 12288, 4096)])
-def test_gemm_gated(M, F, K, act):
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_gemm_gated(M, F, K, act, dt):
     g = torch.Generator(device="cuda").manual_seed(M + F)
-    A = rand_bf16(M, K, gen=g)
-    Wg = rand_bf16(F, K, scale=K ** -0.5, gen=g)
-    Wu = rand_bf16(F, K, scale=K ** -0.5, gen=g)
+    A = rand16(dt, M, K, gen=g)
+    Wg = rand16(dt, F, K, scale=K ** -0.5, gen=g)
+    Wu = rand16(dt, F, K, scale=K ** -0.5, gen=g)
     # Interleave 128-row blocks: [g0, u0, g1, u1, ...]
     W = torch.stack([Wg.view(F // 128, 128, K), Wu.view(F // 128, 128, K)], 1).reshape(2 * F, K).contiguous()
-    out = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
-    run(lib().vdk_gemm, P(A), P(W), M, 2 * F, K, EPI_GATED, ACT[act], None, P(out), F)
+    out = torch.empty(M, F, device="cuda", dtype=DTYPES[dt][0])
+    run(lib().vdk_gemm, P(A), P(W), M, 2 * F, K, DTYPES[dt][1], EPI_GATED, ACT[act], None, P(out), F)
     ref = torch_act(A.float() @ Wg.float().T, act) * (A.float() @ Wu.float().T)
-    close_bf16(out, ref, rel=1.5e-2)
+    close16(out, ref, rel=1.5e-2)
 
 
 def rope_ref(x, pos, theta):
@@ -119,19 +124,20 @@ def rope_ref(x, pos, theta):
     (128, 2, 1, True, False, False),    # k block narrower than a 256-wide tile
     (256, 8, 1, False, False, True),    # Gemma-2B-shaped MQA
 ])
-def test_gemm_qkrope(hd, nq, nkv, qk_norm, bias, plus_one):
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_gemm_qkrope(hd, nq, nkv, qk_norm, bias, plus_one, dt):
     g = torch.Generator(device="cuda").manual_seed(hd + nq)
     M, K = 777, 512
     N = (nq + 2 * nkv) * hd
-    A = rand_bf16(M, K, gen=g)
-    W = rand_bf16(N, K, scale=K ** -0.5, gen=g)
+    A = rand16(dt, M, K, gen=g)
+    W = rand16(dt, N, K, scale=K ** -0.5, gen=g)
     b = torch.randn(N, generator=g, device="cuda") * 0.1 if bias else None
     qn = (1 + 0.1 * torch.randn(hd, generator=g, device="cuda")) if qk_norm else None
     kn = (1 + 0.1 * torch.randn(hd, generator=g, device="cuda")) if qk_norm else None
     pos = torch.randint(0, 4000, (M,), generator=g, device="cuda", dtype=torch.int32)
-    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=DTYPES[dt][0])
     theta = 1e6 if hd == 128 else 1e4
-    run(lib().vdk_gemm_qkrope, P(A), P(W), M, N, K, P(b), P(qn), P(kn), nq * hd, nkv * hd, hd,
+    run(lib().vdk_gemm_qkrope, P(A), P(W), M, N, K, DTYPES[dt][1], P(b), P(qn), P(kn), nq * hd, nkv * hd, hd,
         1 if plus_one else 0, ctypes.c_float(1e-6), P(pos), ctypes.c_double(theta), 4096, P(out), N)
     y = A.float() @ W.float().T
     if b is not None:
@@ -145,7 +151,7 @@ def test_gemm_qkrope(hd, nq, nkv, qk_norm, bias, plus_one):
         q, k = rms(q, qn), rms(k, kn)
     q, k = rope_ref(q, pos, theta), rope_ref(k, pos, theta)
     ref = torch.cat([q.reshape(M, -1), k.reshape(M, -1), v], 1)
-    close_bf16(out, ref)
+    close16(out, ref)
 
 
 def attention_ref(qkv, cu, nq, nkv, hd, q0, k0, v0, causal):
@@ -163,19 +169,20 @@ def attention_ref(qkv, cu, nq, nkv, hd, q0, k0, v0, causal):
 
 @pytest.mark.parametrize("hd,nq,nkv,causal", [(128, 32, 8, True), (256, 8, 1, True), (64, 12, 12, False),
                                               (128, 4, 4, True)])
-def test_attention_varlen(hd, nq, nkv, causal):
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_attention_varlen(hd, nq, nkv, causal, dt):
     g = torch.Generator(device="cuda").manual_seed(hd * 3 + nq)
     lens = [1, 63, 64, 65, 200, 17, 1000, 128]
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     T = int(cu[-1])
     width = (nq + 2 * nkv) * hd
-    qkv = rand_bf16(T, width, gen=g)
-    out = torch.zeros(T, nq * hd, device="cuda", dtype=torch.bfloat16)
+    qkv = rand16(dt, T, width, gen=g)
+    out = torch.zeros(T, nq * hd, device="cuda", dtype=DTYPES[dt][0])
     q0, k0, v0 = 0, nq * hd, (nq + nkv) * hd
-    run(lib().vdk_attention, P(qkv), width, q0, k0, v0, nq, nkv, hd, 1 if causal else 0,
+    run(lib().vdk_attention, P(qkv), width, q0, k0, v0, nq, nkv, hd, DTYPES[dt][1], 1 if causal else 0,
         ctypes.c_void_p(cu.ctypes.data), len(lens), P(out), nq * hd)
     ref = attention_ref(qkv, cu.tolist(), nq, nkv, hd, q0, k0, v0, causal)
-    close_bf16(out, ref, rel=2e-2)
+    close16(out, ref, rel=2e-2)
 
 
 def test_gemm_rejects_bad_shapes():
@@ -183,5 +190,5 @@ def test_gemm_rejects_bad_shapes():
     W = torch.zeros(100, 64, device="cuda", dtype=torch.bfloat16)
     out = torch.zeros(4, 100, device="cuda", dtype=torch.bfloat16)
     err = ctypes.create_string_buffer(256)
-    rc = lib().vdk_gemm(P(A), P(W), 4, 100, 64, 0, 0, None, P(out), 100, None, err, 256)
+    rc = lib().vdk_gemm(P(A), P(W), 4, 100, 64, 1, 0, 0, None, P(out), 100, None, err, 256)
     assert rc == _abi.VD_EINVAL and b"N % 128" in err.value

@@ -77,6 +77,18 @@ def test_decoder_golden(path):
         eng.close()
 
 
+@pytest.mark.parametrize("path", DECODER_FIXTURES, ids=os.path.basename)
+def test_decoder_golden_bf16_activations(path):
+    """The bf16 activation mode (for checkpoints whose activations exceed fp16
+    range) on the reference's golden batches."""
+    spec, batch, ref_logits = load_fixture(path)
+    eng = B200Engine(spec, max_tokens=4096, max_rows=64, max_seq=2048, act_dtype="bf16")
+    try:
+        assert_decoder_parity(engine_logprobs(eng, batch), ref_logits, batch.nopts)
+    finally:
+        eng.close()
+
+
 @pytest.mark.parametrize("path", DECODER_FIXTURES[:1], ids=os.path.basename)
 def test_decoder_golden_raw_logits(path):
     spec, batch, ref_logits = load_fixture(path)
@@ -129,6 +141,27 @@ def test_decoder_shapes_vs_oracle(preset, layers, n_rows, max_len):
         assert_decoder_parity(got, ref, batch.nopts)
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("preset,lens", [("onejev-9b", (48, 130, 300)), ("decider-2b", (64, 257, 700))])
+def test_decoder_full_depth_vs_oracle(preset, lens):
+    """All layers of the benchmark shapes (40 for OneJev-9B, 18 for the 2B
+    decider) against the fp32 oracle, which regenerates each layer's weights
+    on the host as it goes."""
+    spec = with_labels(specs.preset(preset, seed=77))
+    rng = np.random.default_rng(77)
+    rows = decoder_rows(rng, len(lens), spec["vocab"], lengths="fixed:8")
+    for r, n in zip(rows, lens):
+        r.ids = rng.integers(3, spec["vocab"], size=n).tolist()
+        r.markers = [n - 1]
+    batch = collate(rows, Layout(pad_id=0))
+    eng = B200Engine(spec, max_tokens=4096, max_rows=8, max_seq=2048)
+    try:
+        got = engine_logprobs(eng, batch)
+    finally:
+        eng.close()
+    ref = DecoderOracle(spec, cache_layers=False).infer(batch)
+    assert_decoder_parity(got, ref, batch.nopts)
 
 
 @pytest.mark.parametrize("preset,lengths", [("laya-bert", "uniform-bert"), ("laya-xlmr", "lognormal-xlmr")])

@@ -14,6 +14,7 @@ from . import build as _build
 
 VD_OK, VD_EINVAL, VD_ECUDA, VD_EDEAD, VD_ENOMEM, VD_ESPEC, VD_EDEVICE = 0, -1, -2, -3, -4, -5, -6
 VD_MEM_HOST, VD_MEM_DEVICE = 0, 1
+VDK_FP16, VDK_BF16 = 0, 1
 
 _P = ctypes.c_void_p
 _I64P = ctypes.POINTER(ctypes.c_int64)
@@ -60,14 +61,14 @@ SIGNATURES = {
     "vd_close": (None, [_P]),
     # include/vdexec_kernels.h
     "vdk_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
-                                _P, _P, ctypes.c_int64, _P, ctypes.c_char_p, ctypes.c_size_t]),
-    "vdk_gemm_qkrope": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P, _P, _P,
+                                ctypes.c_int, _P, _P, ctypes.c_int64, _P, ctypes.c_char_p, ctypes.c_size_t]),
+    "vdk_gemm_qkrope": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _P, _P, _P,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _P,
                                        ctypes.c_double, ctypes.c_int, _P, ctypes.c_int64, _P, ctypes.c_char_p,
                                        ctypes.c_size_t]),
     "vdk_attention": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
-                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int64, _P, ctypes.c_int64,
-                                     _P, ctypes.c_char_p, ctypes.c_size_t]),
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int64, _P,
+                                     ctypes.c_int64, _P, ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 _lib = None

@@ -2,7 +2,7 @@
 // forward: causal for the decoders, bidirectional for the marker-head encoders,
 // with grouped K/V heads (GQA / MQA).
 //
-// Input is the fused projection output qkv[T, ld] (bf16): head h of Q at column
+// Input is the fused projection output qkv[T, ld] (16-bit T: fp16 or bf16): head h of Q at column
 // q_col0 + h*HD, its K/V head (h / group) at k_col0 / v_col0 + (h/group)*HD.
 // Output attn[T, ld_out] at column h*HD.  Sequences are given by cu_seqlens; a
 // CTA processes one 64-row query tile of one sequence for one query head, as
@@ -26,10 +26,10 @@ struct AttnTile {
 };
 
 struct AttnParams {
-  const __nv_bfloat16* qkv;
+  const void* qkv;        // T [T, ld_qkv]
   int ld_qkv;
   int q_col0, k_col0, v_col0;
-  __nv_bfloat16* out;
+  void* out;              // T [T, ld_out]
   int ld_out;
   const AttnTile* tiles;
   int group;          // query heads per K/V head
@@ -50,8 +50,8 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return static_cast<uint32_t>(r * HD * 2 + ((c ^ (r & 7)) << 4));
 }
 
-template <int HD>
-__device__ __forceinline__ void load_tile_async(uint32_t s_base, const __nv_bfloat16* g, int ld, int row0,
+template <int HD, class T>
+__device__ __forceinline__ void load_tile_async(uint32_t s_base, const T* g, int ld, int row0,
                                                 int rows_valid, int tid) {
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   constexpr int TOTAL = 64 * CH;
@@ -59,12 +59,12 @@ __device__ __forceinline__ void load_tile_async(uint32_t s_base, const __nv_bflo
   for (int i = tid; i < TOTAL; i += 128) {
     const int r = i / CH, c = i % CH;
     const bool ok = r < rows_valid;
-    const __nv_bfloat16* src = g + static_cast<size_t>(row0 + (ok ? r : 0)) * ld + c * 8;
+    const T* src = g + static_cast<size_t>(row0 + (ok ? r : 0)) * ld + c * 8;
     cp_async16(s_base + swz<HD>(r, c), src, ok);
   }
 }
 
-template <int HD, bool CAUSAL>
+template <int HD, bool CAUSAL, class T>
 __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
   using Cfg = AttnConfig<HD>;
   constexpr int NB = Cfg::BN / 8;   // n-blocks of S per warp (8)
@@ -79,18 +79,19 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
   const int kvh = head / p.group;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  const __nv_bfloat16* gq = p.qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.q_col0 + head * HD;
-  const __nv_bfloat16* gk = p.qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.k_col0 + kvh * HD;
-  const __nv_bfloat16* gv = p.qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.v_col0 + kvh * HD;
+  const T* qkv = static_cast<const T*>(p.qkv);
+  const T* gq = qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.q_col0 + head * HD;
+  const T* gk = qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.k_col0 + kvh * HD;
+  const T* gv = qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.v_col0 + kvh * HD;
 
   const int q_rows = min(Cfg::BM, tile.seq_len - tile.q_start);
   int kv_end = tile.seq_len;
   if (CAUSAL) kv_end = min(tile.seq_len, tile.q_start + Cfg::BM);
   const int n_kv = (kv_end + Cfg::BN - 1) / Cfg::BN;
 
-  load_tile_async<HD>(sQ, gq, p.ld_qkv, tile.q_start, q_rows, tid);
-  load_tile_async<HD>(sK0, gk, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
-  load_tile_async<HD>(sV0, gv, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
+  load_tile_async<HD, T>(sQ, gq, p.ld_qkv, tile.q_start, q_rows, tid);
+  load_tile_async<HD, T>(sK0, gk, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
+  load_tile_async<HD, T>(sV0, gv, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
   cp_async_commit();
 
   float o[ND][4];
@@ -106,8 +107,8 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
     if (j + 1 < n_kv) {
       const int kv0n = (j + 1) * Cfg::BN;
       const uint32_t nb = (buf ^ 1) * Cfg::KV_BYTES;
-      load_tile_async<HD>(sK0 + nb, gk, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
-      load_tile_async<HD>(sV0 + nb, gv, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
+      load_tile_async<HD, T>(sK0 + nb, gk, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
+      load_tile_async<HD, T>(sV0 + nb, gv, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -137,8 +138,8 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
         const int r = nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
         const int c = ks * 2 + ((lane >> 3) & 1);
         ldmatrix_x4(sK + swz<HD>(r, c), b0, b1, b2, b3);
-        mma_bf16_16816(s[2 * nb2], a, b0, b1);
-        mma_bf16_16816(s[2 * nb2 + 1], a, b2, b3);
+        mma_16816<T>(s[2 * nb2], a, b0, b1);
+        mma_16816<T>(s[2 * nb2 + 1], a, b2, b3);
       }
     }
 
@@ -202,18 +203,18 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
 #pragma unroll
     for (int ks = 0; ks < Cfg::BN / 16; ++ks) {
       uint32_t a[4];
-      a[0] = pack_bf16x2(s[2 * ks][0], s[2 * ks][1]);
-      a[1] = pack_bf16x2(s[2 * ks][2], s[2 * ks][3]);
-      a[2] = pack_bf16x2(s[2 * ks + 1][0], s[2 * ks + 1][1]);
-      a[3] = pack_bf16x2(s[2 * ks + 1][2], s[2 * ks + 1][3]);
+      a[0] = Elem<T>::pack2(s[2 * ks][0], s[2 * ks][1]);
+      a[1] = Elem<T>::pack2(s[2 * ks][2], s[2 * ks][3]);
+      a[2] = Elem<T>::pack2(s[2 * ks + 1][0], s[2 * ks + 1][1]);
+      a[3] = Elem<T>::pack2(s[2 * ks + 1][2], s[2 * ks + 1][3]);
 #pragma unroll
       for (int nd2 = 0; nd2 < ND / 2; ++nd2) {
         uint32_t b0, b1, b2, b3;
         const int r = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
         const int c = nd2 * 2 + (lane >> 4);
         ldmatrix_x4_trans(sV + swz<HD>(r, c), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * nd2], a, b0, b1);
-        mma_bf16_16816(o[2 * nd2 + 1], a, b2, b3);
+        mma_16816<T>(o[2 * nd2], a, b0, b1);
+        mma_16816<T>(o[2 * nd2 + 1], a, b2, b3);
       }
     }
     __syncthreads();
@@ -228,14 +229,14 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
   const float inv0 = l_run[0] > 0.0f ? 1.0f / l_run[0] : 0.0f;
   const float inv1 = l_run[1] > 0.0f ? 1.0f / l_run[1] : 0.0f;
   const int r0 = warp * 16 + (lane >> 2);
-  __nv_bfloat16* out0 = p.out + static_cast<size_t>(tile.seq_start + tile.q_start + r0) * p.ld_out + head * HD;
-  __nv_bfloat16* out1 = out0 + static_cast<size_t>(8) * p.ld_out;
+  T* out0 = static_cast<T*>(p.out) + static_cast<size_t>(tile.seq_start + tile.q_start + r0) * p.ld_out + head * HD;
+  T* out1 = out0 + static_cast<size_t>(8) * p.ld_out;
   const bool ok0 = r0 < q_rows, ok1 = r0 + 8 < q_rows;
 #pragma unroll
   for (int nd = 0; nd < ND; ++nd) {
     const int col = nd * 8 + ((lane & 3) << 1);
-    if (ok0) *reinterpret_cast<uint32_t*>(out0 + col) = pack_bf16x2(o[nd][0] * inv0, o[nd][1] * inv0);
-    if (ok1) *reinterpret_cast<uint32_t*>(out1 + col) = pack_bf16x2(o[nd][2] * inv1, o[nd][3] * inv1);
+    if (ok0) *reinterpret_cast<uint32_t*>(out0 + col) = Elem<T>::pack2(o[nd][0] * inv0, o[nd][1] * inv0);
+    if (ok1) *reinterpret_cast<uint32_t*>(out1 + col) = Elem<T>::pack2(o[nd][2] * inv1, o[nd][3] * inv1);
   }
 }
 

@@ -9,6 +9,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -52,6 +53,36 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
   __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(b);
 }
+
+// The 16-bit element type of activations and projection weights: fp16 (the
+// default: 10 mantissa bits, exact for every bf16 checkpoint value >= 2^-14 in
+// magnitude) or bf16.  Both feed the tensor cores at the same rate.
+template <class T>
+struct Elem;
+
+template <>
+struct Elem<__half> {
+  static constexpr uint32_t kUmmaFormat = 0;  // kind::f16 operand format F16
+  __device__ __forceinline__ static uint32_t pack2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __device__ __forceinline__ static float2 unpack2(uint32_t v) {
+    __half2 h = *reinterpret_cast<__half2*>(&v);
+    return __half22float2(h);
+  }
+  __device__ __forceinline__ static __half from(float x) { return __float2half_rn(x); }
+  __device__ __forceinline__ static float to(__half x) { return __half2float(x); }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr uint32_t kUmmaFormat = 1;  // kind::f16 operand format BF16
+  __device__ __forceinline__ static uint32_t pack2(float lo, float hi) { return pack_bf16x2(lo, hi); }
+  __device__ __forceinline__ static float2 unpack2(uint32_t v) { return unpack_bf16x2(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from(float x) { return __float2bfloat16_rn(x); }
+  __device__ __forceinline__ static float to(__nv_bfloat16 x) { return __bfloat162float(x); }
+};
 
 // ---------------------------------------------------------------------------
 // mbarrier
@@ -141,8 +172,9 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 inputs, fp32 accumulate).
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 or bf16 inputs per the
+// instruction descriptor, fp32 accumulate).
+__device__ __forceinline__ void umma_f16kind(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -170,11 +202,12 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, MxN tile.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+// Instruction descriptor: 16-bit x 16-bit -> fp32, both operands K-major, MxN
+// tile; fmt = 0 for fp16 operands, 1 for bf16 (A and B always share the type).
+__host__ __device__ constexpr uint32_t umma_idesc_f16kind(int m, int n, uint32_t fmt) {
   return (1u << 4)                                  // D format: f32
-         | (1u << 7)                                // A format: bf16
-         | (1u << 10)                               // B format: bf16
+         | (fmt << 7)                               // A format
+         | (fmt << 10)                              // B format
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
@@ -208,12 +241,21 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+template <class T>
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (Elem<T>::kUmmaFormat == 1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
 }
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
   const int n = pred ? 16 : 0;  // zero-fill when the row is outside the sequence

@@ -63,12 +63,11 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int T, const __nv_b
   }
 }
 
-// RMSNorm of fp32 rows -> bf16: out = bf16(x * rsqrt(mean(x^2) + eps) * g),
+// RMSNorm of fp32 rows -> 16-bit T: out = T(x * rsqrt(mean(x^2) + eps) * g),
 // g = w or (1 + w).
-template <int NT>
+template <int NT, class T>
 __global__ void __launch_bounds__(NT) rmsnorm_kernel(const float* __restrict__ x, int d, const float* __restrict__ w,
-                                                     int plus_one, float eps, __nv_bfloat16* __restrict__ out,
-                                                     int rows) {
+                                                     int plus_one, float eps, T* __restrict__ out, int rows) {
   __shared__ float red[NT / 32 + 1];
   const int r = blockIdx.x;
   if (r >= rows) return;
@@ -87,20 +86,18 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const float* __restrict__ x
     const float4 v = xr[i];
     const float4 g = __ldg(wv + i);
     uint2 pk;
-    pk.x = pack_bf16x2(v.x * rstd * (g.x + add), v.y * rstd * (g.y + add));
-    pk.y = pack_bf16x2(v.z * rstd * (g.z + add), v.w * rstd * (g.w + add));
+    pk.x = Elem<T>::pack2(v.x * rstd * (g.x + add), v.y * rstd * (g.y + add));
+    pk.y = Elem<T>::pack2(v.z * rstd * (g.z + add), v.w * rstd * (g.w + add));
     o[i] = pk;
   }
 }
 
 // LayerNorm of fp32 rows: y = (x - mean) / sqrt(var + eps) * w + b.  Writes the
-// fp32 result back in place when `inplace` and always a bf16 copy to `out`.
-// With `src_rows` it gathers row src_rows[r] of x (no in-place write then) and
-// writes fp32 rows to out_f.
-template <int NT>
+// fp32 result back in place when `inplace` and always a 16-bit copy to `out`.
+template <int NT, class T>
 __global__ void __launch_bounds__(NT)
     layernorm_kernel(float* __restrict__ x, int d, const float* __restrict__ w, const float* __restrict__ bvec,
-                     float eps, int inplace, __nv_bfloat16* __restrict__ out, int rows) {
+                     float eps, int inplace, T* __restrict__ out, int rows) {
   __shared__ float red[NT / 32 + 1];
   const int r = blockIdx.x;
   if (r >= rows) return;
@@ -130,22 +127,21 @@ __global__ void __launch_bounds__(NT)
     v.w = (v.w - mean) * rstd * g.w + bb.w;
     if (inplace) xr[i] = v;
     uint2 pk;
-    pk.x = pack_bf16x2(v.x, v.y);
-    pk.y = pack_bf16x2(v.z, v.w);
+    pk.x = Elem<T>::pack2(v.x, v.y);
+    pk.y = Elem<T>::pack2(v.z, v.w);
     o[i] = pk;
   }
 }
 
-// Encoder embeddings: h = LN(word[tok] + pos[p] + type[0]); fp32 h and bf16 copy.
-template <int NT>
+// Encoder embeddings: h = LN(word[tok] + pos[p] + type[0]); fp32 h and a 16-bit copy.
+template <int NT, class T>
 __global__ void __launch_bounds__(NT)
-    embed_ln_kernel(const int* __restrict__ tokens, const int* __restrict__ positions, int T,
+    embed_ln_kernel(const int* __restrict__ tokens, const int* __restrict__ positions, int n_tokens,
                     const __nv_bfloat16* __restrict__ word, const __nv_bfloat16* __restrict__ pos_emb,
                     const __nv_bfloat16* __restrict__ type0, int d, const float* __restrict__ w,
-                    const float* __restrict__ bvec, float eps, float* __restrict__ h,
-                    __nv_bfloat16* __restrict__ out) {
+                    const float* __restrict__ bvec, float eps, float* __restrict__ h, T* __restrict__ out) {
   const int t = blockIdx.x;
-  if (t >= T) return;
+  if (t >= n_tokens) return;
   const __nv_bfloat16* a = word + static_cast<size_t>(tokens[t]) * d;
   const __nv_bfloat16* p = pos_emb + static_cast<size_t>(positions[t]) * d;
   float* hr = h + static_cast<size_t>(t) * d;
@@ -166,7 +162,7 @@ __global__ void __launch_bounds__(NT)
   for (int i = threadIdx.x; i < d; i += NT) {
     const float v = (hr[i] - mean) * rstd * w[i] + bvec[i];
     hr[i] = v;
-    out[static_cast<size_t>(t) * d + i] = __float2bfloat16_rn(v);
+    out[static_cast<size_t>(t) * d + i] = Elem<T>::from(v);
   }
 }
 
@@ -271,12 +267,12 @@ __global__ void marker_index_kernel(const int* __restrict__ cu, const int64_t* _
   idx[q] = start + static_cast<int>(p);
 }
 
-// Gather + LayerNorm of marker rows -> bf16 scorer input.
-template <int NT>
+// Gather + LayerNorm of marker rows -> 16-bit scorer input.
+template <int NT, class T>
 __global__ void __launch_bounds__(NT)
     gather_layernorm_kernel(const float* __restrict__ h, const int* __restrict__ idx, int n, int d,
                             const float* __restrict__ w, const float* __restrict__ bvec, float eps,
-                            __nv_bfloat16* __restrict__ out) {
+                            T* __restrict__ out) {
   __shared__ float red[NT / 32 + 1];
   const int r = blockIdx.x;
   if (r >= n) return;
@@ -291,13 +287,14 @@ __global__ void __launch_bounds__(NT)
   }
   const float rstd = rsqrtf(block_sum<NT>(ss, red) / static_cast<float>(d) + eps);
   for (int i = threadIdx.x; i < d; i += NT)
-    out[static_cast<size_t>(r) * d + i] = __float2bfloat16_rn((x[i] - mean) * rstd * w[i] + bvec[i]);
+    out[static_cast<size_t>(r) * d + i] = Elem<T>::from((x[i] - mean) * rstd * w[i] + bvec[i]);
 }
 
 // Final scorer projection Linear(d, 1) on the GELU'd rows, then the marker mask:
 // out[i, j] = y[i*k + j] . w + b for live markers, -1e4 otherwise; columns
 // j >= k of a wider output are -1e4.
-__global__ void marker_score_kernel(const __nv_bfloat16* __restrict__ y, int d, const float* __restrict__ w,
+template <class T>
+__global__ void marker_score_kernel(const T* __restrict__ y, int d, const float* __restrict__ w,
                                     const float* __restrict__ bias, const uint8_t* __restrict__ marker_mask, int b,
                                     int k, float* __restrict__ out, int width) {
   const int i = blockIdx.x;
@@ -305,8 +302,8 @@ __global__ void marker_score_kernel(const __nv_bfloat16* __restrict__ y, int d, 
   for (int j = warp; j < width; j += nw) {
     float acc = 0.0f;
     if (j < k && marker_mask[i * k + j]) {
-      const __nv_bfloat16* yr = y + static_cast<size_t>(i * k + j) * d;
-      for (int c = lane; c < d; c += 32) acc += __bfloat162float(yr[c]) * w[c];
+      const T* yr = y + static_cast<size_t>(i * k + j) * d;
+      for (int c = lane; c < d; c += 32) acc += Elem<T>::to(yr[c]) * w[c];
 #pragma unroll
       for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
       acc += bias[0];

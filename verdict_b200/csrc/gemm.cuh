@@ -1,4 +1,4 @@
-// Persistent tcgen05 GEMM for sm_100a: C[M, N] = A[M, K] * W[N, K]^T, bf16 in,
+// Persistent tcgen05 GEMM for sm_100a: C[M, N] = A[M, K] * W[N, K]^T, 16-bit in,
 // fp32 accumulate in tensor memory, with the layer's elementwise work fused
 // into the epilogue.
 //
@@ -13,9 +13,9 @@
 // ~148 tiles in flight share A row-blocks and W column-blocks in L2.
 //
 // Epilogues:
-//   kEpiStore     : out_bf16 = act(acc + bias)
+//   kEpiStore     : out_T = act(acc + bias)            (T = fp16 or bf16)
 //   kEpiResidual  : out_f32 += acc + bias                (residual stream in fp32)
-//   kEpiGated     : out_bf16[:, n/2 + j] = act(acc[:, j]) * acc[:, BN/2 + j]
+//   kEpiGated     : out_T[:, n/2 + j] = act(acc[:, j]) * acc[:, BN/2 + j]
 //                   (W rows are interleaved at load time in blocks of BN/2: gate, up)
 //   kEpiQKRope    : per attention head of the tile: optional bias, optional
 //                   q/k RMSNorm over the head, rotary embedding for q and k
@@ -30,7 +30,7 @@ enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiGated = 2, kEpiQKRope 
 enum ActKind : int { kActNone = 0, kActGeluErf = 1, kActGeluTanh = 2, kActRelu = 3, kActSilu = 4 };
 
 struct EpiParams {
-  void* out;              // bf16 (store / gated / qkrope) or fp32 (residual)
+  void* out;              // T (store / gated / qkrope) or fp32 (residual)
   int ld_out;             // row stride of out, elements
   const float* bias;      // [N] or null
   int act;                // ActKind
@@ -70,15 +70,16 @@ __device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32])
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+template <class T>
+__device__ __forceinline__ void store_x32(T* dst, const float (&v)[32]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint4 w;
-    w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-    w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-    w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-    w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    w.x = Elem<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = Elem<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = Elem<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = Elem<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
     d[q] = w;
   }
 }
@@ -97,7 +98,7 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const float* bias, in
 }
 
 // One head of kEpiQKRope: columns [col0, col0 + hd) of row `row`, TMEM at tbase.
-template <int HD>
+template <int HD, class T>
 __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_ok, int col0, const EpiParams& p,
                                               const float* gain) {
   constexpr int HALF = HD / 2;
@@ -117,7 +118,7 @@ __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_
   }
   const int pos = row_ok ? __ldg(p.positions + row) : 0;
   const float2* rope = p.rope + static_cast<size_t>(pos) * HALF;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out;
+  T* out = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out;
 #pragma unroll 1
   for (int c = 0; c < CHUNKS; ++c) {
     float x1[32], x2[32];
@@ -145,13 +146,13 @@ __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_
         x1[j] = a * cs.x - b * cs.y;
         x2[j] = b * cs.x + a * cs.y;
       }
-      store_bf16x32(out + col0 + c * 32, x1);
-      store_bf16x32(out + col0 + HALF + c * 32, x2);
+      store_x32<T>(out + col0 + c * 32, x1);
+      store_x32<T>(out + col0 + HALF + c * 32, x2);
     }
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, class T>
 __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_ok, int n0, const EpiParams& p) {
   if constexpr (EPI == kEpiStore) {
 #pragma unroll 1
@@ -162,7 +163,7 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], p.act);
       if (row_ok)
-        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 + c * 32, v);
+        store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 + c * 32, v);
     }
   } else if constexpr (EPI == kEpiResidual) {
 #pragma unroll 1
@@ -194,8 +195,7 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
 #pragma unroll
       for (int j = 0; j < 32; ++j) g[j] = apply_act(g[j], p.act) * u[j];
       if (row_ok)
-        store_bf16x32(
-            reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 / 2 + c * 32, g);
+        store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 / 2 + c * 32, g);
     }
   } else if constexpr (EPI == kEpiQKRope) {
     // One or two heads per tile (head_dim 256 or 128); heads never straddle tiles.
@@ -205,7 +205,7 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
         const int col0 = n0 + h * 128;
         const uint32_t tb = taddr + h * 128;
         if (col0 < p.q_cols + p.k_cols) {
-          epi_head_rope<128>(tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
+          epi_head_rope<128, T>(tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
         } else {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
@@ -213,15 +213,15 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
             tmem_load_f32x32(tb + c * 32, v);
             add_bias32(v, p.bias, col0 + c * 32);
             if (row_ok)
-              store_bf16x32(
-                  reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
+              store_x32<T>(
+                  reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
           }
         }
       }
     } else if constexpr (BN == 256) {
       const int col0 = n0;
       if (col0 < p.q_cols + p.k_cols) {
-        epi_head_rope<256>(taddr, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
+        epi_head_rope<256, T>(taddr, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
       } else {
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
@@ -229,8 +229,8 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
           tmem_load_f32x32(taddr + c * 32, v);
           add_bias32(v, p.bias, col0 + c * 32);
           if (row_ok)
-            store_bf16x32(
-                reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
+            store_x32<T>(
+                reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
         }
       }
     }
@@ -262,13 +262,13 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
   n = local / gm;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, class T>
 __global__ void __launch_bounds__(192, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shape, EpiParams ep, int* err) {
   using Cfg = GemmConfig<BN>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+  constexpr uint32_t IDESC = umma_idesc_f16kind(BM, BN, Elem<T>::kUmmaFormat);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32), IDESC,
+            umma_f16kind(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32), IDESC,
                       (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row = m * BM + row_in_tile;
-      gemm_epilogue<BN, EPI>(taddr, row, row < shape.M, n * BN, ep);
+      gemm_epilogue<BN, EPI, T>(taddr, row, row < shape.M, n * BN, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);

@@ -38,18 +38,30 @@ static void ops_attrs_once() {
   std::call_once(once[dev & 63], [] { init_kernel_attrs(); });
 }
 
-template <int EPI>
-static void ops_gemm_launch(const CUtensorMap& a, const CUtensorMap& w, int bn, int M, int N, int K,
-                            const EpiParams& ep, cudaStream_t s, int* word, int sms) {
+template <int EPI, class T>
+static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, int bn, int M, int N, int K,
+                              const EpiParams& ep, cudaStream_t s, int* word, int sms) {
   const int tiles = ((M + 127) / 128) * (N / bn);
   const int grid = std::min(tiles, sms);
   const GemmShape shape{M, N, K};
   if (bn == 256)
-    gemm_tcgen05_kernel<256, EPI><<<grid, 192, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
+    gemm_tcgen05_kernel<256, EPI, T><<<grid, 192, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
   else if constexpr (EPI != kEpiGated)
-    gemm_tcgen05_kernel<128, EPI><<<grid, 192, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
+    gemm_tcgen05_kernel<128, EPI, T><<<grid, 192, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
   else
     fail(VD_EINVAL, "gated GEMM needs N % 256 == 0");
+}
+
+template <int EPI>
+static void ops_gemm_launch(bool f16, const CUtensorMap& a, const CUtensorMap& w, int bn, int M, int N, int K,
+                            const EpiParams& ep, cudaStream_t s, int* word, int sms) {
+  if (f16) ops_gemm_launch_t<EPI, __half>(a, w, bn, M, N, K, ep, s, word, sms);
+  else ops_gemm_launch_t<EPI, __nv_bfloat16>(a, w, bn, M, N, K, ep, s, word, sms);
+}
+
+static bool ops_dtype(int dtype) {
+  if (dtype != VDK_FP16 && dtype != VDK_BF16) fail(VD_EINVAL, "dtype must be VDK_FP16 or VDK_BF16");
+  return dtype == VDK_FP16;
 }
 
 static int device_sms() {
@@ -61,7 +73,7 @@ static int device_sms() {
 
 }  // namespace vd
 
-extern "C" VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int epi, int act,
+extern "C" VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int dtype, int epi, int act,
                                const float* bias, void* out, int64_t ld_out, void* stream, char* err, size_t errlen) {
   return guarded(nullptr, err, errlen, [&] {
     if (M < 1 || N % 128 != 0 || K % 64 != 0 || K < 64) fail(VD_EINVAL, "need M >= 1, N % 128 == 0, K % 64 == 0");
@@ -69,27 +81,29 @@ extern "C" VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t 
     if (epi < 0 || epi > kEpiGated) fail(VD_EINVAL, "unknown epilogue (use vdk_gemm_qkrope for QK-RoPE)");
     if (ld_out < (epi == kEpiGated ? N / 2 : N)) fail(VD_EINVAL, "ld_out smaller than the output width");
     if (!A || !W || !out) fail(VD_EINVAL, "null buffer");
+    const bool f16 = ops_dtype(dtype);
     ops_attrs_once();
     int dev = 0;
     cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
     int* word = ops_error_word(dev);
     const int bn = (N % 256 == 0) ? 256 : 128;
-    const CUtensorMap a = make_map(A, M, K, 128);
-    const CUtensorMap w = make_map(W, N, K, bn);
+    const CUtensorMap a = make_map(A, M, K, 128, f16);
+    const CUtensorMap w = make_map(W, N, K, bn, f16);
     EpiParams ep = epi_params_for(out, static_cast<int>(ld_out), bias, act);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int sms = device_sms();
     const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
     switch (epi) {
-      case kEpiStore: ops_gemm_launch<kEpiStore>(a, w, bn, m, n, k, ep, s, word, sms); break;
-      case kEpiResidual: ops_gemm_launch<kEpiResidual>(a, w, bn, m, n, k, ep, s, word, sms); break;
-      case kEpiGated: ops_gemm_launch<kEpiGated>(a, w, bn, m, n, k, ep, s, word, sms); break;
+      case kEpiStore: ops_gemm_launch<kEpiStore>(f16, a, w, bn, m, n, k, ep, s, word, sms); break;
+      case kEpiResidual: ops_gemm_launch<kEpiResidual>(f16, a, w, bn, m, n, k, ep, s, word, sms); break;
+      case kEpiGated: ops_gemm_launch<kEpiGated>(f16, a, w, bn, m, n, k, ep, s, word, sms); break;
     }
     ops_finish(s, word);
   });
 }
 
-extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, int64_t N, int64_t K, const float* bias,
+extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int dtype,
+                                      const float* bias,
                                       const float* q_norm, const float* k_norm, int q_cols, int k_cols, int head_dim,
                                       int plus_one, float eps, const int32_t* positions, double theta, int max_pos,
                                       void* out, int64_t ld_out, void* stream, char* err, size_t errlen) {
@@ -98,6 +112,7 @@ extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, i
     if (head_dim != 128 && head_dim != 256) fail(VD_EINVAL, "head_dim must be 128 or 256");
     if (ld_out < N || !A || !W || !out || !positions) fail(VD_EINVAL, "bad output stride or null buffer");
     if (max_pos < 1) fail(VD_EINVAL, "max_pos must be positive");
+    const bool f16 = ops_dtype(dtype);
     int bn = 256;
     if (head_dim == 128 && (q_cols % 256 != 0 || k_cols % 256 != 0 || N % 256 != 0)) bn = 128;
     if (head_dim == 256 && (q_cols % 256 != 0 || k_cols % 256 != 0 || N % 256 != 0))
@@ -121,8 +136,8 @@ extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, i
     cuda_check(cudaMalloc(&rope, tab.size() * sizeof(float2)), "rope table");
     std::unique_ptr<float2, decltype(&cudaFree)> guard(rope, &cudaFree);
     cuda_check(cudaMemcpy(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope table");
-    const CUtensorMap a = make_map(A, M, K, 128);
-    const CUtensorMap w = make_map(W, N, K, bn);
+    const CUtensorMap a = make_map(A, M, K, 128, f16);
+    const CUtensorMap w = make_map(W, N, K, bn, f16);
     EpiParams ep = epi_params_for(out, static_cast<int>(ld_out), bias, kActNone);
     ep.q_norm = q_norm;
     ep.k_norm = k_norm;
@@ -133,18 +148,20 @@ extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, i
     ep.eps = eps;
     ep.positions = positions;
     ep.rope = rope;
-    ops_gemm_launch<kEpiQKRope>(a, w, bn, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ep, s, word,
+    ops_gemm_launch<kEpiQKRope>(f16, a, w, bn, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ep, s, word,
                                 device_sms());
     ops_finish(s, word);
   });
 }
 
 extern "C" VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0, int64_t v_col0,
-                                    int heads, int kv_heads, int head_dim, int causal, const int32_t* cu_seqlens_host,
-                                    int64_t nseq, void* out, int64_t ld_out, void* stream, char* err, size_t errlen) {
+                                    int heads, int kv_heads, int head_dim, int dtype, int causal,
+                                    const int32_t* cu_seqlens_host, int64_t nseq, void* out, int64_t ld_out,
+                                    void* stream, char* err, size_t errlen) {
   return guarded(nullptr, err, errlen, [&] {
     if (heads < 1 || kv_heads < 1 || heads % kv_heads != 0) fail(VD_EINVAL, "heads must be a multiple of kv_heads");
     if (nseq < 1 || !cu_seqlens_host) fail(VD_EINVAL, "need at least one sequence");
+    const bool f16 = ops_dtype(dtype);
     ops_attrs_once();
     std::vector<AttnTile> tiles;
     for (int64_t i = 0; i < nseq; ++i) {
@@ -159,25 +176,30 @@ extern "C" VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_c
     std::unique_ptr<AttnTile, decltype(&cudaFree)> guard(d_tiles, &cudaFree);
     cuda_check(cudaMemcpy(d_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice), "tiles");
     AttnParams p;
-    p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+    p.qkv = qkv;
     p.ld_qkv = static_cast<int>(ld_qkv);
     p.q_col0 = static_cast<int>(q_col0);
     p.k_col0 = static_cast<int>(k_col0);
     p.v_col0 = static_cast<int>(v_col0);
-    p.out = static_cast<__nv_bfloat16*>(out);
+    p.out = out;
     p.ld_out = static_cast<int>(ld_out);
     p.tiles = d_tiles;
     p.group = heads / kv_heads;
     p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)) * 1.4426950408889634);
     dim3 grid(static_cast<unsigned>(tiles.size()), heads);
-    if (head_dim == 64 && !causal)
-      attention_varlen_kernel<64, false><<<grid, 128, AttnConfig<64>::SMEM_BYTES, s>>>(p);
-    else if (head_dim == 128 && causal)
-      attention_varlen_kernel<128, true><<<grid, 128, AttnConfig<128>::SMEM_BYTES, s>>>(p);
-    else if (head_dim == 256 && causal)
-      attention_varlen_kernel<256, true><<<grid, 128, AttnConfig<256>::SMEM_BYTES, s>>>(p);
-    else
-      fail(VD_EINVAL, "supported: head_dim 64 bidirectional, 128 / 256 causal");
+    auto run = [&](auto tag) {
+      using T = decltype(tag);
+      if (head_dim == 64 && !causal)
+        attention_varlen_kernel<64, false, T><<<grid, 128, AttnConfig<64>::SMEM_BYTES, s>>>(p);
+      else if (head_dim == 128 && causal)
+        attention_varlen_kernel<128, true, T><<<grid, 128, AttnConfig<128>::SMEM_BYTES, s>>>(p);
+      else if (head_dim == 256 && causal)
+        attention_varlen_kernel<256, true, T><<<grid, 128, AttnConfig<256>::SMEM_BYTES, s>>>(p);
+      else
+        fail(VD_EINVAL, "supported: head_dim 64 bidirectional, 128 / 256 causal");
+    };
+    if (f16) run(__half());
+    else run(__nv_bfloat16());
     cuda_check(cudaGetLastError(), "attention launch");
     cuda_check(cudaStreamSynchronize(s), "synchronize");
   });

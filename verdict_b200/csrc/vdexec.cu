@@ -172,14 +172,14 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Row-major [rows, cols] bf16 matrix, box = [box_rows, 64] with 128-byte swizzle.
-static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+// Row-major [rows, cols] 16-bit matrix, box = [box_rows, 64] with 128-byte swizzle.
+static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16 = true) {
   CUtensorMap m;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
   cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+  CUresult r = encode_fn()(&m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fail(VD_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
@@ -190,7 +190,7 @@ static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box
 // Weights
 // ---------------------------------------------------------------------------
 struct Linear {
-  bf16* w = nullptr;    // [n, k]
+  void* w = nullptr;    // [n, k] 16-bit (the handle's element type)
   float* b = nullptr;   // [n] or null
   int n = 0, k = 0, bn = 256;
   CUtensorMap map;
@@ -214,6 +214,7 @@ struct Handle;
 struct Options {
   int64_t max_tokens = 65536, max_rows = 512, max_seq = 8192, max_markers = 16384;
   bool logprobs = true;
+  bool f16 = true;  // activations and projection weights in fp16 (else bf16)
 };
 
 }  // namespace vd
@@ -242,7 +243,7 @@ struct vd_handle {
   vd::Linear sc1;
   // workspace
   float* h = nullptr;
-  __nv_bfloat16 *xn = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *mrow = nullptr, *mhid = nullptr;
+  void *xn = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *mrow = nullptr, *mhid = nullptr;  // 16-bit
   int *tokens = nullptr, *positions = nullptr, *seq_id = nullptr, *cu = nullptr, *midx = nullptr, *d_err = nullptr;
   vd::AttnTile* tiles = nullptr;
   int64_t max_tiles = 0;
@@ -329,11 +330,25 @@ static void prof_collect(vd_handle* H) {
 
 static int grid_for(int64_t n) { return static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16)); }
 
+// A synthetic tensor in the element type `f16` selects (embedding tables are always bf16).
+static void synth_w(vd_handle* H, void* dst, bool f16, const std::string& name, int64_t rows, int64_t cols,
+                    float scale, float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
+  if (group == 0) group = rows;
+  const uint64_t base = tensor_base(H->spec.seed, name);
+  if (f16)
+    synth_rows_kernel<__half><<<grid_for(rows * cols), 256, 0, H->stream>>>(
+        static_cast<__half*>(dst), rows, cols, base, scale, offset, group, stride, off);
+  else
+    synth_rows_kernel<__nv_bfloat16><<<grid_for(rows * cols), 256, 0, H->stream>>>(
+        static_cast<__nv_bfloat16*>(dst), rows, cols, base, scale, offset, group, stride, off);
+}
 static void synth_bf16(vd_handle* H, bf16* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
                        float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
-  if (group == 0) group = rows;
-  synth_rows_bf16_kernel<<<grid_for(rows * cols), 256, 0, H->stream>>>(
-      dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, group, stride, off);
+  synth_w(H, dst, false, name, rows, cols, scale, offset, group, stride, off);
+}
+static void synth_lin(vd_handle* H, void* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
+                      float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
+  synth_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off);
 }
 static void synth_f32(vd_handle* H, float* dst, const std::string& name, int64_t n, float scale, float offset) {
   synth_f32_kernel<<<grid_for(n), 256, 0, H->stream>>>(dst, n, tensor_base(H->spec.seed, name), scale, offset);
@@ -346,9 +361,9 @@ static void init_linear(vd_handle* H, Linear& L, int n, int k, bool bias, int bn
   L.n = n;
   L.k = k;
   L.bn = bn ? bn : pick_bn(n);
-  L.w = dalloc<bf16>(H, static_cast<size_t>(n) * k);
+  L.w = dalloc<uint16_t>(H, static_cast<size_t>(n) * k);
   L.b = bias ? dalloc<float>(H, n) : nullptr;
-  L.map = make_map(L.w, n, k, L.bn);
+  L.map = make_map(L.w, n, k, L.bn, H->opt.f16);
 }
 
 static void load_decoder(vd_handle* H) {
@@ -371,9 +386,9 @@ static void load_decoder(vd_handle* H) {
     synth_f32(H, L.in_norm, p + "input_layernorm.weight", d, n_scale, n_off);
     synth_f32(H, L.post_norm, p + "post_attention_layernorm.weight", d, n_scale, n_off);
     init_linear(H, L.qkv, s.qkv_width(), d, s.qkv_bias, bn_qkv);
-    synth_bf16(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
-    synth_bf16(H, L.qkv.w, p + "self_attn.k_proj.weight", kc, d, lin, 0.0f, kc, 0, qc);
-    synth_bf16(H, L.qkv.w, p + "self_attn.v_proj.weight", kc, d, lin, 0.0f, kc, 0, qc + kc);
+    synth_lin(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
+    synth_lin(H, L.qkv.w, p + "self_attn.k_proj.weight", kc, d, lin, 0.0f, kc, 0, qc);
+    synth_lin(H, L.qkv.w, p + "self_attn.v_proj.weight", kc, d, lin, 0.0f, kc, 0, qc + kc);
     if (s.qkv_bias) {
       synth_f32(H, L.qkv.b, p + "self_attn.q_proj.bias", qc, lin, 0.0f);
       synth_f32(H, L.qkv.b + qc, p + "self_attn.k_proj.bias", kc, lin, 0.0f);
@@ -386,12 +401,12 @@ static void load_decoder(vd_handle* H) {
       synth_f32(H, L.k_norm, p + "self_attn.k_norm.weight", hd, n_scale, n_off);
     }
     init_linear(H, L.o, d, qc, false);
-    synth_bf16(H, L.o.w, p + "self_attn.o_proj.weight", d, qc, lin, 0.0f);
+    synth_lin(H, L.o.w, p + "self_attn.o_proj.weight", d, qc, lin, 0.0f);
     init_linear(H, L.gu, 2 * f, d, false, 256);
-    synth_bf16(H, L.gu.w, p + "mlp.gate_proj.weight", f, d, lin, 0.0f, 128, 256, 0);
-    synth_bf16(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
+    synth_lin(H, L.gu.w, p + "mlp.gate_proj.weight", f, d, lin, 0.0f, 128, 256, 0);
+    synth_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
     init_linear(H, L.down, d, f, false);
-    synth_bf16(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
+    synth_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
   }
   H->final_norm = dalloc<float>(H, d);
   synth_f32(H, H->final_norm, "model.norm.weight", d, n_scale, n_off);
@@ -422,7 +437,7 @@ static void load_decoder(vd_handle* H) {
 static void enc_linear(vd_handle* H, Linear& L, const std::string& wname, const std::string& bname, int n, int k,
                        float lin) {
   init_linear(H, L, n, k, true);
-  synth_bf16(H, L.w, wname, n, k, lin, 0.0f);
+  synth_lin(H, L.w, wname, n, k, lin, 0.0f);
   synth_f32(H, L.b, bname, n, lin, 0.0f);
 }
 
@@ -449,7 +464,7 @@ static void load_encoder(vd_handle* H) {
     init_linear(H, L.qkv, 3 * d, d, true);
     const char* parts[3] = {"query", "key", "value"};
     for (int j = 0; j < 3; ++j) {
-      synth_bf16(H, L.qkv.w, p + "attention.self." + parts[j] + ".weight", d, d, lin, 0.0f, d, 0,
+      synth_lin(H, L.qkv.w, p + "attention.self." + parts[j] + ".weight", d, d, lin, 0.0f, d, 0,
                  static_cast<int64_t>(j) * d);
       synth_f32(H, L.qkv.b + j * d, p + "attention.self." + parts[j] + ".bias", d, lin, 0.0f);
     }
@@ -540,10 +555,10 @@ static void alloc_workspace(vd_handle* H) {
   const int attw = s.decoder() ? s.heads * s.head_dim : d;
   const int actw = s.decoder() ? s.ffn : std::max(s.ffn, 4 * d);
   H->h = dalloc<float>(H, T * d);
-  H->xn = dalloc<bf16>(H, T * d);
-  H->qkv = dalloc<bf16>(H, T * qkvw);
-  H->attn = dalloc<bf16>(H, T * attw);
-  H->act = dalloc<bf16>(H, T * actw);
+  H->xn = dalloc<uint16_t>(H, T * d);
+  H->qkv = dalloc<uint16_t>(H, T * qkvw);
+  H->attn = dalloc<uint16_t>(H, T * attw);
+  H->act = dalloc<uint16_t>(H, T * actw);
   H->tokens = dalloc<int>(H, T);
   H->positions = dalloc<int>(H, T);
   H->seq_id = dalloc<int>(H, T);
@@ -552,17 +567,16 @@ static void alloc_workspace(vd_handle* H) {
   H->tiles = dalloc<AttnTile>(H, H->max_tiles);
   H->d_err = dalloc<int>(H, 1);
   cuda_check(cudaMemset(H->d_err, 0, sizeof(int)), "clear error word");
-  H->map_xn = make_map(H->xn, T, d, 128);
-  H->map_attn = make_map(H->attn, T, attw, 128);
-  if (s.decoder()) {
-    H->map_act = make_map(H->act, T, s.ffn, 128);
-  } else {
-    H->map_act = make_map(H->act, T, s.ffn, 128);
-    H->map_act2 = make_map(H->act, T, 4 * d, 128);
+  const bool f16 = o.f16;
+  H->map_xn = make_map(H->xn, T, d, 128, f16);
+  H->map_attn = make_map(H->attn, T, attw, 128, f16);
+  H->map_act = make_map(H->act, T, s.ffn, 128, f16);
+  if (!s.decoder()) {
+    H->map_act2 = make_map(H->act, T, 4 * d, 128, f16);
     H->midx = dalloc<int>(H, o.max_markers);
-    H->mrow = dalloc<bf16>(H, o.max_markers * d);
-    H->mhid = dalloc<bf16>(H, o.max_markers * d);
-    H->map_mrow = make_map(H->mrow, o.max_markers, d, 128);
+    H->mrow = dalloc<uint16_t>(H, o.max_markers * d);
+    H->mhid = dalloc<uint16_t>(H, o.max_markers * d);
+    H->map_mrow = make_map(H->mrow, o.max_markers, d, 128, f16);
   }
   ensure_host_inputs(H, o.max_rows * 1024, std::max(o.max_rows, o.max_markers), o.max_rows,
                      std::max<int64_t>(o.max_rows * 256, o.max_markers));
@@ -580,33 +594,39 @@ static void alloc_workspace(vd_handle* H) {
 // ---------------------------------------------------------------------------
 // Kernel launch helpers
 // ---------------------------------------------------------------------------
-template <int BN, int EPI>
+template <int BN, int EPI, class T>
 static void set_gemm_attr() {
-  cuda_check(cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cuda_check(cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   GemmConfig<BN>::SMEM_BYTES),
              "gemm smem attribute");
 }
-template <int HD, bool C>
+template <int HD, bool C, class T>
 static void set_attn_attr() {
-  cuda_check(cudaFuncSetAttribute(attention_varlen_kernel<HD, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cuda_check(cudaFuncSetAttribute(attention_varlen_kernel<HD, C, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnConfig<HD>::SMEM_BYTES),
              "attention smem attribute");
 }
 
-static void init_kernel_attrs() {
-  set_gemm_attr<256, kEpiStore>();
-  set_gemm_attr<128, kEpiStore>();
-  set_gemm_attr<256, kEpiResidual>();
-  set_gemm_attr<128, kEpiResidual>();
-  set_gemm_attr<256, kEpiGated>();
-  set_gemm_attr<256, kEpiQKRope>();
-  set_gemm_attr<128, kEpiQKRope>();
-  set_attn_attr<64, false>();
-  set_attn_attr<128, true>();
-  set_attn_attr<256, true>();
+template <class T>
+static void init_kernel_attrs_t() {
+  set_gemm_attr<256, kEpiStore, T>();
+  set_gemm_attr<128, kEpiStore, T>();
+  set_gemm_attr<256, kEpiResidual, T>();
+  set_gemm_attr<128, kEpiResidual, T>();
+  set_gemm_attr<256, kEpiGated, T>();
+  set_gemm_attr<256, kEpiQKRope, T>();
+  set_gemm_attr<128, kEpiQKRope, T>();
+  set_attn_attr<64, false, T>();
+  set_attn_attr<128, true, T>();
+  set_attn_attr<256, true, T>();
 }
 
-template <int EPI>
+static void init_kernel_attrs() {
+  init_kernel_attrs_t<__half>();
+  init_kernel_attrs_t<__nv_bfloat16>();
+}
+
+template <int EPI, class T>
 static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, int M, const EpiParams& ep) {
   if (M <= 0) return;
   const int num_m = (M + 127) / 128;
@@ -616,12 +636,12 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
-      gemm_tcgen05_kernel<256, EPI>
+      gemm_tcgen05_kernel<256, EPI, T>
           <<<grid, 192, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
     } else {
       if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
       else
-        gemm_tcgen05_kernel<128, EPI>
+        gemm_tcgen05_kernel<128, EPI, T>
             <<<grid, 192, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
     }
   });
@@ -638,6 +658,7 @@ static EpiParams epi(void* out, int ld, const float* bias = nullptr, int act = k
 
 static EpiParams epi_params_for(void* out, int ld, const float* bias, int act) { return epi(out, ld, bias, act); }
 
+template <class T>
 static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd, bool causal, int ld_qkv, int q0,
                       int k0, int v0, int group, int ld_out) {
   AttnParams p;
@@ -656,11 +677,11 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
     fail(VD_ESPEC, "no attention kernel for this head size / mask");
   launch(H, VD_K_ATTN, flops, [&] {
     if (hd == 64)
-      attention_varlen_kernel<64, false><<<grid, 128, AttnConfig<64>::SMEM_BYTES, H->stream>>>(p);
+      attention_varlen_kernel<64, false, T><<<grid, 128, AttnConfig<64>::SMEM_BYTES, H->stream>>>(p);
     else if (hd == 128)
-      attention_varlen_kernel<128, true><<<grid, 128, AttnConfig<128>::SMEM_BYTES, H->stream>>>(p);
+      attention_varlen_kernel<128, true, T><<<grid, 128, AttnConfig<128>::SMEM_BYTES, H->stream>>>(p);
     else
-      attention_varlen_kernel<256, true><<<grid, 128, AttnConfig<256>::SMEM_BYTES, H->stream>>>(p);
+      attention_varlen_kernel<256, true, T><<<grid, 128, AttnConfig<256>::SMEM_BYTES, H->stream>>>(p);
   });
 }
 
@@ -721,15 +742,16 @@ static void pack(vd_handle* H, const Chunk& c, int max_len, int pos_offset) {
   });
 }
 
+template <class T>
 static double decoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads;
-  int T = 0, max_len = 0;
-  const int n_tiles = plan_chunk(H, c, T, max_len, true);
+  int ntok = 0, max_len = 0;
+  const int n_tiles = plan_chunk(H, c, ntok, max_len, true);
   pack(H, c, max_len, 0);
   const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
   launch(H, VD_K_OTHER, 0.0,
-         [&] { embed_kernel<<<T, 128, 0, H->stream>>>(H->tokens, T, H->embed, d, escale, H->h); });
+         [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h); });
   const int qkvw = s.qkv_width(), qc = nq * hd, kc = nkv * hd;
   const float eps = static_cast<float>(s.rms_eps);
   const int pone = s.norm_plus_one ? 1 : 0;
@@ -739,7 +761,7 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   for (int i = 0; i < s.layers; ++i) {
     const DecLayer& L = H->dec[i];
     launch(H, VD_K_NORM, 0.0, [&] {
-      rmsnorm_kernel<256><<<T, 256, 0, H->stream>>>(H->h, d, L.in_norm, pone, eps, H->xn, T);
+      rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.in_norm, pone, eps, static_cast<T*>(H->xn), ntok);
     });
     EpiParams q = epi(H->qkv, qkvw, L.qkv.b);
     q.q_norm = L.q_norm;
@@ -751,14 +773,15 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     q.eps = eps;
     q.positions = H->positions;
     q.rope = H->rope;
-    gemm<kEpiQKRope>(H, VD_K_QKV, H->map_xn, L.qkv, T, q);
-    attention(H, attn_flops, n_tiles, nq, hd, true, qkvw, 0, qc, qc + kc, nq / nkv, qc);
-    gemm<kEpiResidual>(H, VD_K_O, H->map_attn, L.o, T, epi(H->h, d));
+    gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q);
+    attention<T>(H, attn_flops, n_tiles, nq, hd, true, qkvw, 0, qc, qc + kc, nq / nkv, qc);
+    gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(H->h, d));
     launch(H, VD_K_NORM, 0.0, [&] {
-      rmsnorm_kernel<256><<<T, 256, 0, H->stream>>>(H->h, d, L.post_norm, pone, eps, H->xn, T);
+      rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.post_norm, pone, eps, static_cast<T*>(H->xn),
+                                                          ntok);
     });
-    gemm<kEpiGated>(H, VD_K_GATEUP, H->map_xn, L.gu, T, epi(H->act, s.ffn, nullptr, s.act));
-    gemm<kEpiResidual>(H, VD_K_DOWN, H->map_act, L.down, T, epi(H->h, d));
+    gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, epi(H->act, s.ffn, nullptr, s.act));
+    gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(H->h, d));
   }
   const size_t smem = sizeof(float) * (d + H->n_labels);
   launch(H, VD_K_OTHER, 0.0, [&] {
@@ -767,52 +790,55 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
                                                         static_cast<int>(c.width), H->opt.logprobs ? 1 : 0, H->d_err);
   });
   H->stats.attn_flops += attn_flops * s.layers;
-  H->stats.gemm_flops += 2.0 * T * (static_cast<double>(d) * qkvw + static_cast<double>(qc) * d + 3.0 * d * s.ffn) *
+  H->stats.gemm_flops += 2.0 * ntok * (static_cast<double>(d) * qkvw + static_cast<double>(qc) * d + 3.0 * d * s.ffn) *
                          s.layers;
-  return T;
+  return ntok;
 }
 
-static void enc_layer(vd_handle* H, const EncLayer& L, int T, int n_tiles, double attn_flops) {
+template <class T>
+static void enc_layer(vd_handle* H, const EncLayer& L, int ntok, int n_tiles, double attn_flops) {
   const int d = H->spec.hidden;
   const int nh = d / 64;
   auto ln = [&](const float* w, const float* b, int inplace) {
     launch(H, VD_K_NORM, 0.0, [&] {
-      layernorm_kernel<256><<<T, 256, 0, H->stream>>>(H->h, d, w, b, L.eps, inplace, H->xn, T);
+      layernorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, w, b, L.eps, inplace, static_cast<T*>(H->xn),
+                                                            ntok);
     });
   };
   if (L.pre_norm) ln(L.ln1_w, L.ln1_b, 0);
-  gemm<kEpiStore>(H, VD_K_QKV, H->map_xn, L.qkv, T, epi(H->qkv, 3 * d, L.qkv.b));
-  attention(H, attn_flops, n_tiles, nh, 64, false, 3 * d, 0, d, 2 * d, 1, d);
-  gemm<kEpiResidual>(H, VD_K_O, H->map_attn, L.o, T, epi(H->h, d, L.o.b));
+  gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, epi(H->qkv, 3 * d, L.qkv.b));
+  attention<T>(H, attn_flops, n_tiles, nh, 64, false, 3 * d, 0, d, 2 * d, 1, d);
+  gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(H->h, d, L.o.b));
   if (L.pre_norm) ln(L.ln2_w, L.ln2_b, 0);
   else ln(L.ln1_w, L.ln1_b, 1);
   const CUtensorMap& amap = (L.f1.n == H->spec.ffn) ? H->map_act : H->map_act2;
-  gemm<kEpiStore>(H, VD_K_GATEUP, H->map_xn, L.f1, T, epi(H->act, L.f1.n, L.f1.b, L.act));
-  gemm<kEpiResidual>(H, VD_K_DOWN, amap, L.f2, T, epi(H->h, d, L.f2.b));
+  gemm<kEpiStore, T>(H, VD_K_GATEUP, H->map_xn, L.f1, ntok, epi(H->act, L.f1.n, L.f1.b, L.act));
+  gemm<kEpiResidual, T>(H, VD_K_DOWN, amap, L.f2, ntok, epi(H->h, d, L.f2.b));
   if (!L.pre_norm) ln(L.ln2_w, L.ln2_b, 1);
 }
 
+template <class T>
 static double encoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden;
-  int T = 0, max_len = 0;
-  const int n_tiles = plan_chunk(H, c, T, max_len, false);
+  int ntok = 0, max_len = 0;
+  const int n_tiles = plan_chunk(H, c, ntok, max_len, false);
   const int pos_offset = s.style == "xlmr" ? s.pad_id + 1 : 0;
   if (max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
   pack(H, c, max_len, pos_offset);
   launch(H, VD_K_OTHER, 0.0, [&] {
-    embed_ln_kernel<256><<<T, 256, 0, H->stream>>>(H->tokens, H->positions, T, H->embed, H->pos_emb, H->type_emb0,
-                                                   d, H->emb_ln_w, H->emb_ln_b, static_cast<float>(s.ln_eps), H->h,
-                                                   H->xn);
+    embed_ln_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed, H->pos_emb,
+                                                         H->type_emb0, d, H->emb_ln_w, H->emb_ln_b,
+                                                         static_cast<float>(s.ln_eps), H->h, static_cast<T*>(H->xn));
   });
   double pairs = 0;
   for (int i = 0; i < c.nb; ++i) pairs += static_cast<double>(c.real_len[i]) * c.real_len[i];
   const double attn_flops = 4.0 * d * pairs;
-  for (const EncLayer& L : H->enc) enc_layer(H, L, T, n_tiles, attn_flops);
+  for (const EncLayer& L : H->enc) enc_layer<T>(H, L, ntok, n_tiles, attn_flops);
   launch(H, VD_K_OTHER, 0.0, [&] {
-    add_type_kernel<<<T, 256, 0, H->stream>>>(H->h, T, d, H->seq_id, c.qtype, H->qtype_emb, 3, H->d_err);
+    add_type_kernel<<<ntok, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3, H->d_err);
   });
-  for (const EncLayer& L : H->head) enc_layer(H, L, T, n_tiles, attn_flops);
+  for (const EncLayer& L : H->head) enc_layer<T>(H, L, ntok, n_tiles, attn_flops);
   const int nm = static_cast<int>(c.nb * c.k);
   if (nm > 0) {
     launch(H, VD_K_OTHER, 0.0, [&] {
@@ -820,18 +846,19 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
                                                                    static_cast<int>(c.k), H->midx, H->d_err);
     });
     launch(H, VD_K_NORM, 0.0, [&] {
-      gather_layernorm_kernel<256><<<nm, 256, 0, H->stream>>>(H->h, H->midx, nm, d, H->sc_ln_w, H->sc_ln_b, 1e-5f,
-                                                              H->mrow);
+      gather_layernorm_kernel<256, T><<<nm, 256, 0, H->stream>>>(H->h, H->midx, nm, d, H->sc_ln_w, H->sc_ln_b,
+                                                                 1e-5f, static_cast<T*>(H->mrow));
     });
-    gemm<kEpiStore>(H, VD_K_OTHER, H->map_mrow, H->sc1, nm, epi(H->mhid, d, H->sc1.b, kActGeluErf));
+    gemm<kEpiStore, T>(H, VD_K_OTHER, H->map_mrow, H->sc1, nm, epi(H->mhid, d, H->sc1.b, kActGeluErf));
   }
   launch(H, VD_K_OTHER, 0.0, [&] {
-    marker_score_kernel<<<c.nb, 256, 0, H->stream>>>(H->mhid, d, H->sc_w3, H->sc_b3, c.mmask, c.nb,
+    marker_score_kernel<T><<<c.nb, 256, 0, H->stream>>>(static_cast<const T*>(H->mhid), d, H->sc_w3, H->sc_b3,
+                                                        c.mmask, c.nb,
                                                      static_cast<int>(c.k), c.out, static_cast<int>(c.width));
   });
   H->stats.attn_flops += attn_flops * (s.layers + s.head_layers);
-  H->stats.gemm_flops += 2.0 * T * ((4.0 * d * d + 2.0 * d * s.ffn) * s.layers + (12.0 * d * d) * s.head_layers);
-  return T;
+  H->stats.gemm_flops += 2.0 * ntok * ((4.0 * d * d + 2.0 * d * s.ffn) * s.layers + (12.0 * d * d) * s.head_layers);
+  return ntok;
 }
 
 // ---------------------------------------------------------------------------
@@ -894,7 +921,12 @@ static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const
     c.real_len = b->real_len + r0;
     c.out = out + r0 * width;
     c.width = width;
-    tokens += static_cast<int64_t>(H->spec.decoder() ? decoder_forward(H, c) : encoder_forward(H, c));
+    double nt = 0;
+    if (H->spec.decoder())
+      nt = H->opt.f16 ? decoder_forward<__half>(H, c) : decoder_forward<__nv_bfloat16>(H, c);
+    else
+      nt = H->opt.f16 ? encoder_forward<__half>(H, c) : encoder_forward<__nv_bfloat16>(H, c);
+    tokens += static_cast<int64_t>(nt);
     ++chunks;
     r0 = r1;
   }
@@ -985,6 +1017,9 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.max_seq = o.integer_or("max_seq", H->opt.max_seq);
       H->opt.max_markers = o.integer_or("max_markers", H->opt.max_markers);
       H->opt.logprobs = o.string_or("output", "logprobs") != "logits";
+      const std::string dt = o.string_or("act_dtype", "fp16");
+      if (dt != "fp16" && dt != "bf16") fail(VD_EINVAL, "act_dtype must be \"fp16\" or \"bf16\"");
+      H->opt.f16 = dt == "fp16";
     }
     if (H->opt.max_tokens < 128 || H->opt.max_rows < 1 || H->opt.max_seq < 1)
       fail(VD_EINVAL, "max_tokens must be >= 128 and max_rows, max_seq >= 1");
