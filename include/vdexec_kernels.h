@@ -72,6 +72,30 @@ VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_
                          int kv_heads, int head_dim, int dtype, int causal, const int32_t* cu_seqlens_host,
                          int64_t nseq, void* out, int64_t ld_out, void* stream, char* err, size_t errlen);
 
+/*
+ * vdk_attention with no allocation of its own.  It has no counterpart in the
+ * reference; it exists for callers that must not call cudaMalloc: a host
+ * process whose GPU memory is entirely owned by another allocator (a serving
+ * framework's caching pool that reserves the HBM budget up front), or a
+ * latency-critical path where cudaMalloc/cudaFree would block on the device.
+ *
+ * Same arguments and results as vdk_attention.  The per-call work table (one
+ * entry per 64-row query tile) lives in a fixed device array of 16384 entries
+ * (256 KiB) that every GPU loading this library keeps until the process
+ * exits; a batch needing more tiles (sum over sequences of ceil(len / 64)) is
+ * rejected with VD_EINVAL before anything is launched.
+ * The first call on a device looks up that array's device address (with the
+ * device current) and keeps it; make that first call before any stream
+ * capture.  All calls in a process share the one array per GPU and it keeps
+ * the last call's contents; calls that overlapped on the GPU would race on it,
+ * so each call holds a process-wide lock until its kernel has finished.  Every
+ * entry a call reads is written by that same call, so nothing needs clearing.
+ */
+VD_API int vdk_attention_noalloc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0, int64_t v_col0,
+                                 int heads, int kv_heads, int head_dim, int dtype, int causal,
+                                 const int32_t* cu_seqlens_host, int64_t nseq, void* out, int64_t ld_out,
+                                 void* stream, char* err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif

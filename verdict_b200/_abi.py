@@ -69,6 +69,10 @@ SIGNATURES = {
     "vdk_attention": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int64, _P,
                                      ctypes.c_int64, _P, ctypes.c_char_p, ctypes.c_size_t]),
+    "vdk_attention_noalloc": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
+                                             ctypes.c_int64, _P, ctypes.c_int64, _P, ctypes.c_char_p,
+                                             ctypes.c_size_t]),
 }
 
 _lib = None

@@ -1200,3 +1200,108 @@ extern "C" VD_API void vd_close(vd_handle* h) {
 
 // Kernel-level entry points share the helpers above.
 #include "ops.cuh"
+
+// ---------------------------------------------------------------------------
+// vdk_attention_noalloc: the varlen attention kernel with its tile table in a
+// fixed device array instead of memory allocated per call.
+//
+// The attention kernel needs one 16-byte work descriptor per 64-row query tile
+// (AttnTile).  vdk_attention allocates that table on every call; this variant
+// keeps it in g_noalloc_tiles below, a file-scope device array that exists on
+// every GPU that loads the library until the process exits.  The host side
+// builds the table in a static host array and copies it over, so the call
+// performs no device or host allocation of its own.
+// ---------------------------------------------------------------------------
+namespace vd {
+
+// At most this many query tiles per call: sum over sequences of ceil(len / 64).
+constexpr int kNoAllocMaxTiles = 16384;  // 256 KiB of device memory per GPU
+
+static __device__ __align__(256) AttnTile g_noalloc_tiles[kNoAllocMaxTiles];
+
+static std::mutex g_noalloc_mu;                         // guards the two arrays below
+static AttnTile g_noalloc_host_tiles[kNoAllocMaxTiles];  // host staging, reused by every call
+static AttnTile* g_noalloc_dev_tiles[64] = {};           // device address of g_noalloc_tiles, per GPU
+
+// Device address of g_noalloc_tiles on the current GPU.  The name
+// g_noalloc_tiles in host code is only a host-side stand-in, so the address is
+// looked up once per device with that device current and kept.
+static AttnTile* noalloc_tiles_on_current_device() {
+  int dev = 0;
+  cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) fail(VD_EINVAL, "device index out of range");
+  if (!g_noalloc_dev_tiles[dev]) {
+    void* p = nullptr;
+    cuda_check(cudaGetSymbolAddress(&p, g_noalloc_tiles), "cudaGetSymbolAddress(g_noalloc_tiles)");
+    g_noalloc_dev_tiles[dev] = static_cast<AttnTile*>(p);
+  }
+  return g_noalloc_dev_tiles[dev];
+}
+
+}  // namespace vd
+
+extern "C" VD_API int vdk_attention_noalloc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0,
+                                            int64_t v_col0, int heads, int kv_heads, int head_dim, int dtype,
+                                            int causal, const int32_t* cu_seqlens_host, int64_t nseq, void* out,
+                                            int64_t ld_out, void* stream, char* err, size_t errlen) {
+  return guarded(nullptr, err, errlen, [&] {
+    if (heads < 1 || kv_heads < 1 || heads % kv_heads != 0) fail(VD_EINVAL, "heads must be a multiple of kv_heads");
+    if (nseq < 1 || !cu_seqlens_host) fail(VD_EINVAL, "need at least one sequence");
+    if (!qkv || !out) fail(VD_EINVAL, "null buffer");
+    if (!((head_dim == 64 && !causal) || (head_dim == 128 && causal) || (head_dim == 256 && causal)))
+      fail(VD_EINVAL, "supported: head_dim 64 bidirectional, 128 / 256 causal");
+    const bool f16 = ops_dtype(dtype);
+    // Count the tiles before touching anything shared or the device.
+    int64_t n = 0;
+    for (int64_t i = 0; i < nseq; ++i) {
+      const int64_t len = static_cast<int64_t>(cu_seqlens_host[i + 1]) - cu_seqlens_host[i];
+      if (len < 0) fail(VD_EINVAL, "cu_seqlens must be non-decreasing");
+      n += (len + 63) / 64;
+    }
+    if (n > kNoAllocMaxTiles)
+      fail(VD_EINVAL, "vdk_attention_noalloc: the batch needs " + std::to_string(n) +
+                          " query tiles of 64 rows; this entry point holds at most " +
+                          std::to_string(kNoAllocMaxTiles) + " (use vdk_attention for larger batches)");
+    if (n == 0) return;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    ops_attrs_once();
+    AttnTile* d_tiles = noalloc_tiles_on_current_device();
+    int t = 0;
+    for (int64_t i = 0; i < nseq; ++i) {
+      const int start = cu_seqlens_host[i], len = cu_seqlens_host[i + 1] - start;
+      for (int q = 0; q < len; q += 64) g_noalloc_host_tiles[t++] = AttnTile{start, len, q, 0};
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Every tile the kernel reads is written here, so nothing left over from an
+    // earlier call is ever read.
+    cuda_check(cudaMemcpyAsync(d_tiles, g_noalloc_host_tiles, sizeof(AttnTile) * t, cudaMemcpyHostToDevice, s),
+               "upload tile table");
+    AttnParams p;
+    p.qkv = qkv;
+    p.ld_qkv = static_cast<int>(ld_qkv);
+    p.q_col0 = static_cast<int>(q_col0);
+    p.k_col0 = static_cast<int>(k_col0);
+    p.v_col0 = static_cast<int>(v_col0);
+    p.out = out;
+    p.ld_out = static_cast<int>(ld_out);
+    p.tiles = d_tiles;
+    p.group = heads / kv_heads;
+    p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)) * 1.4426950408889634);
+    dim3 grid(static_cast<unsigned>(t), heads);
+    auto run = [&](auto tag) {
+      using T = decltype(tag);
+      if (head_dim == 64)
+        attention_varlen_kernel<64, false, T><<<grid, 128, AttnConfig<64>::SMEM_BYTES, s>>>(p);
+      else if (head_dim == 128)
+        attention_varlen_kernel<128, true, T><<<grid, 128, AttnConfig<128>::SMEM_BYTES, s>>>(p);
+      else
+        attention_varlen_kernel<256, true, T><<<grid, 128, AttnConfig<256>::SMEM_BYTES, s>>>(p);
+    };
+    if (f16) run(__half());
+    else run(__nv_bfloat16());
+    cuda_check(cudaGetLastError(), "attention launch");
+    // The table stays in use until the kernel finishes; returning only then
+    // keeps back-to-back calls from the same thread from overwriting it early.
+    cuda_check(cudaStreamSynchronize(s), "synchronize");
+  });
+}
