@@ -114,7 +114,25 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def max_over_ranks(x: float, world: int, device: str = "cpu") -> float:
+    """The slowest rank's value (all ranks take part; no-op on one rank)."""
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(decisions_per_rank: int, world: int, max_ms: float) -> float:
+    """decisions/s of the whole job: every rank's decisions over the slowest rank's time."""
+    return decisions_per_rank * world / (max_ms / 1e3)
+
+
 def make_batches(rank, n_batches, per_batch, vocab, seed):
+    """Each rank's own shard of the workload: batch j of rank r is seeded by
+    (seed, r, j), so ranks never share a decision."""
     from verdict_b200.batch import Layout, collate, decoder_rows
     out = []
     for j in range(n_batches):
@@ -244,12 +262,8 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    def reduce_max(x):
+        return max_over_ranks(x, world, f"cuda:{local}")
 
     # Warm-up.
     for j in range(args.warmup):
@@ -271,10 +285,10 @@ def main():
     barrier()
     clk = clocks.stop()
     step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
-    total_ms = max_over_ranks(evs[0].elapsed_time(evs[-1]))
-    p99_ms = max_over_ranks(float(np.percentile(step_ms, 99)))
+    total_ms = reduce_max(evs[0].elapsed_time(evs[-1]))
+    p99_ms = reduce_max(float(np.percentile(step_ms, 99)))
     decisions = args.batch * args.steps * world
-    value = decisions / (total_ms / 1e3)
+    value = whole_job_rate(args.batch * args.steps, world, total_ms)
     tokens_per_step = float(np.mean([b.real_len().sum() for b in batches[args.warmup:]]))
 
     # Per-kernel timing pass (events around each launch), for the roofline.
@@ -362,8 +376,8 @@ def main():
             d2h += bo
         e1.record(stream)
         barrier()
-        e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-        e2e = {"value": decisions / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+        e2e_ms = reduce_max(e0.elapsed_time(e1))
+        e2e = {"value": whole_job_rate(args.batch * args.steps, world, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
                "d2h_bytes_per_step": d2h // args.steps}
 
     cpu = None
