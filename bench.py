@@ -210,6 +210,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2, help="layers timed per CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--attention", default="mma", choices=["tc", "mma"],
+                    help="head_dim-128 causal attention kernel: tcgen05 (tc) or warp-level mma.sync")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -237,7 +239,7 @@ def main():
     batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed)
     max_tokens = max(int(b.real_len().sum()) for b in batches)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
-                     max_seq=4096)
+                     max_seq=4096, attention=args.attention)
     width = eng.width
     stream_ptr = eng.stream()
     stream = torch.cuda.ExternalStream(stream_ptr)
@@ -391,7 +393,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
-            "config": {"workload": WORKLOAD, "model": "onejev-9b", "layers": spec["layers"],
+            "config": {"workload": WORKLOAD, "model": "onejev-9b", "layers": spec["layers"], "attention": args.attention,
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
                        "parallelism": f"replicas x{world} (one full-weight replica per GPU, no collectives)",
                        "l2": "no flush: each step streams 15.4 GB of weights and ~0.5 GB of activations, "

@@ -73,6 +73,17 @@ VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_
                          int64_t nseq, void* out, int64_t ld_out, void* stream, char* err, size_t errlen);
 
 /*
+ * The same causal attention on the 5th-generation tensor cores (tcgen05 MMAs
+ * with TMEM accumulators, TMA-fed), head_dim 128 only, 128-row query tiles;
+ * the kernel the engine uses for OneJev-shaped decoders.  Same arguments and
+ * result as vdk_attention; strides and column offsets multiples of 8.
+ */
+VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0, int64_t v_col0,
+                            int heads, int kv_heads, int head_dim, int dtype, int causal,
+                            const int32_t* cu_seqlens_host, int64_t nseq, void* out, int64_t ld_out, void* stream,
+                            char* err, size_t errlen);
+
+/*
  * vdk_attention with no allocation of its own.  It has no counterpart in the
  * reference; it exists for callers that must not call cudaMalloc: a host
  * process whose GPU memory is entirely owned by another allocator (a serving

@@ -192,3 +192,24 @@ def test_gemm_rejects_bad_shapes():
     err = ctypes.create_string_buffer(256)
     rc = lib().vdk_gemm(P(A), P(W), 4, 100, 64, 1, 0, 0, None, P(out), 100, None, err, 256)
     assert rc == _abi.VD_EINVAL and b"N % 128" in err.value
+
+
+@pytest.mark.parametrize("nq,nkv", [(32, 8), (4, 4), (40, 8)])
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_attention_tc_varlen(nq, nkv, dt):
+    """The tcgen05 / TMEM attention kernel (head_dim 128, causal) vs torch fp32 SDPA."""
+    hd = 128
+    g = torch.Generator(device="cuda").manual_seed(nq * 7 + nkv)
+    lens = [1, 127, 128, 129, 300, 17, 1000, 256, 2100]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    width = (nq + 2 * nkv) * hd
+    qkv = rand16(dt, T, width, gen=g)
+    out = torch.zeros(T, nq * hd, device="cuda", dtype=DTYPES[dt][0])
+    q0, k0, v0 = 0, nq * hd, (nq + nkv) * hd
+    run(lib().vdk_attention_tc, P(qkv), width, q0, k0, v0, nq, nkv, hd, DTYPES[dt][1], 1,
+        ctypes.c_void_p(cu.ctypes.data), len(lens), P(out), nq * hd)
+    ref = attention_ref(qkv, cu.tolist(), nq, nkv, hd, q0, k0, v0, True)
+    # P enters the P.V product in the 16-bit type; with bf16 (8-bit mantissa)
+    # and up to 2100 keys a few outputs drift just past 2e-2, hence 3e-2.
+    close16(out, ref, rel=2e-2 if dt == "fp16" else 3e-2)

@@ -69,6 +69,9 @@ SIGNATURES = {
     "vdk_attention": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int64, _P,
                                      ctypes.c_int64, _P, ctypes.c_char_p, ctypes.c_size_t]),
+    "vdk_attention_tc": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
+                                        ctypes.c_int64, _P, ctypes.c_int64, _P, ctypes.c_char_p, ctypes.c_size_t]),
     "vdk_attention_noalloc": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
                                              ctypes.c_int64, _P, ctypes.c_int64, _P, ctypes.c_char_p,

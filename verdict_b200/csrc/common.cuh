@@ -227,6 +227,30 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 fp32 values -> 32 consecutive 16-bit elements (64 bytes, 16-byte aligned).
+template <class T>
+__device__ __forceinline__ void store_x32(T* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = Elem<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = Elem<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = Elem<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = Elem<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
+    d[q] = w;
+  }
+}
+
+// 32 fp32 accumulator columns of this thread's TMEM lane, loads completed.
+__device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
 // ---------------------------------------------------------------------------
 // Legacy warp-level MMA helpers (attention v1): ldmatrix + mma.sync m16n8k16.
 // ---------------------------------------------------------------------------

@@ -2,11 +2,14 @@
 // fp32 accumulate in tensor memory, with the layer's elementwise work fused
 // into the epilogue.
 //
-// CTA layout (192 threads, one CTA per SM):
+// CTA layout (320 threads, one CTA per SM):
 //   warp 0      : TMA producer (one elected lane) - A and W tiles, 128-byte swizzle
 //   warp 1      : TMEM allocator + MMA issuer (one lane issues tcgen05.mma)
-//   warps 2..5  : epilogue - each warp drains the 32 TMEM lanes it may access
-//                 (lanes 32*(warp%4) .. +31), one accumulator row per thread.
+//   warps 2..9  : epilogue - two warps per TMEM lane quarter (lanes
+//                 32*(warp%4) .. +31, the quarter a warp may access), each
+//                 draining half of the tile's columns, one accumulator row per
+//                 thread; two warps per quarter double the memory-level
+//                 parallelism of the residual read-modify-write and stores.
 // Tiles are BM=128 x BN (128 or 256) x BK=64; a STAGES-deep smem ring feeds the
 // MMA warp, and two TMEM accumulators (2*BN columns) let the epilogue of tile i
 // overlap the MMAs of tile i+1.  Tiles are visited in groups of 16 M-tiles so the
@@ -62,28 +65,6 @@ __device__ __forceinline__ float apply_act(float x, int act) {
   }
 }
 
-__device__ __forceinline__ void tmem_load_f32x32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  tmem_ld32(taddr, r);
-  tmem_wait_ld();
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-template <class T>
-__device__ __forceinline__ void store_x32(T* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w;
-    w.x = Elem<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
-    w.y = Elem<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
-    w.z = Elem<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
-    w.w = Elem<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
-    d[q] = w;
-  }
-}
-
 __device__ __forceinline__ void add_bias32(float (&v)[32], const float* bias, int col) {
   if (bias == nullptr) return;
   const float4* b = reinterpret_cast<const float4*>(bias + col);
@@ -98,11 +79,14 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const float* bias, in
 }
 
 // One head of kEpiQKRope: columns [col0, col0 + hd) of row `row`, TMEM at tbase.
+// This warp handles the rotary chunk pairs c in [c_begin, c_end) (chunk c is
+// columns [32c, 32c+32) paired with [hd/2 + 32c, ...)); with a gain it first
+// computes the RMS over the whole head itself, so the two warps sharing a head
+// need no exchange.
 template <int HD, class T>
 __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_ok, int col0, const EpiParams& p,
-                                              const float* gain) {
+                                              const float* gain, int c_begin, int c_end) {
   constexpr int HALF = HD / 2;
-  constexpr int CHUNKS = HALF / 32;
   float rstd = 1.0f;
   if (gain != nullptr) {
     float ss = 0.0f;
@@ -120,7 +104,7 @@ __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_
   const float2* rope = p.rope + static_cast<size_t>(pos) * HALF;
   T* out = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out;
 #pragma unroll 1
-  for (int c = 0; c < CHUNKS; ++c) {
+  for (int c = c_begin; c < c_end; ++c) {
     float x1[32], x2[32];
     tmem_load_f32x32(tbase + c * 32, x1);
     tmem_load_f32x32(tbase + HALF + c * 32, x2);
@@ -152,43 +136,57 @@ __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_
   }
 }
 
-template <int BN, int EPI, class T>
-__device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_ok, int n0, const EpiParams& p) {
-  if constexpr (EPI == kEpiStore) {
+// Plain store of 32-column chunks [c_begin, c_end) starting at column col0.
+template <class T>
+__device__ __forceinline__ void epi_store_chunks(uint32_t tbase, int row, bool row_ok, int col0, const EpiParams& p,
+                                                 int c_begin, int c_end) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      float v[32];
-      tmem_load_f32x32(taddr + c * 32, v);
-      add_bias32(v, p.bias, n0 + c * 32);
+  for (int c = c_begin; c < c_end; ++c) {
+    float v[32];
+    tmem_load_f32x32(tbase + c * 32, v);
+    add_bias32(v, p.bias, col0 + c * 32);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], p.act);
-      if (row_ok)
-        store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 + c * 32, v);
-    }
+    for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], p.act);
+    if (row_ok) store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
+  }
+}
+
+// Epilogue of one accumulator row for one of the two warps that share a TMEM
+// lane quarter: `half` (0 or 1) selects which half of the tile's columns (or
+// heads) this warp drains.
+template <int BN, int EPI, class T>
+__device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_ok, int n0, int half,
+                                              const EpiParams& p) {
+  constexpr int CH = BN / 32;  // 32-column chunks per tile
+  if constexpr (EPI == kEpiStore) {
+    epi_store_chunks<T>(taddr, row, row_ok, n0, p, half * CH / 2, (half + 1) * CH / 2);
   } else if constexpr (EPI == kEpiResidual) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
       float v[32];
       tmem_load_f32x32(taddr + c * 32, v);
       add_bias32(v, p.bias, n0 + c * 32);
       if (row_ok) {
         float4* h = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(row) * p.ld_out +
                                               n0 + c * 32);
+        float4 t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = h[q];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          float4 t = h[q];
-          t.x += v[q * 4 + 0];
-          t.y += v[q * 4 + 1];
-          t.z += v[q * 4 + 2];
-          t.w += v[q * 4 + 3];
-          h[q] = t;
+          t[q].x += v[q * 4 + 0];
+          t[q].y += v[q * 4 + 1];
+          t[q].z += v[q * 4 + 2];
+          t[q].w += v[q * 4 + 3];
+          h[q] = t[q];
         }
       }
     }
   } else if constexpr (EPI == kEpiGated) {
-    constexpr int HALF = BN / 2;
+    constexpr int HALF = BN / 2;         // output columns of the tile
+    constexpr int OC = HALF / 32;        // output chunks
 #pragma unroll 1
-    for (int c = 0; c < HALF / 32; ++c) {
+    for (int c = half * OC / 2; c < (half + 1) * OC / 2; ++c) {
       float g[32], u[32];
       tmem_load_f32x32(taddr + c * 32, g);
       tmem_load_f32x32(taddr + HALF + c * 32, u);
@@ -198,41 +196,26 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
         store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 / 2 + c * 32, g);
     }
   } else if constexpr (EPI == kEpiQKRope) {
-    // One or two heads per tile (head_dim 256 or 128); heads never straddle tiles.
+    // Heads never straddle tiles.  head_dim 128: with two heads per tile each
+    // warp takes one head; with one head (BN = 128) the warps split its two
+    // rotary chunk pairs.  head_dim 256 (one head per 256-wide tile): the warps
+    // split its four chunk pairs.
     if (p.head_dim == 128) {
-#pragma unroll 1
-      for (int h = 0; h < BN / 128; ++h) {
-        const int col0 = n0 + h * 128;
-        const uint32_t tb = taddr + h * 128;
-        if (col0 < p.q_cols + p.k_cols) {
-          epi_head_rope<128, T>(tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
-        } else {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float v[32];
-            tmem_load_f32x32(tb + c * 32, v);
-            add_bias32(v, p.bias, col0 + c * 32);
-            if (row_ok)
-              store_x32<T>(
-                  reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
-          }
-        }
-      }
+      constexpr int HEADS = BN / 128;
+      const int h = HEADS == 2 ? half : 0;
+      const int cb = HEADS == 2 ? 0 : half, ce = HEADS == 2 ? 2 : half + 1;
+      const int col0 = n0 + h * 128;
+      const uint32_t tb = taddr + h * 128;
+      if (col0 < p.q_cols + p.k_cols)
+        epi_head_rope<128, T>(tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, cb, ce);
+      else
+        epi_store_chunks<T>(tb, row, row_ok, col0, p, 2 * cb, 2 * ce);
     } else if constexpr (BN == 256) {
-      const int col0 = n0;
-      if (col0 < p.q_cols + p.k_cols) {
-        epi_head_rope<256, T>(taddr, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm);
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          float v[32];
-          tmem_load_f32x32(taddr + c * 32, v);
-          add_bias32(v, p.bias, col0 + c * 32);
-          if (row_ok)
-            store_x32<T>(
-                reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
-        }
-      }
+      if (n0 < p.q_cols + p.k_cols)
+        epi_head_rope<256, T>(taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, 2 * half,
+                              2 * half + 2);
+      else
+        epi_store_chunks<T>(taddr, row, row_ok, n0, p, 4 * half, 4 * half + 4);
     }
   }
 }
@@ -248,10 +231,14 @@ struct GemmConfig {
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
-  static constexpr int THREADS = 192;
+  static constexpr int EPI_WARPS = 8;       // two warps per TMEM lane quarter
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int GROUP_M = 16;
 };
 
+// Tile order: groups of `group_m` M-tiles; inside a group N is the slow index.
+// Odd groups walk N backwards, so the W column-blocks a group ends on are the
+// ones still in L2 when the next group starts.
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& m, int& n) {
   const int group_size = group_m * num_n;
   const int g = tile / group_size;
@@ -260,10 +247,11 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
   const int local = tile - g * group_size;
   m = first_m + local % gm;
   n = local / gm;
+  if (g & 1) n = num_n - 1 - n;
 }
 
 template <int BN, int EPI, class T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmShape shape, EpiParams ep, int* err) {
   using Cfg = GemmConfig<BN>;
@@ -291,7 +279,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&acc_full[j], 1);
-      mbar_init(&acc_empty[j], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[j], Cfg::EPI_WARPS);  // one arrival per epilogue warp
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -380,8 +368,10 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5.
+    // Epilogue warps 2..9: warp w drains TMEM lanes 32*(w%4).. (the quarter it
+    // may access) and column half (w-2)/4 of the tile.
     const int lane_group = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = lane_group * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -392,7 +382,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row = m * BM + row_in_tile;
-      gemm_epilogue<BN, EPI, T>(taddr, row, row < shape.M, n * BN, ep);
+      gemm_epilogue<BN, EPI, T>(taddr, row, row < shape.M, n * BN, half, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);

@@ -45,9 +45,9 @@ static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, int bn
   const int grid = std::min(tiles, sms);
   const GemmShape shape{M, N, K};
   if (bn == 256)
-    gemm_tcgen05_kernel<256, EPI, T><<<grid, 192, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
+    gemm_tcgen05_kernel<256, EPI, T><<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
   else if constexpr (EPI != kEpiGated)
-    gemm_tcgen05_kernel<128, EPI, T><<<grid, 192, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
+    gemm_tcgen05_kernel<128, EPI, T><<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, shape, ep, word);
   else
     fail(VD_EINVAL, "gated GEMM needs N % 256 == 0");
 }
@@ -202,5 +202,54 @@ extern "C" VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_c
     else run(__nv_bfloat16());
     cuda_check(cudaGetLastError(), "attention launch");
     cuda_check(cudaStreamSynchronize(s), "synchronize");
+  });
+}
+
+extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0,
+                                       int64_t v_col0, int heads, int kv_heads, int head_dim, int dtype, int causal,
+                                       const int32_t* cu_seqlens_host, int64_t nseq, void* out, int64_t ld_out,
+                                       void* stream, char* err, size_t errlen) {
+  return guarded(nullptr, err, errlen, [&] {
+    if (head_dim != 128 || !causal) fail(VD_EINVAL, "the tcgen05 attention kernel is causal with head_dim 128");
+    if (heads < 1 || kv_heads < 1 || heads % kv_heads != 0) fail(VD_EINVAL, "heads must be a multiple of kv_heads");
+    if (nseq < 1 || !cu_seqlens_host || !qkv || !out) fail(VD_EINVAL, "need at least one sequence and buffers");
+    if (ld_qkv % 8 != 0 || q_col0 % 8 != 0 || k_col0 % 8 != 0 || v_col0 % 8 != 0 || ld_out % 8 != 0)
+      fail(VD_EINVAL, "qkv / out strides and column offsets must be multiples of 8 elements");
+    const bool f16 = ops_dtype(dtype);
+    ops_attrs_once();
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    int* word = ops_error_word(dev);
+    std::vector<AttnTile> tiles;
+    for (int64_t i = 0; i < nseq; ++i) {
+      const int start = cu_seqlens_host[i], len = cu_seqlens_host[i + 1] - start;
+      if (len < 0) fail(VD_EINVAL, "cu_seqlens must be non-decreasing");
+      for (int q = 0; q < len; q += 128) tiles.push_back(AttnTile{start, len, q, 0});
+    }
+    if (tiles.empty()) return;
+    const int64_t T = cu_seqlens_host[nseq];
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    AttnTile* d_tiles = nullptr;
+    cuda_check(cudaMalloc(&d_tiles, tiles.size() * sizeof(AttnTile)), "tile table");
+    std::unique_ptr<AttnTile, decltype(&cudaFree)> guard(d_tiles, &cudaFree);
+    cuda_check(cudaMemcpy(d_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice), "tiles");
+    const CUtensorMap map = make_map(qkv, T, ld_qkv, 128, f16);
+    AttnTcParams p;
+    p.out = out;
+    p.ld_out = static_cast<int>(ld_out);
+    p.q_col0 = static_cast<int>(q_col0);
+    p.k_col0 = static_cast<int>(k_col0);
+    p.v_col0 = static_cast<int>(v_col0);
+    p.tiles = d_tiles;
+    p.group = heads / kv_heads;
+    p.pairs_per_kv = (p.group + 1) / 2;
+    p.scale_log2 = static_cast<float>(1.0 / std::sqrt(128.0) * 1.4426950408889634);
+    p.err = word;
+    dim3 grid(static_cast<unsigned>(tiles.size()), kv_heads * p.pairs_per_kv);
+    if (f16)
+      attention_tc_kernel<__half><<<grid, AttnTcConfig::THREADS, AttnTcConfig::SMEM_BYTES, s>>>(map, p);
+    else
+      attention_tc_kernel<__nv_bfloat16><<<grid, AttnTcConfig::THREADS, AttnTcConfig::SMEM_BYTES, s>>>(map, p);
+    ops_finish(s, word);
   });
 }

@@ -34,6 +34,7 @@
 
 #include "vdexec.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "common.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
@@ -215,6 +216,7 @@ struct Options {
   int64_t max_tokens = 65536, max_rows = 512, max_seq = 8192, max_markers = 16384;
   bool logprobs = true;
   bool f16 = true;  // activations and projection weights in fp16 (else bf16)
+  bool tc_attention = false;  // head_dim 128 causal attention on tcgen05 (default: the mma.sync kernel)
 };
 
 }  // namespace vd
@@ -248,7 +250,7 @@ struct vd_handle {
   vd::AttnTile* tiles = nullptr;
   int64_t max_tiles = 0;
   float2* rope = nullptr;
-  CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow;
+  CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow, map_qkv;
   // device copies of host batches
   int64_t *in_ids = nullptr, *in_mpos = nullptr, *in_nopts = nullptr, *in_qtype = nullptr;
   uint8_t* in_mmask = nullptr;
@@ -557,6 +559,9 @@ static void alloc_workspace(vd_handle* H) {
   H->h = dalloc<float>(H, T * d);
   H->xn = dalloc<uint16_t>(H, T * d);
   H->qkv = dalloc<uint16_t>(H, T * qkvw);
+  // Attention tiles read whole 128-row K/V blocks, including rows past the
+  // batch (masked to probability 0); zeroing once keeps those rows finite.
+  cuda_check(cudaMemset(H->qkv, 0, static_cast<size_t>(T) * qkvw * 2), "clear qkv workspace");
   H->attn = dalloc<uint16_t>(H, T * attw);
   H->act = dalloc<uint16_t>(H, T * actw);
   H->tokens = dalloc<int>(H, T);
@@ -570,6 +575,7 @@ static void alloc_workspace(vd_handle* H) {
   const bool f16 = o.f16;
   H->map_xn = make_map(H->xn, T, d, 128, f16);
   H->map_attn = make_map(H->attn, T, attw, 128, f16);
+  H->map_qkv = make_map(H->qkv, T, qkvw, 128, f16);
   H->map_act = make_map(H->act, T, s.ffn, 128, f16);
   if (!s.decoder()) {
     H->map_act2 = make_map(H->act, T, 4 * d, 128, f16);
@@ -619,6 +625,9 @@ static void init_kernel_attrs_t() {
   set_attn_attr<64, false, T>();
   set_attn_attr<128, true, T>();
   set_attn_attr<256, true, T>();
+  cuda_check(cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnTcConfig::SMEM_BYTES),
+             "tcgen05 attention smem attribute");
 }
 
 static void init_kernel_attrs() {
@@ -637,12 +646,12 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
       gemm_tcgen05_kernel<256, EPI, T>
-          <<<grid, 192, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
+          <<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
     } else {
       if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
       else
         gemm_tcgen05_kernel<128, EPI, T>
-            <<<grid, 192, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
+            <<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
     }
   });
 }
@@ -657,6 +666,14 @@ static EpiParams epi(void* out, int ld, const float* bias = nullptr, int act = k
 }
 
 static EpiParams epi_params_for(void* out, int ld, const float* bias, int act) { return epi(out, ld, bias, act); }
+
+// The tcgen05 kernel covers causal head_dim 128 with 128-row query tiles; the
+// warp-level kernel takes the rest with 64-row tiles.
+static bool use_tc_attention(const vd_handle* H, int hd, bool causal) {
+  return H->opt.tc_attention && hd == 128 && causal;
+}
+
+static int attn_tile_rows(const vd_handle* H, int hd, bool causal) { return use_tc_attention(H, hd, causal) ? 128 : 64; }
 
 template <class T>
 static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd, bool causal, int ld_qkv, int q0,
@@ -675,6 +692,24 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
   dim3 grid(n_tiles, heads);
   if (!((hd == 64 && !causal) || (hd == 128 && causal) || (hd == 256 && causal)))
     fail(VD_ESPEC, "no attention kernel for this head size / mask");
+  if (use_tc_attention(H, hd, causal)) {
+    AttnTcParams tp;
+    tp.out = H->attn;
+    tp.ld_out = ld_out;
+    tp.q_col0 = q0;
+    tp.k_col0 = k0;
+    tp.v_col0 = v0;
+    tp.tiles = H->tiles;
+    tp.group = group;
+    tp.pairs_per_kv = (group + 1) / 2;
+    tp.scale_log2 = p.scale_log2;
+    tp.err = H->d_err;
+    const dim3 tgrid(n_tiles, (heads / group) * tp.pairs_per_kv);
+    launch(H, VD_K_ATTN, flops, [&] {
+      attention_tc_kernel<T><<<tgrid, AttnTcConfig::THREADS, AttnTcConfig::SMEM_BYTES, H->stream>>>(H->map_qkv, tp);
+    });
+    return;
+  }
   launch(H, VD_K_ATTN, flops, [&] {
     if (hd == 64)
       attention_varlen_kernel<64, false, T><<<grid, 128, AttnConfig<64>::SMEM_BYTES, H->stream>>>(p);
@@ -702,7 +737,7 @@ struct Chunk {
 };
 
 // Host plan: cu_seqlens and the attention tile table, staged through pinned memory.
-static int plan_chunk(vd_handle* H, const Chunk& c, int& T, int& max_len, bool causal) {
+static int plan_chunk(vd_handle* H, const Chunk& c, int& T, int& max_len, bool causal, int tile_rows) {
   H->slot = (H->slot + 1) % vd_handle::kSlots;
   char* buf = H->pinned[H->slot];
   cuda_check(cudaEventSynchronize(H->slot_ev[H->slot]), "staging slot");
@@ -718,12 +753,12 @@ static int plan_chunk(vd_handle* H, const Chunk& c, int& T, int& max_len, bool c
   int n = 0;
   for (int i = 0; i < c.nb; ++i) {
     const int len = static_cast<int>(c.real_len[i]);
-    for (int q = 0; q < len; q += 64) tiles[n++] = AttnTile{cu[i], len, q, 0};
+    for (int q = 0; q < len; q += tile_rows) tiles[n++] = AttnTile{cu[i], len, q, 0};
   }
   // Longest work first: causal tiles cost ~ q_start + 64 keys, bidirectional ~ len.
-  std::stable_sort(tiles, tiles + n, [causal](const AttnTile& a, const AttnTile& b) {
-    const int wa = causal ? std::min(a.seq_len, a.q_start + 64) : a.seq_len;
-    const int wb = causal ? std::min(b.seq_len, b.q_start + 64) : b.seq_len;
+  std::stable_sort(tiles, tiles + n, [causal, tile_rows](const AttnTile& a, const AttnTile& b) {
+    const int wa = causal ? std::min(a.seq_len, a.q_start + tile_rows) : a.seq_len;
+    const int wb = causal ? std::min(b.seq_len, b.q_start + tile_rows) : b.seq_len;
     return wa > wb;
   });
   const size_t tiles_off = reinterpret_cast<char*>(tiles) - buf;
@@ -747,7 +782,7 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads;
   int ntok = 0, max_len = 0;
-  const int n_tiles = plan_chunk(H, c, ntok, max_len, true);
+  const int n_tiles = plan_chunk(H, c, ntok, max_len, true, attn_tile_rows(H, hd, true));
   pack(H, c, max_len, 0);
   const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
   launch(H, VD_K_OTHER, 0.0,
@@ -822,7 +857,7 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden;
   int ntok = 0, max_len = 0;
-  const int n_tiles = plan_chunk(H, c, ntok, max_len, false);
+  const int n_tiles = plan_chunk(H, c, ntok, max_len, false, 64);
   const int pos_offset = s.style == "xlmr" ? s.pad_id + 1 : 0;
   if (max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
   pack(H, c, max_len, pos_offset);
@@ -1017,6 +1052,9 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.max_seq = o.integer_or("max_seq", H->opt.max_seq);
       H->opt.max_markers = o.integer_or("max_markers", H->opt.max_markers);
       H->opt.logprobs = o.string_or("output", "logprobs") != "logits";
+      const std::string at = o.string_or("attention", "mma");
+      if (at != "tc" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\" or \"mma\"");
+      H->opt.tc_attention = at == "tc";
       const std::string dt = o.string_or("act_dtype", "fp16");
       if (dt != "fp16" && dt != "bf16") fail(VD_EINVAL, "act_dtype must be \"fp16\" or \"bf16\"");
       H->opt.f16 = dt == "fp16";
