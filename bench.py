@@ -46,9 +46,11 @@ WORKLOAD = ("OneJev-9B-shaped text decisions: 40 layers, d=4096, 32/8 heads hd=1
             "vocab 152064, causal varlen prefill + option log-softmax; lengths clip(lognormal(6,0.7),32,4096), "
             "2-8 options")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM traffic of one gate/up GEMM launch from an ncu capture (profiles/gemm_gateup_onejev9b.md),
-# scaled per launch to the bench's token count; None until captured.
-GATEUP_TRAFFIC_BYTES_PER_TOKEN = None
+# DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
+# full-size ncu capture of this bench's first timed launch (profiles/gemm_gateup_onejev9b.md), and the
+# token count that launch had.  Weight re-reads dominate it, so it is reported as measured, not scaled.
+GATEUP_TRAFFIC_BYTES = 3.70e9 + 0.82e9
+GATEUP_TRAFFIC_TOKENS = 33763
 
 
 def peaks():
@@ -327,7 +329,9 @@ def main():
         "kernel": "gemm_tcgen05_kernel<256,gated> (gate/up projection)",
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": f"{pk_kind} bf16_tflops_sustained (dense fp16 and bf16 share the tensor-core rate)",
-        "traffic": (GATEUP_TRAFFIC_BYTES_PER_TOKEN * tokens_per_step) if GATEUP_TRAFFIC_BYTES_PER_TOKEN else None,
+        "traffic": GATEUP_TRAFFIC_BYTES, "traffic_tokens": GATEUP_TRAFFIC_TOKENS,
+        "algorithmic_bytes_per_launch": 2.0 * tokens_per_step * (spec["hidden"] + 2 * spec["ffn"])
+        + 2.0 * 2 * spec["ffn"] * spec["hidden"],
         "flops_per_launch": gu_flops, "launch_ms": gu_launch_ms,
         "all_gemms": {"tflops": gemm_tf, "frac": gemm_tf / peak, "ms_per_step": gemm_ms},
     }
