@@ -212,7 +212,7 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2, help="layers timed per CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--attention", default="mma", choices=["tc", "mma"],
+    ap.add_argument("--attention", default="tc", choices=["tc", "mma"],
                     help="head_dim-128 causal attention kernel: tcgen05 (tc) or warp-level mma.sync")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -203,6 +203,19 @@ def test_tensor_core_attention_matches_warp_level_attention():
         b.close()
 
 
+def test_last_layer_on_slot_rows_is_bit_exact():
+    """Running the last layer's O projection and MLP on the slot rows only
+    changes no bit of the result (each row's arithmetic is the same)."""
+    spec, batch = decoder_case("onejev-9b", 2, 5, seed=17, max_len=900)
+    full = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, prune_last_layer=False)
+    pruned = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096)
+    try:
+        np.testing.assert_array_equal(engine_logprobs(full, batch), engine_logprobs(pruned, batch))
+    finally:
+        full.close()
+        pruned.close()
+
+
 def test_chunking_and_batching_are_bit_exact():
     """Rows are independent: splitting a batch by rows (small workspace) or
     running rows alone gives the same bits as one packed forward."""

@@ -75,6 +75,26 @@ __device__ __forceinline__ void tmem_st32f(uint32_t taddr, const float (&v)[32])
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 32 columns of this thread's TMEM lane into r; completes at the next tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// 2^x with the hardware approximation (flush-to-zero; exp2(-inf) = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct AttnTcParams {
   void* out;                   // T [tokens, ld_out]
   int ld_out;
@@ -244,38 +264,40 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
         const bool need_mask = kv0 + C::BN > tile.seq_len || kv0 + C::BN > tile.q_start;
-        // Pass 1: row max of the masked scores.
+        // The whole 128-column S row: four loads in flight, one wait.
+        uint32_t sr[128];
+        tmem_ld32_nowait(s_tm + 0, sr + 0);
+        tmem_ld32_nowait(s_tm + 32, sr + 32);
+        tmem_ld32_nowait(s_tm + 64, sr + 64);
+        tmem_ld32_nowait(s_tm + 96, sr + 96);
+        tmem_wait_ld();
         float mx = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_load_f32x32(s_tm + c * 32, v);
+        if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int kv = kv0 + c * 32 + i;
-            const bool dead = need_mask && (kv >= tile.seq_len || kv > q_row);
-            mx = fmaxf(mx, dead ? -INFINITY : v[i]);
+          for (int i = 0; i < 128; ++i) {
+            const int kv = kv0 + i;
+            if (kv >= tile.seq_len || kv > q_row) sr[i] = __float_as_uint(-INFINITY);
+            mx = fmaxf(mx, __uint_as_float(sr[i]));
           }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
         }
         const float m_tile = mx * p.scale_log2;
         const bool raise = m_tile > m_run + C::RESCALE_THRESHOLD;
         const bool warp_raise = __any_sync(0xffffffffu, raise);
         const float m_new = raise ? m_tile : m_run;
-        const float alpha = raise ? exp2f(m_run - m_new) : 1.0f;
-        // Pass 2: P = exp2(s * scale - m) as packed 16-bit pairs over S.
+        const float alpha = raise ? fast_exp2(m_run - m_new) : 1.0f;
+        // P = exp2(s * scale - m) as packed 16-bit pairs written over S
+        // (masked scores are -inf and give exactly 0).
         float rs = 0.0f;
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_load_f32x32(s_tm + c * 32, v);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const int kv = kv0 + c * 32 + i;
-            const bool d0 = need_mask && (kv >= tile.seq_len || kv > q_row);
-            const bool d1 = need_mask && (kv + 1 >= tile.seq_len || kv + 1 > q_row);
-            const float e0 = d0 ? 0.0f : exp2f(v[i] * p.scale_log2 - m_new);
-            const float e1 = d1 ? 0.0f : exp2f(v[i + 1] * p.scale_log2 - m_new);
+            const float e0 = fast_exp2(__uint_as_float(sr[c * 32 + i]) * p.scale_log2 - m_new);
+            const float e1 = fast_exp2(__uint_as_float(sr[c * 32 + i + 1]) * p.scale_log2 - m_new);
             rs += e0 + e1;
             pk[i >> 1] = Elem<T>::pack2(e0, e1);
           }

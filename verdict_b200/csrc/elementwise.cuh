@@ -182,6 +182,29 @@ __global__ void add_type_kernel(float* __restrict__ h, int T, int d, const int* 
   for (int i = threadIdx.x; i < d; i += blockDim.x) hr[i] += __bfloat162float(e[i]);
 }
 
+// Slot rows of the packed batch -> compact per-decision buffers for the last
+// layer, whose O projection and MLP only the slot rows need:
+// attn_s[i] = attn[t_i], h_s[i] = h[t_i] with t_i = cu[i] + marker_pos[i*k].
+template <class T>
+__global__ void gather_slot_rows_kernel(const int* __restrict__ cu, const int64_t* __restrict__ marker_pos, int k,
+                                        const T* __restrict__ attn, int ld_attn, const float* __restrict__ h, int d,
+                                        T* __restrict__ attn_s, float* __restrict__ h_s, int* err) {
+  const int i = blockIdx.x;
+  const int start = cu[i], len = cu[i + 1] - start;
+  int64_t slot = marker_pos[static_cast<int64_t>(i) * k];
+  if (slot < 0 || slot >= len) {
+    if (threadIdx.x == 0) record_error(err, kErrSlotRange);
+    slot = 0;
+  }
+  const int64_t t = start + slot;
+  const uint4* a = reinterpret_cast<const uint4*>(attn + t * ld_attn);
+  uint4* as = reinterpret_cast<uint4*>(attn_s + static_cast<int64_t>(i) * ld_attn);
+  for (int j = threadIdx.x; j < ld_attn / 8; j += blockDim.x) as[j] = a[j];
+  const float4* x = reinterpret_cast<const float4*>(h + t * d);
+  float4* xs = reinterpret_cast<float4*>(h_s + static_cast<int64_t>(i) * d);
+  for (int j = threadIdx.x; j < d / 4; j += blockDim.x) xs[j] = x[j];
+}
+
 // Decoder readout, one CTA per row: final RMSNorm of the slot token's hidden
 // state, dot products with the first n option-label rows of the LM head (fp32,
 // as `hs[slot].float() @ head_w.T`), then either the log-softmax restricted to
@@ -191,7 +214,7 @@ __global__ void __launch_bounds__(NT)
     readout_kernel(const float* __restrict__ h, int d, const int* __restrict__ cu,
                    const int64_t* __restrict__ marker_pos, int k, const int64_t* __restrict__ nopts,
                    const float* __restrict__ norm_w, int plus_one, float eps, const float* __restrict__ head,
-                   int n_labels, float* __restrict__ out, int width, int logprobs, int* err) {
+                   int n_labels, float* __restrict__ out, int width, int logprobs, int compact, int* err) {
   extern __shared__ float sm[];
   float* xs = sm;                 // [d]
   float* lg = sm + d;             // [n_labels]
@@ -207,7 +230,9 @@ __global__ void __launch_bounds__(NT)
     for (int j = threadIdx.x; j < width; j += NT) orow[j] = kSentinel;
     return;
   }
-  const float* x = h + static_cast<size_t>(start + slot) * d;
+  // compact: h holds one row per decision (the slot rows, gathered before the
+  // last layer's O projection); otherwise h is the packed batch.
+  const float* x = compact ? h + static_cast<size_t>(i) * d : h + static_cast<size_t>(start + slot) * d;
   float ss = 0.0f;
   for (int j = threadIdx.x; j < d; j += NT) {
     const float v = x[j];

@@ -216,7 +216,8 @@ struct Options {
   int64_t max_tokens = 65536, max_rows = 512, max_seq = 8192, max_markers = 16384;
   bool logprobs = true;
   bool f16 = true;  // activations and projection weights in fp16 (else bf16)
-  bool tc_attention = false;  // head_dim 128 causal attention on tcgen05 (default: the mma.sync kernel)
+  bool prune_last_layer = true;  // last layer's O projection and MLP on the slot rows only
+  bool tc_attention = true;  // head_dim 128 causal attention on tcgen05 (else the mma.sync kernel)
 };
 
 }  // namespace vd
@@ -251,6 +252,10 @@ struct vd_handle {
   int64_t max_tiles = 0;
   float2* rope = nullptr;
   CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow, map_qkv;
+  // last-layer slot rows (one per decision of a chunk)
+  float* h_s = nullptr;
+  void *xn_s = nullptr, *attn_s = nullptr, *act_s = nullptr;
+  CUtensorMap map_xn_s, map_attn_s, map_act_s;
   // device copies of host batches
   int64_t *in_ids = nullptr, *in_mpos = nullptr, *in_nopts = nullptr, *in_qtype = nullptr;
   uint8_t* in_mmask = nullptr;
@@ -576,6 +581,16 @@ static void alloc_workspace(vd_handle* H) {
   H->map_xn = make_map(H->xn, T, d, 128, f16);
   H->map_attn = make_map(H->attn, T, attw, 128, f16);
   H->map_qkv = make_map(H->qkv, T, qkvw, 128, f16);
+  if (s.decoder()) {
+    const int64_t R = std::max<int64_t>(o.max_rows, 128);  // at least one 128-row TMA box
+    H->h_s = dalloc<float>(H, R * d);
+    H->xn_s = dalloc<uint16_t>(H, R * d);
+    H->attn_s = dalloc<uint16_t>(H, R * attw);
+    H->act_s = dalloc<uint16_t>(H, R * s.ffn);
+    H->map_xn_s = make_map(H->xn_s, R, d, 128, f16);
+    H->map_attn_s = make_map(H->attn_s, R, attw, 128, f16);
+    H->map_act_s = make_map(H->act_s, R, s.ffn, 128, f16);
+  }
   H->map_act = make_map(H->act, T, s.ffn, 128, f16);
   if (!s.decoder()) {
     H->map_act2 = make_map(H->act, T, 4 * d, 128, f16);
@@ -810,6 +825,24 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     q.rope = H->rope;
     gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q);
     attention<T>(H, attn_flops, n_tiles, nq, hd, true, qkvw, 0, qc, qc + kc, nq / nkv, qc);
+    const bool last = i + 1 == s.layers;
+    if (last && H->opt.prune_last_layer) {
+      // Only the slot rows feed the readout: gather them (attention output and
+      // residual) and finish the layer on nb rows instead of ntok.
+      launch(H, VD_K_OTHER, 0.0, [&] {
+        gather_slot_rows_kernel<T><<<c.nb, 256, 0, H->stream>>>(H->cu, c.mpos, static_cast<int>(c.k),
+                                                                 static_cast<const T*>(H->attn), qc, H->h, d,
+                                                                 static_cast<T*>(H->attn_s), H->h_s, H->d_err);
+      });
+      gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(H->h_s, d));
+      launch(H, VD_K_NORM, 0.0, [&] {
+        rmsnorm_kernel<256, T><<<c.nb, 256, 0, H->stream>>>(H->h_s, d, L.post_norm, pone, eps,
+                                                            static_cast<T*>(H->xn_s), c.nb);
+      });
+      gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn_s, L.gu, c.nb, epi(H->act_s, s.ffn, nullptr, s.act));
+      gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act_s, L.down, c.nb, epi(H->h_s, d));
+      continue;
+    }
     gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(H->h, d));
     launch(H, VD_K_NORM, 0.0, [&] {
       rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.post_norm, pone, eps, static_cast<T*>(H->xn),
@@ -818,15 +851,20 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, epi(H->act, s.ffn, nullptr, s.act));
     gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(H->h, d));
   }
+  const bool compact = H->opt.prune_last_layer;
   const size_t smem = sizeof(float) * (d + H->n_labels);
   launch(H, VD_K_OTHER, 0.0, [&] {
-    readout_kernel<256><<<c.nb, 256, smem, H->stream>>>(H->h, d, H->cu, c.mpos, static_cast<int>(c.k), c.nopts,
-                                                        H->final_norm, pone, eps, H->head_rows, H->n_labels, c.out,
-                                                        static_cast<int>(c.width), H->opt.logprobs ? 1 : 0, H->d_err);
+    readout_kernel<256><<<c.nb, 256, smem, H->stream>>>(compact ? H->h_s : H->h, d, H->cu, c.mpos,
+                                                        static_cast<int>(c.k), c.nopts, H->final_norm, pone, eps,
+                                                        H->head_rows, H->n_labels, c.out, static_cast<int>(c.width),
+                                                        H->opt.logprobs ? 1 : 0, compact ? 1 : 0, H->d_err);
   });
   H->stats.attn_flops += attn_flops * s.layers;
-  H->stats.gemm_flops += 2.0 * ntok * (static_cast<double>(d) * qkvw + static_cast<double>(qc) * d + 3.0 * d * s.ffn) *
-                         s.layers;
+  // Projection FLOPs executed: every layer's QKV over all tokens, the rest over
+  // all tokens except in a pruned last layer (slot rows only).
+  const double per_row_rest = static_cast<double>(qc) * d + 3.0 * d * s.ffn;
+  const double rest_rows = static_cast<double>(ntok) * (s.layers - (compact ? 1 : 0)) + (compact ? c.nb : 0);
+  H->stats.gemm_flops += 2.0 * (static_cast<double>(ntok) * s.layers * d * qkvw + rest_rows * per_row_rest);
   return ntok;
 }
 
@@ -1052,7 +1090,8 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.max_seq = o.integer_or("max_seq", H->opt.max_seq);
       H->opt.max_markers = o.integer_or("max_markers", H->opt.max_markers);
       H->opt.logprobs = o.string_or("output", "logprobs") != "logits";
-      const std::string at = o.string_or("attention", "mma");
+      H->opt.prune_last_layer = o.boolean_or("prune_last_layer", true);
+      const std::string at = o.string_or("attention", "tc");
       if (at != "tc" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\" or \"mma\"");
       H->opt.tc_attention = at == "tc";
       const std::string dt = o.string_or("act_dtype", "fp16");

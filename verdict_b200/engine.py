@@ -70,14 +70,15 @@ class B200Engine(Engine):
 
     def __init__(self, spec: dict, device: int = 0, *, max_tokens: int = 65536, max_rows: int = 512,
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
-                 act_dtype: str = "fp16", attention: str = "mma"):
+                 act_dtype: str = "fp16", attention: str = "tc",
+                 prune_last_layer: bool = True):
         self.lib = _abi.load()
         self.spec = with_labels(spec)
         self.device = device
         self.decoder = self.spec["arch"] == "decoder"
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
-                               attention=attention))
+                               attention=attention, prune_last_layer=prune_last_layer))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
         rc = self.lib.vd_open(json.dumps(self.spec).encode(), device, opts.encode(), ctypes.byref(h), err,
