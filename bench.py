@@ -374,16 +374,24 @@ def main():
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        e2e_clocks = Clocks(local)
         e0.record(stream)
         h2d = d2h = 0
+        host_ms, fwd_ms = [], []
         for i in range(args.steps):
+            t0 = time.perf_counter()
             bi, bo = step_host(args.warmup + i)
+            host_ms.append((time.perf_counter() - t0) * 1e3)
+            fwd_ms.append(eng.last_stats()["forward_ms"])
             h2d += bi
             d2h += bo
         e1.record(stream)
         barrier()
+        e2e_clk = e2e_clocks.stop()
         e2e_ms = reduce_max(e0.elapsed_time(e1))
-        e2e = {"value": whole_job_rate(args.batch * args.steps, world, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+        e2e = {"value": whole_job_rate(args.batch * args.steps, world, e2e_ms), "unit": UNIT,
+               "host_ms_per_call": float(np.mean(host_ms)), "device_forward_ms_per_call": float(np.mean(fwd_ms)),
+               "clocks": e2e_clk, "h2d_bytes_per_step": h2d // args.steps,
                "d2h_bytes_per_step": d2h // args.steps}
 
     cpu = None

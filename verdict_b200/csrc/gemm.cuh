@@ -8,8 +8,8 @@
 //   warps 2..9  : epilogue - two warps per TMEM lane quarter (lanes
 //                 32*(warp%4) .. +31, the quarter a warp may access), each
 //                 draining half of the tile's columns, one accumulator row per
-//                 thread; two warps per quarter double the memory-level
-//                 parallelism of the residual read-modify-write and stores.
+//                 thread, results leaving through shared memory and TMA
+//                 (tensor stores; reduce-add into the fp32 residual).
 // Tiles are BM=128 x BN (128 or 256) x BK=64; a STAGES-deep smem ring feeds the
 // MMA warp, and two TMEM accumulators (2*BN columns) let the epilogue of tile i
 // overlap the MMAs of tile i+1.  Tiles are visited in groups of 16 M-tiles so the
@@ -33,8 +33,6 @@ enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiGated = 2, kEpiQKRope 
 enum ActKind : int { kActNone = 0, kActGeluErf = 1, kActGeluTanh = 2, kActRelu = 3, kActSilu = 4 };
 
 struct EpiParams {
-  void* out;              // T (store / gated / qkrope) or fp32 (residual)
-  int ld_out;             // row stride of out, elements
   const float* bias;      // [N] or null
   int act;                // ActKind
   // kEpiQKRope
@@ -78,14 +76,96 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const float* bias, in
   }
 }
 
+// ---------------------------------------------------------------------------
+// Epilogue output through shared memory and TMA.  Each epilogue warp owns a
+// 4 KB staging buffer; a chunk is this warp's 32 rows x 32 columns.  16-bit
+// chunks (2 KB, 64-byte swizzle) are written with a TMA tensor store, two
+// buffers in flight; fp32 residual chunks (4 KB, 128-byte swizzle) are added
+// into the residual stream with a TMA reduce-add performed at L2, so the SM
+// never reads the residual.  Rows past M land in rows of the output that no
+// one reads (tensor maps built for the workspace extent) or are clipped by the
+// map (per-call maps).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem_gemm() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+struct EpiOut {
+  uint8_t* stage;          // this warp's 4 KB staging buffer (1024-byte aligned)
+  const CUtensorMap* map;  // output tensor map (16-bit box 32x32 SW64, or fp32 box 32x32 SW128)
+  int y;                   // first output row of this warp's 32 rows
+  int lane;
+  int n16;                 // 16-bit chunks issued so far (selects the staging half)
+};
+
+// One 32x32 chunk of 16-bit outputs at column x.
+template <class T>
+__device__ __forceinline__ void out_chunk16(EpiOut& o, const float (&v)[32], int x) {
+  const int b = o.n16++ & 1;
+  if (o.lane == 0) bulk_wait_read<1>();  // the store that last used this half has read it
+  __syncwarp();
+  uint8_t* buf = o.stage + b * 2048;
+  const int r = o.lane;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = Elem<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = Elem<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = Elem<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = Elem<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(buf + r * 64 + ((q ^ ((r >> 1) & 3)) << 4)) = w;
+  }
+  fence_proxy_async_smem_gemm();
+  __syncwarp();
+  if (o.lane == 0) {
+    tma_store_2d(o.map, buf, x, o.y);
+    bulk_commit();
+  }
+}
+
+// One 32x32 chunk of fp32 values added into the output at column x.
+__device__ __forceinline__ void out_chunk_add32(EpiOut& o, const float (&v)[32], int x) {
+  if (o.lane == 0) bulk_wait_read<0>();
+  __syncwarp();
+  const int r = o.lane;
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<float4*>(o.stage + r * 128 + ((q ^ (r & 7)) << 4)) =
+        make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+  fence_proxy_async_smem_gemm();
+  __syncwarp();
+  if (o.lane == 0) {
+    tma_reduce_add_2d(o.map, o.stage, x, o.y);
+    bulk_commit();
+  }
+}
+
 // One head of kEpiQKRope: columns [col0, col0 + hd) of row `row`, TMEM at tbase.
 // This warp handles the rotary chunk pairs c in [c_begin, c_end) (chunk c is
 // columns [32c, 32c+32) paired with [hd/2 + 32c, ...)); with a gain it first
 // computes the RMS over the whole head itself, so the two warps sharing a head
 // need no exchange.
 template <int HD, class T>
-__device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_ok, int col0, const EpiParams& p,
-                                              const float* gain, int c_begin, int c_end) {
+__device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row, bool row_ok, int col0,
+                                              const EpiParams& p, const float* gain, int c_begin, int c_end) {
   constexpr int HALF = HD / 2;
   float rstd = 1.0f;
   if (gain != nullptr) {
@@ -101,8 +181,8 @@ __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_
     rstd = rsqrtf(ss / static_cast<float>(HD) + p.eps);
   }
   const int pos = row_ok ? __ldg(p.positions + row) : 0;
-  const float2* rope = p.rope + static_cast<size_t>(pos) * HALF;
-  T* out = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out;
+  const float4* rope = reinterpret_cast<const float4*>(p.rope + static_cast<size_t>(pos) * HALF);
+  const float add = p.plus_one ? 1.0f : 0.0f;
 #pragma unroll 1
   for (int c = c_begin; c < c_end; ++c) {
     float x1[32], x2[32];
@@ -111,34 +191,38 @@ __device__ __forceinline__ void epi_head_rope(uint32_t tbase, int row, bool row_
     add_bias32(x1, p.bias, col0 + c * 32);
     add_bias32(x2, p.bias, col0 + HALF + c * 32);
     if (gain != nullptr) {
+      const float4* g1 = reinterpret_cast<const float4*>(gain + c * 32);
+      const float4* g2 = reinterpret_cast<const float4*>(gain + HALF + c * 32);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float g1 = __ldg(gain + c * 32 + j), g2 = __ldg(gain + HALF + c * 32 + j);
-        if (p.plus_one) {
-          g1 += 1.0f;
-          g2 += 1.0f;
-        }
-        x1[j] = x1[j] * rstd * g1;
-        x2[j] = x2[j] * rstd * g2;
+      for (int q = 0; q < 8; ++q) {
+        const float4 a = __ldg(g1 + q), b = __ldg(g2 + q);
+        x1[4 * q + 0] *= rstd * (a.x + add);
+        x1[4 * q + 1] *= rstd * (a.y + add);
+        x1[4 * q + 2] *= rstd * (a.z + add);
+        x1[4 * q + 3] *= rstd * (a.w + add);
+        x2[4 * q + 0] *= rstd * (b.x + add);
+        x2[4 * q + 1] *= rstd * (b.y + add);
+        x2[4 * q + 2] *= rstd * (b.z + add);
+        x2[4 * q + 3] *= rstd * (b.w + add);
       }
     }
-    if (row_ok) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float2 cs = __ldg(rope + c * 32 + j);
-        const float a = x1[j], b = x2[j];
-        x1[j] = a * cs.x - b * cs.y;
-        x2[j] = b * cs.x + a * cs.y;
-      }
-      store_x32<T>(out + col0 + c * 32, x1);
-      store_x32<T>(out + col0 + HALF + c * 32, x2);
+    for (int q = 0; q < 16; ++q) {  // (cos, sin) pairs of columns 2q and 2q+1
+      const float4 cs = __ldg(rope + c * 16 + q);
+      const float a0 = x1[2 * q], b0 = x2[2 * q], a1 = x1[2 * q + 1], b1 = x2[2 * q + 1];
+      x1[2 * q] = a0 * cs.x - b0 * cs.y;
+      x2[2 * q] = b0 * cs.x + a0 * cs.y;
+      x1[2 * q + 1] = a1 * cs.z - b1 * cs.w;
+      x2[2 * q + 1] = b1 * cs.z + a1 * cs.w;
     }
+    out_chunk16<T>(o, x1, col0 + c * 32);
+    out_chunk16<T>(o, x2, col0 + HALF + c * 32);
   }
 }
 
 // Plain store of 32-column chunks [c_begin, c_end) starting at column col0.
 template <class T>
-__device__ __forceinline__ void epi_store_chunks(uint32_t tbase, int row, bool row_ok, int col0, const EpiParams& p,
+__device__ __forceinline__ void epi_store_chunks(EpiOut& o, uint32_t tbase, int col0, const EpiParams& p,
                                                  int c_begin, int c_end) {
 #pragma unroll 1
   for (int c = c_begin; c < c_end; ++c) {
@@ -147,7 +231,7 @@ __device__ __forceinline__ void epi_store_chunks(uint32_t tbase, int row, bool r
     add_bias32(v, p.bias, col0 + c * 32);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], p.act);
-    if (row_ok) store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + col0 + c * 32, v);
+    out_chunk16<T>(o, v, col0 + c * 32);
   }
 }
 
@@ -155,32 +239,18 @@ __device__ __forceinline__ void epi_store_chunks(uint32_t tbase, int row, bool r
 // lane quarter: `half` (0 or 1) selects which half of the tile's columns (or
 // heads) this warp drains.
 template <int BN, int EPI, class T>
-__device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_ok, int n0, int half,
+__device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row, bool row_ok, int n0, int half,
                                               const EpiParams& p) {
   constexpr int CH = BN / 32;  // 32-column chunks per tile
   if constexpr (EPI == kEpiStore) {
-    epi_store_chunks<T>(taddr, row, row_ok, n0, p, half * CH / 2, (half + 1) * CH / 2);
+    epi_store_chunks<T>(o, taddr, n0, p, half * CH / 2, (half + 1) * CH / 2);
   } else if constexpr (EPI == kEpiResidual) {
 #pragma unroll 1
     for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
       float v[32];
       tmem_load_f32x32(taddr + c * 32, v);
       add_bias32(v, p.bias, n0 + c * 32);
-      if (row_ok) {
-        float4* h = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(row) * p.ld_out +
-                                              n0 + c * 32);
-        float4 t[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) t[q] = h[q];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          t[q].x += v[q * 4 + 0];
-          t[q].y += v[q * 4 + 1];
-          t[q].z += v[q * 4 + 2];
-          t[q].w += v[q * 4 + 3];
-          h[q] = t[q];
-        }
-      }
+      out_chunk_add32(o, v, n0 + c * 32);
     }
   } else if constexpr (EPI == kEpiGated) {
     constexpr int HALF = BN / 2;         // output columns of the tile
@@ -192,8 +262,7 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
       tmem_load_f32x32(taddr + HALF + c * 32, u);
 #pragma unroll
       for (int j = 0; j < 32; ++j) g[j] = apply_act(g[j], p.act) * u[j];
-      if (row_ok)
-        store_x32<T>(reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + n0 / 2 + c * 32, g);
+      out_chunk16<T>(o, g, n0 / 2 + c * 32);
     }
   } else if constexpr (EPI == kEpiQKRope) {
     // Heads never straddle tiles.  head_dim 128: with two heads per tile each
@@ -207,15 +276,15 @@ __device__ __forceinline__ void gemm_epilogue(uint32_t taddr, int row, bool row_
       const int col0 = n0 + h * 128;
       const uint32_t tb = taddr + h * 128;
       if (col0 < p.q_cols + p.k_cols)
-        epi_head_rope<128, T>(tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, cb, ce);
+        epi_head_rope<128, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, cb, ce);
       else
-        epi_store_chunks<T>(tb, row, row_ok, col0, p, 2 * cb, 2 * ce);
+        epi_store_chunks<T>(o, tb, col0, p, 2 * cb, 2 * ce);
     } else if constexpr (BN == 256) {
       if (n0 < p.q_cols + p.k_cols)
-        epi_head_rope<256, T>(taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, 2 * half,
+        epi_head_rope<256, T>(o, taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, 2 * half,
                               2 * half + 2);
       else
-        epi_store_chunks<T>(taddr, row, row_ok, n0, p, 4 * half, 4 * half + 4);
+        epi_store_chunks<T>(o, taddr, n0, p, 4 * half, 4 * half + 4);
     }
   }
 }
@@ -229,9 +298,11 @@ struct GemmConfig {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int BAR_BYTES = 1024;    // barriers, padded so the staging buffers stay 1 KB aligned
   static constexpr int EPI_WARPS = 8;       // two warps per TMEM lane quarter
+  static constexpr int EPI_STAGE_BYTES = 4096;  // per epilogue warp: one fp32 or two 16-bit 32x32 chunks
+  static constexpr int SMEM_BYTES =
+      1024 /*alignment slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + EPI_WARPS * EPI_STAGE_BYTES;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int GROUP_M = 16;
 };
@@ -253,7 +324,7 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
 template <int BN, int EPI, class T>
 __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        GemmShape shape, EpiParams ep, int* err) {
+                        const __grid_constant__ CUtensorMap tmC, GemmShape shape, EpiParams ep, int* err) {
   using Cfg = GemmConfig<BN>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = umma_idesc_f16kind(BM, BN, Elem<T>::kUmmaFormat);
@@ -268,6 +339,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -302,6 +374,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
+      tma_prefetch_desc(&tmC);
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -373,6 +446,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     const int lane_group = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = lane_group * 32 + lane;
+    EpiOut o{epi_stage + (warp - 2) * Cfg::EPI_STAGE_BYTES, &tmC, 0, lane, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -382,7 +456,8 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row = m * BM + row_in_tile;
-      gemm_epilogue<BN, EPI, T>(taddr, row, row < shape.M, n * BN, half, ep);
+      o.y = m * BM + lane_group * 32;
+      gemm_epilogue<BN, EPI, T>(o, taddr, row, row < shape.M, n * BN, half, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -391,6 +466,9 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
         acc_phase ^= 1;
       }
     }
+    // Every TMA store / reduce of this warp has finished before the CTA exits.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();

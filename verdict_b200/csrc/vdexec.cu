@@ -187,6 +187,26 @@ static CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box
   return m;
 }
 
+// Output map of a GEMM epilogue: 32x32 boxes; 16-bit data with the 64-byte
+// swizzle (TMA store), fp32 with the 128-byte swizzle (TMA reduce-add).
+static CUtensorMap make_out_map(const void* ptr, int64_t rows, int64_t cols, bool fp32, bool f16 = true) {
+  CUtensorMap m;
+  const int elem = fp32 ? 4 : 2;
+  if ((cols * elem) % 16 != 0) fail(VD_EINVAL, "output row stride must be a multiple of 16 bytes");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * elem};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : (f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  CUresult r = encode_fn()(&m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    fail(VD_ECUDA, "cuTensorMapEncodeTiled (output) failed (" + std::to_string(static_cast<int>(r)) + ")");
+  return m;
+}
+
 // ---------------------------------------------------------------------------
 // Weights
 // ---------------------------------------------------------------------------
@@ -256,6 +276,8 @@ struct vd_handle {
   float* h_s = nullptr;
   void *xn_s = nullptr, *attn_s = nullptr, *act_s = nullptr;
   CUtensorMap map_xn_s, map_attn_s, map_act_s;
+  // GEMM output maps (epilogue TMA stores / reduce-adds)
+  CUtensorMap out_qkv, out_act, out_act2, out_h, out_h_s, out_act_s, out_mhid;
   // device copies of host batches
   int64_t *in_ids = nullptr, *in_mpos = nullptr, *in_nopts = nullptr, *in_qtype = nullptr;
   uint8_t* in_mmask = nullptr;
@@ -581,6 +603,8 @@ static void alloc_workspace(vd_handle* H) {
   H->map_xn = make_map(H->xn, T, d, 128, f16);
   H->map_attn = make_map(H->attn, T, attw, 128, f16);
   H->map_qkv = make_map(H->qkv, T, qkvw, 128, f16);
+  H->out_qkv = make_out_map(H->qkv, T, qkvw, false, f16);
+  H->out_h = make_out_map(H->h, T, d, true);
   if (s.decoder()) {
     const int64_t R = std::max<int64_t>(o.max_rows, 128);  // at least one 128-row TMA box
     H->h_s = dalloc<float>(H, R * d);
@@ -590,14 +614,19 @@ static void alloc_workspace(vd_handle* H) {
     H->map_xn_s = make_map(H->xn_s, R, d, 128, f16);
     H->map_attn_s = make_map(H->attn_s, R, attw, 128, f16);
     H->map_act_s = make_map(H->act_s, R, s.ffn, 128, f16);
+    H->out_act_s = make_out_map(H->act_s, R, s.ffn, false, f16);
+    H->out_h_s = make_out_map(H->h_s, R, d, true);
   }
   H->map_act = make_map(H->act, T, s.ffn, 128, f16);
+  H->out_act = make_out_map(H->act, T, s.ffn, false, f16);
   if (!s.decoder()) {
     H->map_act2 = make_map(H->act, T, 4 * d, 128, f16);
+    H->out_act2 = make_out_map(H->act, T, 4 * d, false, f16);
     H->midx = dalloc<int>(H, o.max_markers);
     H->mrow = dalloc<uint16_t>(H, o.max_markers * d);
     H->mhid = dalloc<uint16_t>(H, o.max_markers * d);
     H->map_mrow = make_map(H->mrow, o.max_markers, d, 128, f16);
+    H->out_mhid = make_out_map(H->mhid, o.max_markers, d, false, f16);
   }
   ensure_host_inputs(H, o.max_rows * 1024, std::max(o.max_rows, o.max_markers), o.max_rows,
                      std::max<int64_t>(o.max_rows * 256, o.max_markers));
@@ -651,7 +680,8 @@ static void init_kernel_attrs() {
 }
 
 template <int EPI, class T>
-static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, int M, const EpiParams& ep) {
+static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, int M, const EpiParams& ep,
+                 const CUtensorMap& c) {
   if (M <= 0) return;
   const int num_m = (M + 127) / 128;
   const int tiles = num_m * (L.n / L.bn);
@@ -661,26 +691,24 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
       gemm_tcgen05_kernel<256, EPI, T>
-          <<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
+          <<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, c, shape, ep, H->d_err);
     } else {
       if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
       else
         gemm_tcgen05_kernel<128, EPI, T>
-            <<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, shape, ep, H->d_err);
+            <<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, c, shape, ep, H->d_err);
     }
   });
 }
 
-static EpiParams epi(void* out, int ld, const float* bias = nullptr, int act = kActNone) {
+static EpiParams epi(const float* bias = nullptr, int act = kActNone) {
   EpiParams p{};
-  p.out = out;
-  p.ld_out = ld;
   p.bias = bias;
   p.act = act;
   return p;
 }
 
-static EpiParams epi_params_for(void* out, int ld, const float* bias, int act) { return epi(out, ld, bias, act); }
+static EpiParams epi_params_for(const float* bias, int act) { return epi(bias, act); }
 
 // The tcgen05 kernel covers causal head_dim 128 with 128-row query tiles; the
 // warp-level kernel takes the rest with 64-row tiles.
@@ -813,7 +841,7 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     launch(H, VD_K_NORM, 0.0, [&] {
       rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.in_norm, pone, eps, static_cast<T*>(H->xn), ntok);
     });
-    EpiParams q = epi(H->qkv, qkvw, L.qkv.b);
+    EpiParams q = epi(L.qkv.b);
     q.q_norm = L.q_norm;
     q.k_norm = L.k_norm;
     q.q_cols = qc;
@@ -823,7 +851,7 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     q.eps = eps;
     q.positions = H->positions;
     q.rope = H->rope;
-    gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q);
+    gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q, H->out_qkv);
     attention<T>(H, attn_flops, n_tiles, nq, hd, true, qkvw, 0, qc, qc + kc, nq / nkv, qc);
     const bool last = i + 1 == s.layers;
     if (last && H->opt.prune_last_layer) {
@@ -834,22 +862,22 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
                                                                  static_cast<const T*>(H->attn), qc, H->h, d,
                                                                  static_cast<T*>(H->attn_s), H->h_s, H->d_err);
       });
-      gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(H->h_s, d));
+      gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(), H->out_h_s);
       launch(H, VD_K_NORM, 0.0, [&] {
         rmsnorm_kernel<256, T><<<c.nb, 256, 0, H->stream>>>(H->h_s, d, L.post_norm, pone, eps,
                                                             static_cast<T*>(H->xn_s), c.nb);
       });
-      gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn_s, L.gu, c.nb, epi(H->act_s, s.ffn, nullptr, s.act));
-      gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act_s, L.down, c.nb, epi(H->h_s, d));
+      gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn_s, L.gu, c.nb, epi(nullptr, s.act), H->out_act_s);
+      gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act_s, L.down, c.nb, epi(), H->out_h_s);
       continue;
     }
-    gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(H->h, d));
+    gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(), H->out_h);
     launch(H, VD_K_NORM, 0.0, [&] {
       rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.post_norm, pone, eps, static_cast<T*>(H->xn),
                                                           ntok);
     });
-    gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, epi(H->act, s.ffn, nullptr, s.act));
-    gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(H->h, d));
+    gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, epi(nullptr, s.act), H->out_act);
+    gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(), H->out_h);
   }
   const bool compact = H->opt.prune_last_layer;
   const size_t smem = sizeof(float) * (d + H->n_labels);
@@ -879,14 +907,15 @@ static void enc_layer(vd_handle* H, const EncLayer& L, int ntok, int n_tiles, do
     });
   };
   if (L.pre_norm) ln(L.ln1_w, L.ln1_b, 0);
-  gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, epi(H->qkv, 3 * d, L.qkv.b));
+  gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, epi(L.qkv.b), H->out_qkv);
   attention<T>(H, attn_flops, n_tiles, nh, 64, false, 3 * d, 0, d, 2 * d, 1, d);
-  gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(H->h, d, L.o.b));
+  gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(L.o.b), H->out_h);
   if (L.pre_norm) ln(L.ln2_w, L.ln2_b, 0);
   else ln(L.ln1_w, L.ln1_b, 1);
   const CUtensorMap& amap = (L.f1.n == H->spec.ffn) ? H->map_act : H->map_act2;
-  gemm<kEpiStore, T>(H, VD_K_GATEUP, H->map_xn, L.f1, ntok, epi(H->act, L.f1.n, L.f1.b, L.act));
-  gemm<kEpiResidual, T>(H, VD_K_DOWN, amap, L.f2, ntok, epi(H->h, d, L.f2.b));
+  const CUtensorMap& omap = (L.f1.n == H->spec.ffn) ? H->out_act : H->out_act2;
+  gemm<kEpiStore, T>(H, VD_K_GATEUP, H->map_xn, L.f1, ntok, epi(L.f1.b, L.act), omap);
+  gemm<kEpiResidual, T>(H, VD_K_DOWN, amap, L.f2, ntok, epi(L.f2.b), H->out_h);
   if (!L.pre_norm) ln(L.ln2_w, L.ln2_b, 1);
 }
 
@@ -922,7 +951,7 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
       gather_layernorm_kernel<256, T><<<nm, 256, 0, H->stream>>>(H->h, H->midx, nm, d, H->sc_ln_w, H->sc_ln_b,
                                                                  1e-5f, static_cast<T*>(H->mrow));
     });
-    gemm<kEpiStore, T>(H, VD_K_OTHER, H->map_mrow, H->sc1, nm, epi(H->mhid, d, H->sc1.b, kActGeluErf));
+    gemm<kEpiStore, T>(H, VD_K_OTHER, H->map_mrow, H->sc1, nm, epi(H->sc1.b, kActGeluErf), H->out_mhid);
   }
   launch(H, VD_K_OTHER, 0.0, [&] {
     marker_score_kernel<T><<<c.nb, 256, 0, H->stream>>>(static_cast<const T*>(H->mhid), d, H->sc_w3, H->sc_b3,
