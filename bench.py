@@ -377,12 +377,15 @@ def main():
         e2e_clocks = Clocks(local)
         e0.record(stream)
         h2d = d2h = 0
-        host_ms, fwd_ms = [], []
+        host_ms, fwd_ms, enq_ms, call_ms = [], [], [], []
         for i in range(args.steps):
             t0 = time.perf_counter()
             bi, bo = step_host(args.warmup + i)
             host_ms.append((time.perf_counter() - t0) * 1e3)
-            fwd_ms.append(eng.last_stats()["forward_ms"])
+            st = eng.last_stats()
+            fwd_ms.append(st["forward_ms"])
+            enq_ms.append(st["enqueue_ms"])
+            call_ms.append(st["host_ms"])
             h2d += bi
             d2h += bo
         e1.record(stream)
@@ -391,6 +394,7 @@ def main():
         e2e_ms = reduce_max(e0.elapsed_time(e1))
         e2e = {"value": whole_job_rate(args.batch * args.steps, world, e2e_ms), "unit": UNIT,
                "host_ms_per_call": float(np.mean(host_ms)), "device_forward_ms_per_call": float(np.mean(fwd_ms)),
+               "library_call_ms": float(np.mean(call_ms)), "enqueue_ms_per_call": float(np.mean(enq_ms)),
                "clocks": e2e_clk, "h2d_bytes_per_step": h2d // args.steps,
                "d2h_bytes_per_step": d2h // args.steps}
 

@@ -94,6 +94,9 @@ typedef struct vd_stats {
   double kernel_ms[VD_K_COUNT];
   int64_t kernel_launches[VD_K_COUNT];
   double kernel_flops[VD_K_COUNT];
+  /* Host wall time of the call and of its enqueue part (up to the last launch). */
+  double host_ms;
+  double enqueue_ms;
 } vd_stats;
 
 /*

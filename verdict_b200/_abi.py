@@ -36,6 +36,7 @@ class VdStats(ctypes.Structure):
         ("gemm_flops", ctypes.c_double), ("attn_flops", ctypes.c_double),
         ("kernel_ms", ctypes.c_double * 8), ("kernel_launches", ctypes.c_int64 * 8),
         ("kernel_flops", ctypes.c_double * 8),
+        ("host_ms", ctypes.c_double), ("enqueue_ms", ctypes.c_double),
     ]
 
 

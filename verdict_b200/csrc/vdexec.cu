@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -1004,6 +1005,7 @@ static void validate_batch(vd_handle* H, const vd_batch* b, int64_t width) {
 
 static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const int64_t* mpos, const uint8_t* mmask,
                       const int64_t* nopts, const int64_t* qtype, float* out, int64_t width) {
+  const auto t_enqueue = std::chrono::steady_clock::now();
   H->stats = vd_stats{};
   H->launches = 0;
   cuda_check(cudaEventRecord(H->ev0, H->stream), "event");
@@ -1034,6 +1036,8 @@ static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const
   }
   cuda_check(cudaGetLastError(), "kernel launch");
   cuda_check(cudaEventRecord(H->ev1, H->stream), "event");
+  H->stats.enqueue_ms =
+      std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_enqueue).count();
   H->stats.rows = b->b;
   H->stats.tokens = tokens;
   H->stats.chunks = chunks;
@@ -1163,11 +1167,19 @@ extern "C" VD_API int vd_infer(vd_handle* h, const vd_batch* batch, float* logit
     put_err(err, errlen, "the executor is dead: " + h->dead_reason);
     return VD_EDEAD;
   }
+  const auto t_call = std::chrono::steady_clock::now();
   return guarded(h, err, errlen, [&] {
     cuda_check(cudaSetDevice(h->device), "cudaSetDevice");
     validate_batch(h, batch, out_width);
     if (batch->b == 0) return;
     if (!logits_out) fail(VD_EINVAL, "null logits_out");
+    struct HostTimer {
+      vd_handle* h;
+      std::chrono::steady_clock::time_point t0;
+      ~HostTimer() {
+        h->stats.host_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+      }
+    } host_timer{h, t_call};
     if (batch->memory == VD_MEM_DEVICE) {
       run_batch(h, batch, batch->input_ids, batch->marker_pos, batch->marker_mask, batch->nopts, batch->qtype,
                 logits_out, out_width);
