@@ -229,7 +229,8 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
 
     from verdict_b200 import spec as specs
     from verdict_b200.engine import B200Engine
