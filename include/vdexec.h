@@ -101,12 +101,21 @@ typedef struct vd_stats {
 
 /*
  * Load a model onto `device` once (weights, workspaces, kernel tables).
- * model: JSON model spec (keys documented in verdict_b200/spec.py) — a
- *   synthetic seeded checkpoint — or a path to a directory holding
- *   `vdexec.json` with the same spec.
+ * model: JSON model spec (keys documented in verdict_b200/spec.py), or a path
+ *   to a directory holding `vdexec.json` with the same spec.  Weights come
+ *   from "checkpoint": a directory of safetensors files (`model.safetensors`,
+ *   or the shards of `model.safetensors.index.json`; BF16, F16 or F32 tensors
+ *   under their HF / DecisionModel state-dict names; relative to the spec
+ *   file's directory), else they are generated from "seed".  A spec with a
+ *   checkpoint and no "hidden" takes its shape from the checkpoint's HF
+ *   config.json (decoders: Qwen3 / Qwen2 / Gemma; encoders: BERT / XLM-R
+ *   under encoder/); decoders still need "label_ids" (the family's table,
+ *   src/tokenize.rs:96-171) and default to "family": "letter_readout".
  * opts_json: NULL or {"max_tokens": N, "max_rows": N, "max_seq": N,
- *   "max_markers": N, "output": "logprobs"|"logits"}.
- * Replaces TorchEngine::with_device (src/torch_engine.rs:280-316).
+ *   "max_markers": N, "output": "logprobs"|"logits", "act_dtype":
+ *   "fp16"|"bf16", "attention": "tc"|"mma", "prune_last_layer": bool}.
+ * Replaces TorchEngine::with_device (src/torch_engine.rs:280-316) and the
+ * executor's checkpoint load (executor/torch_exec.py:2341-2386).
  */
 VD_API int vd_open(const char* model, int device, const char* opts_json, vd_handle** out, char* err, size_t errlen);
 
@@ -161,6 +170,11 @@ VD_API int vd_last_stats(vd_handle* h, vd_stats* out);
 
 /* Free everything the handle owns. */
 VD_API void vd_close(vd_handle* h);
+
+/* The spec vd_open would load for `model`, as one JSON object (checkpoint
+ * path resolved, HF config keys filled in); host only, no device needed.
+ * VD_EINVAL when out[0..outlen) cannot hold it (the message gives the size). */
+VD_API int vd_resolve_spec(const char* model, char* out, size_t outlen, char* err, size_t errlen);
 
 /* ABI version (VDEXEC_ABI_VERSION). */
 VD_API int vd_abi_version(void);

@@ -16,7 +16,7 @@ What it restates (fp32, numpy):
 - `encoder.py`: the marker-head `DecisionModel.forward`
   (`convert/marker_head/marker_head_converter.py:40-57`) over an HF BERT /
   XLM-RoBERTa encoder.
-- `labels.py`: the option-label table rules (`src/tokenize.rs:147-222`,
+- `labels.py`: the option-label table rules (`src/tokenize.rs:96-171`,
   `executor/torch_exec.py:2254-2323`).
 
 Pinning: `tests/golden/make_golden.py` runs the reference's own code

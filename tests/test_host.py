@@ -95,7 +95,7 @@ def test_synthetic_labels_distinct_and_in_range():
     assert len(with_labels(specs.preset("decider-2b"))["label_ids"]) == 255
 
 
-# --- label rules (src/tokenize.rs:147-222) ---------------------------------------
+# --- label rules (src/tokenize.rs:96-171) ---------------------------------------
 
 class _Tok:
     def __init__(self, vocab):

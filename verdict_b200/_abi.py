@@ -46,6 +46,8 @@ KERNEL_CLASSES = ["qkv", "o", "gateup", "down", "attention", "norm", "other"]
 # Every entry point of include/vdexec.h: name -> (restype, argtypes)
 SIGNATURES = {
     "vd_abi_version": (ctypes.c_int, []),
+    "vd_resolve_spec": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p,
+                                       ctypes.c_size_t]),
     "vd_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_char_p, ctypes.POINTER(_P),
                                ctypes.c_char_p, ctypes.c_size_t]),
     "vd_infer": (ctypes.c_int, [_P, ctypes.POINTER(VdBatch), _P, ctypes.c_int64, ctypes.c_char_p, ctypes.c_size_t]),

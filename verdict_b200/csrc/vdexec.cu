@@ -36,7 +36,9 @@
 #include "vdexec.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "checkpoint.hpp"
 #include "common.cuh"
+#include "convert.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "json.hpp"
@@ -67,6 +69,7 @@ struct ModelSpec {
   bool qk_norm = false, qkv_bias = false, tied = false, embed_scale = false, norm_plus_one = false;
   int act = kActSilu;
   uint64_t seed = 0;
+  std::string checkpoint;  // safetensors directory; empty = seeded synthetic weights
   std::vector<int> label_ids;
   int max_pos = 512, type_vocab = 2, pad_id = 0, head_layers = 2;
 
@@ -85,8 +88,10 @@ static ModelSpec parse_spec(const Json& j) {
   s.vocab = static_cast<int>(j.integer("vocab"));
   s.seed = static_cast<uint64_t>(j.integer_or("seed", 0));
   s.init_std = j.number_or("init_std", 0.02);
+  s.checkpoint = j.string_or("checkpoint", "");
   if (s.decoder()) {
     s.family = j.string_or("family", "letter_branches");
+    std::replace(s.family.begin(), s.family.end(), '-', '_');
     s.kv_heads = static_cast<int>(j.integer("kv_heads"));
     s.head_dim = static_cast<int>(j.integer("head_dim"));
     s.rms_eps = j.number_or("rms_eps", 1e-6);
@@ -114,6 +119,177 @@ static ModelSpec parse_spec(const Json& j) {
     s.ln_eps = j.number_or("ln_eps", 1e-12);
   }
   return s;
+}
+
+// ---------------------------------------------------------------------------
+// Specs that name a checkpoint and leave its shape out take the shape from the
+// checkpoint's HF config: `config.json` of a Qwen3 / Qwen2 / Gemma CausalLM, or
+// `encoder/config.json` (else `config.json`) of the BERT / XLM-R encoder of a
+// marker-head DecisionModel.  Keys given in the spec win.  verdict_b200's
+// checkpoint.spec_from_checkpoint applies the same mapping.
+// ---------------------------------------------------------------------------
+static Json jnum(double v) {
+  Json j;
+  j.kind = Json::Number;
+  j.num = v;
+  return j;
+}
+static Json jbool(bool v) {
+  Json j;
+  j.kind = Json::Bool;
+  j.b = v;
+  return j;
+}
+static Json jstr(const std::string& v) {
+  Json j;
+  j.kind = Json::String;
+  j.str = v;
+  return j;
+}
+
+static bool file_exists(const std::string& path) {
+  std::ifstream f(path);
+  return static_cast<bool>(f);
+}
+
+static Json read_json_file(const std::string& path) {
+  std::ifstream f(path);
+  if (!f) fail(VD_ESPEC, "cannot read " + path);
+  std::stringstream ss;
+  ss << f.rdbuf();
+  return parse_json(ss.str());
+}
+
+static Json spec_from_hf_config(const Json& c) {
+  Json o;
+  o.kind = Json::Object;
+  const std::string mt = c.string_or("model_type", "");
+  auto need_num = [&](const char* k) {
+    if (!c.has(k) || c.at(k).kind != Json::Number) fail(VD_ESPEC, std::string("HF config has no number \"") + k + "\"");
+    return c.at(k).num;
+  };
+  if (mt == "bert" || mt == "xlm-roberta") {
+    const std::string pe = c.string_or("position_embedding_type", "absolute");
+    if (pe != "absolute") fail(VD_ESPEC, "only absolute position embeddings are supported, not " + pe);
+    const std::string act = c.string_or("hidden_act", "gelu");
+    if (act != "gelu") fail(VD_ESPEC, "unsupported encoder activation " + act);
+    o.obj["arch"] = jstr("encoder");
+    o.obj["style"] = jstr(mt == "bert" ? "bert" : "xlmr");
+    o.obj["hidden"] = jnum(need_num("hidden_size"));
+    o.obj["layers"] = jnum(need_num("num_hidden_layers"));
+    o.obj["heads"] = jnum(need_num("num_attention_heads"));
+    o.obj["ffn"] = jnum(need_num("intermediate_size"));
+    o.obj["vocab"] = jnum(need_num("vocab_size"));
+    o.obj["max_pos"] = jnum(need_num("max_position_embeddings"));
+    o.obj["type_vocab"] = jnum(c.number_or("type_vocab_size", 2));
+    o.obj["ln_eps"] = jnum(c.number_or("layer_norm_eps", 1e-12));
+    o.obj["pad_id"] = jnum(c.number_or("pad_token_id", 0));
+    o.obj["family"] = jstr("marker_head");
+    return o;
+  }
+  if (mt != "qwen3" && mt != "qwen2" && mt != "gemma")
+    fail(VD_ESPEC, "unsupported model_type \"" + mt + "\" (qwen3, qwen2, gemma, bert, xlm-roberta are supported)");
+  const double heads = need_num("num_attention_heads"), hidden = need_num("hidden_size");
+  o.obj["arch"] = jstr("decoder");
+  o.obj["style"] = jstr(mt);
+  o.obj["hidden"] = jnum(hidden);
+  o.obj["layers"] = jnum(need_num("num_hidden_layers"));
+  o.obj["heads"] = jnum(heads);
+  o.obj["kv_heads"] = jnum(c.number_or("num_key_value_heads", heads));
+  o.obj["head_dim"] = jnum(c.number_or("head_dim", hidden / heads));
+  o.obj["ffn"] = jnum(need_num("intermediate_size"));
+  o.obj["vocab"] = jnum(need_num("vocab_size"));
+  o.obj["rms_eps"] = jnum(c.number_or("rms_norm_eps", 1e-6));
+  double theta = c.number_or("rope_theta", 0.0);
+  std::string rope_type = "default";
+  if (c.has("rope_parameters") && c.at("rope_parameters").kind == Json::Object) {
+    const Json& rp = c.at("rope_parameters");
+    if (theta == 0.0) theta = rp.number_or("rope_theta", 0.0);
+    rope_type = rp.string_or("rope_type", "default");
+  }
+  if ((c.has("rope_scaling") && c.at("rope_scaling").kind == Json::Object) || rope_type != "default")
+    fail(VD_ESPEC, "rope scaling is not supported");
+  o.obj["rope_theta"] = jnum(theta == 0.0 ? 10000.0 : theta);
+  o.obj["tied"] = jbool(c.boolean_or("tie_word_embeddings", mt == "gemma"));
+  if (c.boolean_or("use_sliding_window", false)) fail(VD_ESPEC, "sliding-window attention is not supported");
+  const std::string act = c.string_or("hidden_activation", c.string_or("hidden_act", ""));
+  const bool gemma = mt == "gemma";
+  if (gemma ? (act != "gelu_pytorch_tanh" && act != "gelu_tanh") : (act != "silu" && act != "swish"))
+    fail(VD_ESPEC, "unsupported " + mt + " activation \"" + act + "\"");
+  if (mt == "qwen3" && c.boolean_or("attention_bias", false))
+    fail(VD_ESPEC, "qwen3 checkpoints with attention_bias (o_proj bias) are not supported");
+  o.obj["qk_norm"] = jbool(mt == "qwen3");
+  o.obj["qkv_bias"] = jbool(mt == "qwen2");
+  o.obj["act"] = jstr(gemma ? "gelu_tanh" : "silu");
+  o.obj["embed_scale"] = jbool(gemma);
+  o.obj["norm_plus_one"] = jbool(gemma);
+  o.obj["family"] = jstr("letter_readout");  // the torch executor's default family
+  return o;
+}
+
+// The effective spec JSON object: `j`, with "checkpoint" resolved against
+// `spec_dir` and, when "hidden" is absent, the checkpoint's HF config beneath it.
+static Json resolve_spec(const Json& j, const std::string& spec_dir) {
+  if (j.kind != Json::Object) fail(VD_ESPEC, "the model spec must be a JSON object");
+  Json out = j;
+  if (!j.has("checkpoint")) return out;
+  std::string ck = j.string_or("checkpoint", "");
+  if (ck.empty()) fail(VD_ESPEC, "\"checkpoint\" must be a non-empty path");
+  if (ck[0] != '/' && !spec_dir.empty()) ck = spec_dir + "/" + ck;
+  out.obj["checkpoint"] = jstr(ck);
+  if (j.has("hidden")) return out;
+  const std::string enc = ck + "/encoder/config.json";
+  Json merged = spec_from_hf_config(read_json_file(file_exists(enc) ? enc : ck + "/config.json"));
+  for (const auto& kv : out.obj) merged.obj[kv.first] = kv.second;
+  return merged;
+}
+
+static void json_write(std::string& o, const Json& v) {
+  char buf[64];
+  switch (v.kind) {
+    case Json::Null: o += "null"; break;
+    case Json::Bool: o += v.b ? "true" : "false"; break;
+    case Json::Number:
+      std::snprintf(buf, sizeof(buf), "%.17g", v.num);
+      o += buf;
+      break;
+    case Json::String:
+      o += '"';
+      for (char c : v.str) {
+        if (c == '"' || c == '\\') {
+          o += '\\';
+          o += c;
+        } else if (static_cast<unsigned char>(c) < 0x20) {
+          std::snprintf(buf, sizeof(buf), "\\u%04x", c);
+          o += buf;
+        } else {
+          o += c;
+        }
+      }
+      o += '"';
+      break;
+    case Json::Array:
+      o += '[';
+      for (size_t i = 0; i < v.arr.size(); ++i) {
+        if (i) o += ',';
+        json_write(o, v.arr[i]);
+      }
+      o += ']';
+      break;
+    case Json::Object: {
+      o += '{';
+      bool first = true;
+      for (const auto& kv : v.obj) {
+        if (!first) o += ',';
+        first = false;
+        json_write(o, jstr(kv.first));
+        o += ':';
+        json_write(o, kv.second);
+      }
+      o += '}';
+      break;
+    }
+  }
 }
 
 static void validate_spec(const ModelSpec& s) {
@@ -253,6 +429,10 @@ struct vd_handle {
   std::atomic<bool> healthy{true};
   std::string dead_reason;
   std::vector<void*> allocations;
+  // open checkpoint (during vd_open only) and its device staging buffer
+  std::unique_ptr<vd::Checkpoint> ckpt;
+  void* ckpt_stage = nullptr;
+  size_t ckpt_stage_bytes = 0;
   // decoder weights
   __nv_bfloat16* embed = nullptr;
   float* final_norm = nullptr;
@@ -360,28 +540,120 @@ static void prof_collect(vd_handle* H) {
 
 static int grid_for(int64_t n) { return static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16)); }
 
-// A synthetic tensor in the element type `f16` selects (embedding tables are always bf16).
-static void synth_w(vd_handle* H, void* dst, bool f16, const std::string& name, int64_t rows, int64_t cols,
-                    float scale, float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
+// Weights come from one of two sources, by state-dict name: the seeded
+// synthetic generator, or the open safetensors checkpoint.  Either way a
+// [rows, cols] tensor lands row r at destination row (r / group) * stride +
+// (r % group) + off (group = rows, stride 0: a plain copy at row `off`).
+static constexpr size_t kStageBytes = size_t(64) << 20;
+
+static std::string shape_str(const std::vector<int64_t>& v) {
+  std::string o = "[";
+  for (size_t i = 0; i < v.size(); ++i) o += (i ? ", " : "") + std::to_string(v[i]);
+  return o + "]";
+}
+
+static const StTensor& ckpt_get(vd_handle* H, const std::string& name) {
+  if (!H->ckpt->has(name)) fail(VD_ESPEC, "checkpoint " + H->spec.checkpoint + " has no tensor " + name);
+  return H->ckpt->get(name);
+}
+
+static const StTensor& ckpt_tensor(vd_handle* H, const std::string& name, const std::vector<int64_t>& shape) {
+  const StTensor& t = ckpt_get(H, name);
+  if (t.shape != shape)
+    fail(VD_ESPEC, "checkpoint tensor " + name + " has shape " + shape_str(t.shape) + ", the spec needs " +
+                       shape_str(shape));
+  return t;
+}
+
+// Host bytes -> staging buffer (stream-ordered, so the next slice waits for the
+// conversion kernel that reads the previous one).
+static void* stage_bytes(vd_handle* H, const void* src, size_t bytes) {
+  if (!H->ckpt_stage) {
+    if (cudaMalloc(&H->ckpt_stage, kStageBytes) != cudaSuccess) {
+      cudaGetLastError();
+      H->ckpt_stage = nullptr;
+      fail(VD_ENOMEM, "cannot allocate the checkpoint staging buffer");
+    }
+  }
+  if (bytes > kStageBytes) fail(VD_ESPEC, "checkpoint row larger than the staging buffer");
+  cuda_check(cudaMemcpyAsync(H->ckpt_stage, src, bytes, cudaMemcpyHostToDevice, H->stream), "checkpoint upload");
+  return H->ckpt_stage;
+}
+
+// Called once the stream has finished with the staging buffer (after a synchronize).
+static void release_checkpoint(vd_handle* H) {
+  if (H->ckpt_stage) cudaFree(H->ckpt_stage);
+  H->ckpt_stage = nullptr;
+  H->ckpt.reset();
+}
+
+template <class T>
+static void fill_rows_t(vd_handle* H, T* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
+                        float offset, int64_t group, int64_t stride, int64_t off) {
+  if (!H->ckpt) {
+    synth_rows_kernel<T><<<grid_for(rows * cols), 256, 0, H->stream>>>(
+        dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, group, stride, off);
+    return;
+  }
+  const StTensor& t = ckpt_tensor(H, name, {rows, cols});
+  const size_t row_bytes = static_cast<size_t>(cols) * (t.dtype == kStF32 ? 4 : 2);
+  const int64_t slice = std::max<int64_t>(1, static_cast<int64_t>(kStageBytes / row_bytes));
+  for (int64_t r0 = 0; r0 < rows; r0 += slice) {
+    const int64_t n = std::min(slice, rows - r0);
+    const void* src = stage_bytes(H, t.data + static_cast<size_t>(r0) * row_bytes, static_cast<size_t>(n) * row_bytes);
+    convert_rows_kernel<T><<<grid_for(n * cols), 256, 0, H->stream>>>(dst, src, t.dtype, r0, n, cols, group, stride,
+                                                                       off);
+  }
+}
+
+// A 16-bit tensor in the element type `f16` selects (embedding tables are always bf16).
+static void fill_w(vd_handle* H, void* dst, bool f16, const std::string& name, int64_t rows, int64_t cols,
+                   float scale, float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
   if (group == 0) group = rows;
-  const uint64_t base = tensor_base(H->spec.seed, name);
-  if (f16)
-    synth_rows_kernel<__half><<<grid_for(rows * cols), 256, 0, H->stream>>>(
-        static_cast<__half*>(dst), rows, cols, base, scale, offset, group, stride, off);
-  else
-    synth_rows_kernel<__nv_bfloat16><<<grid_for(rows * cols), 256, 0, H->stream>>>(
-        static_cast<__nv_bfloat16*>(dst), rows, cols, base, scale, offset, group, stride, off);
+  if (f16) fill_rows_t(H, static_cast<__half*>(dst), name, rows, cols, scale, offset, group, stride, off);
+  else fill_rows_t(H, static_cast<__nv_bfloat16*>(dst), name, rows, cols, scale, offset, group, stride, off);
 }
-static void synth_bf16(vd_handle* H, bf16* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
-                       float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
-  synth_w(H, dst, false, name, rows, cols, scale, offset, group, stride, off);
+static void fill_bf16(vd_handle* H, bf16* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
+                      float offset) {
+  fill_w(H, dst, false, name, rows, cols, scale, offset);
 }
-static void synth_lin(vd_handle* H, void* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
-                      float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
-  synth_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off);
+static void fill_lin(vd_handle* H, void* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
+                     float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
+  fill_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off);
 }
-static void synth_f32(vd_handle* H, float* dst, const std::string& name, int64_t n, float scale, float offset) {
-  synth_f32_kernel<<<grid_for(n), 256, 0, H->stream>>>(dst, n, tensor_base(H->spec.seed, name), scale, offset);
+// An fp32 vector of n elements (gains, biases; a [1, n] Linear weight qualifies).
+static void fill_f32(vd_handle* H, float* dst, const std::string& name, int64_t n, float scale, float offset) {
+  if (!H->ckpt) {
+    synth_f32_kernel<<<grid_for(n), 256, 0, H->stream>>>(dst, n, tensor_base(H->spec.seed, name), scale, offset);
+    return;
+  }
+  const StTensor& t = ckpt_get(H, name);
+  if (t.numel() != n)
+    fail(VD_ESPEC, "checkpoint tensor " + name + " has shape " + shape_str(t.shape) + ", the spec needs " +
+                       std::to_string(n) + " elements");
+  const void* src = stage_bytes(H, t.data, t.nbytes);
+  convert_f32_kernel<<<grid_for(n), 256, 0, H->stream>>>(dst, src, t.dtype, n);
+}
+// Rows `ids` of a [vocab, cols] tensor as fp32 (the option-label rows of the LM head).
+static void fill_rows_gather_f32(vd_handle* H, float* dst, const std::string& name, const std::vector<int>& ids,
+                                 int64_t vocab, int64_t cols, float scale, float offset) {
+  const int n = static_cast<int>(ids.size());
+  if (!H->ckpt) {
+    int* rows = dalloc<int>(H, n);
+    cuda_check(cudaMemcpyAsync(rows, ids.data(), sizeof(int) * n, cudaMemcpyHostToDevice, H->stream),
+               "upload label ids");
+    synth_rows_gather_f32_kernel<<<grid_for(static_cast<int64_t>(n) * cols), 256, 0, H->stream>>>(
+        dst, rows, n, cols, tensor_base(H->spec.seed, name), scale, offset);
+    return;
+  }
+  const StTensor& t = ckpt_tensor(H, name, {vocab, cols});
+  const size_t row_bytes = static_cast<size_t>(cols) * (t.dtype == kStF32 ? 4 : 2);
+  std::vector<uint8_t> host(row_bytes * n);
+  for (int i = 0; i < n; ++i) std::memcpy(host.data() + i * row_bytes, t.data + ids[i] * row_bytes, row_bytes);
+  const void* src = stage_bytes(H, host.data(), host.size());
+  convert_f32_kernel<<<grid_for(static_cast<int64_t>(n) * cols), 256, 0, H->stream>>>(dst, src, t.dtype,
+                                                                                     static_cast<int64_t>(n) * cols);
+  // `host` is pageable: the copy above has left it before returning.
 }
 
 static int pick_bn(int n) { return n % 256 == 0 ? 256 : 128; }
@@ -402,7 +674,7 @@ static void load_decoder(vd_handle* H) {
   const float lin = static_cast<float>(s.init_std * std::sqrt(3.0));
   const float n_scale = 0.1f, n_off = s.norm_plus_one ? 0.0f : 1.0f;
   H->embed = dalloc<bf16>(H, static_cast<size_t>(s.vocab) * d);
-  synth_bf16(H, H->embed, "model.embed_tokens.weight", s.vocab, d, lin, 0.0f);
+  fill_bf16(H, H->embed, "model.embed_tokens.weight", s.vocab, d, lin, 0.0f);
   const int qc = nq * hd, kc = nkv * hd;
   // QKV tiles must not straddle the q / k / v column blocks.
   int bn_qkv = 256;
@@ -413,41 +685,37 @@ static void load_decoder(vd_handle* H) {
     const std::string p = "model.layers." + std::to_string(i) + ".";
     L.in_norm = dalloc<float>(H, d);
     L.post_norm = dalloc<float>(H, d);
-    synth_f32(H, L.in_norm, p + "input_layernorm.weight", d, n_scale, n_off);
-    synth_f32(H, L.post_norm, p + "post_attention_layernorm.weight", d, n_scale, n_off);
+    fill_f32(H, L.in_norm, p + "input_layernorm.weight", d, n_scale, n_off);
+    fill_f32(H, L.post_norm, p + "post_attention_layernorm.weight", d, n_scale, n_off);
     init_linear(H, L.qkv, s.qkv_width(), d, s.qkv_bias, bn_qkv);
-    synth_lin(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
-    synth_lin(H, L.qkv.w, p + "self_attn.k_proj.weight", kc, d, lin, 0.0f, kc, 0, qc);
-    synth_lin(H, L.qkv.w, p + "self_attn.v_proj.weight", kc, d, lin, 0.0f, kc, 0, qc + kc);
+    fill_lin(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
+    fill_lin(H, L.qkv.w, p + "self_attn.k_proj.weight", kc, d, lin, 0.0f, kc, 0, qc);
+    fill_lin(H, L.qkv.w, p + "self_attn.v_proj.weight", kc, d, lin, 0.0f, kc, 0, qc + kc);
     if (s.qkv_bias) {
-      synth_f32(H, L.qkv.b, p + "self_attn.q_proj.bias", qc, lin, 0.0f);
-      synth_f32(H, L.qkv.b + qc, p + "self_attn.k_proj.bias", kc, lin, 0.0f);
-      synth_f32(H, L.qkv.b + qc + kc, p + "self_attn.v_proj.bias", kc, lin, 0.0f);
+      fill_f32(H, L.qkv.b, p + "self_attn.q_proj.bias", qc, lin, 0.0f);
+      fill_f32(H, L.qkv.b + qc, p + "self_attn.k_proj.bias", kc, lin, 0.0f);
+      fill_f32(H, L.qkv.b + qc + kc, p + "self_attn.v_proj.bias", kc, lin, 0.0f);
     }
     if (s.qk_norm) {
       L.q_norm = dalloc<float>(H, hd);
       L.k_norm = dalloc<float>(H, hd);
-      synth_f32(H, L.q_norm, p + "self_attn.q_norm.weight", hd, n_scale, n_off);
-      synth_f32(H, L.k_norm, p + "self_attn.k_norm.weight", hd, n_scale, n_off);
+      fill_f32(H, L.q_norm, p + "self_attn.q_norm.weight", hd, n_scale, n_off);
+      fill_f32(H, L.k_norm, p + "self_attn.k_norm.weight", hd, n_scale, n_off);
     }
     init_linear(H, L.o, d, qc, false);
-    synth_lin(H, L.o.w, p + "self_attn.o_proj.weight", d, qc, lin, 0.0f);
+    fill_lin(H, L.o.w, p + "self_attn.o_proj.weight", d, qc, lin, 0.0f);
     init_linear(H, L.gu, 2 * f, d, false, 256);
-    synth_lin(H, L.gu.w, p + "mlp.gate_proj.weight", f, d, lin, 0.0f, 128, 256, 0);
-    synth_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
+    fill_lin(H, L.gu.w, p + "mlp.gate_proj.weight", f, d, lin, 0.0f, 128, 256, 0);
+    fill_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
     init_linear(H, L.down, d, f, false);
-    synth_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
+    fill_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
   }
   H->final_norm = dalloc<float>(H, d);
-  synth_f32(H, H->final_norm, "model.norm.weight", d, n_scale, n_off);
+  fill_f32(H, H->final_norm, "model.norm.weight", d, n_scale, n_off);
   H->n_labels = static_cast<int>(s.label_ids.size());
   H->head_rows = dalloc<float>(H, static_cast<size_t>(H->n_labels) * d);
-  int* rows = dalloc<int>(H, H->n_labels);
-  cuda_check(cudaMemcpyAsync(rows, s.label_ids.data(), sizeof(int) * H->n_labels, cudaMemcpyHostToDevice, H->stream),
-             "upload label ids");
   const std::string head_name = s.tied ? "model.embed_tokens.weight" : "lm_head.weight";
-  synth_rows_gather_f32_kernel<<<grid_for(static_cast<int64_t>(H->n_labels) * d), 256, 0, H->stream>>>(
-      H->head_rows, rows, H->n_labels, d, tensor_base(s.seed, head_name), lin, 0.0f);
+  fill_rows_gather_f32(H, H->head_rows, head_name, s.label_ids, s.vocab, d, lin, 0.0f);
   // RoPE table: cos/sin(pos * inv_freq_i), inv_freq_i = 1 / theta^(2i/hd) in fp32.
   const int half = hd / 2;
   std::vector<float2> tab(static_cast<size_t>(H->opt.max_seq) * half);
@@ -467,8 +735,8 @@ static void load_decoder(vd_handle* H) {
 static void enc_linear(vd_handle* H, Linear& L, const std::string& wname, const std::string& bname, int n, int k,
                        float lin) {
   init_linear(H, L, n, k, true);
-  synth_lin(H, L.w, wname, n, k, lin, 0.0f);
-  synth_f32(H, L.b, bname, n, lin, 0.0f);
+  fill_lin(H, L.w, wname, n, k, lin, 0.0f);
+  fill_f32(H, L.b, bname, n, lin, 0.0f);
 }
 
 static void load_encoder(vd_handle* H) {
@@ -478,15 +746,15 @@ static void load_encoder(vd_handle* H) {
   const float g_scale = 0.1f, g_off = 1.0f;
   const std::string e = "encoder.embeddings.";
   H->embed = dalloc<bf16>(H, static_cast<size_t>(s.vocab) * d);
-  synth_bf16(H, H->embed, e + "word_embeddings.weight", s.vocab, d, lin, 0.0f);
+  fill_bf16(H, H->embed, e + "word_embeddings.weight", s.vocab, d, lin, 0.0f);
   H->pos_emb = dalloc<bf16>(H, static_cast<size_t>(s.max_pos) * d);
-  synth_bf16(H, H->pos_emb, e + "position_embeddings.weight", s.max_pos, d, lin, 0.0f);
+  fill_bf16(H, H->pos_emb, e + "position_embeddings.weight", s.max_pos, d, lin, 0.0f);
   H->type_emb0 = dalloc<bf16>(H, static_cast<size_t>(s.type_vocab) * d);
-  synth_bf16(H, H->type_emb0, e + "token_type_embeddings.weight", s.type_vocab, d, lin, 0.0f);
+  fill_bf16(H, H->type_emb0, e + "token_type_embeddings.weight", s.type_vocab, d, lin, 0.0f);
   H->emb_ln_w = dalloc<float>(H, d);
   H->emb_ln_b = dalloc<float>(H, d);
-  synth_f32(H, H->emb_ln_w, e + "LayerNorm.weight", d, g_scale, g_off);
-  synth_f32(H, H->emb_ln_b, e + "LayerNorm.bias", d, lin, 0.0f);
+  fill_f32(H, H->emb_ln_w, e + "LayerNorm.weight", d, g_scale, g_off);
+  fill_f32(H, H->emb_ln_b, e + "LayerNorm.bias", d, lin, 0.0f);
   H->enc.resize(s.layers);
   for (int i = 0; i < s.layers; ++i) {
     EncLayer& L = H->enc[i];
@@ -494,9 +762,9 @@ static void load_encoder(vd_handle* H) {
     init_linear(H, L.qkv, 3 * d, d, true);
     const char* parts[3] = {"query", "key", "value"};
     for (int j = 0; j < 3; ++j) {
-      synth_lin(H, L.qkv.w, p + "attention.self." + parts[j] + ".weight", d, d, lin, 0.0f, d, 0,
+      fill_lin(H, L.qkv.w, p + "attention.self." + parts[j] + ".weight", d, d, lin, 0.0f, d, 0,
                  static_cast<int64_t>(j) * d);
-      synth_f32(H, L.qkv.b + j * d, p + "attention.self." + parts[j] + ".bias", d, lin, 0.0f);
+      fill_f32(H, L.qkv.b + j * d, p + "attention.self." + parts[j] + ".bias", d, lin, 0.0f);
     }
     enc_linear(H, L.o, p + "attention.output.dense.weight", p + "attention.output.dense.bias", d, d, lin);
     enc_linear(H, L.f1, p + "intermediate.dense.weight", p + "intermediate.dense.bias", f, d, lin);
@@ -505,16 +773,16 @@ static void load_encoder(vd_handle* H) {
     L.ln1_b = dalloc<float>(H, d);
     L.ln2_w = dalloc<float>(H, d);
     L.ln2_b = dalloc<float>(H, d);
-    synth_f32(H, L.ln1_w, p + "attention.output.LayerNorm.weight", d, g_scale, g_off);
-    synth_f32(H, L.ln1_b, p + "attention.output.LayerNorm.bias", d, lin, 0.0f);
-    synth_f32(H, L.ln2_w, p + "output.LayerNorm.weight", d, g_scale, g_off);
-    synth_f32(H, L.ln2_b, p + "output.LayerNorm.bias", d, lin, 0.0f);
+    fill_f32(H, L.ln1_w, p + "attention.output.LayerNorm.weight", d, g_scale, g_off);
+    fill_f32(H, L.ln1_b, p + "attention.output.LayerNorm.bias", d, lin, 0.0f);
+    fill_f32(H, L.ln2_w, p + "output.LayerNorm.weight", d, g_scale, g_off);
+    fill_f32(H, L.ln2_b, p + "output.LayerNorm.bias", d, lin, 0.0f);
     L.pre_norm = false;
     L.act = kActGeluErf;
     L.eps = static_cast<float>(s.ln_eps);
   }
   H->qtype_emb = dalloc<bf16>(H, 3 * static_cast<size_t>(d));
-  synth_bf16(H, H->qtype_emb, "type_emb.weight", 3, d, lin, 0.0f);
+  fill_bf16(H, H->qtype_emb, "type_emb.weight", 3, d, lin, 0.0f);
   H->head.resize(s.head_layers);
   for (int i = 0; i < s.head_layers; ++i) {
     EncLayer& L = H->head[i];
@@ -527,23 +795,23 @@ static void load_encoder(vd_handle* H) {
     L.ln1_b = dalloc<float>(H, d);
     L.ln2_w = dalloc<float>(H, d);
     L.ln2_b = dalloc<float>(H, d);
-    synth_f32(H, L.ln1_w, p + "norm1.weight", d, g_scale, g_off);
-    synth_f32(H, L.ln1_b, p + "norm1.bias", d, lin, 0.0f);
-    synth_f32(H, L.ln2_w, p + "norm2.weight", d, g_scale, g_off);
-    synth_f32(H, L.ln2_b, p + "norm2.bias", d, lin, 0.0f);
+    fill_f32(H, L.ln1_w, p + "norm1.weight", d, g_scale, g_off);
+    fill_f32(H, L.ln1_b, p + "norm1.bias", d, lin, 0.0f);
+    fill_f32(H, L.ln2_w, p + "norm2.weight", d, g_scale, g_off);
+    fill_f32(H, L.ln2_b, p + "norm2.bias", d, lin, 0.0f);
     L.pre_norm = true;
     L.act = kActRelu;
     L.eps = 1e-5f;  // nn.TransformerEncoderLayer default layer_norm_eps
   }
   H->sc_ln_w = dalloc<float>(H, d);
   H->sc_ln_b = dalloc<float>(H, d);
-  synth_f32(H, H->sc_ln_w, "scorer.0.weight", d, g_scale, g_off);
-  synth_f32(H, H->sc_ln_b, "scorer.0.bias", d, lin, 0.0f);
+  fill_f32(H, H->sc_ln_w, "scorer.0.weight", d, g_scale, g_off);
+  fill_f32(H, H->sc_ln_b, "scorer.0.bias", d, lin, 0.0f);
   enc_linear(H, H->sc1, "scorer.1.weight", "scorer.1.bias", d, d, lin);
   H->sc_w3 = dalloc<float>(H, d);
   H->sc_b3 = dalloc<float>(H, 1);
-  synth_f32(H, H->sc_w3, "scorer.3.weight", d, lin, 0.0f);
-  synth_f32(H, H->sc_b3, "scorer.3.bias", 1, lin, 0.0f);
+  fill_f32(H, H->sc_w3, "scorer.3.weight", d, lin, 0.0f);
+  fill_f32(H, H->sc_b3, "scorer.3.bias", 1, lin, 0.0f);
 }
 
 // Device copies of host-memory batches; grown on demand (only when a batch is
@@ -1096,6 +1364,34 @@ static int guarded(vd_handle* h, char* err, size_t errlen, F&& body) {
 
 extern "C" VD_API int vd_abi_version(void) { return VDEXEC_ABI_VERSION; }
 
+// `model` as vd_open reads it: a JSON spec, or a directory holding vdexec.json.
+static Json load_spec(const char* model) {
+  if (!model) fail(VD_EINVAL, "null model");
+  std::string text(model), spec_dir;
+  if (text.empty() || text[0] != '{') {
+    spec_dir = text;
+    std::ifstream f(text + "/vdexec.json");
+    if (!f) fail(VD_ESPEC, "no JSON spec given and no vdexec.json in " + text);
+    std::stringstream ss;
+    ss << f.rdbuf();
+    text = ss.str();
+  }
+  return resolve_spec(parse_json(text), spec_dir);
+}
+
+extern "C" VD_API int vd_resolve_spec(const char* model, char* out, size_t outlen, char* err, size_t errlen) {
+  return guarded(nullptr, err, errlen, [&] {
+    Json j = load_spec(model);
+    validate_spec(parse_spec(j));
+    std::string text;
+    json_write(text, j);
+    if (!out || outlen < text.size() + 1)
+      fail(VD_EINVAL, "the resolved spec needs " + std::to_string(text.size() + 1) + " bytes");
+    std::memcpy(out, text.data(), text.size());
+    out[text.size()] = '\0';
+  });
+}
+
 extern "C" VD_API int vd_open(const char* model, int device, const char* opts_json, vd_handle** out, char* err,
                        size_t errlen) {
   if (!out) {
@@ -1105,16 +1401,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
   *out = nullptr;
   vd_handle* H = new vd_handle();
   int rc = guarded(nullptr, err, errlen, [&] {
-    if (!model) fail(VD_EINVAL, "null model");
-    std::string text(model);
-    if (text.empty() || text[0] != '{') {
-      std::ifstream f(text + "/vdexec.json");
-      if (!f) fail(VD_ESPEC, "no JSON spec given and no vdexec.json in " + text);
-      std::stringstream ss;
-      ss << f.rdbuf();
-      text = ss.str();
-    }
-    H->spec = parse_spec(parse_json(text));
+    H->spec = parse_spec(load_spec(model));
     validate_spec(H->spec);
     if (opts_json && *opts_json) {
       Json o = parse_json(opts_json);
@@ -1134,6 +1421,14 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
     if (H->opt.max_tokens < 128 || H->opt.max_rows < 1 || H->opt.max_seq < 1)
       fail(VD_EINVAL, "max_tokens must be >= 128 and max_rows, max_seq >= 1");
     H->opt.max_tokens = (H->opt.max_tokens + 127) / 128 * 128;
+    // Headers are parsed (and the files mapped) before any device work.
+    if (!H->spec.checkpoint.empty()) {
+      try {
+        H->ckpt.reset(new Checkpoint(H->spec.checkpoint));
+      } catch (const std::runtime_error& e) {
+        fail(VD_ESPEC, e.what());
+      }
+    }
     H->device = device;
     cuda_check(cudaSetDevice(device), "cudaSetDevice");
     cudaDeviceProp prop;
@@ -1145,8 +1440,9 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
     if (H->spec.decoder()) load_decoder(H);
     else load_encoder(H);
     alloc_workspace(H);
-    cuda_check(cudaGetLastError(), "weight generation launch");
-    cuda_check(cudaStreamSynchronize(H->stream), "weight generation");
+    cuda_check(cudaGetLastError(), "weight load launch");
+    cuda_check(cudaStreamSynchronize(H->stream), "weight load");
+    release_checkpoint(H);
   });
   if (rc != VD_OK) {
     vd_close(H);
@@ -1299,6 +1595,7 @@ extern "C" VD_API void vd_close(vd_handle* h) {
     if (cudaSetDevice(h->device) == cudaSuccess) {
       if (h->stream) cudaStreamSynchronize(h->stream);
       for (void* p : h->allocations) cudaFree(p);
+      release_checkpoint(h);
       for (void* p : {static_cast<void*>(h->in_ids), static_cast<void*>(h->in_mpos), static_cast<void*>(h->in_mmask),
                       static_cast<void*>(h->in_nopts), static_cast<void*>(h->in_qtype), static_cast<void*>(h->out_dev)})
         if (p) cudaFree(p);

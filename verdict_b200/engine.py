@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import os
 import threading
 from dataclasses import dataclass
 from typing import Optional, Sequence
@@ -27,6 +28,7 @@ import numpy as np
 
 from . import _abi
 from .batch import CollatedBatch
+from .checkpoint import resolve_spec
 from .synth import with_labels
 
 
@@ -68,12 +70,21 @@ def _ptr(a: Optional[np.ndarray]):
 class B200Engine(Engine):
     """One model replica on one GPU (`TorchEngine::with_device`, `src/torch_engine.rs:280-316`)."""
 
-    def __init__(self, spec: dict, device: int = 0, *, max_tokens: int = 65536, max_rows: int = 512,
+    def __init__(self, spec, device: int = 0, *, max_tokens: int = 65536, max_rows: int = 512,
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
                  prune_last_layer: bool = True):
+        """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
+        relative "checkpoint" path is taken from that directory)."""
         self.lib = _abi.load()
-        self.spec = with_labels(spec)
+        if isinstance(spec, (str, os.PathLike)):
+            model = os.fspath(spec).encode()
+            self.spec = resolve_spec(spec)
+        else:
+            if "hidden" not in spec and "checkpoint" in spec:
+                spec = resolve_spec(spec)  # shape from the checkpoint's HF config
+            self.spec = with_labels(spec)
+            model = json.dumps(self.spec).encode()
         self.device = device
         self.decoder = self.spec["arch"] == "decoder"
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
@@ -81,8 +92,7 @@ class B200Engine(Engine):
                                attention=attention, prune_last_layer=prune_last_layer))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
-        rc = self.lib.vd_open(json.dumps(self.spec).encode(), device, opts.encode(), ctypes.byref(h), err,
-                              len(err))
+        rc = self.lib.vd_open(model, device, opts.encode(), ctypes.byref(h), err, len(err))
         _abi.check(rc, err)
         self.h = h
         self._lock = threading.Lock()

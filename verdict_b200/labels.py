@@ -1,10 +1,10 @@
 """Option-label tables: which LM-head rows the letter families read.
 
 Restates the two rules the reference implements twice (Rust and Python):
-- letter_readout: `derive_letter_table` (`src/tokenize.rs:147-185`) /
+- letter_readout: `derive_letter_table` (`src/tokenize.rs:96-134`) /
   `derive_letter_ids` (`executor/torch_exec.py:2254-2290`): the single-token ids
   of "A".."Z", then of "AA".."ZZ" in order, until 255 labels.
-- letter_branches: `derive_branch_table` (`src/tokenize.rs:187-222`) /
+- letter_branches: `derive_branch_table` (`src/tokenize.rs:136-171`) /
   `derive_branch_ids` (`executor/torch_exec.py:2292-2323`): the 26 letters (each
   must round-trip as one token), then the pair labels of `slot_labels()`
   (`src/family/letter_branches.rs:30-44`), i.e. "AA".."ZZ" minus the 25 pairs

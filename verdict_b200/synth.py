@@ -234,8 +234,8 @@ def synthetic_label_ids(spec: dict) -> list:
 
 
 def with_labels(spec: dict) -> dict:
-    """The spec with its label table filled in (decoders only)."""
+    """The spec with its label table filled in where it has none (decoders only)."""
     out = dict(spec)
-    if out["arch"] == "decoder":
+    if out["arch"] == "decoder" and out.get("label_ids") is None:
         out["label_ids"] = synthetic_label_ids(out)
     return out
