@@ -45,6 +45,9 @@ UNIT = "decisions/s"
 WORKLOAD = ("OneJev-9B-shaped text decisions: 40 layers, d=4096, 32/8 heads hd=128, SwiGLU 12288, "
             "vocab 152064, causal varlen prefill + option log-softmax; lengths clip(lognormal(6,0.7),32,4096), "
             "2-8 options")
+SHARED_WORKLOAD = ("OneJev-9B-shaped letter-branches decisions, 8 questions per state: rows of a state share "
+                   "its prefix (declared prefix_len), state prefix clip(lognormal(6.5,0.5),128,3072) tokens, "
+                   "question suffix U[40,160] tokens, 2-8 options")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
 # full-size ncu capture of this bench's first timed launch (profiles/gemm_gateup_onejev9b.md), and the
@@ -132,14 +135,17 @@ def whole_job_rate(decisions_per_rank: int, world: int, max_ms: float) -> float:
     return decisions_per_rank * world / (max_ms / 1e3)
 
 
-def make_batches(rank, n_batches, per_batch, vocab, seed):
+def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice"):
     """Each rank's own shard of the workload: batch j of rank r is seeded by
     (seed, r, j), so ranks never share a decision."""
-    from verdict_b200.batch import Layout, collate, decoder_rows
+    from verdict_b200.batch import Layout, collate, decoder_rows, shared_prefix_rows
     out = []
     for j in range(n_batches):
         rng = np.random.default_rng([seed, rank, j])
-        rows = decoder_rows(rng, per_batch, vocab, lengths="lognormal-9b")
+        if workload == "shared-prefix":
+            rows = shared_prefix_rows(rng, per_batch, vocab)
+        else:
+            rows = decoder_rows(rng, per_batch, vocab, lengths="lognormal-9b")
         out.append(collate(rows, Layout(pad_id=0)))
     return out
 
@@ -214,6 +220,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--attention", default="tc", choices=["tc", "mma"],
                     help="head_dim-128 causal attention kernel: tcgen05 (tc) or warp-level mma.sync")
+    ap.add_argument("--workload", default="choice", choices=["choice", "shared-prefix"],
+                    help="choice: the OneJev-9B decision workload (headline); shared-prefix: 8 questions "
+                         "per state, rows of a state share the state prefix (prefix_len declared)")
+    ap.add_argument("--fork", default="on", choices=["on", "off"],
+                    help="compute shared prefixes once (on) or every row whole (off)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -239,10 +250,12 @@ def main():
     over = {} if args.layers is None else {"layers": args.layers}
     spec = with_labels(specs.preset("onejev-9b", **over))
     n_batches = args.warmup + args.steps
-    batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed)
+    batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed, args.workload)
     max_tokens = max(int(b.real_len().sum()) for b in batches)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
-                     max_seq=4096, attention=args.attention)
+                     max_seq=4096, attention=args.attention, fork=args.fork == "on")
+    # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
+    shared = args.workload == "shared-prefix"
     width = eng.width
     stream_ptr = eng.stream()
     stream = torch.cuda.ExternalStream(stream_ptr)
@@ -259,7 +272,7 @@ def main():
     def step_dev(j):
         b = batches[j]
         eng.infer_device(b.b, b.l, b.k, {k: v.data_ptr() for k, v in dev[j].items()}, b.real_len(),
-                         out.data_ptr(), width)
+                         out.data_ptr(), width, prefix_len=b.prefix_len() if shared else None)
 
     def barrier():
         torch.cuda.synchronize()
@@ -287,6 +300,7 @@ def main():
             evs[i + 1].record(stream)
     eng.sync()
     launches = eng.last_stats()["launches"] * args.steps
+    computed_tokens = eng.last_stats()["tokens"]  # last timed step, after any shared-prefix fork
     barrier()
     clk = clocks.stop()
     step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
@@ -306,7 +320,7 @@ def main():
     for i in range(prof_steps):
         b = batches[args.warmup + i]
         eng.infer_device(b.b, b.l, b.k, {k: v.data_ptr() for k, v in dev[args.warmup + i].items()}, b.real_len(),
-                         out.data_ptr(), width, sync=True)
+                         out.data_ptr(), width, sync=True, prefix_len=b.prefix_len() if shared else None)
         st = eng.last_stats()
         acc_ms += np.array(st["kernel_ms"][:])
         acc_fl += np.array(st["kernel_flops"][:])
@@ -363,6 +377,9 @@ def main():
             st.qtype = ctypes.c_void_p(p["qtype"].data_ptr())
             rl = b.real_len()
             st.real_len = ctypes.c_void_p(rl.ctypes.data)
+            pl = b.prefix_len()
+            if shared:
+                st.prefix_len = ctypes.c_void_p(pl.ctypes.data)
             err = ctypes.create_string_buffer(512)
             rc = eng.lib.vd_infer(eng.h, ctypes.byref(st), ctypes.c_void_p(out_h.data_ptr()), width, err, 512)
             if rc != 0:
@@ -410,8 +427,10 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
-            "config": {"workload": WORKLOAD, "model": "onejev-9b", "layers": spec["layers"], "attention": args.attention,
+            "config": {"workload": SHARED_WORKLOAD if shared else WORKLOAD, "model": "onejev-9b",
+                       "layers": spec["layers"], "attention": args.attention, "fork": args.fork,
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
+                       "computed_tokens_last_step": int(computed_tokens),
                        "parallelism": f"replicas x{world} (one full-weight replica per GPU, no collectives)",
                        "l2": "no flush: each step streams 15.4 GB of weights and ~0.5 GB of activations, "
                              "far above the 126 MB L2"},

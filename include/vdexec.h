@@ -97,6 +97,11 @@ typedef struct vd_stats {
   /* Host wall time of the call and of its enqueue part (up to the last launch). */
   double host_ms;
   double enqueue_ms;
+  /* Shared-prefix fork: groups formed, rows in them, prefix tokens computed
+   * once instead of once per row. */
+  int64_t fork_groups;
+  int64_t fork_rows;
+  int64_t shared_tokens;
 } vd_stats;
 
 /*
@@ -113,7 +118,12 @@ typedef struct vd_stats {
  *   src/tokenize.rs:96-171) and default to "family": "letter_readout".
  * opts_json: NULL or {"max_tokens": N, "max_rows": N, "max_seq": N,
  *   "max_markers": N, "output": "logprobs"|"logits", "act_dtype":
- *   "fp16"|"bf16", "attention": "tc"|"mma", "prune_last_layer": bool}.
+ *   "fp16"|"bf16", "attention": "tc"|"mma", "prune_last_layer": bool,
+ *   "fork": bool (default true: decoder rows that share a prefix — declared
+ *   prefix_len, else a common prefix of >= 32 tokens — compute it once, as
+ *   executor/torch_exec.py:1935-2022 does; planned on the host from the ids:
+ *   host-memory batches always, device-memory batches when they pass
+ *   prefix_len, at the cost of one copy back and synchronisation)}.
  * Replaces TorchEngine::with_device (src/torch_engine.rs:280-316) and the
  * executor's checkpoint load (executor/torch_exec.py:2341-2386).
  */

@@ -92,7 +92,7 @@ VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int
  *
  * Same arguments and results as vdk_attention.  The per-call work table (one
  * entry per 64-row query tile) lives in a fixed device array of 16384 entries
- * (256 KiB) that every GPU loading this library keeps until the process
+ * (512 KiB) that every GPU loading this library keeps until the process
  * exits; a batch needing more tiles (sum over sequences of ceil(len / 64)) is
  * rejected with VD_EINVAL before anything is launched.
  * The first call on a device looks up that array's device address (with the

@@ -26,7 +26,7 @@ def load(path):
     return z, spec, batch
 
 
-DEC = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz")) if "_marker_" not in p)
+DEC = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz")) if "_marker_" not in p and "fork_" not in p)
 ENC = sorted(glob.glob(os.path.join(GOLDEN, "*_marker_*.npz")))
 
 

@@ -61,7 +61,8 @@ def assert_decoder_parity(got_lp, ref_logits, nopts, tol=LOGPROB_TOL):
             assert int(np.argmax(got_lp[i, :k])) == int(np.argmax(ref_lp[i, :k])), f"row {i}: choice differs"
 
 
-DECODER_FIXTURES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz")) if "_marker_" not in p)
+DECODER_FIXTURES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                          if "_marker_" not in p and "fork_" not in p)
 ENCODER_FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*_marker_*.npz")))
 
 

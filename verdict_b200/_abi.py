@@ -37,6 +37,7 @@ class VdStats(ctypes.Structure):
         ("kernel_ms", ctypes.c_double * 8), ("kernel_launches", ctypes.c_int64 * 8),
         ("kernel_flops", ctypes.c_double * 8),
         ("host_ms", ctypes.c_double), ("enqueue_ms", ctypes.c_double),
+        ("fork_groups", ctypes.c_int64), ("fork_rows", ctypes.c_int64), ("shared_tokens", ctypes.c_int64),
     ]
 
 

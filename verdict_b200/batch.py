@@ -144,6 +144,27 @@ def decoder_rows(rng: np.random.Generator, n: int, vocab: int, *, lengths: str,
     return rows
 
 
+def shared_prefix_rows(rng: np.random.Generator, n: int, vocab: int, *, per_state: int = 8,
+                       min_opts: int = 2, max_opts: int = 8, id_low: int = 3) -> list:
+    """Letter-branches rows that ask `per_state` questions about each state:
+    the rendered prompt is chat prefix + state, then question + options + answer
+    line (`build_row`, `src/family/letter_branches.rs:89-121`), so the rows of
+    one state share the prompt up to `prefix_len`.  State (prefix) lengths
+    clip(lognormal(6.5, 0.5), 128, 3072) (mean ~750), question suffixes
+    U[40, 160] tokens; slot = last token."""
+    rows = []
+    while len(rows) < n:
+        plen = int(np.clip(np.rint(rng.lognormal(6.5, 0.5)), 128, 3072))
+        prefix = rng.integers(id_low, vocab, size=plen).tolist()
+        for _ in range(min(per_state, n - len(rows))):
+            ids = prefix + rng.integers(id_low, vocab, size=int(rng.integers(40, 161))).tolist()
+            k = int(rng.integers(min_opts, max_opts + 1))
+            rows.append(BuiltSequence(ids=ids, markers=[len(ids) - 1], nopts=[k], prefix_len=plen,
+                                      full_len=len(ids)))
+    order = rng.permutation(len(rows))
+    return [rows[i] for i in order]
+
+
 def encoder_rows(rng: np.random.Generator, n: int, vocab: int, *, lengths: str,
                  cls_id: int, sep_id: int, id_low: int, k_low: int = 2, k_high: int = 6,
                  max_len: int = 512) -> list:

@@ -18,11 +18,17 @@
 
 namespace vd {
 
+// One query tile of one packed sequence.  A sequence that continues a shared
+// prefix (the suffix of a forked row) also attends to that prefix's keys,
+// stored once elsewhere in the packed batch: all of them, before its own keys
+// (every prefix position precedes every suffix position).
 struct AttnTile {
   int seq_start;  // first token of the sequence in the packed batch
   int seq_len;
   int q_start;    // first query row of this tile inside the sequence
-  int pad;
+  int pre_start;  // first token of the shared prefix in the packed batch
+  int pre_len;    // prefix keys (0: none)
+  int pad[3];
 };
 
 struct AttnParams {
@@ -81,17 +87,23 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
 
   const T* qkv = static_cast<const T*>(p.qkv);
   const T* gq = qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.q_col0 + head * HD;
-  const T* gk = qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.k_col0 + kvh * HD;
-  const T* gv = qkv + static_cast<size_t>(tile.seq_start) * p.ld_qkv + p.v_col0 + kvh * HD;
+  const T* gk = qkv + p.k_col0 + kvh * HD;  // rows are absolute packed-token indices
+  const T* gv = qkv + p.v_col0 + kvh * HD;
 
   const int q_rows = min(Cfg::BM, tile.seq_len - tile.q_start);
   int kv_end = tile.seq_len;
   if (CAUSAL) kv_end = min(tile.seq_len, tile.q_start + Cfg::BM);
-  const int n_kv = (kv_end + Cfg::BN - 1) / Cfg::BN;
+  // Key tiles: first the shared prefix's (n_pre), then the sequence's own.
+  const int n_pre = (tile.pre_len + Cfg::BN - 1) / Cfg::BN;
+  const int n_kv = n_pre + (kv_end + Cfg::BN - 1) / Cfg::BN;
+  auto kv_row = [&](int j) { return j < n_pre ? tile.pre_start + j * Cfg::BN : tile.seq_start + (j - n_pre) * Cfg::BN; };
+  auto kv_rows = [&](int j) {
+    return j < n_pre ? min(Cfg::BN, tile.pre_len - j * Cfg::BN) : min(Cfg::BN, tile.seq_len - (j - n_pre) * Cfg::BN);
+  };
 
   load_tile_async<HD, T>(sQ, gq, p.ld_qkv, tile.q_start, q_rows, tid);
-  load_tile_async<HD, T>(sK0, gk, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
-  load_tile_async<HD, T>(sV0, gv, p.ld_qkv, 0, min(Cfg::BN, tile.seq_len), tid);
+  load_tile_async<HD, T>(sK0, gk, p.ld_qkv, kv_row(0), kv_rows(0), tid);
+  load_tile_async<HD, T>(sV0, gv, p.ld_qkv, kv_row(0), kv_rows(0), tid);
   cp_async_commit();
 
   float o[ND][4];
@@ -105,10 +117,9 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
   for (int j = 0; j < n_kv; ++j) {
     const int buf = j & 1;
     if (j + 1 < n_kv) {
-      const int kv0n = (j + 1) * Cfg::BN;
       const uint32_t nb = (buf ^ 1) * Cfg::KV_BYTES;
-      load_tile_async<HD, T>(sK0 + nb, gk, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
-      load_tile_async<HD, T>(sV0 + nb, gv, p.ld_qkv, kv0n, min(Cfg::BN, tile.seq_len - kv0n), tid);
+      load_tile_async<HD, T>(sK0 + nb, gk, p.ld_qkv, kv_row(j + 1), kv_rows(j + 1), tid);
+      load_tile_async<HD, T>(sV0 + nb, gv, p.ld_qkv, kv_row(j + 1), kv_rows(j + 1), tid);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -118,7 +129,8 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
 
     const uint32_t sK = sK0 + buf * Cfg::KV_BYTES;
     const uint32_t sV = sV0 + buf * Cfg::KV_BYTES;
-    const int kv0 = j * Cfg::BN;
+    const bool in_pre = j < n_pre;
+    const int kv0 = (in_pre ? j : j - n_pre) * Cfg::BN;  // key index inside its segment
 
     // S = Q K^T for this warp's 16 query rows x 64 keys.
     float s[NB][4];
@@ -143,8 +155,9 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
       }
     }
 
-    // Mask keys past the sequence end and (causal) past the query row.
-    const bool need_mask = (kv0 + Cfg::BN > tile.seq_len) || (CAUSAL && kv0 + Cfg::BN > tile.q_start);
+    // Mask keys past the segment end and (causal, own keys only) past the query row.
+    const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
+    const bool need_mask = (kv0 + Cfg::BN > seg_len) || (CAUSAL && !in_pre && kv0 + Cfg::BN > tile.q_start);
     if (need_mask) {
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
@@ -152,8 +165,8 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
         for (int e = 0; e < 4; ++e) {
           const int kv = kv0 + nb * 8 + ((lane & 3) << 1) + (e & 1);
           const int qr = q_row_a + ((e >> 1) << 3);
-          bool dead = kv >= tile.seq_len;
-          if (CAUSAL) dead = dead || kv > qr;
+          bool dead = kv >= seg_len;
+          if (CAUSAL && !in_pre) dead = dead || kv > qr;
           if (dead) s[nb][e] = -INFINITY;
         }
       }

@@ -148,7 +148,10 @@ __global__ void __launch_bounds__(320, 1)
   const int head0 = kvh * p.group + 2 * pair;
   const int nheads = (2 * pair + 1 < p.group) ? 2 : 1;
   const int kv_end = min(tile.seq_len, tile.q_start + C::BM);
-  const int n_kv = (kv_end + C::BN - 1) / C::BN;
+  // Key tiles: first the shared prefix's (n_pre, unmasked but for its end),
+  // then the sequence's own (causal).
+  const int n_pre = (tile.pre_len + C::BN - 1) / C::BN;
+  const int n_kv = n_pre + (kv_end + C::BN - 1) / C::BN;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
-        const int y = row0 + j * C::BN;
+        const int y = j < n_pre ? tile.pre_start + j * C::BN : row0 + (j - n_pre) * C::BN;
         mbar_arrive_expect_tx(&k_full[s], C::TILE_BYTES);
         tma_load_2d(smem + C::K_OFF + s * C::TILE_BYTES, &tm_qkv, &k_full[s], kx, y);
         tma_load_2d(smem + C::K_OFF + s * C::TILE_BYTES + C::HALF_BYTES, &tm_qkv, &k_full[s], kx + 64, y);
@@ -257,13 +260,17 @@ __global__ void __launch_bounds__(320, 1)
       float m_run = -INFINITY, l_run = 0.0f;
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
-        const int kv0 = j * C::BN;
+        const bool in_pre = j < n_pre;
+        const int kv0 = (in_pre ? j : j - n_pre) * C::BN;  // key index inside its segment
+        const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
+        // Prefix keys precede every query row: only the causal limit of own keys applies.
+        const int causal_row = in_pre ? 0x7fffffff : q_row;
         if (!mbar_wait(&s_full[h], j & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const bool need_mask = kv0 + C::BN > tile.seq_len || kv0 + C::BN > tile.q_start;
+        const bool need_mask = kv0 + C::BN > seg_len || (!in_pre && kv0 + C::BN > tile.q_start);
         // The whole 128-column S row: four loads in flight, one wait.
         uint32_t sr[128];
         tmem_ld32_nowait(s_tm + 0, sr + 0);
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int i = 0; i < 128; ++i) {
             const int kv = kv0 + i;
-            if (kv >= tile.seq_len || kv > q_row) sr[i] = __float_as_uint(-INFINITY);
+            if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
             mx = fmaxf(mx, __uint_as_float(sr[i]));
           }
         } else {

@@ -27,24 +27,38 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return r;
 }
 
-// Right-padded [b, l] int64 ids -> packed int32 tokens, in-sequence positions and
-// sequence index per token.  Token ids outside [0, vocab) are reported and
-// replaced by 0 so no gather reads outside the table.
-__global__ void pack_tokens_kernel(const int64_t* __restrict__ ids, int64_t l, const int* __restrict__ cu, int b,
-                                   int vocab, int pos_offset, int* __restrict__ tokens, int* __restrict__ positions,
-                                   int* __restrict__ seq_id, int* err) {
-  const int row = blockIdx.y;
-  if (row >= b) return;
-  const int start = cu[row], len = cu[row + 1] - start;
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < len; j += gridDim.x * blockDim.x) {
-    int64_t id = ids[static_cast<int64_t>(row) * l + j];
+// One packed sequence: `len` tokens taken from columns [col0, col0 + len) of
+// batch row `src_row`, stored from packed index `start` on.  A whole row has
+// col0 = 0; a shared prefix is stored once (from its first member's row) and
+// each member's suffix starts at col0 = prefix length.
+struct PackSeg {
+  int start, len, col0, src_row;
+};
+
+// Where a decision's slot lives: packed token base + slot, slot in [lo, hi).
+struct RowMap {
+  int base, lo, hi, pad;
+};
+
+// Packed int32 tokens, positions and source row of every sequence (grid.y =
+// sequences).  Token ids outside [0, vocab) are reported and replaced by 0 so
+// no gather reads outside the table.
+__global__ void pack_segments_kernel(const int64_t* __restrict__ ids, int64_t l, const PackSeg* __restrict__ segs,
+                                     int n_seg, int vocab, int pos_offset, int* __restrict__ tokens,
+                                     int* __restrict__ positions, int* __restrict__ seq_id, int* err) {
+  const int sgi = blockIdx.y;
+  if (sgi >= n_seg) return;
+  const PackSeg sg = segs[sgi];
+  const int64_t* row = ids + static_cast<int64_t>(sg.src_row) * l + sg.col0;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < sg.len; j += gridDim.x * blockDim.x) {
+    int64_t id = row[j];
     if (id < 0 || id >= vocab) {
       record_error(err, kErrTokenRange);
       id = 0;
     }
-    tokens[start + j] = static_cast<int>(id);
-    positions[start + j] = j + pos_offset;
-    seq_id[start + j] = row;
+    tokens[sg.start + j] = static_cast<int>(id);
+    positions[sg.start + j] = sg.col0 + j + pos_offset;
+    seq_id[sg.start + j] = sg.src_row;
   }
 }
 
@@ -184,19 +198,19 @@ __global__ void add_type_kernel(float* __restrict__ h, int T, int d, const int* 
 
 // Slot rows of the packed batch -> compact per-decision buffers for the last
 // layer, whose O projection and MLP only the slot rows need:
-// attn_s[i] = attn[t_i], h_s[i] = h[t_i] with t_i = cu[i] + marker_pos[i*k].
+// attn_s[i] = attn[t_i], h_s[i] = h[t_i] with t_i = rows[i].base + marker_pos[i*k].
 template <class T>
-__global__ void gather_slot_rows_kernel(const int* __restrict__ cu, const int64_t* __restrict__ marker_pos, int k,
-                                        const T* __restrict__ attn, int ld_attn, const float* __restrict__ h, int d,
-                                        T* __restrict__ attn_s, float* __restrict__ h_s, int* err) {
+__global__ void gather_slot_rows_kernel(const RowMap* __restrict__ rows, const int64_t* __restrict__ marker_pos,
+                                        int k, const T* __restrict__ attn, int ld_attn, const float* __restrict__ h,
+                                        int d, T* __restrict__ attn_s, float* __restrict__ h_s, int* err) {
   const int i = blockIdx.x;
-  const int start = cu[i], len = cu[i + 1] - start;
+  const RowMap rm = rows[i];
   int64_t slot = marker_pos[static_cast<int64_t>(i) * k];
-  if (slot < 0 || slot >= len) {
+  if (slot < rm.lo || slot >= rm.hi) {
     if (threadIdx.x == 0) record_error(err, kErrSlotRange);
-    slot = 0;
+    slot = rm.lo;
   }
-  const int64_t t = start + slot;
+  const int64_t t = rm.base + slot;
   const uint4* a = reinterpret_cast<const uint4*>(attn + t * ld_attn);
   uint4* as = reinterpret_cast<uint4*>(attn_s + static_cast<int64_t>(i) * ld_attn);
   for (int j = threadIdx.x; j < ld_attn / 8; j += blockDim.x) as[j] = a[j];
@@ -211,7 +225,7 @@ __global__ void gather_slot_rows_kernel(const int* __restrict__ cu, const int64_
 // the n options or the raw logits; columns >= n are -1e4.
 template <int NT>
 __global__ void __launch_bounds__(NT)
-    readout_kernel(const float* __restrict__ h, int d, const int* __restrict__ cu,
+    readout_kernel(const float* __restrict__ h, int d, const RowMap* __restrict__ rows,
                    const int64_t* __restrict__ marker_pos, int k, const int64_t* __restrict__ nopts,
                    const float* __restrict__ norm_w, int plus_one, float eps, const float* __restrict__ head,
                    int n_labels, float* __restrict__ out, int width, int logprobs, int compact, int* err) {
@@ -220,19 +234,19 @@ __global__ void __launch_bounds__(NT)
   float* lg = sm + d;             // [n_labels]
   __shared__ float red[NT / 32 + 1];
   const int i = blockIdx.x;
-  const int start = cu[i], len = cu[i + 1] - start;
+  const RowMap rm = rows[i];
   const int64_t slot = marker_pos[static_cast<int64_t>(i) * k];
   int n = nopts ? static_cast<int>(nopts[i]) : n_labels;
   n = max(0, min(n, min(n_labels, width)));
   float* orow = out + static_cast<size_t>(i) * width;
-  if (slot < 0 || slot >= len) {
+  if (slot < rm.lo || slot >= rm.hi) {
     if (threadIdx.x == 0) record_error(err, kErrSlotRange);
     for (int j = threadIdx.x; j < width; j += NT) orow[j] = kSentinel;
     return;
   }
   // compact: h holds one row per decision (the slot rows, gathered before the
   // last layer's O projection); otherwise h is the packed batch.
-  const float* x = compact ? h + static_cast<size_t>(i) * d : h + static_cast<size_t>(start + slot) * d;
+  const float* x = compact ? h + static_cast<size_t>(i) * d : h + static_cast<size_t>(rm.base + slot) * d;
   float ss = 0.0f;
   for (int j = threadIdx.x; j < d; j += NT) {
     const float v = x[j];

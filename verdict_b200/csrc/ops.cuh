@@ -169,7 +169,7 @@ extern "C" VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_c
     for (int64_t i = 0; i < nseq; ++i) {
       const int start = cu_seqlens_host[i], len = cu_seqlens_host[i + 1] - start;
       if (len < 0) fail(VD_EINVAL, "cu_seqlens must be non-decreasing");
-      for (int q = 0; q < len; q += 64) tiles.push_back(AttnTile{start, len, q, 0});
+      for (int q = 0; q < len; q += 64) tiles.push_back(AttnTile{start, len, q, 0, 0, {0, 0, 0}});
     }
     if (tiles.empty()) return;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -226,7 +226,7 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
     for (int64_t i = 0; i < nseq; ++i) {
       const int start = cu_seqlens_host[i], len = cu_seqlens_host[i + 1] - start;
       if (len < 0) fail(VD_EINVAL, "cu_seqlens must be non-decreasing");
-      for (int q = 0; q < len; q += 128) tiles.push_back(AttnTile{start, len, q, 0});
+      for (int q = 0; q < len; q += 128) tiles.push_back(AttnTile{start, len, q, 0, 0, {0, 0, 0}});
     }
     if (tiles.empty()) return;
     const int64_t T = cu_seqlens_host[nseq];

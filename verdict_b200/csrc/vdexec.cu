@@ -415,6 +415,7 @@ struct Options {
   bool f16 = true;  // activations and projection weights in fp16 (else bf16)
   bool prune_last_layer = true;  // last layer's O projection and MLP on the slot rows only
   bool tc_attention = true;  // head_dim 128 causal attention on tcgen05 (else the mma.sync kernel)
+  bool fork = true;          // shared-prefix rows: prefix computed once (host-memory decoder batches)
 };
 
 }  // namespace vd
@@ -451,6 +452,8 @@ struct vd_handle {
   int *tokens = nullptr, *positions = nullptr, *seq_id = nullptr, *cu = nullptr, *midx = nullptr, *d_err = nullptr;
   vd::AttnTile* tiles = nullptr;
   int64_t max_tiles = 0;
+  vd::PackSeg* segs = nullptr;  // packed sequences of a chunk (rows, shared prefixes, suffixes)
+  vd::RowMap* rowmap = nullptr; // per decision: where its slot token is packed
   float2* rope = nullptr;
   CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow, map_qkv;
   // last-layer slot rows (one per decision of a chunk)
@@ -864,8 +867,11 @@ static void alloc_workspace(vd_handle* H) {
   H->positions = dalloc<int>(H, T);
   H->seq_id = dalloc<int>(H, T);
   H->cu = dalloc<int>(H, o.max_rows + 1);
-  H->max_tiles = T / 64 + o.max_rows + 1;
+  // A chunk packs at most 2 sequences per row (a shared prefix and a suffix).
+  H->max_tiles = T / 64 + 2 * o.max_rows + 1;
   H->tiles = dalloc<AttnTile>(H, H->max_tiles);
+  H->segs = dalloc<PackSeg>(H, 2 * o.max_rows);
+  H->rowmap = dalloc<RowMap>(H, o.max_rows);
   H->d_err = dalloc<int>(H, 1);
   cuda_check(cudaMemset(H->d_err, 0, sizeof(int)), "clear error word");
   const bool f16 = o.f16;
@@ -899,7 +905,8 @@ static void alloc_workspace(vd_handle* H) {
   }
   ensure_host_inputs(H, o.max_rows * 1024, std::max(o.max_rows, o.max_markers), o.max_rows,
                      std::max<int64_t>(o.max_rows * 256, o.max_markers));
-  H->pinned_bytes = sizeof(int) * (o.max_rows + 1) + sizeof(AttnTile) * H->max_tiles + 256;
+  H->pinned_bytes = sizeof(int) * (o.max_rows + 1) + sizeof(PackSeg) * 2 * o.max_rows +
+                    sizeof(RowMap) * o.max_rows + sizeof(AttnTile) * H->max_tiles + 256;
   for (int i = 0; i < vd_handle::kSlots; ++i) {
     cuda_check(cudaHostAlloc(reinterpret_cast<void**>(&H->pinned[i]), H->pinned_bytes, cudaHostAllocDefault),
                "pinned staging");
@@ -1044,48 +1051,184 @@ struct Chunk {
   const int64_t* nopts = nullptr;    // device [nb] or null
   const int64_t* qtype = nullptr;    // device [nb] or null
   const int64_t* real_len = nullptr; // host [nb]
+  // host copies for the shared-prefix plan (null: rows run whole)
+  const int64_t* ids_h = nullptr;    // host [nb*l]
+  const int64_t* mpos_h = nullptr;   // host [nb*k]
+  const int64_t* prefix_len = nullptr;  // host [nb] or null
   float* out = nullptr;              // device [nb*width]
   int64_t width = 0;
 };
 
-// Host plan: cu_seqlens and the attention tile table, staged through pinned memory.
-static int plan_chunk(vd_handle* H, const Chunk& c, int& T, int& max_len, bool causal, int tile_rows) {
+struct ChunkPlan {
+  int ntok = 0;       // packed tokens
+  int max_len = 0;    // longest packed sequence
+  int n_seg = 0, n_tiles = 0;
+  double pairs = 0;   // attention (query, key) pairs per head
+  int fork_groups = 0, fork_rows = 0;
+  int64_t shared_tokens = 0;  // prefix tokens not recomputed
+};
+
+// Shared-prefix groups of a chunk, the grouping of `_text_fork_forward`
+// (executor/torch_exec.py:1935-1977): a row whose slot is its last token joins
+// the group keyed by its declared prefix_len (>= 32 and < real_len) and those
+// prefix tokens; otherwise a row longer than 32 tokens joins the group keyed by
+// its first 32 tokens, whose prefix is then its members' longest common prefix.
+// A group runs its prefix once; groups of one row, and groups whose prefix is
+// under 32 tokens or leaves a member no suffix, run their rows whole (the
+// result is the same, computing it whole is cheaper).
+struct ForkGroup {
+  int n = 0;                // prefix tokens
+  std::vector<int> rows;
+};
+
+static constexpr int kForkFloor = 32;  // TEXT_FORK_MIN_PREFIX (GRAPH_PREFIX_STEP)
+
+static std::vector<ForkGroup> plan_fork(const Chunk& c) {
+  std::vector<ForkGroup> out;
+  if (!c.ids_h || !c.mpos_h || c.nb < 2) return out;
+  auto row_ids = [&](int i) { return c.ids_h + static_cast<int64_t>(i) * c.l; };
+  auto hash = [&](int i, int n) {
+    uint64_t h = 0xCBF29CE484222325ull;
+    const int64_t* r = row_ids(i);
+    for (int j = 0; j < n; ++j) {
+      h ^= static_cast<uint64_t>(r[j]);
+      h *= 0x100000001B3ull;
+    }
+    return h;
+  };
+  // key: (declared prefix length or 0 for the 32-token key, hash) -> groups whose keys compare equal
+  std::map<std::pair<int, uint64_t>, std::vector<ForkGroup>> buckets;
+  std::vector<std::pair<int, uint64_t>> order;
+  for (int i = 0; i < c.nb; ++i) {
+    const int len = static_cast<int>(c.real_len[i]);
+    if (c.mpos_h[static_cast<int64_t>(i) * c.k] != len - 1) continue;
+    const int declared = c.prefix_len ? static_cast<int>(c.prefix_len[i]) : 0;
+    int key_len;
+    if (declared >= kForkFloor && declared < len) key_len = declared;
+    else if (len > kForkFloor) key_len = 0;
+    else continue;
+    const int cmp = key_len ? key_len : kForkFloor;
+    const auto key = std::make_pair(key_len, hash(i, cmp));
+    auto& groups = buckets[key];
+    if (groups.empty()) order.push_back(key);
+    ForkGroup* g = nullptr;
+    for (ForkGroup& cand : groups)
+      if (std::equal(row_ids(i), row_ids(i) + cmp, row_ids(cand.rows[0]))) g = &cand;
+    if (!g) {
+      groups.emplace_back();
+      g = &groups.back();
+      g->n = key_len;
+    }
+    g->rows.push_back(i);
+  }
+  for (const auto& key : order)
+    for (ForkGroup& g : buckets[key]) {
+      if (g.rows.size() < 2) continue;
+      int min_len = INT32_MAX;
+      for (int i : g.rows) min_len = std::min(min_len, static_cast<int>(c.real_len[i]));
+      if (g.n == 0) {  // longest common prefix of the members
+        const int64_t* r0 = row_ids(g.rows[0]);
+        int n = kForkFloor;
+        while (n < min_len) {
+          bool same = true;
+          for (size_t m = 1; m < g.rows.size() && same; ++m) same = row_ids(g.rows[m])[n] == r0[n];
+          if (!same) break;
+          ++n;
+        }
+        g.n = n;
+      }
+      if (g.n < kForkFloor || g.n >= min_len) continue;  // every member keeps a suffix
+      out.push_back(std::move(g));
+    }
+  return out;
+}
+
+// Host plan of a chunk: the packed sequences (whole rows, or shared prefixes
+// followed by their members' suffixes), each decision's slot location, and the
+// attention tile table, staged through pinned memory.
+static ChunkPlan plan_chunk(vd_handle* H, const Chunk& c, bool causal, int tile_rows) {
+  ChunkPlan P;
   H->slot = (H->slot + 1) % vd_handle::kSlots;
   char* buf = H->pinned[H->slot];
   cuda_check(cudaEventSynchronize(H->slot_ev[H->slot]), "staging slot");
-  int* cu = reinterpret_cast<int*>(buf);
-  AttnTile* tiles = reinterpret_cast<AttnTile*>(buf + ((sizeof(int) * (c.nb + 1) + 15) & ~size_t(15)));
-  cu[0] = 0;
-  max_len = 0;
-  for (int i = 0; i < c.nb; ++i) {
-    cu[i + 1] = cu[i] + static_cast<int>(c.real_len[i]);
-    max_len = std::max(max_len, static_cast<int>(c.real_len[i]));
-  }
-  T = cu[c.nb];
+  auto align16 = [](size_t x) { return (x + 15) & ~size_t(15); };
+  size_t off = 0;
+  int* cu = reinterpret_cast<int*>(buf + off);
+  off = align16(off + sizeof(int) * (c.nb + 1));
+  PackSeg* segs = reinterpret_cast<PackSeg*>(buf + off);
+  off = align16(off + sizeof(PackSeg) * 2 * c.nb);
+  RowMap* rows = reinterpret_cast<RowMap*>(buf + off);
+  off = align16(off + sizeof(RowMap) * c.nb);
+  AttnTile* tiles = reinterpret_cast<AttnTile*>(buf + off);
+
+  std::vector<ForkGroup> groups;
+  if (causal && H->opt.fork) groups = plan_fork(c);
+  std::vector<int> group_of(c.nb, -1);
+  for (size_t g = 0; g < groups.size(); ++g)
+    for (int i : groups[g].rows) group_of[i] = static_cast<int>(g);
+  std::vector<char> emitted(groups.size(), 0);
   int n = 0;
+  auto add_seq = [&](int src_row, int col0, int len, int pre_start, int pre_len) {
+    const int start = P.ntok;
+    segs[P.n_seg++] = PackSeg{start, len, col0, src_row};
+    P.ntok += len;
+    P.max_len = std::max(P.max_len, len);
+    for (int q = 0; q < len; q += tile_rows) tiles[n++] = AttnTile{start, len, q, pre_start, pre_len, {0, 0, 0}};
+    P.pairs += causal ? 0.5 * len * (len + 1.0) + static_cast<double>(len) * pre_len : static_cast<double>(len) * len;
+    return start;
+  };
   for (int i = 0; i < c.nb; ++i) {
     const int len = static_cast<int>(c.real_len[i]);
-    for (int q = 0; q < len; q += tile_rows) tiles[n++] = AttnTile{cu[i], len, q, 0};
+    const int g = group_of[i];
+    if (g < 0) {
+      const int start = add_seq(i, 0, len, 0, 0);
+      rows[i] = RowMap{start, 0, len, 0};
+      cu[i] = start;
+      continue;
+    }
+    if (emitted[g]) continue;
+    emitted[g] = 1;
+    const ForkGroup& fg = groups[g];
+    const int pre = add_seq(fg.rows[0], 0, fg.n, 0, 0);
+    for (int m : fg.rows) {
+      const int mlen = static_cast<int>(c.real_len[m]);
+      const int start = add_seq(m, fg.n, mlen - fg.n, pre, fg.n);
+      rows[m] = RowMap{start - fg.n, fg.n, mlen, 0};
+      cu[m] = start - fg.n;
+    }
+    ++P.fork_groups;
+    P.fork_rows += static_cast<int>(fg.rows.size());
+    P.shared_tokens += static_cast<int64_t>(fg.n) * (fg.rows.size() - 1);
   }
-  // Longest work first: causal tiles cost ~ q_start + 64 keys, bidirectional ~ len.
+  cu[c.nb] = P.ntok;
+  P.n_tiles = n;
+  // Longest work first: a causal tile costs ~ its last query row's keys.
   std::stable_sort(tiles, tiles + n, [causal, tile_rows](const AttnTile& a, const AttnTile& b) {
-    const int wa = causal ? std::min(a.seq_len, a.q_start + tile_rows) : a.seq_len;
-    const int wb = causal ? std::min(b.seq_len, b.q_start + tile_rows) : b.seq_len;
+    const int wa = (causal ? std::min(a.seq_len, a.q_start + tile_rows) : a.seq_len) + a.pre_len;
+    const int wb = (causal ? std::min(b.seq_len, b.q_start + tile_rows) : b.seq_len) + b.pre_len;
     return wa > wb;
   });
-  const size_t tiles_off = reinterpret_cast<char*>(tiles) - buf;
+  const size_t seg_off = reinterpret_cast<char*>(segs) - buf, row_off = reinterpret_cast<char*>(rows) - buf,
+               tile_off = reinterpret_cast<char*>(tiles) - buf;
   cuda_check(cudaMemcpyAsync(H->cu, cu, sizeof(int) * (c.nb + 1), cudaMemcpyHostToDevice, H->stream), "upload cu");
-  cuda_check(cudaMemcpyAsync(H->tiles, buf + tiles_off, sizeof(AttnTile) * n, cudaMemcpyHostToDevice, H->stream),
+  cuda_check(cudaMemcpyAsync(H->segs, buf + seg_off, sizeof(PackSeg) * P.n_seg, cudaMemcpyHostToDevice, H->stream),
+             "upload segments");
+  cuda_check(cudaMemcpyAsync(H->rowmap, buf + row_off, sizeof(RowMap) * c.nb, cudaMemcpyHostToDevice, H->stream),
+             "upload row map");
+  cuda_check(cudaMemcpyAsync(H->tiles, buf + tile_off, sizeof(AttnTile) * n, cudaMemcpyHostToDevice, H->stream),
              "upload tiles");
   cuda_check(cudaEventRecord(H->slot_ev[H->slot], H->stream), "staging event");
-  return n;
+  H->stats.fork_groups += P.fork_groups;
+  H->stats.fork_rows += P.fork_rows;
+  H->stats.shared_tokens += P.shared_tokens;
+  return P;
 }
 
-static void pack(vd_handle* H, const Chunk& c, int max_len, int pos_offset) {
-  dim3 grid(std::max(1, std::min((max_len + 255) / 256, 64)), c.nb);
+static void pack(vd_handle* H, const Chunk& c, const ChunkPlan& P, int pos_offset) {
+  dim3 grid(std::max(1, std::min((P.max_len + 255) / 256, 64)), P.n_seg);
   launch(H, VD_K_OTHER, 0.0, [&] {
-    pack_tokens_kernel<<<grid, 256, 0, H->stream>>>(c.ids, c.l, H->cu, c.nb, H->spec.vocab, pos_offset, H->tokens,
-                                                    H->positions, H->seq_id, H->d_err);
+    pack_segments_kernel<<<grid, 256, 0, H->stream>>>(c.ids, c.l, H->segs, P.n_seg, H->spec.vocab, pos_offset,
+                                                      H->tokens, H->positions, H->seq_id, H->d_err);
   });
 }
 
@@ -1093,18 +1236,16 @@ template <class T>
 static double decoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads;
-  int ntok = 0, max_len = 0;
-  const int n_tiles = plan_chunk(H, c, ntok, max_len, true, attn_tile_rows(H, hd, true));
-  pack(H, c, max_len, 0);
+  const ChunkPlan P = plan_chunk(H, c, true, attn_tile_rows(H, hd, true));
+  const int ntok = P.ntok, n_tiles = P.n_tiles;
+  pack(H, c, P, 0);
   const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
   launch(H, VD_K_OTHER, 0.0,
          [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h); });
   const int qkvw = s.qkv_width(), qc = nq * hd, kc = nkv * hd;
   const float eps = static_cast<float>(s.rms_eps);
   const int pone = s.norm_plus_one ? 1 : 0;
-  double attn_pairs = 0;
-  for (int i = 0; i < c.nb; ++i) attn_pairs += 0.5 * static_cast<double>(c.real_len[i]) * (c.real_len[i] + 1);
-  const double attn_flops = 4.0 * hd * nq * attn_pairs;
+  const double attn_flops = 4.0 * hd * nq * P.pairs;
   for (int i = 0; i < s.layers; ++i) {
     const DecLayer& L = H->dec[i];
     launch(H, VD_K_NORM, 0.0, [&] {
@@ -1127,7 +1268,7 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
       // Only the slot rows feed the readout: gather them (attention output and
       // residual) and finish the layer on nb rows instead of ntok.
       launch(H, VD_K_OTHER, 0.0, [&] {
-        gather_slot_rows_kernel<T><<<c.nb, 256, 0, H->stream>>>(H->cu, c.mpos, static_cast<int>(c.k),
+        gather_slot_rows_kernel<T><<<c.nb, 256, 0, H->stream>>>(H->rowmap, c.mpos, static_cast<int>(c.k),
                                                                  static_cast<const T*>(H->attn), qc, H->h, d,
                                                                  static_cast<T*>(H->attn_s), H->h_s, H->d_err);
       });
@@ -1151,7 +1292,7 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   const bool compact = H->opt.prune_last_layer;
   const size_t smem = sizeof(float) * (d + H->n_labels);
   launch(H, VD_K_OTHER, 0.0, [&] {
-    readout_kernel<256><<<c.nb, 256, smem, H->stream>>>(compact ? H->h_s : H->h, d, H->cu, c.mpos,
+    readout_kernel<256><<<c.nb, 256, smem, H->stream>>>(compact ? H->h_s : H->h, d, H->rowmap, c.mpos,
                                                         static_cast<int>(c.k), c.nopts, H->final_norm, pone, eps,
                                                         H->head_rows, H->n_labels, c.out, static_cast<int>(c.width),
                                                         H->opt.logprobs ? 1 : 0, compact ? 1 : 0, H->d_err);
@@ -1192,19 +1333,17 @@ template <class T>
 static double encoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden;
-  int ntok = 0, max_len = 0;
-  const int n_tiles = plan_chunk(H, c, ntok, max_len, false, 64);
+  const ChunkPlan P = plan_chunk(H, c, false, 64);
+  const int ntok = P.ntok, n_tiles = P.n_tiles;
   const int pos_offset = s.style == "xlmr" ? s.pad_id + 1 : 0;
-  if (max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
-  pack(H, c, max_len, pos_offset);
+  if (P.max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
+  pack(H, c, P, pos_offset);
   launch(H, VD_K_OTHER, 0.0, [&] {
     embed_ln_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed, H->pos_emb,
                                                          H->type_emb0, d, H->emb_ln_w, H->emb_ln_b,
                                                          static_cast<float>(s.ln_eps), H->h, static_cast<T*>(H->xn));
   });
-  double pairs = 0;
-  for (int i = 0; i < c.nb; ++i) pairs += static_cast<double>(c.real_len[i]) * c.real_len[i];
-  const double attn_flops = 4.0 * d * pairs;
+  const double attn_flops = 4.0 * d * P.pairs;
   for (const EncLayer& L : H->enc) enc_layer<T>(H, L, ntok, n_tiles, attn_flops);
   launch(H, VD_K_OTHER, 0.0, [&] {
     add_type_kernel<<<ntok, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3, H->d_err);
@@ -1273,6 +1412,28 @@ static void validate_batch(vd_handle* H, const vd_batch* b, int64_t width) {
 
 static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const int64_t* mpos, const uint8_t* mmask,
                       const int64_t* nopts, const int64_t* qtype, float* out, int64_t width) {
+  // Shared-prefix planning reads token ids and slots on the host.  A
+  // device-memory batch is planned only when it declares prefix lengths: its
+  // ids and slots are then copied back first (one synchronisation).
+  const int64_t* ids_h = nullptr;
+  const int64_t* mpos_h = nullptr;
+  std::vector<int64_t> ids_copy, mpos_copy;
+  if (H->spec.decoder() && H->opt.fork && b->b > 1) {
+    if (b->memory == VD_MEM_HOST) {
+      ids_h = b->input_ids;
+      mpos_h = b->marker_pos;
+    } else if (b->prefix_len) {
+      ids_copy.resize(static_cast<size_t>(b->b * b->l));
+      mpos_copy.resize(static_cast<size_t>(b->b * b->k));
+      cuda_check(cudaMemcpyAsync(ids_copy.data(), b->input_ids, ids_copy.size() * 8, cudaMemcpyDeviceToHost,
+                                 H->stream), "copy ids for the prefix plan");
+      cuda_check(cudaMemcpyAsync(mpos_copy.data(), b->marker_pos, mpos_copy.size() * 8, cudaMemcpyDeviceToHost,
+                                 H->stream), "copy slots for the prefix plan");
+      cuda_check(cudaStreamSynchronize(H->stream), "prefix plan copies");
+      ids_h = ids_copy.data();
+      mpos_h = mpos_copy.data();
+    }
+  }
   const auto t_enqueue = std::chrono::steady_clock::now();
   H->stats = vd_stats{};
   H->launches = 0;
@@ -1291,6 +1452,11 @@ static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const
     c.nopts = nopts ? nopts + r0 : nullptr;
     c.qtype = qtype ? qtype + r0 : nullptr;
     c.real_len = b->real_len + r0;
+    if (ids_h) {
+      c.ids_h = ids_h + r0 * b->l;
+      c.mpos_h = mpos_h + r0 * b->k;
+      c.prefix_len = b->prefix_len ? b->prefix_len + r0 : nullptr;
+    }
     c.out = out + r0 * width;
     c.width = width;
     double nt = 0;
@@ -1411,6 +1577,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.max_markers = o.integer_or("max_markers", H->opt.max_markers);
       H->opt.logprobs = o.string_or("output", "logprobs") != "logits";
       H->opt.prune_last_layer = o.boolean_or("prune_last_layer", true);
+      H->opt.fork = o.boolean_or("fork", true);
       const std::string at = o.string_or("attention", "tc");
       if (at != "tc" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\" or \"mma\"");
       H->opt.tc_attention = at == "tc";
@@ -1630,7 +1797,7 @@ extern "C" VD_API void vd_close(vd_handle* h) {
 namespace vd {
 
 // At most this many query tiles per call: sum over sequences of ceil(len / 64).
-constexpr int kNoAllocMaxTiles = 16384;  // 256 KiB of device memory per GPU
+constexpr int kNoAllocMaxTiles = 16384;  // 512 KiB of device memory per GPU
 
 static __device__ __align__(256) AttnTile g_noalloc_tiles[kNoAllocMaxTiles];
 
@@ -1684,7 +1851,7 @@ extern "C" VD_API int vdk_attention_noalloc(const void* qkv, int64_t ld_qkv, int
     int t = 0;
     for (int64_t i = 0; i < nseq; ++i) {
       const int start = cu_seqlens_host[i], len = cu_seqlens_host[i + 1] - start;
-      for (int q = 0; q < len; q += 64) g_noalloc_host_tiles[t++] = AttnTile{start, len, q, 0};
+      for (int q = 0; q < len; q += 64) g_noalloc_host_tiles[t++] = AttnTile{start, len, q, 0, 0, {0, 0, 0}};
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // Every tile the kernel reads is written here, so nothing left over from an

@@ -73,7 +73,7 @@ class B200Engine(Engine):
     def __init__(self, spec, device: int = 0, *, max_tokens: int = 65536, max_rows: int = 512,
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
-                 prune_last_layer: bool = True):
+                 prune_last_layer: bool = True, fork: bool = True):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory)."""
         self.lib = _abi.load()
@@ -89,7 +89,7 @@ class B200Engine(Engine):
         self.decoder = self.spec["arch"] == "decoder"
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
-                               attention=attention, prune_last_layer=prune_last_layer))
+                               attention=attention, prune_last_layer=prune_last_layer, fork=fork))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
         rc = self.lib.vd_open(model, device, opts.encode(), ctypes.byref(h), err, len(err))
@@ -164,8 +164,10 @@ class B200Engine(Engine):
         _abi.check(rc, err)
 
     def infer_device(self, b: int, l: int, k: int, ptrs: dict, real_len: np.ndarray, out_ptr: int, width: int,
-                     stream: Optional[int] = None, sync: bool = False) -> None:
-        """vd_infer_async on device-resident arrays (`ptrs`: integer device addresses)."""
+                     stream: Optional[int] = None, sync: bool = False,
+                     prefix_len: Optional[np.ndarray] = None) -> None:
+        """vd_infer_async on device-resident arrays (`ptrs`: integer device
+        addresses); `prefix_len` (host) lets the engine fork shared prefixes."""
         st = _abi.VdBatch()
         st.b, st.l, st.k = b, l, k
         st.memory = _abi.VD_MEM_DEVICE
@@ -174,6 +176,9 @@ class B200Engine(Engine):
             setattr(st, name, None if v is None else ctypes.c_void_p(v))
         real_len = np.ascontiguousarray(real_len, dtype=np.int64)
         st.real_len = ctypes.c_void_p(real_len.ctypes.data)
+        if prefix_len is not None:
+            prefix_len = np.ascontiguousarray(prefix_len, dtype=np.int64)
+            st.prefix_len = ctypes.c_void_p(prefix_len.ctypes.data)
         err = ctypes.create_string_buffer(1024)
         with self._lock:
             rc = self.lib.vd_infer_async(self.h, ctypes.byref(st), ctypes.c_void_p(out_ptr), width,
