@@ -50,9 +50,9 @@ SHARED_WORKLOAD = ("OneJev-9B-shaped letter-branches decisions, 8 questions per 
                    "question suffix U[40,160] tokens, 2-8 options")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
-# full-size ncu capture of this bench's first timed launch (profiles/gemm_gateup_onejev9b.md), and the
-# token count that launch had.  Weight re-reads dominate it, so it is reported as measured, not scaled.
-GATEUP_TRAFFIC_BYTES = 3.70e9 + 0.82e9
+# full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
+# launch had.  Weight re-reads dominate it, so it is reported as measured, not scaled.
+GATEUP_TRAFFIC_BYTES = 3.3236e9 + 0.8198e9
 GATEUP_TRAFFIC_TOKENS = 33763
 
 
