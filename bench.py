@@ -225,6 +225,8 @@ def main():
                          "per state, rows of a state share the state prefix (prefix_len declared)")
     ap.add_argument("--fork", default="on", choices=["on", "off"],
                     help="compute shared prefixes once (on) or every row whole (off)")
+    ap.add_argument("--gemm", default="2sm", choices=["2sm", "1sm"],
+                    help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -253,7 +255,7 @@ def main():
     batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed, args.workload)
     max_tokens = max(int(b.real_len().sum()) for b in batches)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
-                     max_seq=4096, attention=args.attention, fork=args.fork == "on")
+                     max_seq=4096, attention=args.attention, fork=args.fork == "on", gemm=args.gemm)
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
     width = eng.width
@@ -428,7 +430,7 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
             "config": {"workload": SHARED_WORKLOAD if shared else WORKLOAD, "model": "onejev-9b",
-                       "layers": spec["layers"], "attention": args.attention, "fork": args.fork,
+                       "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
                        "computed_tokens_last_step": int(computed_tokens),
                        "parallelism": f"replicas x{world} (one full-weight replica per GPU, no collectives)",

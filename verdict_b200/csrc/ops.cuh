@@ -38,13 +38,21 @@ static void ops_attrs_once() {
   std::call_once(once[dev & 63], [] { init_kernel_attrs(); });
 }
 
+// 256-wide tiles run on CTA pairs (two-CTA kernel, W maps with 128-row boxes)
+// when the device can co-schedule them; other shapes on one CTA per tile.
 template <int EPI, class T>
-static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& c, int bn, int M, int N,
-                              int K, const EpiParams& ep, cudaStream_t s, int* word, int sms) {
+static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& w_half,
+                              const CUtensorMap& c, int bn, int M, int N, int K, const EpiParams& ep, cudaStream_t s,
+                              int* word, int sms) {
   const int tiles = ((M + 127) / 128) * (N / bn);
   const int grid = std::min(tiles, sms);
   const GemmShape shape{M, N, K};
-  if (bn == 256)
+  const int pairs = bn == 256 ? gemm2_max_pairs(sms) : 0;
+  if (pairs > 0) {
+    const int grid2 = 2 * std::min(((M + 255) / 256) * (N / 256), pairs);
+    gemm2_tcgen05_kernel<EPI, T><<<grid2, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, s>>>(a, w_half, c, shape,
+                                                                                             ep, word);
+  } else if (bn == 256)
     gemm_tcgen05_kernel<256, EPI, T><<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, c, shape, ep, word);
   else if constexpr (EPI != kEpiGated)
     gemm_tcgen05_kernel<128, EPI, T><<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, c, shape, ep, word);
@@ -53,10 +61,11 @@ static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, const 
 }
 
 template <int EPI>
-static void ops_gemm_launch(bool f16, const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& c, int bn, int M,
-                            int N, int K, const EpiParams& ep, cudaStream_t s, int* word, int sms) {
-  if (f16) ops_gemm_launch_t<EPI, __half>(a, w, c, bn, M, N, K, ep, s, word, sms);
-  else ops_gemm_launch_t<EPI, __nv_bfloat16>(a, w, c, bn, M, N, K, ep, s, word, sms);
+static void ops_gemm_launch(bool f16, const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& w_half,
+                            const CUtensorMap& c, int bn, int M, int N, int K, const EpiParams& ep, cudaStream_t s,
+                            int* word, int sms) {
+  if (f16) ops_gemm_launch_t<EPI, __half>(a, w, w_half, c, bn, M, N, K, ep, s, word, sms);
+  else ops_gemm_launch_t<EPI, __nv_bfloat16>(a, w, w_half, c, bn, M, N, K, ep, s, word, sms);
 }
 
 static bool ops_dtype(int dtype) {
@@ -89,15 +98,16 @@ extern "C" VD_API int vdk_gemm(const void* A, const void* W, int64_t M, int64_t 
     const int bn = (N % 256 == 0) ? 256 : 128;
     const CUtensorMap a = make_map(A, M, K, 128, f16);
     const CUtensorMap w = make_map(W, N, K, bn, f16);
+    const CUtensorMap w_half = make_map(W, N, K, 128, f16);
     EpiParams ep = epi_params_for(bias, act);
     const CUtensorMap c = make_out_map(out, M, ld_out, epi == kEpiResidual, f16);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int sms = device_sms();
     const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
     switch (epi) {
-      case kEpiStore: ops_gemm_launch<kEpiStore>(f16, a, w, c, bn, m, n, k, ep, s, word, sms); break;
-      case kEpiResidual: ops_gemm_launch<kEpiResidual>(f16, a, w, c, bn, m, n, k, ep, s, word, sms); break;
-      case kEpiGated: ops_gemm_launch<kEpiGated>(f16, a, w, c, bn, m, n, k, ep, s, word, sms); break;
+      case kEpiStore: ops_gemm_launch<kEpiStore>(f16, a, w, w_half, c, bn, m, n, k, ep, s, word, sms); break;
+      case kEpiResidual: ops_gemm_launch<kEpiResidual>(f16, a, w, w_half, c, bn, m, n, k, ep, s, word, sms); break;
+      case kEpiGated: ops_gemm_launch<kEpiGated>(f16, a, w, w_half, c, bn, m, n, k, ep, s, word, sms); break;
     }
     ops_finish(s, word);
   });
@@ -139,6 +149,7 @@ extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, i
     cuda_check(cudaMemcpy(rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope table");
     const CUtensorMap a = make_map(A, M, K, 128, f16);
     const CUtensorMap w = make_map(W, N, K, bn, f16);
+    const CUtensorMap w_half = make_map(W, N, K, 128, f16);
     EpiParams ep = epi_params_for(bias, kActNone);
     const CUtensorMap c = make_out_map(out, M, ld_out, false, f16);
     ep.q_norm = q_norm;
@@ -150,7 +161,7 @@ extern "C" VD_API int vdk_gemm_qkrope(const void* A, const void* W, int64_t M, i
     ep.eps = eps;
     ep.positions = positions;
     ep.rope = rope;
-    ops_gemm_launch<kEpiQKRope>(f16, a, w, c, bn, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ep, s, word,
+    ops_gemm_launch<kEpiQKRope>(f16, a, w, w_half, c, bn, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), ep, s, word,
                                 device_sms());
     ops_finish(s, word);
   });

@@ -41,6 +41,7 @@
 #include "convert.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "json.hpp"
 #include "synth.cuh"
 
@@ -392,6 +393,7 @@ struct Linear {
   float* b = nullptr;   // [n] or null
   int n = 0, k = 0, bn = 256;
   CUtensorMap map;
+  CUtensorMap map_half;  // 128-row boxes: one CTA's half of a 256-row tile (two-CTA GEMM)
 };
 
 struct DecLayer {
@@ -416,6 +418,7 @@ struct Options {
   bool prune_last_layer = true;  // last layer's O projection and MLP on the slot rows only
   bool tc_attention = true;  // head_dim 128 causal attention on tcgen05 (else the mma.sync kernel)
   bool fork = true;          // shared-prefix rows: prefix computed once (host-memory decoder batches)
+  bool gemm2 = true;         // 256-wide projections on CTA pairs (cta_group::2), else one CTA per tile
 };
 
 }  // namespace vd
@@ -427,6 +430,7 @@ struct vd_handle {
   vd::Options opt;
   cudaStream_t stream = nullptr;
   int num_sms = 148;
+  int gemm2_pairs = 0;  // concurrent CTA pairs of the two-CTA GEMM
   std::atomic<bool> healthy{true};
   std::string dead_reason;
   std::vector<void*> allocations;
@@ -669,6 +673,7 @@ static void init_linear(vd_handle* H, Linear& L, int n, int k, bool bias, int bn
   L.w = dalloc<uint16_t>(H, static_cast<size_t>(n) * k);
   L.b = bias ? dalloc<float>(H, n) : nullptr;
   L.map = make_map(L.w, n, k, L.bn, H->opt.f16);
+  if (L.bn == 256) L.map_half = make_map(L.w, n, k, 128, H->opt.f16);
 }
 
 static void load_decoder(vd_handle* H) {
@@ -942,6 +947,10 @@ static void init_kernel_attrs_t() {
   set_gemm_attr<256, kEpiGated, T>();
   set_gemm_attr<256, kEpiQKRope, T>();
   set_gemm_attr<128, kEpiQKRope, T>();
+  for (auto f : {gemm2_tcgen05_kernel<kEpiStore, T>, gemm2_tcgen05_kernel<kEpiResidual, T>,
+                 gemm2_tcgen05_kernel<kEpiGated, T>, gemm2_tcgen05_kernel<kEpiQKRope, T>})
+    cuda_check(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Config::SMEM_BYTES),
+               "two-CTA gemm smem attribute");
   set_attn_attr<64, false, T>();
   set_attn_attr<128, true, T>();
   set_attn_attr<256, true, T>();
@@ -955,6 +964,20 @@ static void init_kernel_attrs() {
   init_kernel_attrs_t<__nv_bfloat16>();
 }
 
+// CTA pairs of the two-CTA GEMM that fit on the current device at once (0: none).
+static int gemm2_max_pairs(int num_sms) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_sms & ~1), 1, 1);
+  cfg.blockDim = dim3(Gemm2Config::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Gemm2Config::SMEM_BYTES;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm2_tcgen05_kernel<kEpiStore, __half>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
 template <int EPI, class T>
 static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, int M, const EpiParams& ep,
                  const CUtensorMap& c) {
@@ -964,6 +987,15 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const int grid = std::min(tiles, H->num_sms);
   const GemmShape shape{M, L.n, L.k};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
+  if (L.bn == 256 && H->opt.gemm2 && H->gemm2_pairs > 0) {
+    const int pair_tiles = ((M + 255) / 256) * (L.n / 256);
+    const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
+    launch(H, kind, flops, [&] {
+      gemm2_tcgen05_kernel<EPI, T><<<grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, H->stream>>>(
+          a, L.map_half, c, shape, ep, H->d_err);
+    });
+    return;
+  }
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
       gemm_tcgen05_kernel<256, EPI, T>
@@ -1578,6 +1610,9 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.logprobs = o.string_or("output", "logprobs") != "logits";
       H->opt.prune_last_layer = o.boolean_or("prune_last_layer", true);
       H->opt.fork = o.boolean_or("fork", true);
+      const std::string gm = o.string_or("gemm", "2sm");
+      if (gm != "2sm" && gm != "1sm") fail(VD_EINVAL, "gemm must be \"2sm\" or \"1sm\"");
+      H->opt.gemm2 = gm == "2sm";
       const std::string at = o.string_or("attention", "tc");
       if (at != "tc" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\" or \"mma\"");
       H->opt.tc_attention = at == "tc";
@@ -1604,6 +1639,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
     H->num_sms = prop.multiProcessorCount;
     cuda_check(cudaStreamCreateWithFlags(&H->stream, cudaStreamNonBlocking), "stream");
     init_kernel_attrs();
+    H->gemm2_pairs = gemm2_max_pairs(H->num_sms);
     if (H->spec.decoder()) load_decoder(H);
     else load_encoder(H);
     alloc_workspace(H);

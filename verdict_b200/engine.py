@@ -73,7 +73,7 @@ class B200Engine(Engine):
     def __init__(self, spec, device: int = 0, *, max_tokens: int = 65536, max_rows: int = 512,
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
-                 prune_last_layer: bool = True, fork: bool = True):
+                 prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm"):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory)."""
         self.lib = _abi.load()
@@ -89,7 +89,8 @@ class B200Engine(Engine):
         self.decoder = self.spec["arch"] == "decoder"
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
-                               attention=attention, prune_last_layer=prune_last_layer, fork=fork))
+                               attention=attention, prune_last_layer=prune_last_layer, fork=fork,
+                               gemm=gemm))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
         rc = self.lib.vd_open(model, device, opts.encode(), ctypes.byref(h), err, len(err))
