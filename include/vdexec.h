@@ -78,6 +78,7 @@ typedef struct vd_batch {
 #define VD_K_ATTN 4     /* varlen attention                                */
 #define VD_K_NORM 5     /* RMSNorm / LayerNorm rows                        */
 #define VD_K_OTHER 6    /* pack, embed, readout, marker scoring            */
+#define VD_K_GDN 7      /* gated delta net: conv + gates, recurrence       */
 #define VD_K_COUNT 8
 
 /* Per-call statistics of the last completed vd_infer / vd_infer_async. */

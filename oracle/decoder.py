@@ -75,6 +75,51 @@ def silu(x: np.ndarray) -> np.ndarray:
     return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
 
 
+def sigmoid(x: np.ndarray) -> np.ndarray:
+    return (np.float32(1.0) / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def softplus(x: np.ndarray) -> np.ndarray:
+    """torch.nn.functional.softplus (beta 1, threshold 20)."""
+    return np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, np.float32(20))))).astype(np.float32)
+
+
+def l2norm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """x * rsqrt(sum(x^2) + eps) over the last axis (the FLA-aligned l2norm of HF Qwen3.5)."""
+    return (x / np.sqrt(np.sum(x * x, axis=-1, keepdims=True, dtype=np.float32) + np.float32(eps))).astype(np.float32)
+
+
+def causal_conv_silu(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """Depthwise causal conv1d (kernel K, zero history) then SiLU; x [n, C], w [C, K]:
+    y[t, c] = silu(sum_j w[c, j] * x[t - (K - 1) + j, c])."""
+    n, _ = x.shape
+    k = w.shape[1]
+    xp = np.concatenate([np.zeros((k - 1, x.shape[1]), np.float32), x], axis=0)
+    y = np.zeros_like(x)
+    for j in range(k):
+        y += xp[j:j + n] * w[:, j][None, :]
+    return silu(y)
+
+
+def gated_delta_rule(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray, beta: np.ndarray) -> np.ndarray:
+    """The gated delta rule in its recurrent form (HF `torch_recurrent_gated_delta_rule`;
+    the chunked form computes the same function): per head, state S [dk, dv] = 0,
+    for each token: S *= exp(g); delta = (v - k^T S) * beta; S += k delta^T; o = q^T S.
+    q, k [n, H, dk] (normalised, q scaled), v [n, H, dv], g, beta [n, H]."""
+    n, heads, dk = k.shape
+    dv = v.shape[-1]
+    S = np.zeros((heads, dk, dv), np.float32)
+    out = np.empty((n, heads, dv), np.float32)
+    decay = np.exp(g).astype(np.float32)
+    for t in range(n):
+        S *= decay[t][:, None, None]
+        kv = np.einsum("hk,hkv->hv", k[t], S)
+        delta = (v[t] - kv) * beta[t][:, None]
+        S += k[t][:, :, None] * delta[:, None, :]
+        out[t] = np.einsum("hk,hkv->hv", q[t], S)
+    return out
+
+
 class DecoderOracle:
     """Holds the synthetic checkpoint (host, fp32 copies of the bf16 weights).
 
@@ -91,9 +136,29 @@ class DecoderOracle:
         self.final_norm = self.ckpt.get("model.norm.weight")
         self.head_w = self.ckpt.get(self.ckpt.head_name(), rows=self.label_ids)
 
+    def _layer_names(self, i: int) -> list:
+        s = self.spec
+        if s.get("style") == "qwen3_5":
+            common = ["input_layernorm.weight", "post_attention_layernorm.weight", "mlp.gate_proj.weight",
+                      "mlp.up_proj.weight", "mlp.down_proj.weight"]
+            if s["layer_types"][i] == "full_attention":
+                return common + ["self_attn." + n for n in ("q_proj.weight", "k_proj.weight", "v_proj.weight",
+                                                            "o_proj.weight", "q_norm.weight", "k_norm.weight")]
+            return common + ["linear_attn." + n for n in (
+                "in_proj_qkv.weight", "in_proj_z.weight", "in_proj_b.weight", "in_proj_a.weight",
+                "conv1d.weight", "dt_bias", "A_log", "norm.weight", "out_proj.weight")]
+        return None
+
     def layer(self, i: int) -> dict:
         if i not in self._layers:
             p = f"model.layers.{i}."
+            hybrid = self._layer_names(i)
+            if hybrid is not None:
+                w = {n: self.ckpt.get(p + n) for n in hybrid}
+                if not self.cache_layers:
+                    return w
+                self._layers[i] = w
+                return w
             names = ["input_layernorm.weight", "self_attn.q_proj.weight", "self_attn.k_proj.weight",
                      "self_attn.v_proj.weight", "self_attn.o_proj.weight",
                      "post_attention_layernorm.weight", "mlp.gate_proj.weight",
@@ -116,8 +181,65 @@ class DecoderOracle:
             h = h * np.float32(self.spec["hidden"] ** 0.5)
         return h
 
+    def hybrid_layer_forward(self, i: int, h: np.ndarray, cos, sin) -> np.ndarray:
+        """One Qwen3.5 decoder layer (HF `Qwen3_5DecoderLayer`): (1 + w) RMSNorms;
+        full attention with q/k norm, partial RoPE and a sigmoid output gate
+        (`Qwen3_5Attention`), or a gated delta net (`Qwen3_5GatedDeltaNet`:
+        in_proj_qkv -> causal depthwise conv + SiLU -> l2-normalised q, k ->
+        gated delta rule with g = -exp(A_log) softplus(a + dt_bias), beta =
+        sigmoid(b) -> RMSNorm(o) * w * silu(z) -> out_proj); then the SiLU MLP."""
+        s = self.spec
+        w = self.layer(i)
+        n = h.shape[0]
+        eps = s["rms_eps"]
+        x = rmsnorm(h, w["input_layernorm.weight"], eps, True)
+        if s["layer_types"][i] == "full_attention":
+            hd, nq, nkv = s["head_dim"], s["heads"], s["kv_heads"]
+            qg = (x @ w["self_attn.q_proj.weight"].T).reshape(n, nq, 2 * hd)
+            q, gate = qg[..., :hd], qg[..., hd:].reshape(n, nq * hd)
+            k = (x @ w["self_attn.k_proj.weight"].T).reshape(n, nkv, hd)
+            v = (x @ w["self_attn.v_proj.weight"].T).reshape(n, nkv, hd)
+            q = rmsnorm(q, w["self_attn.q_norm.weight"], eps, True)
+            k = rmsnorm(k, w["self_attn.k_norm.weight"], eps, True)
+            rd = cos.shape[-1]
+            q = np.concatenate([apply_rope(q[..., :rd], cos, sin), q[..., rd:]], axis=-1)
+            k = np.concatenate([apply_rope(k[..., :rd], cos, sin), k[..., rd:]], axis=-1)
+            a = attention(q, k, v, causal=True).reshape(n, nq * hd) * sigmoid(gate)
+            h = h + a @ w["self_attn.o_proj.weight"].T
+        else:
+            lk, lv, dk, dv = s["lin_k_heads"], s["lin_v_heads"], s["lin_k_dim"], s["lin_v_dim"]
+            kd, vd = lk * dk, lv * dv
+            p = "linear_attn."
+            mixed = x @ w[p + "in_proj_qkv.weight"].T
+            z = (x @ w[p + "in_proj_z.weight"].T).reshape(n, lv, dv)
+            b = x @ w[p + "in_proj_b.weight"].T
+            a = x @ w[p + "in_proj_a.weight"].T
+            conv = causal_conv_silu(mixed, w[p + "conv1d.weight"][:, 0, :])
+            q = conv[:, :kd].reshape(n, lk, dk)
+            k = conv[:, kd:2 * kd].reshape(n, lk, dk)
+            v = conv[:, 2 * kd:].reshape(n, lv, dv)
+            beta = sigmoid(b)
+            g = (-np.exp(w[p + "A_log"]) * softplus(a + w[p + "dt_bias"])).astype(np.float32)
+            rep = lv // lk
+            q = l2norm(np.repeat(q, rep, axis=1)) * np.float32(dk ** -0.5)
+            k = l2norm(np.repeat(k, rep, axis=1))
+            o = gated_delta_rule(q, k, v, g, beta)
+            o = rmsnorm(o, w[p + "norm.weight"], eps, False) * silu(z)
+            h = h + o.reshape(n, vd) @ w[p + "out_proj.weight"].T
+        x = rmsnorm(h, w["post_attention_layernorm.weight"], eps, True)
+        act = silu(x @ w["mlp.gate_proj.weight"].T) * (x @ w["mlp.up_proj.weight"].T)
+        h = h + act @ w["mlp.down_proj.weight"].T
+        return h.astype(np.float32)
+
+    def rope(self, n: int):
+        s = self.spec
+        rd = int(s["head_dim"] * s.get("partial_rotary", 1.0)) if s.get("style") == "qwen3_5" else s["head_dim"]
+        return rope_tables(np.arange(n), rd, s["rope_theta"])
+
     def layer_forward(self, i: int, h: np.ndarray, cos, sin) -> np.ndarray:
         s = self.spec
+        if s.get("style") == "qwen3_5":
+            return self.hybrid_layer_forward(i, h, cos, sin)
         w = self.layer(i)
         hd, nq, nkv = s["head_dim"], s["heads"], s["kv_heads"]
         n = h.shape[0]
@@ -150,7 +272,7 @@ class DecoderOracle:
         """Final-norm hidden states of one sequence, [n, d] fp32."""
         ids = np.asarray(ids, dtype=np.int64)
         n = ids.shape[0]
-        cos, sin = rope_tables(np.arange(n), self.spec["head_dim"], self.spec["rope_theta"])
+        cos, sin = self.rope(n)
         h = self.embed(ids)
         for i in range(self.n_layers):
             h = self.layer_forward(i, h, cos, sin)
@@ -178,7 +300,7 @@ class DecoderOracle:
         for i, row in enumerate(batch.rows):
             ids = np.asarray(batch.input_ids[i * batch.l:i * batch.l + row.real_len], dtype=np.int64)
             hs.append(self.embed(ids))
-            tabs.append(rope_tables(np.arange(len(ids)), s["head_dim"], s["rope_theta"]))
+            tabs.append(self.rope(len(ids)))
         for layer in range(self.n_layers):
             w = self.layer(layer)
             self._layers[layer] = w

@@ -92,7 +92,16 @@ def hf_decoder(spec):
                   vocab_size=spec["vocab"], rms_norm_eps=spec["rms_eps"],
                   max_position_embeddings=8192, tie_word_embeddings=spec["tied"],
                   pad_token_id=1, bos_token_id=2, eos_token_id=2)
-    if spec["style"] == "qwen3":
+    if spec["style"] == "qwen3_5":
+        from transformers import Qwen3_5TextConfig
+        cfg = Qwen3_5TextConfig(
+            rope_parameters={"rope_type": "default", "rope_theta": spec["rope_theta"],
+                             "partial_rotary_factor": spec["partial_rotary"]},
+            layer_types=list(spec["layer_types"]), linear_conv_kernel_dim=spec["conv_kernel"],
+            linear_key_head_dim=spec["lin_k_dim"], linear_value_head_dim=spec["lin_v_dim"],
+            linear_num_key_heads=spec["lin_k_heads"], linear_num_value_heads=spec["lin_v_heads"],
+            hidden_act="silu", **common)
+    elif spec["style"] == "qwen3":
         cfg = Qwen3Config(rope_theta=spec["rope_theta"], attention_bias=spec["qkv_bias"], **common)
     elif spec["style"] == "qwen2":
         # Qwen2: bias on q/k/v only, no q/k norm
@@ -258,6 +267,27 @@ def main():
         r.ids, r.markers = r.ids[:n], [n - 1]
     decoder_case(ex, "gemma_tiny_readout", gemma, collate(rows, Layout(pad_id=1)),
                  "Gemma-style letter_readout (255 labels), rng seed 13")
+
+    # Qwen3.5 text stacks (gated delta net + gated full attention), the executor's
+    # fp32 CPU path through HF's torch fallbacks (chunked gated delta rule, Conv1d).
+    hybrid = specs.preset("onejev16-9b", hidden=256, layers=4, heads=2, kv_heads=1, head_dim=256,
+                          ffn=512, vocab=8448, lin_k_heads=2, lin_v_heads=4, seed=404)
+    rng = np.random.default_rng(16)
+    rows = decoder_rows(rng, 4, hybrid["vocab"], lengths="fixed:8")
+    for r, n in zip(rows, [1, 9, 70, 150]):
+        r.ids = rng.integers(3, hybrid["vocab"], size=n).tolist()
+        r.markers = [n - 1]
+    decoder_case(ex, "qwen35_tiny_hybrid", hybrid, collate(rows, Layout(pad_id=1)),
+                 "Qwen3.5 text stack, layers linear/linear/linear/full, lengths 1/9/70/150, rng seed 16")
+    hybrid2 = dict(hybrid, layers=3, layer_types=["linear_attention", "full_attention", "linear_attention"],
+                   family="letter_readout", seed=405)
+    rng = np.random.default_rng(17)
+    rows = decoder_rows(rng, 3, hybrid2["vocab"], lengths="uniform-2b")
+    for r in rows:
+        n = min(len(r.ids), 200)
+        r.ids, r.markers = r.ids[:n], [n - 1]
+    decoder_case(ex, "qwen35_tiny_lastlinear", hybrid2, collate(rows, Layout(pad_id=1)),
+                 "Qwen3.5 text stack ending in a gated-delta-net layer, letter_readout, rng seed 17")
 
     encoder_case(ref_root, "bert_tiny_marker", encoder_spec("bert"), seed=14)
     encoder_case(ref_root, "xlmr_tiny_marker", encoder_spec("xlmr"), seed=15)

@@ -35,6 +35,12 @@ def tiny_gemma(**over):
                                                                    head_dim=256, ffn=512, vocab=1024), **over)))
 
 
+def tiny_hybrid(**over):
+    return with_labels(specs.preset("onejev16-9b", **dict(dict(hidden=256, layers=4, heads=2, kv_heads=1, head_dim=256,
+                                                                ffn=512, vocab=1024, lin_k_heads=2, lin_v_heads=4),
+                                                           **over)))
+
+
 def tiny_encoder(preset="laya-bert", **over):
     return specs.preset(preset, **dict(dict(hidden=256, layers=2, heads=4, ffn=512, vocab=2048), **over))
 
@@ -75,7 +81,7 @@ def test_sharded_writer_and_index(tmp_path):
     assert ck.has_weights(str(tmp_path))
 
 
-@pytest.mark.parametrize("make", [tiny_decoder, lambda: tiny_decoder("qwen2"), tiny_gemma])
+@pytest.mark.parametrize("make", [tiny_decoder, lambda: tiny_decoder("qwen2"), tiny_gemma, tiny_hybrid])
 def test_hf_loads_the_written_decoder_with_no_missing_or_extra_tensors(tmp_path, make):
     from transformers import AutoModelForCausalLM
     spec = make()
@@ -84,13 +90,13 @@ def test_hf_loads_the_written_decoder_with_no_missing_or_extra_tensors(tmp_path,
                                                        dtype=torch.float32)
     assert not info["missing_keys"] and not info["unexpected_keys"], info
     sd = model.state_dict()
-    name = "model.layers.1.mlp.up_proj.weight"
+    name = "model.layers.1.mlp.up_proj.weight"  # (every layer type has an MLP)
     shape = tuple(sd[name].shape)
     want = gen_tensor(spec["seed"], name, shape, spec["init_std"] * 3 ** 0.5, 0.0)
     np.testing.assert_array_equal(sd[name].numpy(), want)
 
 
-@pytest.mark.parametrize("make", [tiny_decoder, lambda: tiny_decoder("qwen2"), tiny_gemma])
+@pytest.mark.parametrize("make", [tiny_decoder, lambda: tiny_decoder("qwen2"), tiny_gemma, tiny_hybrid])
 def test_spec_from_checkpoint_round_trips_the_config(tmp_path, make):
     spec = make()
     ck.save_synthetic(spec, str(tmp_path))
@@ -199,16 +205,17 @@ def test_c_reader_rejects_missing_and_malformed_checkpoints(tmp_path):
 
 SHAPE_KEYS = ("arch", "style", "hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab", "rms_eps",
               "rope_theta", "qk_norm", "qkv_bias", "act", "tied", "embed_scale", "norm_plus_one", "family")
+HYBRID_KEYS = ("layer_types", "partial_rotary", "lin_k_heads", "lin_v_heads", "lin_k_dim", "lin_v_dim", "conv_kernel")
 
 
-@pytest.mark.parametrize("make", [tiny_decoder, lambda: tiny_decoder("qwen2"), tiny_gemma])
+@pytest.mark.parametrize("make", [tiny_decoder, lambda: tiny_decoder("qwen2"), tiny_gemma, tiny_hybrid])
 def test_c_library_fills_a_decoder_spec_from_the_hf_config(tmp_path, make):
     spec = make()
     ck.save_synthetic(spec, str(tmp_path))
     py = ck.spec_from_checkpoint(str(tmp_path), family=spec["family"], label_ids=spec["label_ids"])
     c = ck.resolve_spec({"checkpoint": str(tmp_path), "family": spec["family"], "label_ids": spec["label_ids"]})
-    for k in SHAPE_KEYS:
-        assert c[k] == py[k], k
+    for k in SHAPE_KEYS + (HYBRID_KEYS if spec["style"] == "qwen3_5" else ()):
+        assert c[k] == py[k] == spec[k], k
     assert c["label_ids"] == spec["label_ids"] and c["checkpoint"] == str(tmp_path)
     # the torch executor's default family when the spec names none
     assert ck.resolve_spec({"checkpoint": str(tmp_path), "label_ids": [1, 2]})["family"] == "letter_readout"

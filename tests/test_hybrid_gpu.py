@@ -1,0 +1,144 @@
+"""Hybrid (Qwen3.5 text stack) decoders on the GPU: gated-delta-net layers
+and gated full-attention layers against the fp32 oracle (pinned to the
+reference's executor by tests/golden/qwen35_*.npz), plus the bit-exact
+properties the dense decoder has (chunking, slot-row pruning) and real
+checkpoint loading."""
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle.decoder import DecoderOracle, option_logprobs  # noqa: E402
+from oracle.fastsynth import gen_tensor as fast_gen  # noqa: E402
+from verdict_b200 import checkpoint as ck  # noqa: E402
+from verdict_b200 import spec as specs  # noqa: E402
+from verdict_b200 import synth  # noqa: E402
+from verdict_b200.batch import Layout, collate, decoder_rows  # noqa: E402
+from verdict_b200.engine import B200Engine  # noqa: E402
+from verdict_b200.synth import with_labels  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+LOGPROB_TOL = 2e-2
+
+
+def hybrid(layers=4, **over):
+    return with_labels(specs.preset("onejev16-9b", **dict(dict(layers=layers, vocab=16384, seed=61), **over)))
+
+
+def batch_of(spec, seed, n, max_len, lengths="lognormal-9b"):
+    rng = np.random.default_rng(seed)
+    rows = decoder_rows(rng, n, spec["vocab"], lengths=lengths)
+    for r in rows:
+        m = min(len(r.ids), max_len)
+        r.ids, r.markers = r.ids[:m], [m - 1]
+    return collate(rows, Layout(pad_id=0))
+
+
+def logprobs(eng, batch):
+    return np.array([r.logits for r in eng.infer(batch)], dtype=np.float64)
+
+
+def check_vs_oracle(got, ref, nopts):
+    ref_lp = option_logprobs(ref, nopts)
+    for i, k in enumerate(nopts):
+        k = int(k)
+        d = np.abs(got[i, :k] - ref_lp[i, :k]).max()
+        assert d <= LOGPROB_TOL, f"row {i}: {d:.3e}"
+        assert np.all(got[i, k:] == -1e4)
+
+
+def test_hybrid_9b_shape_vs_oracle():
+    spec = hybrid(4)
+    batch = batch_of(spec, 3, 6, 900)
+    eng = B200Engine(spec, max_tokens=8192, max_rows=32, max_seq=4096)
+    try:
+        got = logprobs(eng, batch)
+        st = eng.last_stats()
+        assert st["kernel_launches"][7] == 2 * 3  # conv + scan for each gated-delta-net layer
+    finally:
+        eng.close()
+    check_vs_oracle(got, DecoderOracle(spec).infer(batch), batch.nopts)
+
+
+def test_hybrid_ending_in_linear_layer_bf16_and_pruning():
+    spec = hybrid(3, layer_types=["full_attention", "linear_attention", "linear_attention"])
+    batch = batch_of(spec, 4, 5, 700)
+    kw = dict(max_tokens=8192, max_rows=32, max_seq=4096)
+    full = B200Engine(spec, prune_last_layer=False, **kw)
+    pruned = B200Engine(spec, **kw)
+    try:
+        a, b = logprobs(full, batch), logprobs(pruned, batch)
+    finally:
+        full.close()
+        pruned.close()
+    np.testing.assert_array_equal(a, b)
+    check_vs_oracle(b, DecoderOracle(spec).infer(batch), batch.nopts)
+    eng = B200Engine(spec, act_dtype="bf16", **kw)
+    try:
+        c = logprobs(eng, batch)
+    finally:
+        eng.close()
+    live = b > -1e4
+    assert np.abs(c - b)[live].max() <= 1e-1  # bf16 rounding only
+
+
+def test_hybrid_chunking_is_bit_exact():
+    spec = hybrid(4)
+    batch = batch_of(spec, 5, 7, 800)
+    big = B200Engine(spec, max_tokens=8192, max_rows=32, max_seq=2048)
+    small = B200Engine(spec, max_tokens=1024, max_rows=2, max_seq=1024)
+    try:
+        a, b = logprobs(big, batch), logprobs(small, batch)
+        assert small.last_stats()["chunks"] >= 4
+    finally:
+        big.close()
+        small.close()
+    np.testing.assert_array_equal(a, b)
+
+
+def test_hybrid_full_depth_vs_oracle():
+    """All 32 layers (24 gated delta nets, 8 gated attentions) of the 9B shape."""
+    spec = with_labels(specs.preset("onejev16-9b", seed=62))
+    rng = np.random.default_rng(62)
+    rows = decoder_rows(rng, 3, spec["vocab"], lengths="fixed:8")
+    for r, n in zip(rows, (40, 150, 333)):
+        r.ids = rng.integers(3, spec["vocab"], size=n).tolist()
+        r.markers = [n - 1]
+    batch = collate(rows, Layout(pad_id=0))
+    eng = B200Engine(spec, max_tokens=4096, max_rows=8, max_seq=2048)
+    try:
+        got = logprobs(eng, batch)
+    finally:
+        eng.close()
+    check_vs_oracle(got, DecoderOracle(spec, cache_layers=False).infer(batch), batch.nopts)
+
+
+@pytest.mark.parametrize("vl", [False, True])
+def test_hybrid_checkpoint_is_bit_identical(tmp_path, vl):
+    """A Qwen3.5 checkpoint written from the generator's values, as a text-only
+    CausalLM or with a vision-language checkpoint's names and nested config."""
+    spec = hybrid(4, hidden=1024, heads=4, kv_heads=1, ffn=2048, vocab=4096, lin_k_heads=4, lin_v_heads=8)
+    if vl:
+        tensors = [(("model.language_model." + n[6:]) if n.startswith("model.") else n,
+                    fast_gen(spec["seed"], n, shape, scale, off), "BF16")
+                   for n, shape, scale, off in synth.tensor_table(spec)]
+        ck.write_safetensors(str(tmp_path / "model.safetensors"), tensors)
+        cfg = {"model_type": "qwen3_5", "architectures": ["Qwen3_5ForConditionalGeneration"],
+               "text_config": ck._hf_config(spec), "vision_config": {"depth": 1}}
+        (tmp_path / "config.json").write_text(json.dumps(cfg))
+    else:
+        ck.save_synthetic(spec, str(tmp_path), gen=fast_gen)
+    batch = batch_of(spec, 6, 5, 600)
+    kw = dict(max_tokens=8192, max_rows=16, max_seq=2048)
+    a = B200Engine(spec, **kw)
+    b = B200Engine({"checkpoint": str(tmp_path), "label_ids": spec["label_ids"], "family": spec["family"]}, **kw)
+    try:
+        np.testing.assert_array_equal(logprobs(b, batch), logprobs(a, batch))
+    finally:
+        a.close()
+        b.close()

@@ -41,7 +41,7 @@ class VdStats(ctypes.Structure):
     ]
 
 
-KERNEL_CLASSES = ["qkv", "o", "gateup", "down", "attention", "norm", "other"]
+KERNEL_CLASSES = ["qkv", "o", "gateup", "down", "attention", "norm", "other", "gdn"]
 
 
 # Every entry point of include/vdexec.h: name -> (restype, argtypes)

@@ -46,9 +46,46 @@ def _rope_theta(cfg: dict) -> float:
     return float(theta if theta is not None else 10000.0)
 
 
+def hybrid_spec_from_config(cfg: dict) -> dict:
+    """The spec keys of an HF Qwen3.5 text stack (`qwen3_5_text`, or the
+    `text_config` of a `qwen3_5` vision-language checkpoint).  Multimodal RoPE
+    sections are accepted: with text-only positions every section sees the same
+    position, which is plain RoPE over the rotary width."""
+    c = cfg.get("text_config") or cfg if cfg.get("model_type") == "qwen3_5" else cfg
+    rp = c.get("rope_parameters") or {}
+    if (rp.get("rope_type") or "default") != "default" or c.get("rope_scaling"):
+        raise ValueError("rope scaling is not supported")
+    theta = rp.get("rope_theta") or c.get("rope_theta") or 10000.0
+    partial = rp.get("partial_rotary_factor", c.get("partial_rotary_factor", 0.25))
+    if c.get("attention_bias"):
+        raise ValueError("qwen3_5 checkpoints with attention bias are not supported")
+    layers = int(c["num_hidden_layers"])
+    types = c.get("layer_types")
+    if not types:
+        from .spec import hybrid_layer_types
+        types = hybrid_layer_types(layers, int(c.get("full_attention_interval", 4)))
+    act = c.get("hidden_act", "silu")
+    if act not in ("silu", "swish"):
+        raise ValueError(f"unsupported qwen3_5 activation {act!r}")
+    heads = int(c["num_attention_heads"])
+    return dict(
+        arch="decoder", style="qwen3_5", hidden=int(c["hidden_size"]), layers=layers, heads=heads,
+        kv_heads=int(c.get("num_key_value_heads") or heads), head_dim=int(c.get("head_dim") or 256),
+        ffn=int(c["intermediate_size"]), vocab=int(c["vocab_size"]), rms_eps=float(c.get("rms_norm_eps", 1e-6)),
+        rope_theta=float(theta), partial_rotary=float(partial),
+        tied=bool(c.get("tie_word_embeddings", cfg.get("tie_word_embeddings", False))),
+        qk_norm=True, qkv_bias=False, act="silu", embed_scale=False, norm_plus_one=True,
+        layer_types=list(types), lin_k_heads=int(c["linear_num_key_heads"]),
+        lin_v_heads=int(c["linear_num_value_heads"]), lin_k_dim=int(c.get("linear_key_head_dim", 128)),
+        lin_v_dim=int(c.get("linear_value_head_dim", 128)), conv_kernel=int(c.get("linear_conv_kernel_dim", 4)),
+    )
+
+
 def decoder_spec_from_config(cfg: dict) -> dict:
-    """The decoder spec keys of an HF Qwen3 / Qwen2 / Gemma config dict."""
+    """The decoder spec keys of an HF Qwen3 / Qwen2 / Gemma / Qwen3.5 config dict."""
     mt = cfg.get("model_type")
+    if mt in ("qwen3_5", "qwen3_5_text"):
+        return hybrid_spec_from_config(cfg)
     if mt not in ("qwen3", "qwen2", "gemma"):
         raise ValueError(f"unsupported decoder model_type {mt!r} (qwen3, qwen2 and gemma are supported)")
     heads = int(cfg["num_attention_heads"])
@@ -191,6 +228,19 @@ def write_safetensors(path: str, tensors) -> int:
 
 
 def _hf_config(spec: dict) -> dict:
+    if spec["arch"] == "decoder" and spec["style"] == "qwen3_5":
+        return dict(
+            model_type="qwen3_5_text", architectures=["Qwen3_5ForCausalLM"], hidden_size=spec["hidden"],
+            num_hidden_layers=spec["layers"], num_attention_heads=spec["heads"],
+            num_key_value_heads=spec["kv_heads"], head_dim=spec["head_dim"], intermediate_size=spec["ffn"],
+            vocab_size=spec["vocab"], rms_norm_eps=spec["rms_eps"], tie_word_embeddings=spec["tied"],
+            hidden_act="silu", attention_bias=False, layer_types=list(spec["layer_types"]),
+            linear_num_key_heads=spec["lin_k_heads"], linear_num_value_heads=spec["lin_v_heads"],
+            linear_key_head_dim=spec["lin_k_dim"], linear_value_head_dim=spec["lin_v_dim"],
+            linear_conv_kernel_dim=spec["conv_kernel"], max_position_embeddings=32768,
+            rope_parameters={"rope_type": "default", "rope_theta": spec["rope_theta"],
+                             "partial_rotary_factor": spec["partial_rotary"]},
+            torch_dtype="bfloat16")
     if spec["arch"] == "decoder":
         cfg = dict(
             model_type=spec["style"], hidden_size=spec["hidden"], num_hidden_layers=spec["layers"],

@@ -40,6 +40,7 @@ struct AttnParams {
   const AttnTile* tiles;
   int group;          // query heads per K/V head
   float scale_log2;   // softmax scale * log2(e)
+  int gate_col0;      // >= 0: output *= sigmoid(qkv[row, gate_col0 + head*HD + c]) (gated attention)
 };
 
 template <int HD>
@@ -245,11 +246,28 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
   T* out0 = static_cast<T*>(p.out) + static_cast<size_t>(tile.seq_start + tile.q_start + r0) * p.ld_out + head * HD;
   T* out1 = out0 + static_cast<size_t>(8) * p.ld_out;
   const bool ok0 = r0 < q_rows, ok1 = r0 + 8 < q_rows;
+  const T* gate0 = p.gate_col0 >= 0
+                       ? qkv + static_cast<size_t>(tile.seq_start + tile.q_start + r0) * p.ld_qkv + p.gate_col0 +
+                             head * HD
+                       : nullptr;
 #pragma unroll
   for (int nd = 0; nd < ND; ++nd) {
     const int col = nd * 8 + ((lane & 3) << 1);
-    if (ok0) *reinterpret_cast<uint32_t*>(out0 + col) = Elem<T>::pack2(o[nd][0] * inv0, o[nd][1] * inv0);
-    if (ok1) *reinterpret_cast<uint32_t*>(out1 + col) = Elem<T>::pack2(o[nd][2] * inv1, o[nd][3] * inv1);
+    float g0 = 1.0f, g1 = 1.0f, g2 = 1.0f, g3 = 1.0f;
+    if (gate0 != nullptr) {
+      if (ok0) {
+        const float2 g = Elem<T>::unpack2(*reinterpret_cast<const uint32_t*>(gate0 + col));
+        g0 = 1.0f / (1.0f + __expf(-g.x));
+        g1 = 1.0f / (1.0f + __expf(-g.y));
+      }
+      if (ok1) {
+        const float2 g = Elem<T>::unpack2(*reinterpret_cast<const uint32_t*>(gate0 + 8 * static_cast<size_t>(p.ld_qkv) + col));
+        g2 = 1.0f / (1.0f + __expf(-g.x));
+        g3 = 1.0f / (1.0f + __expf(-g.y));
+      }
+    }
+    if (ok0) *reinterpret_cast<uint32_t*>(out0 + col) = Elem<T>::pack2(o[nd][0] * inv0 * g0, o[nd][1] * inv0 * g1);
+    if (ok1) *reinterpret_cast<uint32_t*>(out1 + col) = Elem<T>::pack2(o[nd][2] * inv1 * g2, o[nd][3] * inv1 * g3);
   }
 }
 

@@ -43,7 +43,8 @@ struct EpiParams {
   int plus_one;           // gain applied as (1 + w)
   float eps;
   const int* positions;   // [M] token position inside its sequence
-  const float2* rope;     // [max_pos][head_dim/2] (cos, sin)
+  const float2* rope;     // [max_pos][rot_dim/2] (cos, sin)
+  int rot_dim;            // rotary width: the first rot_dim columns of a head (multiple of 64; 0 = head_dim)
 };
 
 struct GemmShape {
@@ -158,15 +159,18 @@ __device__ __forceinline__ void out_chunk_add32(EpiOut& o, const float (&v)[32],
   }
 }
 
-// One head of kEpiQKRope: columns [col0, col0 + hd) of row `row`, TMEM at tbase.
-// This warp handles the rotary chunk pairs c in [c_begin, c_end) (chunk c is
-// columns [32c, 32c+32) paired with [hd/2 + 32c, ...)); with a gain it first
-// computes the RMS over the whole head itself, so the two warps sharing a head
-// need no exchange.
+// One head of kEpiQKRope: columns [col0, col0 + HD) of row `row`, TMEM at tbase.
+// The head is split into work units: rotary pairs first (pair c rotates chunk
+// c with chunk c + R/32, chunk c = columns [32c, 32c + 32), R = rot_dim / 2),
+// then the chunks past rot_dim, which are only normalised.  This warp handles
+// units [u_begin, u_end); with a gain it first computes the RMS over the whole
+// head itself, so the two warps sharing a head need no exchange.
 template <int HD, class T>
 __device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row, bool row_ok, int col0,
-                                              const EpiParams& p, const float* gain, int c_begin, int c_end) {
-  constexpr int HALF = HD / 2;
+                                              const EpiParams& p, const float* gain, int u_begin, int u_end) {
+  const int rot = p.rot_dim ? p.rot_dim : HD;
+  const int R = rot / 2;            // rotary half-width (columns)
+  const int pairs = R / 32;         // rotary work units
   float rstd = 1.0f;
   if (gain != nullptr) {
     float ss = 0.0f;
@@ -181,43 +185,67 @@ __device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row
     rstd = rsqrtf(ss / static_cast<float>(HD) + p.eps);
   }
   const int pos = row_ok ? __ldg(p.positions + row) : 0;
-  const float4* rope = reinterpret_cast<const float4*>(p.rope + static_cast<size_t>(pos) * HALF);
+  const float4* rope = reinterpret_cast<const float4*>(p.rope + static_cast<size_t>(pos) * R);
   const float add = p.plus_one ? 1.0f : 0.0f;
+  auto scale = [&](float (&x)[32], int colh) {
+    if (gain == nullptr) return;
+    const float4* g = reinterpret_cast<const float4*>(gain + colh);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 a = __ldg(g + q);
+      x[4 * q + 0] *= rstd * (a.x + add);
+      x[4 * q + 1] *= rstd * (a.y + add);
+      x[4 * q + 2] *= rstd * (a.z + add);
+      x[4 * q + 3] *= rstd * (a.w + add);
+    }
+  };
 #pragma unroll 1
-  for (int c = c_begin; c < c_end; ++c) {
-    float x1[32], x2[32];
-    tmem_load_f32x32(tbase + c * 32, x1);
-    tmem_load_f32x32(tbase + HALF + c * 32, x2);
-    add_bias32(x1, p.bias, col0 + c * 32);
-    add_bias32(x2, p.bias, col0 + HALF + c * 32);
-    if (gain != nullptr) {
-      const float4* g1 = reinterpret_cast<const float4*>(gain + c * 32);
-      const float4* g2 = reinterpret_cast<const float4*>(gain + HALF + c * 32);
+  for (int u = u_begin; u < u_end; ++u) {
+    if (u < pairs) {
+      const int c = u;
+      float x1[32], x2[32];
+      tmem_load_f32x32(tbase + c * 32, x1);
+      tmem_load_f32x32(tbase + R + c * 32, x2);
+      add_bias32(x1, p.bias, col0 + c * 32);
+      add_bias32(x2, p.bias, col0 + R + c * 32);
+      scale(x1, c * 32);
+      scale(x2, R + c * 32);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 a = __ldg(g1 + q), b = __ldg(g2 + q);
-        x1[4 * q + 0] *= rstd * (a.x + add);
-        x1[4 * q + 1] *= rstd * (a.y + add);
-        x1[4 * q + 2] *= rstd * (a.z + add);
-        x1[4 * q + 3] *= rstd * (a.w + add);
-        x2[4 * q + 0] *= rstd * (b.x + add);
-        x2[4 * q + 1] *= rstd * (b.y + add);
-        x2[4 * q + 2] *= rstd * (b.z + add);
-        x2[4 * q + 3] *= rstd * (b.w + add);
+      for (int q = 0; q < 16; ++q) {  // (cos, sin) pairs of columns 2q and 2q+1
+        const float4 cs = __ldg(rope + c * 16 + q);
+        const float a0 = x1[2 * q], b0 = x2[2 * q], a1 = x1[2 * q + 1], b1 = x2[2 * q + 1];
+        x1[2 * q] = a0 * cs.x - b0 * cs.y;
+        x2[2 * q] = b0 * cs.x + a0 * cs.y;
+        x1[2 * q + 1] = a1 * cs.z - b1 * cs.w;
+        x2[2 * q + 1] = b1 * cs.z + a1 * cs.w;
       }
+      out_chunk16<T>(o, x1, col0 + c * 32);
+      out_chunk16<T>(o, x2, col0 + R + c * 32);
+    } else {
+      const int c = rot / 32 + (u - pairs);  // a chunk past the rotary columns
+      float x[32];
+      tmem_load_f32x32(tbase + c * 32, x);
+      add_bias32(x, p.bias, col0 + c * 32);
+      scale(x, c * 32);
+      out_chunk16<T>(o, x, col0 + c * 32);
     }
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {  // (cos, sin) pairs of columns 2q and 2q+1
-      const float4 cs = __ldg(rope + c * 16 + q);
-      const float a0 = x1[2 * q], b0 = x2[2 * q], a1 = x1[2 * q + 1], b1 = x2[2 * q + 1];
-      x1[2 * q] = a0 * cs.x - b0 * cs.y;
-      x2[2 * q] = b0 * cs.x + a0 * cs.y;
-      x1[2 * q + 1] = a1 * cs.z - b1 * cs.w;
-      x2[2 * q + 1] = b1 * cs.z + a1 * cs.w;
-    }
-    out_chunk16<T>(o, x1, col0 + c * 32);
-    out_chunk16<T>(o, x2, col0 + HALF + c * 32);
   }
+}
+
+// Work units [begin, end) of `half` (0 or 1) when two warps share one head:
+// units cost 2 chunks (rotary pairs) or 1 (plain chunks); each warp gets half
+// of the head's HD/32 chunks.
+template <int HD>
+__device__ __forceinline__ void head_units(const EpiParams& p, int half, int& begin, int& end) {
+  const int rot = p.rot_dim ? p.rot_dim : HD;
+  const int pairs = rot / 64, units = pairs + (HD - rot) / 32;
+  int split = 0, cost = 0;
+  while (split < units && cost < HD / 64) {
+    cost += split < pairs ? 2 : 1;
+    ++split;
+  }
+  begin = half ? split : 0;
+  end = half ? units : split;
 }
 
 // Plain store of 32-column chunks [c_begin, c_end) starting at column col0.
@@ -269,22 +297,31 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
     // warp takes one head; with one head (BN = 128) the warps split its two
     // rotary chunk pairs.  head_dim 256 (one head per 256-wide tile): the warps
     // split its four chunk pairs.
+    // Columns past the q and k blocks (v, and a hybrid's output gate) are stored as they are.
     if (p.head_dim == 128) {
       constexpr int HEADS = BN / 128;
       const int h = HEADS == 2 ? half : 0;
-      const int cb = HEADS == 2 ? 0 : half, ce = HEADS == 2 ? 2 : half + 1;
       const int col0 = n0 + h * 128;
       const uint32_t tb = taddr + h * 128;
+      int ub = 0, ue = 0;
+      if (HEADS == 2) {
+        const int rot = p.rot_dim ? p.rot_dim : 128;
+        ue = rot / 64 + (128 - rot) / 32;  // the whole head
+      } else {
+        head_units<128>(p, half, ub, ue);
+      }
       if (col0 < p.q_cols + p.k_cols)
-        epi_head_rope<128, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, cb, ce);
+        epi_head_rope<128, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, ub, ue);
       else
-        epi_store_chunks<T>(o, tb, col0, p, 2 * cb, 2 * ce);
+        epi_store_chunks<T>(o, tb, col0, p, HEADS == 2 ? 0 : 2 * half, HEADS == 2 ? 4 : 2 * half + 2);
     } else if constexpr (BN == 256) {
-      if (n0 < p.q_cols + p.k_cols)
-        epi_head_rope<256, T>(o, taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, 2 * half,
-                              2 * half + 2);
-      else
+      if (n0 < p.q_cols + p.k_cols) {
+        int ub = 0, ue = 0;
+        head_units<256>(p, half, ub, ue);
+        epi_head_rope<256, T>(o, taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, ub, ue);
+      } else {
         epi_store_chunks<T>(o, taddr, n0, p, 4 * half, 4 * half + 4);
+      }
     }
   }
 }

@@ -188,7 +188,8 @@ extern "C" VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_c
     cuda_check(cudaMalloc(&d_tiles, tiles.size() * sizeof(AttnTile)), "tile table");
     std::unique_ptr<AttnTile, decltype(&cudaFree)> guard(d_tiles, &cudaFree);
     cuda_check(cudaMemcpy(d_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice), "tiles");
-    AttnParams p;
+    AttnParams p{};
+    p.gate_col0 = -1;
     p.qkv = qkv;
     p.ld_qkv = static_cast<int>(ld_qkv);
     p.q_col0 = static_cast<int>(q_col0);

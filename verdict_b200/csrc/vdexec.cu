@@ -42,6 +42,7 @@
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "gemm2.cuh"
+#include "gdn.cuh"
 #include "json.hpp"
 #include "synth.cuh"
 
@@ -73,9 +74,26 @@ struct ModelSpec {
   std::string checkpoint;  // safetensors directory; empty = seeded synthetic weights
   std::vector<int> label_ids;
   int max_pos = 512, type_vocab = 2, pad_id = 0, head_layers = 2;
+  // hybrid (Qwen3.5) stacks: per-layer token mixer and gated-delta-net sizes
+  std::vector<char> linear_layer;  // 1: gated delta net, 0: full attention
+  double partial_rotary = 1.0;
+  int lin_k_heads = 0, lin_v_heads = 0, lin_k_dim = 128, lin_v_dim = 128, conv_kernel = 4;
 
   bool decoder() const { return arch == "decoder"; }
-  int qkv_width() const { return (heads + 2 * kv_heads) * head_dim; }
+  bool hybrid() const { return style == "qwen3_5"; }
+  // fused full-attention projection: q, k, v (and the output gate of a hybrid)
+  int qkv_width() const { return (heads + 2 * kv_heads + (hybrid() ? heads : 0)) * head_dim; }
+  int rot_dim() const { return static_cast<int>(head_dim * partial_rotary); }
+  int gdn_kd() const { return lin_k_heads * lin_k_dim; }
+  int gdn_vd() const { return lin_v_heads * lin_v_dim; }
+  int gdn_conv() const { return 2 * gdn_kd() + gdn_vd(); }
+  // fused in_proj columns: conv input, z, a, b, padded to 256-wide GEMM tiles
+  int gdn_proj() const { return (gdn_conv() + gdn_vd() + 2 * lin_v_heads + 255) / 256 * 256; }
+  bool any_linear() const {
+    for (char c : linear_layer)
+      if (c) return true;
+    return false;
+  }
 };
 
 static ModelSpec parse_spec(const Json& j) {
@@ -101,7 +119,22 @@ static ModelSpec parse_spec(const Json& j) {
     s.qkv_bias = j.boolean_or("qkv_bias", s.style == "qwen2");
     s.tied = j.boolean_or("tied", false);
     s.embed_scale = j.boolean_or("embed_scale", false);
-    s.norm_plus_one = j.boolean_or("norm_plus_one", false);
+    s.norm_plus_one = j.boolean_or("norm_plus_one", s.style == "qwen3_5");
+    if (s.hybrid()) {
+      if (!j.has("layer_types") || j.at("layer_types").kind != Json::Array)
+        fail(VD_ESPEC, "a qwen3_5 spec needs \"layer_types\"");
+      for (const Json& v : j.at("layer_types").arr) {
+        if (v.str == "linear_attention") s.linear_layer.push_back(1);
+        else if (v.str == "full_attention") s.linear_layer.push_back(0);
+        else fail(VD_ESPEC, "unknown layer type \"" + v.str + "\"");
+      }
+      s.partial_rotary = j.number_or("partial_rotary", 0.25);
+      s.lin_k_heads = static_cast<int>(j.integer("lin_k_heads"));
+      s.lin_v_heads = static_cast<int>(j.integer("lin_v_heads"));
+      s.lin_k_dim = static_cast<int>(j.integer_or("lin_k_dim", 128));
+      s.lin_v_dim = static_cast<int>(j.integer_or("lin_v_dim", 128));
+      s.conv_kernel = static_cast<int>(j.integer_or("conv_kernel", 4));
+    }
     const std::string act = j.string_or("act", "silu");
     if (act == "silu") s.act = kActSilu;
     else if (act == "gelu_tanh") s.act = kActGeluTanh;
@@ -188,8 +221,68 @@ static Json spec_from_hf_config(const Json& c) {
     o.obj["family"] = jstr("marker_head");
     return o;
   }
+  if (mt == "qwen3_5" || mt == "qwen3_5_text") {
+    // A Qwen3.5 text stack (the text_config of a vision-language checkpoint).
+    const Json& t = (mt == "qwen3_5" && c.has("text_config") && c.at("text_config").kind == Json::Object)
+                        ? c.at("text_config")
+                        : c;
+    auto num = [&](const char* k) {
+      if (!t.has(k) || t.at(k).kind != Json::Number) fail(VD_ESPEC, std::string("HF config has no number \"") + k + "\"");
+      return t.at(k).num;
+    };
+    double theta = t.number_or("rope_theta", 0.0), partial = t.number_or("partial_rotary_factor", 0.25);
+    std::string rope_type = "default";
+    if (t.has("rope_parameters") && t.at("rope_parameters").kind == Json::Object) {
+      const Json& rp = t.at("rope_parameters");
+      if (theta == 0.0) theta = rp.number_or("rope_theta", 0.0);
+      partial = rp.number_or("partial_rotary_factor", partial);
+      rope_type = rp.string_or("rope_type", "default");
+    }
+    if ((t.has("rope_scaling") && t.at("rope_scaling").kind == Json::Object) || rope_type != "default")
+      fail(VD_ESPEC, "rope scaling is not supported");
+    if (t.boolean_or("attention_bias", false)) fail(VD_ESPEC, "qwen3_5 checkpoints with attention bias are not supported");
+    const std::string act = t.string_or("hidden_act", "silu");
+    if (act != "silu" && act != "swish") fail(VD_ESPEC, "unsupported qwen3_5 activation \"" + act + "\"");
+    const double heads = num("num_attention_heads"), layers = num("num_hidden_layers");
+    o.obj["arch"] = jstr("decoder");
+    o.obj["style"] = jstr("qwen3_5");
+    o.obj["hidden"] = jnum(num("hidden_size"));
+    o.obj["layers"] = jnum(layers);
+    o.obj["heads"] = jnum(heads);
+    o.obj["kv_heads"] = jnum(t.number_or("num_key_value_heads", heads));
+    o.obj["head_dim"] = jnum(t.number_or("head_dim", 256));
+    o.obj["ffn"] = jnum(num("intermediate_size"));
+    o.obj["vocab"] = jnum(num("vocab_size"));
+    o.obj["rms_eps"] = jnum(t.number_or("rms_norm_eps", 1e-6));
+    o.obj["rope_theta"] = jnum(theta == 0.0 ? 10000.0 : theta);
+    o.obj["partial_rotary"] = jnum(partial);
+    o.obj["tied"] = jbool(t.boolean_or("tie_word_embeddings", c.boolean_or("tie_word_embeddings", false)));
+    o.obj["qk_norm"] = jbool(true);
+    o.obj["qkv_bias"] = jbool(false);
+    o.obj["act"] = jstr("silu");
+    o.obj["embed_scale"] = jbool(false);
+    o.obj["norm_plus_one"] = jbool(true);
+    o.obj["lin_k_heads"] = jnum(num("linear_num_key_heads"));
+    o.obj["lin_v_heads"] = jnum(num("linear_num_value_heads"));
+    o.obj["lin_k_dim"] = jnum(t.number_or("linear_key_head_dim", 128));
+    o.obj["lin_v_dim"] = jnum(t.number_or("linear_value_head_dim", 128));
+    o.obj["conv_kernel"] = jnum(t.number_or("linear_conv_kernel_dim", 4));
+    Json types;
+    types.kind = Json::Array;
+    if (t.has("layer_types") && t.at("layer_types").kind == Json::Array) {
+      types = t.at("layer_types");
+    } else {
+      const int every = static_cast<int>(t.number_or("full_attention_interval", 4));
+      for (int i = 0; i < static_cast<int>(layers); ++i)
+        types.arr.push_back(jstr((i + 1) % every ? "linear_attention" : "full_attention"));
+    }
+    o.obj["layer_types"] = types;
+    o.obj["family"] = jstr("letter_readout");
+    return o;
+  }
   if (mt != "qwen3" && mt != "qwen2" && mt != "gemma")
-    fail(VD_ESPEC, "unsupported model_type \"" + mt + "\" (qwen3, qwen2, gemma, bert, xlm-roberta are supported)");
+    fail(VD_ESPEC, "unsupported model_type \"" + mt +
+                       "\" (qwen3, qwen2, gemma, qwen3_5, bert, xlm-roberta are supported)");
   const double heads = need_num("num_attention_heads"), hidden = need_num("hidden_size");
   o.obj["arch"] = jstr("decoder");
   o.obj["style"] = jstr(mt);
@@ -301,7 +394,19 @@ static void validate_spec(const ModelSpec& s) {
   need(s.layers > 0 && s.heads > 0, "layers and heads must be positive");
   need(s.ffn % 128 == 0, "ffn must be a multiple of 128");
   if (s.decoder()) {
-    need(s.style == "qwen3" || s.style == "qwen2" || s.style == "gemma", "decoder style must be qwen3/qwen2/gemma");
+    need(s.style == "qwen3" || s.style == "qwen2" || s.style == "gemma" || s.style == "qwen3_5",
+         "decoder style must be qwen3/qwen2/gemma/qwen3_5");
+    if (s.hybrid()) {
+      need(static_cast<int>(s.linear_layer.size()) == s.layers, "layer_types must list every layer");
+      need(s.rot_dim() % 64 == 0 && s.rot_dim() > 0 && s.rot_dim() <= s.head_dim,
+           "the rotary width (head_dim * partial_rotary) must be a positive multiple of 64");
+      need(s.lin_k_dim == 128 && s.lin_v_dim == 128, "gated-delta-net head dims must be 128");
+      need(s.lin_k_heads > 0 && s.lin_v_heads % s.lin_k_heads == 0, "lin_v_heads must be a multiple of lin_k_heads");
+      need(s.conv_kernel == 4, "the gated delta net's conv kernel must be 4 wide");
+      need(!s.any_linear() || s.gdn_vd() == s.heads * s.head_dim,
+           "the gated delta net's value width must equal heads * head_dim (shared output buffer)");
+      need(s.qkv_bias == false, "qwen3_5 has no attention bias");
+    }
     need(s.head_dim == 128 || s.head_dim == 256, "decoder head_dim must be 128 or 256");
     need(s.kv_heads > 0 && s.heads % s.kv_heads == 0, "heads must be a multiple of kv_heads");
     need((s.heads * s.head_dim) % 128 == 0, "heads*head_dim must be a multiple of 128");
@@ -399,6 +504,9 @@ struct Linear {
 struct DecLayer {
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   Linear qkv, o, gu, down;
+  // gated-delta-net layers (hybrid stacks): qkv = fused in_proj, o = out_proj
+  bool linear = false;
+  float *conv_w = nullptr, *A_log = nullptr, *dt_bias = nullptr, *gdn_norm = nullptr;
 };
 
 struct EncLayer {
@@ -466,6 +574,11 @@ struct vd_handle {
   CUtensorMap map_xn_s, map_attn_s, map_act_s;
   // GEMM output maps (epilogue TMA stores / reduce-adds)
   CUtensorMap out_qkv, out_act, out_act2, out_h, out_h_s, out_act_s, out_mhid;
+  // gated-delta-net workspace (hybrid stacks)
+  int ld_qkv = 0;        // row stride of qkv (elements)
+  void* proj = nullptr;  // 16-bit [T, gdn_proj]
+  float *gdn_g = nullptr, *gdn_beta = nullptr;
+  CUtensorMap out_proj;
   // device copies of host batches
   int64_t *in_ids = nullptr, *in_mpos = nullptr, *in_nopts = nullptr, *in_qtype = nullptr;
   uint8_t* in_mmask = nullptr;
@@ -559,9 +672,15 @@ static std::string shape_str(const std::vector<int64_t>& v) {
   return o + "]";
 }
 
+// Tensors of a vision-language checkpoint's text stack live under
+// "model.language_model." instead of "model."; both are accepted.
 static const StTensor& ckpt_get(vd_handle* H, const std::string& name) {
-  if (!H->ckpt->has(name)) fail(VD_ESPEC, "checkpoint " + H->spec.checkpoint + " has no tensor " + name);
-  return H->ckpt->get(name);
+  if (H->ckpt->has(name)) return H->ckpt->get(name);
+  if (name.compare(0, 6, "model.") == 0) {
+    const std::string vl = "model.language_model." + name.substr(6);
+    if (H->ckpt->has(vl)) return H->ckpt->get(vl);
+  }
+  fail(VD_ESPEC, "checkpoint " + H->spec.checkpoint + " has no tensor " + name);
 }
 
 static const StTensor& ckpt_tensor(vd_handle* H, const std::string& name, const std::vector<int64_t>& shape) {
@@ -596,10 +715,10 @@ static void release_checkpoint(vd_handle* H) {
 
 template <class T>
 static void fill_rows_t(vd_handle* H, T* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
-                        float offset, int64_t group, int64_t stride, int64_t off) {
+                        float offset, int64_t group, int64_t stride, int64_t off, int64_t alt_off) {
   if (!H->ckpt) {
     synth_rows_kernel<T><<<grid_for(rows * cols), 256, 0, H->stream>>>(
-        dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, group, stride, off);
+        dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, group, stride, off, alt_off);
     return;
   }
   const StTensor& t = ckpt_tensor(H, name, {rows, cols});
@@ -609,24 +728,25 @@ static void fill_rows_t(vd_handle* H, T* dst, const std::string& name, int64_t r
     const int64_t n = std::min(slice, rows - r0);
     const void* src = stage_bytes(H, t.data + static_cast<size_t>(r0) * row_bytes, static_cast<size_t>(n) * row_bytes);
     convert_rows_kernel<T><<<grid_for(n * cols), 256, 0, H->stream>>>(dst, src, t.dtype, r0, n, cols, group, stride,
-                                                                       off);
+                                                                       off, alt_off);
   }
 }
 
 // A 16-bit tensor in the element type `f16` selects (embedding tables are always bf16).
 static void fill_w(vd_handle* H, void* dst, bool f16, const std::string& name, int64_t rows, int64_t cols,
-                   float scale, float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
+                   float scale, float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0,
+                   int64_t alt_off = -1) {
   if (group == 0) group = rows;
-  if (f16) fill_rows_t(H, static_cast<__half*>(dst), name, rows, cols, scale, offset, group, stride, off);
-  else fill_rows_t(H, static_cast<__nv_bfloat16*>(dst), name, rows, cols, scale, offset, group, stride, off);
+  if (f16) fill_rows_t(H, static_cast<__half*>(dst), name, rows, cols, scale, offset, group, stride, off, alt_off);
+  else fill_rows_t(H, static_cast<__nv_bfloat16*>(dst), name, rows, cols, scale, offset, group, stride, off, alt_off);
 }
 static void fill_bf16(vd_handle* H, bf16* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
                       float offset) {
   fill_w(H, dst, false, name, rows, cols, scale, offset);
 }
 static void fill_lin(vd_handle* H, void* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
-                     float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0) {
-  fill_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off);
+                     float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0, int64_t alt_off = -1) {
+  fill_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off, alt_off);
 }
 // An fp32 vector of n elements (gains, biases; a [1, n] Linear weight qualifies).
 static void fill_f32(vd_handle* H, float* dst, const std::string& name, int64_t n, float scale, float offset) {
@@ -695,8 +815,42 @@ static void load_decoder(vd_handle* H) {
     L.post_norm = dalloc<float>(H, d);
     fill_f32(H, L.in_norm, p + "input_layernorm.weight", d, n_scale, n_off);
     fill_f32(H, L.post_norm, p + "post_attention_layernorm.weight", d, n_scale, n_off);
+    if (s.hybrid() && s.linear_layer[i]) {
+      // Gated delta net: fused in_proj rows [conv input (C) | z | a | b | zero pad].
+      const std::string a = p + "linear_attn.";
+      const int C = s.gdn_conv(), vd = s.gdn_vd(), lv = s.lin_v_heads;
+      L.linear = true;
+      init_linear(H, L.qkv, s.gdn_proj(), d, false, 256);
+      cuda_check(cudaMemsetAsync(L.qkv.w, 0, static_cast<size_t>(L.qkv.n) * d * 2, H->stream), "clear in_proj");
+      fill_lin(H, L.qkv.w, a + "in_proj_qkv.weight", C, d, lin, 0.0f, C, 0, 0);
+      fill_lin(H, L.qkv.w, a + "in_proj_z.weight", vd, d, lin, 0.0f, vd, 0, C);
+      fill_lin(H, L.qkv.w, a + "in_proj_a.weight", lv, d, lin, 0.0f, lv, 0, C + vd);
+      fill_lin(H, L.qkv.w, a + "in_proj_b.weight", lv, d, lin, 0.0f, lv, 0, C + vd + lv);
+      L.conv_w = dalloc<float>(H, static_cast<size_t>(C) * s.conv_kernel);
+      fill_f32(H, L.conv_w, a + "conv1d.weight", static_cast<int64_t>(C) * s.conv_kernel, 0.5f, 0.0f);
+      L.A_log = dalloc<float>(H, lv);
+      L.dt_bias = dalloc<float>(H, lv);
+      L.gdn_norm = dalloc<float>(H, s.lin_v_dim);
+      fill_f32(H, L.A_log, a + "A_log", lv, 1.0f, 1.0f);
+      fill_f32(H, L.dt_bias, a + "dt_bias", lv, 0.1f, 1.0f);
+      fill_f32(H, L.gdn_norm, a + "norm.weight", s.lin_v_dim, 0.1f, 1.0f);
+      init_linear(H, L.o, d, vd, false);
+      fill_lin(H, L.o.w, a + "out_proj.weight", d, vd, lin, 0.0f);
+      init_linear(H, L.gu, 2 * f, d, false, 256);
+      fill_lin(H, L.gu.w, p + "mlp.gate_proj.weight", f, d, lin, 0.0f, 128, 256, 0);
+      fill_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
+      init_linear(H, L.down, d, f, false);
+      fill_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
+      continue;
+    }
     init_linear(H, L.qkv, s.qkv_width(), d, s.qkv_bias, bn_qkv);
-    fill_lin(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
+    if (s.hybrid()) {
+      // Gated attention: q_proj holds [query | gate] per head; queries go to the
+      // q block, gates after v.
+      fill_lin(H, L.qkv.w, p + "self_attn.q_proj.weight", 2 * qc, d, lin, 0.0f, hd, hd, 0, qc + 2 * kc);
+    } else {
+      fill_lin(H, L.qkv.w, p + "self_attn.q_proj.weight", qc, d, lin, 0.0f, qc, 0, 0);
+    }
     fill_lin(H, L.qkv.w, p + "self_attn.k_proj.weight", kc, d, lin, 0.0f, kc, 0, qc);
     fill_lin(H, L.qkv.w, p + "self_attn.v_proj.weight", kc, d, lin, 0.0f, kc, 0, qc + kc);
     if (s.qkv_bias) {
@@ -724,12 +878,14 @@ static void load_decoder(vd_handle* H) {
   H->head_rows = dalloc<float>(H, static_cast<size_t>(H->n_labels) * d);
   const std::string head_name = s.tied ? "model.embed_tokens.weight" : "lm_head.weight";
   fill_rows_gather_f32(H, H->head_rows, head_name, s.label_ids, s.vocab, d, lin, 0.0f);
-  // RoPE table: cos/sin(pos * inv_freq_i), inv_freq_i = 1 / theta^(2i/hd) in fp32.
-  const int half = hd / 2;
+  // RoPE table: cos/sin(pos * inv_freq_i), inv_freq_i = 1 / theta^(2i/rot) in fp32, rot the
+  // rotary width (head_dim, or its partial_rotary fraction in a hybrid's attention).
+  const int rot = s.hybrid() ? s.rot_dim() : hd;
+  const int half = rot / 2;
   std::vector<float2> tab(static_cast<size_t>(H->opt.max_seq) * half);
   std::vector<float> inv(half);
   for (int i = 0; i < half; ++i)
-    inv[i] = 1.0f / std::pow(static_cast<float>(s.rope_theta), static_cast<float>(2 * i) / static_cast<float>(hd));
+    inv[i] = 1.0f / std::pow(static_cast<float>(s.rope_theta), static_cast<float>(2 * i) / static_cast<float>(rot));
   for (int64_t pos = 0; pos < H->opt.max_seq; ++pos)
     for (int i = 0; i < half; ++i) {
       const float a = static_cast<float>(pos) * inv[i];
@@ -857,12 +1013,13 @@ static void alloc_workspace(vd_handle* H) {
   const Options& o = H->opt;
   const int64_t T = o.max_tokens;
   const int d = s.hidden;
-  const int qkvw = s.decoder() ? s.qkv_width() : 3 * d;
+  const int qkvw = s.decoder() ? std::max(s.qkv_width(), s.hybrid() ? s.gdn_conv() : 0) : 3 * d;
   const int attw = s.decoder() ? s.heads * s.head_dim : d;
   const int actw = s.decoder() ? s.ffn : std::max(s.ffn, 4 * d);
   H->h = dalloc<float>(H, T * d);
   H->xn = dalloc<uint16_t>(H, T * d);
   H->qkv = dalloc<uint16_t>(H, T * qkvw);
+  H->ld_qkv = qkvw;
   // Attention tiles read whole 128-row K/V blocks, including rows past the
   // batch (masked to probability 0); zeroing once keeps those rows finite.
   cuda_check(cudaMemset(H->qkv, 0, static_cast<size_t>(T) * qkvw * 2), "clear qkv workspace");
@@ -899,6 +1056,13 @@ static void alloc_workspace(vd_handle* H) {
   }
   H->map_act = make_map(H->act, T, s.ffn, 128, f16);
   H->out_act = make_out_map(H->act, T, s.ffn, false, f16);
+  if (s.decoder() && s.any_linear()) {
+    // gated-delta-net in_proj output and per-(token, v head) gates
+    H->proj = dalloc<uint16_t>(H, T * s.gdn_proj());
+    H->out_proj = make_out_map(H->proj, T, s.gdn_proj(), false, f16);
+    H->gdn_g = dalloc<float>(H, T * s.lin_v_heads);
+    H->gdn_beta = dalloc<float>(H, T * s.lin_v_heads);
+  }
   if (!s.decoder()) {
     H->map_act2 = make_map(H->act, T, 4 * d, 128, f16);
     H->out_act2 = make_out_map(H->act, T, 4 * d, false, f16);
@@ -1024,12 +1188,17 @@ static bool use_tc_attention(const vd_handle* H, int hd, bool causal) {
   return H->opt.tc_attention && hd == 128 && causal;
 }
 
-static int attn_tile_rows(const vd_handle* H, int hd, bool causal) { return use_tc_attention(H, hd, causal) ? 128 : 64; }
+static int attn_tile_rows(const vd_handle* H, int hd, bool causal, bool gated = false) {
+  return !gated && use_tc_attention(H, hd, causal) ? 128 : 64;
+}
 
+// gate_col0 >= 0: gated attention (the output is multiplied by the sigmoid of
+// the gate columns of qkv), served by the warp-level kernel.
 template <class T>
 static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd, bool causal, int ld_qkv, int q0,
-                      int k0, int v0, int group, int ld_out) {
-  AttnParams p;
+                      int k0, int v0, int group, int ld_out, int gate_col0 = -1) {
+  AttnParams p{};
+  p.gate_col0 = gate_col0;
   p.qkv = H->qkv;
   p.ld_qkv = ld_qkv;
   p.q_col0 = q0;
@@ -1043,7 +1212,7 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
   dim3 grid(n_tiles, heads);
   if (!((hd == 64 && !causal) || (hd == 128 && causal) || (hd == 256 && causal)))
     fail(VD_ESPEC, "no attention kernel for this head size / mask");
-  if (use_tc_attention(H, hd, causal)) {
+  if (gate_col0 < 0 && use_tc_attention(H, hd, causal)) {
     AttnTcParams tp;
     tp.out = H->attn;
     tp.ld_out = ld_out;
@@ -1194,7 +1363,10 @@ static ChunkPlan plan_chunk(vd_handle* H, const Chunk& c, bool causal, int tile_
   AttnTile* tiles = reinterpret_cast<AttnTile*>(buf + off);
 
   std::vector<ForkGroup> groups;
-  if (causal && H->opt.fork) groups = plan_fork(c);
+  // Gated-delta-net layers carry a recurrent state along the sequence; a
+  // shared prefix would have to hand its state to every suffix, which this
+  // executor does not do, so hybrid stacks run whole rows.
+  if (causal && H->opt.fork && !H->spec.any_linear()) groups = plan_fork(c);
   std::vector<int> group_of(c.nb, -1);
   for (size_t g = 0; g < groups.size(); ++g)
     for (int i : groups[g].rows) group_of[i] = static_cast<int>(g);
@@ -1264,37 +1436,94 @@ static void pack(vd_handle* H, const Chunk& c, const ChunkPlan& P, int pos_offse
   });
 }
 
+// Full attention of one decoder layer: fused QKV GEMM (bias, q/k RMSNorm and
+// RoPE in the epilogue; a hybrid's output-gate columns pass through), then
+// varlen causal attention (gated in a hybrid) into H->attn.
+template <class T>
+static void full_attention_mixer(vd_handle* H, const DecLayer& L, int ntok, int n_tiles, double attn_flops) {
+  const ModelSpec& s = H->spec;
+  const int hd = s.head_dim, nq = s.heads, nkv = s.kv_heads, qc = nq * hd, kc = nkv * hd;
+  EpiParams q = epi(L.qkv.b);
+  q.q_norm = L.q_norm;
+  q.k_norm = L.k_norm;
+  q.q_cols = qc;
+  q.k_cols = kc;
+  q.head_dim = hd;
+  q.plus_one = s.norm_plus_one ? 1 : 0;
+  q.eps = static_cast<float>(s.rms_eps);
+  q.positions = H->positions;
+  q.rope = H->rope;
+  q.rot_dim = s.hybrid() ? s.rot_dim() : 0;
+  gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q, H->out_qkv);
+  attention<T>(H, attn_flops, n_tiles, nq, hd, true, H->ld_qkv, 0, qc, qc + kc, nq / nkv, qc,
+               s.hybrid() ? qc + 2 * kc : -1);
+}
+
+// Gated delta net of one hybrid layer: fused in_proj GEMM into H->proj, conv +
+// l2 norms + gates into H->qkv / gdn_g / gdn_beta, then the recurrence with the
+// gated norm into H->attn (one CTA per sequence and value head).
+template <class T>
+static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan& P) {
+  const ModelSpec& s = H->spec;
+  gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, epi(), H->out_proj);
+  GdnParams g{};
+  g.proj = H->proj;
+  g.ld_proj = s.gdn_proj();
+  g.conv_w = L.conv_w;
+  g.A_log = L.A_log;
+  g.dt_bias = L.dt_bias;
+  g.norm_w = L.gdn_norm;
+  g.positions = H->positions;
+  g.ntok = ntok;
+  g.kd = s.gdn_kd();
+  g.vd = s.gdn_vd();
+  g.lk = s.lin_k_heads;
+  g.lv = s.lin_v_heads;
+  g.col_z = s.gdn_conv();
+  g.col_a = s.gdn_conv() + s.gdn_vd();
+  g.col_b = g.col_a + s.lin_v_heads;
+  g.qkv = H->qkv;
+  g.ld_qkv = H->ld_qkv;
+  g.g = H->gdn_g;
+  g.beta = H->gdn_beta;
+  g.out = H->attn;
+  g.ld_out = s.heads * s.head_dim;
+  g.q_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(s.lin_k_dim)));
+  g.eps = static_cast<float>(s.rms_eps);
+  g.segs = reinterpret_cast<const int4*>(H->segs);
+  launch(H, VD_K_GDN, 0.0, [&] { gdn_conv_prep_kernel<T, 4><<<ntok, 256, 0, H->stream>>>(g); });
+  // per token and value head: decay + two rank-1 passes over the 128 x 128 state
+  const double flops = 4.0 * ntok * s.lin_v_heads * s.lin_k_dim * s.lin_v_dim;
+  launch(H, VD_K_GDN, flops, [&] {
+    gdn_scan_kernel<T><<<dim3(P.n_seg, s.lin_v_heads), 128, 0, H->stream>>>(g);
+  });
+}
+
 template <class T>
 static double decoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads;
-  const ChunkPlan P = plan_chunk(H, c, true, attn_tile_rows(H, hd, true));
+  const ChunkPlan P = plan_chunk(H, c, true, attn_tile_rows(H, hd, true, s.hybrid()));
   const int ntok = P.ntok, n_tiles = P.n_tiles;
   pack(H, c, P, 0);
   const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
   launch(H, VD_K_OTHER, 0.0,
          [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h); });
-  const int qkvw = s.qkv_width(), qc = nq * hd, kc = nkv * hd;
+  const int qkvw = H->ld_qkv, qc = nq * hd, kc = nkv * hd;
   const float eps = static_cast<float>(s.rms_eps);
   const int pone = s.norm_plus_one ? 1 : 0;
   const double attn_flops = 4.0 * hd * nq * P.pairs;
+  (void)qkvw;
   for (int i = 0; i < s.layers; ++i) {
     const DecLayer& L = H->dec[i];
     launch(H, VD_K_NORM, 0.0, [&] {
       rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.in_norm, pone, eps, static_cast<T*>(H->xn), ntok);
     });
-    EpiParams q = epi(L.qkv.b);
-    q.q_norm = L.q_norm;
-    q.k_norm = L.k_norm;
-    q.q_cols = qc;
-    q.k_cols = kc;
-    q.head_dim = hd;
-    q.plus_one = pone;
-    q.eps = eps;
-    q.positions = H->positions;
-    q.rope = H->rope;
-    gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q, H->out_qkv);
-    attention<T>(H, attn_flops, n_tiles, nq, hd, true, qkvw, 0, qc, qc + kc, nq / nkv, qc);
+    if (L.linear) {
+      gdn_mixer<T>(H, L, ntok, P);
+    } else {
+      full_attention_mixer<T>(H, L, ntok, n_tiles, attn_flops);
+    }
     const bool last = i + 1 == s.layers;
     if (last && H->opt.prune_last_layer) {
       // Only the slot rows feed the readout: gather them (attention output and
@@ -1329,12 +1558,6 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
                                                         H->head_rows, H->n_labels, c.out, static_cast<int>(c.width),
                                                         H->opt.logprobs ? 1 : 0, compact ? 1 : 0, H->d_err);
   });
-  H->stats.attn_flops += attn_flops * s.layers;
-  // Projection FLOPs executed: every layer's QKV over all tokens, the rest over
-  // all tokens except in a pruned last layer (slot rows only).
-  const double per_row_rest = static_cast<double>(qc) * d + 3.0 * d * s.ffn;
-  const double rest_rows = static_cast<double>(ntok) * (s.layers - (compact ? 1 : 0)) + (compact ? c.nb : 0);
-  H->stats.gemm_flops += 2.0 * (static_cast<double>(ntok) * s.layers * d * qkvw + rest_rows * per_row_rest);
   return ntok;
 }
 
@@ -1398,8 +1621,6 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
                                                         c.mmask, c.nb,
                                                      static_cast<int>(c.k), c.out, static_cast<int>(c.width));
   });
-  H->stats.attn_flops += attn_flops * (s.layers + s.head_layers);
-  H->stats.gemm_flops += 2.0 * ntok * ((4.0 * d * d + 2.0 * d * s.ffn) * s.layers + (12.0 * d * d) * s.head_layers);
   return ntok;
 }
 
@@ -1502,6 +1723,10 @@ static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const
   }
   cuda_check(cudaGetLastError(), "kernel launch");
   cuda_check(cudaEventRecord(H->ev1, H->stream), "event");
+  // Algorithmic work actually launched, from the per-class counts of launch().
+  H->stats.gemm_flops = H->stats.kernel_flops[VD_K_QKV] + H->stats.kernel_flops[VD_K_O] +
+                        H->stats.kernel_flops[VD_K_GATEUP] + H->stats.kernel_flops[VD_K_DOWN];
+  H->stats.attn_flops = H->stats.kernel_flops[VD_K_ATTN];
   H->stats.enqueue_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_enqueue).count();
   H->stats.rows = b->b;
@@ -1894,7 +2119,8 @@ extern "C" VD_API int vdk_attention_noalloc(const void* qkv, int64_t ld_qkv, int
     // earlier call is ever read.
     cuda_check(cudaMemcpyAsync(d_tiles, g_noalloc_host_tiles, sizeof(AttnTile) * t, cudaMemcpyHostToDevice, s),
                "upload tile table");
-    AttnParams p;
+    AttnParams p{};
+    p.gate_col0 = -1;
     p.qkv = qkv;
     p.ld_qkv = static_cast<int>(ld_qkv);
     p.q_col0 = static_cast<int>(q_col0);

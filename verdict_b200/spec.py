@@ -9,6 +9,15 @@ as HF CausalLMs):
     act in {"silu", "gelu_tanh"}, tied, embed_scale, norm_plus_one,
     family in {"letter_branches", "letter_readout"}, label_ids, seed, init_std
 
+hybrid decoder keys (style "qwen3_5": HF Qwen3.5 text stacks, gated-delta-net
+linear-attention layers with a full-attention layer every few; loaded by the
+same executor path as any CausalLM):
+    the decoder keys above (heads / kv_heads / head_dim describe the full-
+    attention layers, whose q_proj also yields a sigmoid output gate), plus
+    layer_types (list of "linear_attention" / "full_attention"),
+    partial_rotary (rotary fraction of head_dim), lin_k_heads, lin_v_heads,
+    lin_k_dim, lin_v_dim, conv_kernel
+
 encoder keys (marker-head family, `convert/marker_head/marker_head_converter.py:19-57`):
     arch="encoder", style in {"bert", "xlmr"}, hidden, layers, heads, ffn,
     vocab, max_pos, type_vocab, ln_eps, pad_id, head_layers, family="marker_head",
@@ -38,6 +47,16 @@ _ENCODER_BASE = dict(
     pad_id=0, head_layers=2, family="marker_head", seed=20261201, init_std=0.02,
 )
 
+def hybrid_layer_types(layers: int, full_attention_interval: int = 4) -> list:
+    """Qwen3.5's default layer pattern: every `interval`-th layer full attention."""
+    return ["linear_attention" if (i + 1) % full_attention_interval else "full_attention" for i in range(layers)]
+
+
+_HYBRID_BASE = dict(
+    _DECODER_BASE, style="qwen3_5", qk_norm=True, norm_plus_one=True, rope_theta=1e7,
+    partial_rotary=0.25, conv_kernel=4, lin_k_heads=16, lin_v_heads=32, lin_k_dim=128, lin_v_dim=128,
+)
+
 PRESETS = {
     # OneJev-9B-shaped text decision model
     "onejev-9b": dict(_DECODER_BASE, hidden=4096, layers=40, heads=32, kv_heads=8,
@@ -50,6 +69,10 @@ PRESETS = {
                        kv_heads=1, head_dim=256, ffn=16384, vocab=256000,
                        rope_theta=1e4, qk_norm=False, act="gelu_tanh", tied=True,
                        embed_scale=True, norm_plus_one=True, family="letter_readout"),
+    # OneJev1.6-9B-shaped hybrid (Qwen3.5 text stack: 24 gated-delta-net + 8 gated
+    # full-attention layers; the shape of transformers' Qwen3_5TextConfig defaults)
+    "onejev16-9b": dict(_HYBRID_BASE, hidden=4096, layers=32, heads=16, kv_heads=4, head_dim=256,
+                        ffn=12288, vocab=248320, layer_types=hybrid_layer_types(32)),
     # BERT-base-shaped marker-head encoder (laya)
     "laya-bert": dict(_ENCODER_BASE, style="bert", hidden=768, layers=12, heads=12,
                       ffn=3072, vocab=30522, pad_id=0),
@@ -61,13 +84,32 @@ PRESETS = {
 
 
 def preset(name: str, **overrides) -> dict:
-    """A copy of a preset with keyword overrides (e.g. layers=2 for a parity case)."""
+    """A copy of a preset with keyword overrides (e.g. layers=2 for a parity case).
+    For hybrid presets a `layers` override without `layer_types` keeps the
+    preset's pattern (every 4th layer full attention, the last one included
+    when `layers` is a multiple of 4)."""
     if name not in PRESETS:
         raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")
     spec = copy.deepcopy(PRESETS[name])
     spec.update(overrides)
+    if spec.get("style") == "qwen3_5" and "layers" in overrides and "layer_types" not in overrides:
+        spec["layer_types"] = hybrid_layer_types(spec["layers"])
     spec["preset"] = name
     return spec
+
+
+def is_hybrid(spec: dict) -> bool:
+    return spec.get("style") == "qwen3_5"
+
+
+def full_attention_layers(spec: dict) -> list:
+    if not is_hybrid(spec):
+        return list(range(spec["layers"]))
+    return [i for i, t in enumerate(spec["layer_types"]) if t == "full_attention"]
+
+
+def rotary_dim(spec: dict) -> int:
+    return int(spec["head_dim"] * spec.get("partial_rotary", 1.0))
 
 
 def label_width(spec: dict) -> int:
@@ -75,16 +117,32 @@ def label_width(spec: dict) -> int:
 
 
 def qkv_width(spec: dict) -> int:
-    return (spec["heads"] + 2 * spec["kv_heads"]) * spec["head_dim"]
+    """Columns of the fused full-attention projection (q, k, v; plus the output
+    gate of a hybrid's gated attention)."""
+    gate = spec["heads"] if is_hybrid(spec) else 0
+    return (spec["heads"] + 2 * spec["kv_heads"] + gate) * spec["head_dim"]
+
+
+def gdn_dims(spec: dict) -> dict:
+    """Gated-delta-net sizes: key/value widths, conv channels, in_proj columns."""
+    kd = spec["lin_k_heads"] * spec["lin_k_dim"]
+    vd = spec["lin_v_heads"] * spec["lin_v_dim"]
+    conv = 2 * kd + vd
+    return dict(kd=kd, vd=vd, conv=conv, proj=conv + vd + 2 * spec["lin_v_heads"])
 
 
 def linear_flops_per_token(spec: dict) -> float:
     """Multiply-add FLOPs (2 per MAC) of every projection GEMM for one token."""
     d, f = spec["hidden"], spec["ffn"]
     if spec["arch"] == "decoder":
-        per_layer = d * qkv_width(spec) + spec["heads"] * spec["head_dim"] * d + 3 * d * f
-    else:
-        per_layer = 4 * d * d + 2 * d * f
+        full = d * qkv_width(spec) + spec["heads"] * spec["head_dim"] * d + 3 * d * f
+        if not is_hybrid(spec):
+            return 2.0 * full * spec["layers"]
+        g = gdn_dims(spec)
+        lin = d * g["proj"] + g["vd"] * d + 3 * d * f
+        n_full = len(full_attention_layers(spec))
+        return 2.0 * (full * n_full + lin * (spec["layers"] - n_full))
+    per_layer = 4 * d * d + 2 * d * f
     return 2.0 * per_layer * spec["layers"]
 
 
@@ -92,7 +150,8 @@ def attention_flops(spec: dict, n: int) -> float:
     """QK^T + PV FLOPs of one sequence of n tokens (causal counts n(n+1)/2 pairs)."""
     hd, h = spec["head_dim"] if spec["arch"] == "decoder" else spec["hidden"] // spec["heads"], spec["heads"]
     pairs = n * (n + 1) / 2 if spec["arch"] == "decoder" else float(n * n)
-    return 4.0 * hd * h * pairs * spec["layers"]
+    layers = len(full_attention_layers(spec)) if spec["arch"] == "decoder" else spec["layers"]
+    return 4.0 * hd * h * pairs * layers
 
 
 def weight_bytes(spec: dict) -> float:

@@ -93,8 +93,60 @@ def _lin(spec):
     return spec["init_std"] * SQRT3
 
 
+def hybrid_tensors(spec: dict):
+    """(name, shape, scale, offset) of a Qwen3.5 text stack (HF `Qwen3_5ForCausalLM` names).
+
+    Every `Qwen3_5RMSNorm` applies (1 + w) and is zero-initialised in HF, so its
+    synthetic w is U(-0.1, 0.1); the gated-delta-net output norm applies w
+    (ones-initialised).  `A_log` = log(A) with A in [1, e^2], `dt_bias` ~ 1,
+    the depthwise conv kernel U(-0.5, 0.5) (PyTorch's Conv1d bound 1/sqrt(4))."""
+    d, hd = spec["hidden"], spec["head_dim"]
+    nq, nkv, f = spec["heads"], spec["kv_heads"], spec["ffn"]
+    kd = spec["lin_k_heads"] * spec["lin_k_dim"]
+    vd = spec["lin_v_heads"] * spec["lin_v_dim"]
+    lv, ck = spec["lin_v_heads"], spec["conv_kernel"]
+    lin = _lin(spec)
+    n_scale = 0.1
+    out = [("model.embed_tokens.weight", (spec["vocab"], d), lin, 0.0)]
+    for i, kind in enumerate(spec["layer_types"]):
+        p = f"model.layers.{i}."
+        out += [(p + "input_layernorm.weight", (d,), n_scale, 0.0),
+                (p + "post_attention_layernorm.weight", (d,), n_scale, 0.0)]
+        if kind == "full_attention":
+            out += [
+                (p + "self_attn.q_proj.weight", (2 * nq * hd, d), lin, 0.0),
+                (p + "self_attn.k_proj.weight", (nkv * hd, d), lin, 0.0),
+                (p + "self_attn.v_proj.weight", (nkv * hd, d), lin, 0.0),
+                (p + "self_attn.o_proj.weight", (d, nq * hd), lin, 0.0),
+                (p + "self_attn.q_norm.weight", (hd,), n_scale, 0.0),
+                (p + "self_attn.k_norm.weight", (hd,), n_scale, 0.0),
+            ]
+        else:
+            a = p + "linear_attn."
+            out += [
+                (a + "in_proj_qkv.weight", (2 * kd + vd, d), lin, 0.0),
+                (a + "in_proj_z.weight", (vd, d), lin, 0.0),
+                (a + "in_proj_b.weight", (lv, d), lin, 0.0),
+                (a + "in_proj_a.weight", (lv, d), lin, 0.0),
+                (a + "conv1d.weight", (2 * kd + vd, 1, ck), 0.5, 0.0),
+                (a + "dt_bias", (lv,), 0.1, 1.0),
+                (a + "A_log", (lv,), 1.0, 1.0),
+                (a + "norm.weight", (spec["lin_v_dim"],), 0.1, 1.0),
+                (a + "out_proj.weight", (d, vd), lin, 0.0),
+            ]
+        out += [(p + "mlp.gate_proj.weight", (f, d), lin, 0.0),
+                (p + "mlp.up_proj.weight", (f, d), lin, 0.0),
+                (p + "mlp.down_proj.weight", (d, f), lin, 0.0)]
+    out.append(("model.norm.weight", (d,), n_scale, 0.0))
+    if not spec["tied"]:
+        out.append(("lm_head.weight", (spec["vocab"], d), lin, 0.0))
+    return out
+
+
 def decoder_tensors(spec: dict):
     """(name, shape, scale, offset) of every decoder tensor, HF Qwen3/Gemma names."""
+    if spec.get("style") == "qwen3_5":
+        return hybrid_tensors(spec)
     d, hd = spec["hidden"], spec["head_dim"]
     nq, nkv, f = spec["heads"], spec["kv_heads"], spec["ffn"]
     lin = _lin(spec)
