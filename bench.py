@@ -48,6 +48,9 @@ WORKLOAD = ("OneJev-9B-shaped text decisions: 40 layers, d=4096, 32/8 heads hd=1
 SHARED_WORKLOAD = ("OneJev-9B-shaped letter-branches decisions, 8 questions per state: rows of a state share "
                    "its prefix (declared prefix_len), state prefix clip(lognormal(6.5,0.5),128,3072) tokens, "
                    "question suffix U[40,160] tokens, 2-8 options")
+HYBRID_WORKLOAD = ("OneJev1.6-9B-shaped hybrid text decisions (Qwen3.5 text stack: 24 gated-delta-net + 8 gated "
+                   "full-attention layers, d=4096, attention 16/4 heads hd=256, linear 16/32 heads of 128, SwiGLU "
+                   "12288, vocab 248320); lengths clip(lognormal(6,0.7),32,4096), 2-8 options")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
 # full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
@@ -153,14 +156,14 @@ def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice"):
 def cpu_baseline_sample(spec, batch, layers_timed):
     """Time the oracle (fp32 numpy) on one decision through `layers_timed` of the
     model's layers and scale to the full depth; returns (decisions/s, sample text)."""
-    from oracle.decoder import DecoderOracle, rmsnorm, rope_tables
+    from oracle.decoder import DecoderOracle, rmsnorm
     orc = DecoderOracle(spec, layers=layers_timed, cache_layers=True)
     n = int(batch.rows[0].real_len)
     ids = batch.input_ids[:n]
     for i in range(layers_timed):
         orc.layer(i)  # generate weights outside the timed region
     t0 = time.perf_counter()
-    cos, sin = rope_tables(np.arange(n), spec["head_dim"], spec["rope_theta"])
+    cos, sin = orc.rope(n)
     h = orc.embed(ids)
     t1 = time.perf_counter()
     for i in range(layers_timed):
@@ -183,7 +186,7 @@ def run_reference(args, world, rank):
     import torch  # noqa: F401  (thread settings only)
     from verdict_b200 import spec as specs
     from verdict_b200.synth import with_labels
-    spec = with_labels(specs.preset("onejev-9b"))
+    spec = with_labels(specs.preset(args.model))
     batches = make_batches(0, args.warmup + args.steps, 1, spec["vocab"], args.seed)
     times = []
     for j, b in enumerate(batches):
@@ -197,7 +200,8 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "model": "onejev-9b", "decisions_per_step": 1,
+        "config": {"workload": WORKLOAD if args.model == "onejev-9b" else HYBRID_WORKLOAD, "model": args.model,
+                   "decisions_per_step": 1,
                    "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"per step 1 decision; {args.ref_layers} of 40 layers timed and scaled"},
@@ -225,6 +229,9 @@ def main():
                          "per state, rows of a state share the state prefix (prefix_len declared)")
     ap.add_argument("--fork", default="on", choices=["on", "off"],
                     help="compute shared prefixes once (on) or every row whole (off)")
+    ap.add_argument("--model", default="onejev-9b", choices=["onejev-9b", "onejev16-9b"],
+                    help="onejev-9b: the dense OneJev-9B shape (headline); onejev16-9b: the Qwen3.5-style hybrid "
+                         "(gated delta nets + gated attention)")
     ap.add_argument("--gemm", default="2sm", choices=["2sm", "1sm"],
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
     args = ap.parse_args()
@@ -250,7 +257,7 @@ def main():
     from verdict_b200.synth import with_labels
 
     over = {} if args.layers is None else {"layers": args.layers}
-    spec = with_labels(specs.preset("onejev-9b", **over))
+    spec = with_labels(specs.preset(args.model, **over))
     n_batches = args.warmup + args.steps
     batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed, args.workload)
     max_tokens = max(int(b.real_len().sum()) for b in batches)
@@ -429,7 +436,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
-            "config": {"workload": SHARED_WORKLOAD if shared else WORKLOAD, "model": "onejev-9b",
+            "config": {"workload": (SHARED_WORKLOAD if shared else WORKLOAD) if args.model == "onejev-9b"
+                       else HYBRID_WORKLOAD, "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
                        "computed_tokens_last_step": int(computed_tokens),

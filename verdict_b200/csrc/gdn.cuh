@@ -13,7 +13,7 @@
 //
 // gdn_conv_prep_kernel does the conv, the l2 norms and the gates for one token
 // per CTA; gdn_scan_kernel runs the recurrence for one (sequence, v head) per
-// CTA with one thread per state column (dk = dv = 128: 128 fp32 registers of
+// CTA with two threads per state column (dk = dv = 128: 64 fp32 registers of
 // state per thread), k and q of the next token staged in shared memory while
 // the current one is consumed, and applies the gated norm of token t in step
 // t + 1 (the head's sum of squares needs the CTA-wide reduction that step's
@@ -113,85 +113,123 @@ __global__ void __launch_bounds__(256) gdn_conv_prep_kernel(GdnParams p) {
   }
 }
 
-// One (sequence, v head) per CTA of 128 threads; thread j owns column j of the
-// head's state.
+// One (sequence, v head) per CTA of 256 threads; thread pair (2c, 2c+1) owns
+// column c of the head's state, each thread 64 of its 128 rows (64 fp32
+// registers), and the pair combines its two partial dot products with one
+// shuffle.  Every global load is issued one token ahead of its use (k and q two
+// tokens ahead, staged through shared memory one token ahead), so the
+// per-token critical path is the state arithmetic only.
 template <class T>
-__global__ void __launch_bounds__(128) gdn_scan_kernel(GdnParams p) {
-  __shared__ __align__(16) float kq[2][2][128];  // [buffer][k, q][dk]
-  __shared__ float red[2][4];                     // per-warp sums of o^2, by token parity
+__global__ void __launch_bounds__(256, 1) gdn_scan_kernel(GdnParams p) {
+  // [buffer][k, q][row half][64 rows + 4 pad]: the pad puts the two halves in
+  // different banks, so the two threads of a pair read without conflict.
+  __shared__ __align__(16) float kq[2][2][2][68];
+  __shared__ float red[2][8];  // per-warp sums of o^2, by token parity
   const int4 sg = p.segs[blockIdx.x];
   const int start = sg.x, len = sg.y;
   const int head = blockIdx.y;
   const int kh = head / (p.lv / p.lk);
-  const int j = threadIdx.x, warp = j >> 5, lane = j & 31;
+  const int tid = threadIdx.x, col = tid >> 1, half = tid & 1, warp = tid >> 5, lane = tid & 31;
   const T* qkv = static_cast<const T*>(p.qkv);
   const T* proj = static_cast<const T*>(p.proj);
   T* out = static_cast<T*>(p.out);
-  const int q_col = kh * 128, k_col = p.kd + kh * 128, v_col = 2 * p.kd + head * 128;
-  const float w_norm = p.norm_w[j];
+  // staging role: thread tid stages element (tid & 127) of k (tid < 128) or q
+  const int st_kind = tid >> 7, st_idx = tid & 127;
+  const int st_col = st_kind ? kh * 128 + st_idx : p.kd + kh * 128 + st_idx;
+  const int v_col = 2 * p.kd + head * 128 + col;
+  const int z_col = p.col_z + head * 128 + col;
+  const float w_norm = p.norm_w[col];
+  if (len <= 0) return;
 
-  float S[128];
+  auto row = [&](int t) { return static_cast<size_t>(start + t); };
+  float S[64];
 #pragma unroll
-  for (int i = 0; i < 128; ++i) S[i] = 0.0f;
+  for (int i = 0; i < 64; ++i) S[i] = 0.0f;
 
-  auto stage = [&](int t, int b) {
-    const size_t row = static_cast<size_t>(start + t) * p.ld_qkv;
-    kq[b][0][j] = Elem<T>::to(qkv[row + k_col + j]);
-    kq[b][1][j] = Elem<T>::to(qkv[row + q_col + j]);
-  };
-  // The gated norm of the token whose o this thread holds: its head's sum of
-  // squares was published in red[parity] before the last barrier.
-  auto finish = [&](int t, float o) {
-    const int b = t & 1;
-    const float ss = red[b][0] + red[b][1] + red[b][2] + red[b][3];
-    const float rstd = rsqrtf(ss / 128.0f + p.eps);
-    const size_t tok = static_cast<size_t>(start + t);
-    const float z = Elem<T>::to(proj[tok * p.ld_proj + p.col_z + head * 128 + j]);
-    out[tok * p.ld_out + head * 128 + j] = Elem<T>::from(o * rstd * w_norm * silu_f(z));
-  };
-
-  if (len > 0) stage(0, 0);
-  __syncthreads();
+  kq[0][st_kind][st_idx >> 6][st_idx & 63] = Elem<T>::to(qkv[row(0) * p.ld_qkv + st_col]);
+  T st_next = Elem<T>::from(0.0f);
+  if (len > 1) st_next = qkv[row(1) * p.ld_qkv + st_col];
+  T v_cur = qkv[row(0) * p.ld_qkv + v_col];
+  float g_cur = p.g[row(0) * p.lv + head], b_cur = p.beta[row(0) * p.lv + head];
+  T z_cur = proj[row(0) * p.ld_proj + z_col];
+  T z_prev = z_cur;
   float o_prev = 0.0f;
+  __syncthreads();
+
   for (int t = 0; t < len; ++t) {
     const int b = t & 1;
-    if (t + 1 < len) stage(t + 1, b ^ 1);
-    if (t > 0) finish(t - 1, o_prev);
-    const size_t tok = static_cast<size_t>(start + t);
-    const float decay = __expf(p.g[tok * p.lv + head]);
-    const float beta = p.beta[tok * p.lv + head];
-    const float v = Elem<T>::to(qkv[tok * p.ld_qkv + v_col + j]);
-    const float4* k4 = reinterpret_cast<const float4*>(kq[b][0]);
-    const float4* q4 = reinterpret_cast<const float4*>(kq[b][1]);
-    float kv = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float4 k = k4[i];
-      S[4 * i + 0] *= decay;
-      S[4 * i + 1] *= decay;
-      S[4 * i + 2] *= decay;
-      S[4 * i + 3] *= decay;
-      kv += S[4 * i + 0] * k.x + S[4 * i + 1] * k.y + S[4 * i + 2] * k.z + S[4 * i + 3] * k.w;
+    if (t + 1 < len) kq[b ^ 1][st_kind][st_idx >> 6][st_idx & 63] = Elem<T>::to(st_next);
+    if (t + 2 < len) st_next = qkv[row(t + 2) * p.ld_qkv + st_col];
+    T v_nxt = v_cur, z_nxt = z_cur;
+    float g_nxt = g_cur, b_nxt = b_cur;
+    if (t + 1 < len) {
+      v_nxt = qkv[row(t + 1) * p.ld_qkv + v_col];
+      g_nxt = p.g[row(t + 1) * p.lv + head];
+      b_nxt = p.beta[row(t + 1) * p.lv + head];
+      z_nxt = proj[row(t + 1) * p.ld_proj + z_col];
     }
-    const float delta = (v - kv) * beta;
-    float o = 0.0f;
+    // The gated norm of token t-1 (its head's sum of squares is in red[b ^ 1]).
+    if (t > 0 && half == 0) {
+      float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float4 k = k4[i], q = q4[i];
-      S[4 * i + 0] += k.x * delta;
-      S[4 * i + 1] += k.y * delta;
-      S[4 * i + 2] += k.z * delta;
-      S[4 * i + 3] += k.w * delta;
-      o += S[4 * i + 0] * q.x + S[4 * i + 1] * q.y + S[4 * i + 2] * q.z + S[4 * i + 3] * q.w;
+      for (int w = 0; w < 8; ++w) ss += red[b ^ 1][w];
+      const float rstd = rsqrtf(ss / 128.0f + p.eps);
+      out[row(t - 1) * p.ld_out + head * 128 + col] =
+          Elem<T>::from(o_prev * rstd * w_norm * silu_f(Elem<T>::to(z_prev)));
     }
-    float ss = o * o;
+    // Token t.
+    const float decay = __expf(g_cur);
+    const float4* k4 = reinterpret_cast<const float4*>(kq[b][0][half]);
+    const float4* q4 = reinterpret_cast<const float4*>(kq[b][1][half]);
+    float kv0 = 0.0f, kv1 = 0.0f;
 #pragma unroll
-    for (int s = 16; s > 0; s >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s);
+    for (int i = 0; i < 16; i += 2) {
+      const float4 ka = k4[i], kb = k4[i + 1];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) S[4 * i + e] *= decay;
+      kv0 += S[4 * i + 0] * ka.x + S[4 * i + 1] * ka.y + S[4 * i + 2] * ka.z + S[4 * i + 3] * ka.w;
+      kv1 += S[4 * i + 4] * kb.x + S[4 * i + 5] * kb.y + S[4 * i + 6] * kb.z + S[4 * i + 7] * kb.w;
+    }
+    float kv = kv0 + kv1;
+    kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+    const float delta = (Elem<T>::to(v_cur) - kv) * b_cur;
+    float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const float4 ka = k4[i], kb = k4[i + 1], qa = q4[i], qb = q4[i + 1];
+      S[4 * i + 0] += ka.x * delta;
+      S[4 * i + 1] += ka.y * delta;
+      S[4 * i + 2] += ka.z * delta;
+      S[4 * i + 3] += ka.w * delta;
+      S[4 * i + 4] += kb.x * delta;
+      S[4 * i + 5] += kb.y * delta;
+      S[4 * i + 6] += kb.z * delta;
+      S[4 * i + 7] += kb.w * delta;
+      o0 += S[4 * i + 0] * qa.x + S[4 * i + 1] * qa.y + S[4 * i + 2] * qa.z + S[4 * i + 3] * qa.w;
+      o1 += S[4 * i + 4] * qb.x + S[4 * i + 5] * qb.y + S[4 * i + 6] * qb.z + S[4 * i + 7] * qb.w;
+    }
+    float o = o0 + o1;
+    o += __shfl_xor_sync(0xffffffffu, o, 1);
+    float ss = half == 0 ? o * o : 0.0f;
+#pragma unroll
+    for (int sft = 16; sft > 0; sft >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sft);
     if (lane == 0) red[b][warp] = ss;
     o_prev = o;
+    z_prev = z_cur;
+    v_cur = v_nxt;
+    g_cur = g_nxt;
+    b_cur = b_nxt;
+    z_cur = z_nxt;
     __syncthreads();  // kq[b ^ 1] staged, red[b] published; kq[b] and red[b ^ 1] free again
   }
-  if (len > 0) finish(len - 1, o_prev);
+  if (half == 0) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) ss += red[(len - 1) & 1][w];
+    const float rstd = rsqrtf(ss / 128.0f + p.eps);
+    out[row(len - 1) * p.ld_out + head * 128 + col] =
+        Elem<T>::from(o_prev * rstd * w_norm * silu_f(Elem<T>::to(z_prev)));
+  }
 }
 
 }  // namespace vd

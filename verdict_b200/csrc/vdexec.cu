@@ -1495,7 +1495,7 @@ static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan
   // per token and value head: decay + two rank-1 passes over the 128 x 128 state
   const double flops = 4.0 * ntok * s.lin_v_heads * s.lin_k_dim * s.lin_v_dim;
   launch(H, VD_K_GDN, flops, [&] {
-    gdn_scan_kernel<T><<<dim3(P.n_seg, s.lin_v_heads), 128, 0, H->stream>>>(g);
+    gdn_scan_kernel<T><<<dim3(P.n_seg, s.lin_v_heads), 256, 0, H->stream>>>(g);
   });
 }
 
