@@ -26,7 +26,9 @@ def load(path):
     return z, spec, batch
 
 
-DEC = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz")) if "_marker_" not in p and "fork_" not in p)
+DEC = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
+             if "_marker_" not in p and "fork_" not in p and "von_" not in p)
+VON = sorted(glob.glob(os.path.join(GOLDEN, "von_*.npz")))
 ENC = sorted(glob.glob(os.path.join(GOLDEN, "*_marker_*.npz")))
 
 
@@ -72,3 +74,13 @@ def test_oracle_is_sensitive():
     bad = dict(spec, rope_theta=spec["rope_theta"] * 0.5)
     got = DecoderOracle(bad).infer(batch)
     assert np.abs(got - z["logits"]).max() > 1e-3
+
+
+@pytest.mark.parametrize("path", VON, ids=os.path.basename)
+def test_von_oracle_matches_hf_modernbert(path):
+    """Independent-options fixtures: HF ModernBertModel with the reference's
+    option masks and positions (tests/golden/make_von_golden.py)."""
+    from oracle.von import VonOracle
+    z, spec, batch = load(path)
+    got = VonOracle(spec).infer(batch)
+    np.testing.assert_allclose(got, z["logits"], atol=2e-5, rtol=0)

@@ -62,7 +62,7 @@ def assert_decoder_parity(got_lp, ref_logits, nopts, tol=LOGPROB_TOL):
 
 
 DECODER_FIXTURES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                          if "_marker_" not in p and "fork_" not in p)
+                          if "_marker_" not in p and "fork_" not in p and "von_" not in p)
 ENCODER_FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*_marker_*.npz")))
 
 

@@ -165,6 +165,30 @@ def shared_prefix_rows(rng: np.random.Generator, n: int, vocab: int, *, per_stat
     return [rows[i] for i in order]
 
 
+def von_rows(rng: np.random.Generator, n: int, vocab: int, *, cls_id: int = 50281, sep_id: int = 50282,
+             mask_id: int = 50284, id_low: int = 5, k_low: int = 2, k_high: int = 6,
+             prefix_low: int = 16, prefix_high: int = 200, desc_high: int = 12) -> list:
+    """Independent-options rows laid out like `independent_options::build_sequence`
+    (`src/family/independent_options.rs:86-130`): [CLS] question+state [SEP]
+    ([MASK] option text)* [SEP], one marker per [MASK].  Prefix U[16, 200]
+    tokens, 2-6 options of U[1, 12] tokens each."""
+    rows = []
+    special = min(cls_id, sep_id, mask_id)
+    top = min(vocab, special) if special > id_low else vocab  # text ids avoid the special ids
+    for _ in range(n):
+        prefix = int(rng.integers(prefix_low, prefix_high + 1))
+        k = int(rng.integers(k_low, k_high + 1))
+        ids = [cls_id] + rng.integers(id_low, top, size=prefix).tolist() + [sep_id]
+        markers = []
+        for _ in range(k):
+            markers.append(len(ids))
+            ids.append(mask_id)
+            ids += rng.integers(id_low, top, size=int(rng.integers(1, desc_high + 1))).tolist()
+        ids.append(sep_id)
+        rows.append(BuiltSequence(ids=ids, markers=markers, nopts=[], full_len=len(ids)))
+    return rows
+
+
 def encoder_rows(rng: np.random.Generator, n: int, vocab: int, *, lengths: str,
                  cls_id: int, sep_id: int, id_low: int, k_low: int = 2, k_high: int = 6,
                  max_len: int = 512) -> list:

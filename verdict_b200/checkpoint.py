@@ -134,6 +134,29 @@ def encoder_spec_from_config(cfg: dict, head_layers: int = 2) -> dict:
     )
 
 
+def von_spec_from_config(cfg: dict) -> dict:
+    """The spec keys of an independent-options model's ModernBERT encoder config."""
+    if cfg.get("norm_bias") or cfg.get("attention_bias") or cfg.get("mlp_bias"):
+        raise ValueError("modernbert checkpoints with norm / attention / MLP biases are not supported")
+    if cfg.get("hidden_activation", "gelu") != "gelu":
+        raise ValueError(f"unsupported modernbert activation {cfg.get('hidden_activation')!r}")
+    rp = cfg.get("rope_parameters") or {}
+    g = (rp.get("full_attention") or {}).get("rope_theta", cfg.get("global_rope_theta", 160000.0))
+    l = (rp.get("sliding_attention") or {}).get("rope_theta", cfg.get("local_rope_theta", 10000.0))
+    layers = int(cfg["num_hidden_layers"])
+    types = cfg.get("layer_types")
+    if not types:
+        from .spec import modernbert_layer_types
+        types = modernbert_layer_types(layers, int(cfg.get("global_attn_every_n_layers", 3)))
+    return dict(
+        arch="encoder", style="modernbert", family="independent_options", hidden=int(cfg["hidden_size"]),
+        layers=layers, heads=int(cfg["num_attention_heads"]), ffn=int(cfg["intermediate_size"]),
+        vocab=int(cfg["vocab_size"]), max_pos=int(cfg.get("max_position_embeddings", 8192)),
+        ln_eps=float(cfg.get("norm_eps", 1e-5)), pad_id=int(cfg.get("pad_token_id") or 0), head_layers=0,
+        type_vocab=0, global_theta=float(g), local_theta=float(l),
+        sliding_window=int(cfg.get("local_attention", 128)) // 2, layer_types=list(types))
+
+
 def _load_tokenizer(path: str):
     from transformers import AutoTokenizer
     tok_dir = os.path.join(path, "tokenizer")
@@ -162,7 +185,9 @@ def spec_from_checkpoint(path: str, *, family: str | None = None, label_ids=None
     cfg_path = enc_cfg if os.path.isfile(enc_cfg) else os.path.join(path, "config.json")
     with open(cfg_path) as f:
         cfg = json.load(f)
-    if cfg.get("model_type") in ("bert", "xlm-roberta"):
+    if cfg.get("model_type") == "modernbert":
+        spec = von_spec_from_config(cfg)
+    elif cfg.get("model_type") in ("bert", "xlm-roberta"):
         spec = encoder_spec_from_config(cfg, 2 if head_layers is None else head_layers)
     else:
         spec = decoder_spec_from_config(cfg)
@@ -259,6 +284,16 @@ def _hf_config(spec: dict) -> dict:
             if cfg["attention_bias"] is None:
                 del cfg["attention_bias"]
         return cfg
+    if spec["style"] == "modernbert":
+        return dict(
+            model_type="modernbert", architectures=["ModernBertModel"], hidden_size=spec["hidden"],
+            num_hidden_layers=spec["layers"], num_attention_heads=spec["heads"], intermediate_size=spec["ffn"],
+            vocab_size=spec["vocab"], max_position_embeddings=spec["max_pos"], norm_eps=spec["ln_eps"],
+            norm_bias=False, attention_bias=False, mlp_bias=False, hidden_activation="gelu",
+            pad_token_id=spec["pad_id"], layer_types=list(spec["layer_types"]),
+            local_attention=2 * spec["sliding_window"],
+            rope_parameters={"full_attention": {"rope_type": "default", "rope_theta": spec["global_theta"]},
+                             "sliding_attention": {"rope_type": "default", "rope_theta": spec["local_theta"]}})
     return dict(
         model_type="bert" if spec["style"] == "bert" else "xlm-roberta", hidden_size=spec["hidden"],
         num_hidden_layers=spec["layers"], num_attention_heads=spec["heads"], intermediate_size=spec["ffn"],

@@ -41,6 +41,12 @@ struct AttnParams {
   int group;          // query heads per K/V head
   float scale_log2;   // softmax scale * log2(e)
   int gate_col0;      // >= 0: output *= sigmoid(qkv[row, gate_col0 + head*HD + c]) (gated attention)
+  // Independent-options masking (null: none): per packed token its option
+  // (-1 = shared) and option-invariant position; a token attends to shared
+  // tokens and to its own option, within `window` positions when window > 0.
+  const int* opt_id;
+  const int* opt_pos;
+  int window;
 };
 
 template <int HD>
@@ -158,8 +164,30 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
 
     // Mask keys past the segment end and (causal, own keys only) past the query row.
     const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
-    const bool need_mask = (kv0 + Cfg::BN > seg_len) || (CAUSAL && !in_pre && kv0 + Cfg::BN > tile.q_start);
-    if (need_mask) {
+    const bool need_mask = (kv0 + Cfg::BN > seg_len) || (CAUSAL && !in_pre && kv0 + Cfg::BN > tile.q_start) ||
+                           p.opt_id != nullptr;
+    if (need_mask && p.opt_id != nullptr) {
+      // Option masks (bidirectional encoders only: no prefix segment here).
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kv = kv0 + nb * 8 + ((lane & 3) << 1) + (e & 1);
+          const int qr = q_row_a + ((e >> 1) << 3);
+          bool dead = kv >= seg_len || qr >= tile.seq_len;
+          if (!dead) {
+            const int kt = tile.seq_start + kv, qt = tile.seq_start + qr;
+            const int ok = __ldg(p.opt_id + kt), oq = __ldg(p.opt_id + qt);
+            dead = oq == -1 ? ok != -1 : (ok != -1 && ok != oq);
+            if (!dead && p.window > 0) {
+              const int d = __ldg(p.opt_pos + qt) - __ldg(p.opt_pos + kt);
+              dead = d > p.window || -d > p.window;
+            }
+          }
+          if (dead) s[nb][e] = -INFINITY;
+        }
+      }
+    } else if (need_mask) {
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll

@@ -22,13 +22,12 @@ __device__ __forceinline__ float load_ckpt(const void* __restrict__ src, int dty
 // magnitudes >= 2^-14.
 template <class T>
 __global__ void convert_rows_kernel(T* __restrict__ dst, const void* __restrict__ src, int src_dtype, int64_t r0,
-                                    int64_t n_rows, int64_t cols, int64_t group, int64_t dst_group_stride,
-                                    int64_t dst_row_off, int64_t alt_off) {
+                                    int64_t n_rows, int64_t cols, RowPlace place) {
   const int64_t total = n_rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = r0 + i / cols, c = i % cols;
-    const int64_t dr = dst_row(r, group, dst_group_stride, dst_row_off, alt_off);
+    const int64_t dr = dst_row(r, place);
     dst[dr * cols + c] = Elem<T>::from(load_ckpt(src, src_dtype, i));
   }
 }

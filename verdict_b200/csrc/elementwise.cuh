@@ -290,6 +290,53 @@ __global__ void __launch_bounds__(NT)
   for (int j = threadIdx.x; j < width; j += NT) orow[j] = j < n ? lg[j] - shift : kSentinel;
 }
 
+// Independent-options layout of every packed token (`independent_options_tensors`,
+// src/engine.rs:544-568): option j spans [marker_j, marker_{j+1}) (the last one
+// up to the row's final token, exclusive); inside a span the position restarts
+// at the first marker, elsewhere it is the column; tokens outside spans get
+// option -1.  Markers are the row's live slots in order.  A row whose first
+// marker is missing or outside the row is reported as a slot error.
+__global__ void von_layout_kernel(const PackSeg* __restrict__ segs, int n_seg, const int64_t* __restrict__ mpos,
+                                  const uint8_t* __restrict__ mmask, int k, int* __restrict__ opt_id,
+                                  int* __restrict__ opt_pos, int* err) {
+  const int si = blockIdx.y;
+  if (si >= n_seg) return;
+  const PackSeg sg = segs[si];
+  const int64_t* mp = mpos + static_cast<int64_t>(sg.src_row) * k;
+  const uint8_t* mm = mmask + static_cast<int64_t>(sg.src_row) * k;
+  int first = -1;
+  for (int j = 0; j < k; ++j)
+    if (mm[j]) {
+      first = static_cast<int>(mp[j]);
+      break;
+    }
+  if (first < 0 || first >= sg.len) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) record_error(err, kErrSlotRange);
+    first = sg.len;  // no spans
+  }
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < sg.len; c += gridDim.x * blockDim.x) {
+    int option = -1, pos = c, j = 0;
+    for (int s = 0; s < k && first < sg.len; ++s) {
+      if (!mm[s]) continue;
+      const int start = static_cast<int>(mp[s]);
+      int end = sg.len - 1;
+      for (int t = s + 1; t < k; ++t)
+        if (mm[t]) {
+          end = static_cast<int>(mp[t]);
+          break;
+        }
+      end = min(end, sg.len);
+      if (c >= start && c < end) {
+        option = j;
+        pos = first + (c - start);
+      }
+      ++j;
+    }
+    opt_id[sg.start + c] = option;
+    opt_pos[sg.start + c] = pos;
+  }
+}
+
 // Encoder markers: flat token index of every (row, slot) pair, clamped like
 // `marker_pos.clamp(min=0)`; a live marker outside its row is an input error.
 __global__ void marker_index_kernel(const int* __restrict__ cu, const int64_t* __restrict__ marker_pos,

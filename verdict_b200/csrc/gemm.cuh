@@ -298,7 +298,21 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
     // rotary chunk pairs.  head_dim 256 (one head per 256-wide tile): the warps
     // split its four chunk pairs.
     // Columns past the q and k blocks (v, and a hybrid's output gate) are stored as they are.
-    if (p.head_dim == 128) {
+    if (p.head_dim == 64) {
+      // head_dim 64 (ModernBERT): BN / 64 heads per tile, each warp half of them;
+      // one rotary pair per head (columns [0, 32) with [32, 64)).
+      constexpr int HEADS = BN / 64;
+#pragma unroll 1
+      for (int hh = 0; hh < HEADS / 2; ++hh) {
+        const int h = half * (HEADS / 2) + hh;
+        const int col0 = n0 + h * 64;
+        const uint32_t tb = taddr + h * 64;
+        if (col0 < p.q_cols + p.k_cols)
+          epi_head_rope<64, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, 0, 1);
+        else
+          epi_store_chunks<T>(o, tb, col0, p, 0, 2);
+      }
+    } else if (p.head_dim == 128) {
       constexpr int HEADS = BN / 128;
       const int h = HEADS == 2 ? half : 0;
       const int col0 = n0 + h * 128;

@@ -26,17 +26,28 @@ __device__ __forceinline__ __nv_bfloat16 synth_bf16(uint64_t base, uint64_t i, f
   return __float2bfloat16_rn(v);
 }
 
-// Destination row of source row r: (r / group) * stride + (r % group) + off.
-// group = n_rows with stride 0 is a plain copy; group 128 with stride 256
-// interleaves gate/up blocks for the fused gated-MLP GEMM.  With alt_off >= 0
-// the groups alternate between two blocks: group b goes to (b / 2) * stride +
-// (b odd ? alt_off : off) — the per-head [query, gate] rows of a gated
-// attention's q_proj split into a query block and a gate block.
-__host__ __device__ __forceinline__ int64_t dst_row(int64_t r, int64_t group, int64_t stride, int64_t off,
-                                                    int64_t alt_off) {
-  if (alt_off < 0) return (r / group) * stride + (r % group) + off;
-  const int64_t b = r / group;
-  return (b >> 1) * stride + ((b & 1) ? alt_off : off) + (r % group);
+// Where the rows of a source tensor land in a fused weight matrix.  Source
+// row r goes to (r / group) * stride + (r % group) + off: group = n_rows with
+// stride 0 is a plain copy; group 128 with stride 256 interleaves gate/up
+// blocks for the fused gated-MLP GEMM.  With alt_off >= 0 the groups alternate
+// between two blocks: group b goes to (b / 2) * stride + (b odd ? alt_off :
+// off) — the per-head [query, gate] rows of a gated attention's q_proj split
+// into a query block and a gate block.  With part_rows > 0 the source is
+// parts of part_rows rows, part p placed as above plus p * part_off — the
+// [input; gate] halves of a GeGLU Wi interleaved into gate/up blocks.
+struct RowPlace {
+  int64_t group = 1, stride = 0, off = 0, alt_off = -1, part_rows = 0, part_off = 0;
+};
+
+__host__ __device__ __forceinline__ int64_t dst_row(int64_t r, const RowPlace& p) {
+  int64_t extra = 0;
+  if (p.part_rows > 0) {
+    extra = (r / p.part_rows) * p.part_off;
+    r %= p.part_rows;
+  }
+  if (p.alt_off < 0) return (r / p.group) * p.stride + (r % p.group) + p.off + extra;
+  const int64_t b = r / p.group;
+  return (b >> 1) * p.stride + ((b & 1) ? p.alt_off : p.off) + (r % p.group) + extra;
 }
 
 // Rows r of a [n_rows, cols] source tensor land at dst_row(r) of a row-major
@@ -45,13 +56,12 @@ __host__ __device__ __forceinline__ int64_t dst_row(int64_t r, int64_t group, in
 // subnormal grid, an absolute change of at most 2^-25).
 template <class T>
 __global__ void synth_rows_kernel(T* __restrict__ dst, int64_t n_rows, int64_t cols, uint64_t base, float scale,
-                                  float offset, int64_t group, int64_t dst_group_stride, int64_t dst_row_off,
-                                  int64_t alt_off) {
+                                  float offset, RowPlace place) {
   const int64_t total = n_rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / cols, c = i - r * cols;
-    const int64_t dr = dst_row(r, group, dst_group_stride, dst_row_off, alt_off);
+    const int64_t dr = dst_row(r, place);
     dst[dr * cols + c] = Elem<T>::from(__bfloat162float(synth_bf16(base, static_cast<uint64_t>(i), scale, offset)));
   }
 }

@@ -77,6 +77,11 @@ struct ModelSpec {
   // hybrid (Qwen3.5) stacks: per-layer token mixer and gated-delta-net sizes
   std::vector<char> linear_layer;  // 1: gated delta net, 0: full attention
   double partial_rotary = 1.0;
+  // independent-options encoders (ModernBERT): sliding-window layers and RoPE thetas
+  std::vector<char> sliding_layer;  // 1: sliding window, 0: full attention
+  double global_theta = 160000.0, local_theta = 10000.0;
+  int sliding_window = 64;
+  bool von() const { return style == "modernbert"; }
   int lin_k_heads = 0, lin_v_heads = 0, lin_k_dim = 128, lin_v_dim = 128, conv_kernel = 4;
 
   bool decoder() const { return arch == "decoder"; }
@@ -143,7 +148,8 @@ static ModelSpec parse_spec(const Json& j) {
       fail(VD_ESPEC, "decoder spec needs the option-label table \"label_ids\"");
     for (const Json& v : j.at("label_ids").arr) s.label_ids.push_back(static_cast<int>(v.num));
   } else {
-    s.family = j.string_or("family", "marker_head");
+    s.family = j.string_or("family", s.style == "modernbert" ? "independent_options" : "marker_head");
+    std::replace(s.family.begin(), s.family.end(), '-', '_');
     s.kv_heads = s.heads;
     s.head_dim = s.hidden / s.heads;
     s.max_pos = static_cast<int>(j.integer_or("max_pos", 512));
@@ -151,6 +157,19 @@ static ModelSpec parse_spec(const Json& j) {
     s.pad_id = static_cast<int>(j.integer_or("pad_id", 0));
     s.head_layers = static_cast<int>(j.integer_or("head_layers", 2));
     s.ln_eps = j.number_or("ln_eps", 1e-12);
+    if (s.von()) {
+      if (!j.has("layer_types") || j.at("layer_types").kind != Json::Array)
+        fail(VD_ESPEC, "a modernbert spec needs \"layer_types\"");
+      for (const Json& v : j.at("layer_types").arr) {
+        if (v.str == "sliding_attention") s.sliding_layer.push_back(1);
+        else if (v.str == "full_attention") s.sliding_layer.push_back(0);
+        else fail(VD_ESPEC, "unknown layer type \"" + v.str + "\"");
+      }
+      s.global_theta = j.number_or("global_theta", 160000.0);
+      s.local_theta = j.number_or("local_theta", 10000.0);
+      s.sliding_window = static_cast<int>(j.integer_or("sliding_window", 64));
+      s.head_layers = 0;
+    }
   }
   return s;
 }
@@ -202,6 +221,49 @@ static Json spec_from_hf_config(const Json& c) {
     if (!c.has(k) || c.at(k).kind != Json::Number) fail(VD_ESPEC, std::string("HF config has no number \"") + k + "\"");
     return c.at(k).num;
   };
+  if (mt == "modernbert") {
+    const double layers = need_num("num_hidden_layers");
+    o.obj["arch"] = jstr("encoder");
+    o.obj["style"] = jstr("modernbert");
+    o.obj["hidden"] = jnum(need_num("hidden_size"));
+    o.obj["layers"] = jnum(layers);
+    o.obj["heads"] = jnum(need_num("num_attention_heads"));
+    o.obj["ffn"] = jnum(need_num("intermediate_size"));
+    o.obj["vocab"] = jnum(need_num("vocab_size"));
+    o.obj["max_pos"] = jnum(c.number_or("max_position_embeddings", 8192));
+    o.obj["ln_eps"] = jnum(c.number_or("norm_eps", 1e-5));
+    o.obj["pad_id"] = jnum(c.number_or("pad_token_id", 0));
+    if (c.boolean_or("norm_bias", false) || c.boolean_or("attention_bias", false) || c.boolean_or("mlp_bias", false))
+      fail(VD_ESPEC, "modernbert checkpoints with norm / attention / MLP biases are not supported");
+    const std::string act = c.string_or("hidden_activation", "gelu");
+    if (act != "gelu") fail(VD_ESPEC, "unsupported modernbert activation \"" + act + "\"");
+    double g_theta = c.number_or("global_rope_theta", 160000.0), l_theta = c.number_or("local_rope_theta", 10000.0);
+    if (c.has("rope_parameters") && c.at("rope_parameters").kind == Json::Object) {
+      const Json& rp = c.at("rope_parameters");
+      for (const char* kind : {"full_attention", "sliding_attention"}) {
+        if (!rp.has(kind) || rp.at(kind).kind != Json::Object) continue;
+        const Json& r = rp.at(kind);
+        if (r.string_or("rope_type", "default") != "default") fail(VD_ESPEC, "rope scaling is not supported");
+        if (std::string(kind) == "full_attention") g_theta = r.number_or("rope_theta", g_theta);
+        else l_theta = r.number_or("rope_theta", l_theta);
+      }
+    }
+    o.obj["global_theta"] = jnum(g_theta);
+    o.obj["local_theta"] = jnum(l_theta);
+    o.obj["sliding_window"] = jnum(c.number_or("local_attention", 128) / 2);
+    Json types;
+    types.kind = Json::Array;
+    if (c.has("layer_types") && c.at("layer_types").kind == Json::Array) {
+      types = c.at("layer_types");
+    } else {
+      const int every = static_cast<int>(c.number_or("global_attn_every_n_layers", 3));
+      for (int i = 0; i < static_cast<int>(layers); ++i)
+        types.arr.push_back(jstr(i % every ? "sliding_attention" : "full_attention"));
+    }
+    o.obj["layer_types"] = types;
+    o.obj["family"] = jstr("independent_options");
+    return o;
+  }
   if (mt == "bert" || mt == "xlm-roberta") {
     const std::string pe = c.string_or("position_embedding_type", "absolute");
     if (pe != "absolute") fail(VD_ESPEC, "only absolute position embeddings are supported, not " + pe);
@@ -414,7 +476,14 @@ static void validate_spec(const ModelSpec& s) {
     need(!s.label_ids.empty(), "empty label table");
     for (int id : s.label_ids) need(id >= 0 && id < s.vocab, "label id outside the vocabulary");
   } else {
-    need(s.style == "bert" || s.style == "xlmr", "encoder style must be bert or xlmr");
+    need(s.style == "bert" || s.style == "xlmr" || s.style == "modernbert",
+         "encoder style must be bert, xlmr or modernbert");
+    if (s.von()) {
+      need(static_cast<int>(s.sliding_layer.size()) == s.layers, "layer_types must list every layer");
+      need(s.family == "independent_options", "a modernbert encoder serves the independent_options family");
+      need(s.sliding_window > 0, "sliding_window must be positive");
+      need((3 * s.hidden) % 128 == 0, "3 * hidden must be a multiple of 128");
+    }
     need(s.hidden % s.heads == 0 && s.hidden / s.heads == 64, "encoder head size must be 64");
     need(s.hidden % 64 == 0, "encoder hidden must be a multiple of 64");
   }
@@ -515,6 +584,7 @@ struct EncLayer {
   bool pre_norm = false;
   int act = kActGeluErf;
   float eps = 1e-12f;
+  bool sliding = false;  // ModernBERT local layer
 };
 
 struct Handle;
@@ -576,6 +646,11 @@ struct vd_handle {
   CUtensorMap out_qkv, out_act, out_act2, out_h, out_h_s, out_act_s, out_mhid;
   // gated-delta-net workspace (hybrid stacks)
   int ld_qkv = 0;        // row stride of qkv (elements)
+  // independent-options encoders: per-token option and option-invariant
+  // position, the local-layer RoPE table, a zero bias for bias-free LayerNorms
+  int *von_opt = nullptr, *von_pos = nullptr;
+  float2* rope_local = nullptr;
+  float* zero_d = nullptr;
   void* proj = nullptr;  // 16-bit [T, gdn_proj]
   float *gdn_g = nullptr, *gdn_beta = nullptr;
   CUtensorMap out_proj;
@@ -715,10 +790,10 @@ static void release_checkpoint(vd_handle* H) {
 
 template <class T>
 static void fill_rows_t(vd_handle* H, T* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
-                        float offset, int64_t group, int64_t stride, int64_t off, int64_t alt_off) {
+                        float offset, const RowPlace& place) {
   if (!H->ckpt) {
     synth_rows_kernel<T><<<grid_for(rows * cols), 256, 0, H->stream>>>(
-        dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, group, stride, off, alt_off);
+        dst, rows, cols, tensor_base(H->spec.seed, name), scale, offset, place);
     return;
   }
   const StTensor& t = ckpt_tensor(H, name, {rows, cols});
@@ -727,26 +802,32 @@ static void fill_rows_t(vd_handle* H, T* dst, const std::string& name, int64_t r
   for (int64_t r0 = 0; r0 < rows; r0 += slice) {
     const int64_t n = std::min(slice, rows - r0);
     const void* src = stage_bytes(H, t.data + static_cast<size_t>(r0) * row_bytes, static_cast<size_t>(n) * row_bytes);
-    convert_rows_kernel<T><<<grid_for(n * cols), 256, 0, H->stream>>>(dst, src, t.dtype, r0, n, cols, group, stride,
-                                                                       off, alt_off);
+    convert_rows_kernel<T><<<grid_for(n * cols), 256, 0, H->stream>>>(dst, src, t.dtype, r0, n, cols, place);
   }
 }
 
 // A 16-bit tensor in the element type `f16` selects (embedding tables are always bf16).
 static void fill_w(vd_handle* H, void* dst, bool f16, const std::string& name, int64_t rows, int64_t cols,
                    float scale, float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0,
-                   int64_t alt_off = -1) {
-  if (group == 0) group = rows;
-  if (f16) fill_rows_t(H, static_cast<__half*>(dst), name, rows, cols, scale, offset, group, stride, off, alt_off);
-  else fill_rows_t(H, static_cast<__nv_bfloat16*>(dst), name, rows, cols, scale, offset, group, stride, off, alt_off);
+                   int64_t alt_off = -1, int64_t part_rows = 0, int64_t part_off = 0) {
+  RowPlace place;
+  place.group = group == 0 ? rows : group;
+  place.stride = stride;
+  place.off = off;
+  place.alt_off = alt_off;
+  place.part_rows = part_rows;
+  place.part_off = part_off;
+  if (f16) fill_rows_t(H, static_cast<__half*>(dst), name, rows, cols, scale, offset, place);
+  else fill_rows_t(H, static_cast<__nv_bfloat16*>(dst), name, rows, cols, scale, offset, place);
 }
 static void fill_bf16(vd_handle* H, bf16* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
                       float offset) {
   fill_w(H, dst, false, name, rows, cols, scale, offset);
 }
 static void fill_lin(vd_handle* H, void* dst, const std::string& name, int64_t rows, int64_t cols, float scale,
-                     float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0, int64_t alt_off = -1) {
-  fill_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off, alt_off);
+                     float offset, int64_t group = 0, int64_t stride = 0, int64_t off = 0, int64_t alt_off = -1,
+                     int64_t part_rows = 0, int64_t part_off = 0) {
+  fill_w(H, dst, H->opt.f16, name, rows, cols, scale, offset, group, stride, off, alt_off, part_rows, part_off);
 }
 // An fp32 vector of n elements (gains, biases; a [1, n] Linear weight qualifies).
 static void fill_f32(vd_handle* H, float* dst, const std::string& name, int64_t n, float scale, float offset) {
@@ -795,6 +876,8 @@ static void init_linear(vd_handle* H, Linear& L, int n, int k, bool bias, int bn
   L.map = make_map(L.w, n, k, L.bn, H->opt.f16);
   if (L.bn == 256) L.map_half = make_map(L.w, n, k, 128, H->opt.f16);
 }
+
+static float2* upload_rope(vd_handle* H, int rot, double theta);
 
 static void load_decoder(vd_handle* H) {
   const ModelSpec& s = H->spec;
@@ -878,22 +961,27 @@ static void load_decoder(vd_handle* H) {
   H->head_rows = dalloc<float>(H, static_cast<size_t>(H->n_labels) * d);
   const std::string head_name = s.tied ? "model.embed_tokens.weight" : "lm_head.weight";
   fill_rows_gather_f32(H, H->head_rows, head_name, s.label_ids, s.vocab, d, lin, 0.0f);
-  // RoPE table: cos/sin(pos * inv_freq_i), inv_freq_i = 1 / theta^(2i/rot) in fp32, rot the
-  // rotary width (head_dim, or its partial_rotary fraction in a hybrid's attention).
-  const int rot = s.hybrid() ? s.rot_dim() : hd;
+  // rotary width: head_dim, or its partial_rotary fraction in a hybrid's attention
+  H->rope = upload_rope(H, s.hybrid() ? s.rot_dim() : hd, s.rope_theta);
+}
+
+// RoPE table [max_seq][rot/2] of (cos, sin)(pos * inv_freq_i), inv_freq_i =
+// 1 / theta^(2i/rot) in fp32.
+static float2* upload_rope(vd_handle* H, int rot, double theta) {
   const int half = rot / 2;
   std::vector<float2> tab(static_cast<size_t>(H->opt.max_seq) * half);
   std::vector<float> inv(half);
   for (int i = 0; i < half; ++i)
-    inv[i] = 1.0f / std::pow(static_cast<float>(s.rope_theta), static_cast<float>(2 * i) / static_cast<float>(rot));
+    inv[i] = 1.0f / std::pow(static_cast<float>(theta), static_cast<float>(2 * i) / static_cast<float>(rot));
   for (int64_t pos = 0; pos < H->opt.max_seq; ++pos)
     for (int i = 0; i < half; ++i) {
       const float a = static_cast<float>(pos) * inv[i];
       tab[pos * half + i] = make_float2(static_cast<float>(std::cos(static_cast<double>(a))),
                                         static_cast<float>(std::sin(static_cast<double>(a))));
     }
-  H->rope = dalloc<float2>(H, tab.size());
-  cuda_check(cudaMemcpy(H->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice), "upload rope");
+  float2* out = dalloc<float2>(H, tab.size());
+  cuda_check(cudaMemcpy(out, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice), "upload rope");
+  return out;
 }
 
 static void enc_linear(vd_handle* H, Linear& L, const std::string& wname, const std::string& bname, int n, int k,
@@ -903,7 +991,73 @@ static void enc_linear(vd_handle* H, Linear& L, const std::string& wname, const 
   fill_f32(H, L.b, bname, n, lin, 0.0f);
 }
 
+// ModernBERT encoder + per-marker scorer (independent-options family), HF
+// `ModernBertModel` names under "encoder.", the scorer under "scorer.".
+static void load_von(vd_handle* H) {
+  const ModelSpec& s = H->spec;
+  const int d = s.hidden, f = s.ffn;
+  const float lin = static_cast<float>(s.init_std * std::sqrt(3.0));
+  const float g_scale = 0.1f, g_off = 1.0f;
+  // scales in double, rounded once, exactly as the host generator computes them
+  const double unit_d = 1.0 / std::sqrt(static_cast<double>(d));
+  const float unit = static_cast<float>(unit_d);
+  const float unit_lin = static_cast<float>(unit_d * std::sqrt(3.0));
+  const float unit_out = static_cast<float>(unit_d * std::sqrt(3.0) * 4.0);
+  const std::string e = "encoder.";
+  H->embed = dalloc<bf16>(H, static_cast<size_t>(s.vocab) * d);
+  fill_bf16(H, H->embed, e + "embeddings.tok_embeddings.weight", s.vocab, d, lin, 0.0f);
+  H->zero_d = dalloc<float>(H, d);
+  cuda_check(cudaMemsetAsync(H->zero_d, 0, sizeof(float) * d, H->stream), "zero bias");
+  H->emb_ln_w = dalloc<float>(H, d);
+  fill_f32(H, H->emb_ln_w, e + "embeddings.norm.weight", d, g_scale, g_off);
+  H->enc.resize(s.layers);
+  for (int i = 0; i < s.layers; ++i) {
+    EncLayer& L = H->enc[i];
+    const std::string p = e + "layers." + std::to_string(i) + ".";
+    init_linear(H, L.qkv, 3 * d, d, false);
+    fill_lin(H, L.qkv.w, p + "attn.Wqkv.weight", 3 * d, d, lin, 0.0f);
+    init_linear(H, L.o, d, d, false);
+    fill_lin(H, L.o.w, p + "attn.Wo.weight", d, d, lin, 0.0f);
+    // Wi = [input; gate]: gelu(input) * gate, interleaved into 128-row gate/up blocks
+    init_linear(H, L.f1, 2 * f, d, false, 256);
+    fill_lin(H, L.f1.w, p + "mlp.Wi.weight", 2 * f, d, lin, 0.0f, 128, 256, 0, -1, f, 128);
+    init_linear(H, L.f2, d, f, false);
+    fill_lin(H, L.f2.w, p + "mlp.Wo.weight", d, f, lin, 0.0f);
+    if (i > 0) {
+      L.ln1_w = dalloc<float>(H, d);
+      fill_f32(H, L.ln1_w, p + "attn_norm.weight", d, g_scale, g_off);
+    }
+    L.ln1_b = H->zero_d;
+    L.ln2_w = dalloc<float>(H, d);
+    fill_f32(H, L.ln2_w, p + "mlp_norm.weight", d, g_scale, g_off);
+    L.ln2_b = H->zero_d;
+    L.pre_norm = true;
+    L.act = kActGeluErf;
+    L.eps = static_cast<float>(s.ln_eps);
+    L.sliding = s.sliding_layer[i] != 0;
+  }
+  H->final_norm = dalloc<float>(H, d);
+  fill_f32(H, H->final_norm, e + "final_norm.weight", d, g_scale, g_off);
+  H->sc_ln_w = dalloc<float>(H, d);
+  H->sc_ln_b = dalloc<float>(H, d);
+  fill_f32(H, H->sc_ln_w, "scorer.0.weight", d, g_scale, g_off);
+  fill_f32(H, H->sc_ln_b, "scorer.0.bias", d, lin, 0.0f);
+  init_linear(H, H->sc1, d, d, true);
+  fill_lin(H, H->sc1.w, "scorer.1.weight", d, d, unit_lin, 0.0f);
+  fill_f32(H, H->sc1.b, "scorer.1.bias", d, unit, 0.0f);
+  H->sc_w3 = dalloc<float>(H, d);
+  H->sc_b3 = dalloc<float>(H, 1);
+  fill_f32(H, H->sc_w3, "scorer.3.weight", d, unit_out, 0.0f);
+  fill_f32(H, H->sc_b3, "scorer.3.bias", 1, unit, 0.0f);
+  H->rope = upload_rope(H, s.head_dim, s.global_theta);
+  H->rope_local = upload_rope(H, s.head_dim, s.local_theta);
+}
+
 static void load_encoder(vd_handle* H) {
+  if (H->spec.von()) {
+    load_von(H);
+    return;
+  }
   const ModelSpec& s = H->spec;
   const int d = s.hidden, f = s.ffn;
   const float lin = static_cast<float>(s.init_std * std::sqrt(3.0));
@@ -1071,6 +1225,10 @@ static void alloc_workspace(vd_handle* H) {
     H->mhid = dalloc<uint16_t>(H, o.max_markers * d);
     H->map_mrow = make_map(H->mrow, o.max_markers, d, 128, f16);
     H->out_mhid = make_out_map(H->mhid, o.max_markers, d, false, f16);
+    if (s.von()) {
+      H->von_opt = dalloc<int>(H, T);
+      H->von_pos = dalloc<int>(H, T);
+    }
   }
   ensure_host_inputs(H, o.max_rows * 1024, std::max(o.max_rows, o.max_markers), o.max_rows,
                      std::max<int64_t>(o.max_rows * 256, o.max_markers));
@@ -1196,9 +1354,13 @@ static int attn_tile_rows(const vd_handle* H, int hd, bool causal, bool gated = 
 // the gate columns of qkv), served by the warp-level kernel.
 template <class T>
 static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd, bool causal, int ld_qkv, int q0,
-                      int k0, int v0, int group, int ld_out, int gate_col0 = -1) {
+                      int k0, int v0, int group, int ld_out, int gate_col0 = -1, const int* opt_id = nullptr,
+                      const int* opt_pos = nullptr, int window = 0) {
   AttnParams p{};
   p.gate_col0 = gate_col0;
+  p.opt_id = opt_id;
+  p.opt_pos = opt_pos;
+  p.window = window;
   p.qkv = H->qkv;
   p.ld_qkv = ld_qkv;
   p.q_col0 = q0;
@@ -1584,9 +1746,73 @@ static void enc_layer(vd_handle* H, const EncLayer& L, int ntok, int n_tiles, do
   if (!L.pre_norm) ln(L.ln2_w, L.ln2_b, 1);
 }
 
+// The independent-options forward: ModernBERT over packed rows with option
+// masks and option-invariant positions, final norm, marker gather + scorer.
+template <class T>
+static double von_forward(vd_handle* H, const Chunk& c) {
+  const ModelSpec& s = H->spec;
+  const int d = s.hidden, nh = d / 64;
+  const ChunkPlan P = plan_chunk(H, c, false, 64);
+  const int ntok = P.ntok, n_tiles = P.n_tiles;
+  pack(H, c, P, 0);
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    dim3 grid(std::max(1, std::min((P.max_len + 255) / 256, 64)), P.n_seg);
+    von_layout_kernel<<<grid, 256, 0, H->stream>>>(H->segs, P.n_seg, c.mpos, c.mmask, static_cast<int>(c.k),
+                                                   H->von_opt, H->von_pos, H->d_err);
+  });
+  const float eps = static_cast<float>(s.ln_eps);
+  auto ln = [&](const float* w, int inplace) {
+    launch(H, VD_K_NORM, 0.0, [&] {
+      layernorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, w, H->zero_d, eps, inplace,
+                                                            static_cast<T*>(H->xn), ntok);
+    });
+  };
+  launch(H, VD_K_OTHER, 0.0,
+         [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, 1.0f, H->h); });
+  ln(H->emb_ln_w, 1);  // the residual stream starts from the normalised embedding
+  const double attn_flops = 4.0 * d * P.pairs;
+  for (const EncLayer& L : H->enc) {
+    if (L.ln1_w) ln(L.ln1_w, 0);  // layer 0 has no attention norm: xn already holds h
+    EpiParams q = epi();
+    q.q_cols = d;
+    q.k_cols = d;
+    q.head_dim = 64;
+    q.eps = eps;
+    q.positions = H->von_pos;
+    q.rope = L.sliding ? H->rope_local : H->rope;
+    gemm<kEpiQKRope, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, q, H->out_qkv);
+    attention<T>(H, attn_flops, n_tiles, nh, 64, false, 3 * d, 0, d, 2 * d, 1, d, -1, H->von_opt, H->von_pos,
+                 L.sliding ? s.sliding_window : 0);
+    gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(), H->out_h);
+    ln(L.ln2_w, 0);
+    gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.f1, ntok, epi(nullptr, L.act), H->out_act);
+    gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.f2, ntok, epi(), H->out_h);
+  }
+  ln(H->final_norm, 1);
+  const int nm = static_cast<int>(c.nb * c.k);
+  if (nm > 0) {
+    launch(H, VD_K_OTHER, 0.0, [&] {
+      marker_index_kernel<<<(nm + 255) / 256, 256, 0, H->stream>>>(H->cu, c.mpos, c.mmask, c.nb,
+                                                                   static_cast<int>(c.k), H->midx, H->d_err);
+    });
+    launch(H, VD_K_NORM, 0.0, [&] {
+      gather_layernorm_kernel<256, T><<<nm, 256, 0, H->stream>>>(H->h, H->midx, nm, d, H->sc_ln_w, H->sc_ln_b,
+                                                                 1e-5f, static_cast<T*>(H->mrow));
+    });
+    gemm<kEpiStore, T>(H, VD_K_OTHER, H->map_mrow, H->sc1, nm, epi(H->sc1.b, kActGeluErf), H->out_mhid);
+  }
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    marker_score_kernel<T><<<c.nb, 256, 0, H->stream>>>(static_cast<const T*>(H->mhid), d, H->sc_w3, H->sc_b3,
+                                                        c.mmask, c.nb, static_cast<int>(c.k), c.out,
+                                                        static_cast<int>(c.width));
+  });
+  return ntok;
+}
+
 template <class T>
 static double encoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
+  if (s.von()) return von_forward<T>(H, c);
   const int d = s.hidden;
   const ChunkPlan P = plan_chunk(H, c, false, 64);
   const int ntok = P.ntok, n_tiles = P.n_tiles;
@@ -1647,6 +1873,18 @@ static void validate_batch(vd_handle* H, const vd_batch* b, int64_t width) {
     if (!b->marker_mask) fail(VD_EINVAL, "marker batches need marker_mask");
     if (width < b->k) fail(VD_EINVAL, "output width is smaller than k");
     if (b->b * b->k > H->opt.max_markers) fail(VD_EINVAL, "too many markers for this handle (max_markers)");
+    if (s.von() && b->memory == VD_MEM_HOST)
+      // independent_options_tensors (src/engine.rs:549-555)
+      for (int64_t i = 0; i < b->b; ++i) {
+        int64_t first = -1;
+        for (int64_t j = 0; j < b->k; ++j)
+          if (b->marker_mask[i * b->k + j]) {
+            first = b->marker_pos[i * b->k + j];
+            break;
+          }
+        if (first < 0 || first >= b->real_len[i])
+          fail(VD_EINVAL, "row " + std::to_string(i) + ": no marker positions inside the real ids");
+      }
   }
   for (int64_t i = 0; i < b->b; ++i) {
     const int64_t n = b->real_len[i];

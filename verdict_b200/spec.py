@@ -18,6 +18,13 @@ same executor path as any CausalLM):
     partial_rotary (rotary fraction of head_dim), lin_k_heads, lin_v_heads,
     lin_k_dim, lin_v_dim, conv_kernel
 
+independent-options encoder keys (style "modernbert", family
+"independent_options": a ModernBERT encoder with option-masked attention and a
+per-marker scorer, the ORT graph of `convert/independent_options/`):
+    arch="encoder", hidden, layers, heads, ffn, vocab, max_pos, ln_eps, pad_id,
+    layer_types ("full_attention" / "sliding_attention"), global_theta,
+    local_theta, sliding_window (half-window in option-invariant positions)
+
 encoder keys (marker-head family, `convert/marker_head/marker_head_converter.py:19-57`):
     arch="encoder", style in {"bert", "xlmr"}, hidden, layers, heads, ffn,
     vocab, max_pos, type_vocab, ln_eps, pad_id, head_layers, family="marker_head",
@@ -57,6 +64,18 @@ _HYBRID_BASE = dict(
     partial_rotary=0.25, conv_kernel=4, lin_k_heads=16, lin_v_heads=32, lin_k_dim=128, lin_v_dim=128,
 )
 
+_VON_BASE = dict(
+    arch="encoder", style="modernbert", family="independent_options", max_pos=8192, ln_eps=1e-5,
+    pad_id=50283, head_layers=0, type_vocab=0, global_theta=160000.0, local_theta=10000.0,
+    sliding_window=64, seed=20261201, init_std=0.02,
+)
+
+
+def modernbert_layer_types(layers: int, global_every: int = 3) -> list:
+    """ModernBERT's default pattern: every `global_every`-th layer (from 0) full attention."""
+    return ["sliding_attention" if i % global_every else "full_attention" for i in range(layers)]
+
+
 PRESETS = {
     # OneJev-9B-shaped text decision model
     "onejev-9b": dict(_DECODER_BASE, hidden=4096, layers=40, heads=32, kv_heads=8,
@@ -73,6 +92,10 @@ PRESETS = {
     # full-attention layers; the shape of transformers' Qwen3_5TextConfig defaults)
     "onejev16-9b": dict(_HYBRID_BASE, hidden=4096, layers=32, heads=16, kv_heads=4, head_dim=256,
                         ffn=12288, vocab=248320, layer_types=hybrid_layer_types(32)),
+    # ModernBERT-base-shaped independent-options encoder (von): 22 layers, every
+    # third global, the rest sliding-window; option-masked attention
+    "von-base": dict(_VON_BASE, hidden=768, layers=22, heads=12, ffn=1152, vocab=50368,
+                     layer_types=modernbert_layer_types(22)),
     # BERT-base-shaped marker-head encoder (laya)
     "laya-bert": dict(_ENCODER_BASE, style="bert", hidden=768, layers=12, heads=12,
                       ffn=3072, vocab=30522, pad_id=0),
@@ -94,6 +117,8 @@ def preset(name: str, **overrides) -> dict:
     spec.update(overrides)
     if spec.get("style") == "qwen3_5" and "layers" in overrides and "layer_types" not in overrides:
         spec["layer_types"] = hybrid_layer_types(spec["layers"])
+    if spec.get("style") == "modernbert" and "layers" in overrides and "layer_types" not in overrides:
+        spec["layer_types"] = modernbert_layer_types(spec["layers"])
     spec["preset"] = name
     return spec
 
@@ -134,6 +159,8 @@ def gdn_dims(spec: dict) -> dict:
 def linear_flops_per_token(spec: dict) -> float:
     """Multiply-add FLOPs (2 per MAC) of every projection GEMM for one token."""
     d, f = spec["hidden"], spec["ffn"]
+    if spec.get("style") == "modernbert":
+        return 2.0 * (4 * d * d + 3 * d * f) * spec["layers"]
     if spec["arch"] == "decoder":
         full = d * qkv_width(spec) + spec["heads"] * spec["head_dim"] * d + 3 * d * f
         if not is_hybrid(spec):

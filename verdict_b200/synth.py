@@ -245,8 +245,43 @@ def encoder_tensors(spec: dict):
     return out
 
 
+def von_tensors(spec: dict):
+    """(name, shape, scale, offset) of an independent-options model: HF
+    `ModernBertModel` under "encoder." (its LayerNorms have no bias) and a
+    per-marker scorer under "scorer." laid out like the marker head's
+    LayerNorm -> Linear -> GELU -> Linear(d, 1)."""
+    d, f = spec["hidden"], spec["ffn"]
+    lin = _lin(spec)
+    g_scale, g_off = 0.1, 1.0
+    e = "encoder."
+    out = [(e + "embeddings.tok_embeddings.weight", (spec["vocab"], d), lin, 0.0),
+           (e + "embeddings.norm.weight", (d,), g_scale, g_off)]
+    for i in range(spec["layers"]):
+        p = f"{e}layers.{i}."
+        if i > 0:
+            out.append((p + "attn_norm.weight", (d,), g_scale, g_off))
+        out += [(p + "attn.Wqkv.weight", (3 * d, d), lin, 0.0),
+                (p + "attn.Wo.weight", (d, d), lin, 0.0),
+                (p + "mlp_norm.weight", (d,), g_scale, g_off),
+                (p + "mlp.Wi.weight", (2 * f, d), lin, 0.0),
+                (p + "mlp.Wo.weight", (d, f), lin, 0.0)]
+    # scorer Linears at PyTorch's default scale (U(+-1/sqrt(fan_in))), so the
+    # option logits are O(1) and their differences carry signal
+    unit = 1.0 / np.sqrt(d)
+    out += [(e + "final_norm.weight", (d,), g_scale, g_off),
+            ("scorer.0.weight", (d,), g_scale, g_off),
+            ("scorer.0.bias", (d,), lin, 0.0),
+            ("scorer.1.weight", (d, d), unit * SQRT3, 0.0),
+            ("scorer.1.bias", (d,), unit, 0.0),
+            ("scorer.3.weight", (1, d), unit * SQRT3 * 4, 0.0),
+            ("scorer.3.bias", (1,), unit, 0.0)]
+    return out
+
+
 def tensor_table(spec: dict):
-    return decoder_tensors(spec) if spec["arch"] == "decoder" else encoder_tensors(spec)
+    if spec["arch"] == "decoder":
+        return decoder_tensors(spec)
+    return von_tensors(spec) if spec.get("style") == "modernbert" else encoder_tensors(spec)
 
 
 class SyntheticCheckpoint:
