@@ -51,6 +51,9 @@ SHARED_WORKLOAD = ("OneJev-9B-shaped letter-branches decisions, 8 questions per 
 HYBRID_WORKLOAD = ("OneJev1.6-9B-shaped hybrid text decisions (Qwen3.5 text stack: 24 gated-delta-net + 8 gated "
                    "full-attention layers, d=4096, attention 16/4 heads hd=256, linear 16/32 heads of 128, SwiGLU "
                    "12288, vocab 248320); lengths clip(lognormal(6,0.7),32,4096), 2-8 options")
+VON_WORKLOAD = ("ModernBERT-base-shaped independent-options decisions (22 layers, d=768, 12 heads, GeGLU 1152, "
+                "vocab 50368, every 3rd layer global, the rest a 64-position window), option-masked attention; "
+                "[CLS] prefix U[16,200] [SEP] then 2-6 [MASK]-led options of U[1,12] tokens")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
 # full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
@@ -138,18 +141,20 @@ def whole_job_rate(decisions_per_rank: int, world: int, max_ms: float) -> float:
     return decisions_per_rank * world / (max_ms / 1e3)
 
 
-def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice"):
+def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad_id=0):
     """Each rank's own shard of the workload: batch j of rank r is seeded by
     (seed, r, j), so ranks never share a decision."""
-    from verdict_b200.batch import Layout, collate, decoder_rows, shared_prefix_rows
+    from verdict_b200.batch import Layout, collate, decoder_rows, shared_prefix_rows, von_rows
     out = []
     for j in range(n_batches):
         rng = np.random.default_rng([seed, rank, j])
         if workload == "shared-prefix":
             rows = shared_prefix_rows(rng, per_batch, vocab)
+        elif workload == "von":
+            rows = von_rows(rng, per_batch, vocab)
         else:
             rows = decoder_rows(rng, per_batch, vocab, lengths="lognormal-9b")
-        out.append(collate(rows, Layout(pad_id=0)))
+        out.append(collate(rows, Layout(pad_id=pad_id)))
     return out
 
 
@@ -178,6 +183,21 @@ def cpu_baseline_sample(spec, batch, layers_timed):
     return 1.0 / per_decision, sample, per_decision
 
 
+def von_cpu_sample(spec, batch):
+    """The oracle (fp32 numpy) on the batch's first 4 rows, all layers; decisions/s."""
+    from oracle.von import VonOracle
+    from verdict_b200.batch import CollatedBatch
+    n = min(4, batch.b)
+    sub = CollatedBatch(batch.input_ids[:n * batch.l], batch.attention_mask[:n * batch.l],
+                        batch.marker_pos[:n * batch.k], batch.marker_mask[:n * batch.k], batch.qtype[:n],
+                        batch.nopts, n, batch.l, batch.k, batch.rows[:n])
+    orc = VonOracle(spec)
+    t0 = time.perf_counter()
+    orc.infer(sub)
+    dt = time.perf_counter() - t0
+    return n / dt, f"{n} rows, all {spec['layers']} layers", dt / n
+
+
 def run_reference(args, world, rank):
     """The reference arm: the CPU path of the reference executor (fp32), as the
     oracle port, on this host's cores; rank 0 only."""
@@ -187,10 +207,12 @@ def run_reference(args, world, rank):
     from verdict_b200 import spec as specs
     from verdict_b200.synth import with_labels
     spec = with_labels(specs.preset(args.model))
-    batches = make_batches(0, args.warmup + args.steps, 1, spec["vocab"], args.seed)
+    encoder = spec["arch"] == "encoder"
+    batches = make_batches(0, args.warmup + args.steps, 4 if encoder else 1, spec["vocab"], args.seed,
+                           "von" if encoder else "choice", spec.get("pad_id", 0))
     times = []
     for j, b in enumerate(batches):
-        _, _, per = cpu_baseline_sample(spec, b, args.ref_layers)
+        _, _, per = von_cpu_sample(spec, b) if encoder else cpu_baseline_sample(spec, b, args.ref_layers)
         if j >= args.warmup:
             times.append(per)
     mean = float(np.mean(times))
@@ -200,11 +222,14 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD if args.model == "onejev-9b" else HYBRID_WORKLOAD, "model": args.model,
-                   "decisions_per_step": 1,
+        "config": {"workload": {"onejev-9b": WORKLOAD, "onejev16-9b": HYBRID_WORKLOAD,
+                                "von-base": VON_WORKLOAD}[args.model], "model": args.model,
+                   "decisions_per_step": 4 if encoder else 1,
                    "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"per step 1 decision; {args.ref_layers} of 40 layers timed and scaled"},
+                         "sample": ("per step 4 decisions, all layers" if encoder else
+                                    f"per step 1 decision; {args.ref_layers} of {spec['layers']} layers timed "
+                                    "and scaled")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -229,9 +254,10 @@ def main():
                          "per state, rows of a state share the state prefix (prefix_len declared)")
     ap.add_argument("--fork", default="on", choices=["on", "off"],
                     help="compute shared prefixes once (on) or every row whole (off)")
-    ap.add_argument("--model", default="onejev-9b", choices=["onejev-9b", "onejev16-9b"],
+    ap.add_argument("--model", default="onejev-9b", choices=["onejev-9b", "onejev16-9b", "von-base"],
                     help="onejev-9b: the dense OneJev-9B shape (headline); onejev16-9b: the Qwen3.5-style hybrid "
-                         "(gated delta nets + gated attention)")
+                         "(gated delta nets + gated attention); von-base: the ModernBERT-base independent-options "
+                         "encoder")
     ap.add_argument("--gemm", default="2sm", choices=["2sm", "1sm"],
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
     args = ap.parse_args()
@@ -259,13 +285,15 @@ def main():
     over = {} if args.layers is None else {"layers": args.layers}
     spec = with_labels(specs.preset(args.model, **over))
     n_batches = args.warmup + args.steps
-    batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed, args.workload)
+    encoder = spec["arch"] == "encoder"
+    batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed,
+                           "von" if encoder else args.workload, spec.get("pad_id", 0))
     max_tokens = max(int(b.real_len().sum()) for b in batches)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
                      max_seq=4096, attention=args.attention, fork=args.fork == "on", gemm=args.gemm)
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
-    width = eng.width
+    width = eng.width if not encoder else max(b.k for b in batches)  # encoders: one logit per marker slot
     stream_ptr = eng.stream()
     stream = torch.cuda.ExternalStream(stream_ptr)
 
@@ -427,7 +455,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, sample, _ = cpu_baseline_sample(spec, batches[0], args.ref_layers)
+        v, sample, _ = (von_cpu_sample(spec, batches[0]) if encoder
+                        else cpu_baseline_sample(spec, batches[0], args.ref_layers))
         cpu = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -436,8 +465,9 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
-            "config": {"workload": (SHARED_WORKLOAD if shared else WORKLOAD) if args.model == "onejev-9b"
-                       else HYBRID_WORKLOAD, "model": args.model,
+            "config": {"workload": {"onejev-9b": SHARED_WORKLOAD if shared else WORKLOAD,
+                                    "onejev16-9b": HYBRID_WORKLOAD, "von-base": VON_WORKLOAD}[args.model],
+                       "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
                        "computed_tokens_last_step": int(computed_tokens),
