@@ -54,6 +54,7 @@ HYBRID_WORKLOAD = ("OneJev1.6-9B-shaped hybrid text decisions (Qwen3.5 text stac
 VON_WORKLOAD = ("ModernBERT-base-shaped independent-options decisions (22 layers, d=768, 12 heads, GeGLU 1152, "
                 "vocab 50368, every 3rd layer global, the rest a 64-position window), option-masked attention; "
                 "[CLS] prefix U[16,200] [SEP] then 2-6 [MASK]-led options of U[1,12] tokens")
+OTHER_WORKLOAD = "{} text decisions (all layers, synthetic weights), lengths {}, 2-8 options"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
 # full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
@@ -141,7 +142,11 @@ def whole_job_rate(decisions_per_rank: int, world: int, max_ms: float) -> float:
     return decisions_per_rank * world / (max_ms / 1e3)
 
 
-def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad_id=0):
+LENGTHS = {"onejev-9b": "lognormal-9b", "onejev16-9b": "lognormal-9b", "decider-2b": "uniform-2b",
+           "onejev-27b": "uniform-27b"}
+
+
+def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad_id=0, lengths="lognormal-9b"):
     """Each rank's own shard of the workload: batch j of rank r is seeded by
     (seed, r, j), so ranks never share a decision."""
     from verdict_b200.batch import Layout, collate, decoder_rows, shared_prefix_rows, von_rows
@@ -153,7 +158,7 @@ def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad
         elif workload == "von":
             rows = von_rows(rng, per_batch, vocab)
         else:
-            rows = decoder_rows(rng, per_batch, vocab, lengths="lognormal-9b")
+            rows = decoder_rows(rng, per_batch, vocab, lengths=lengths)
         out.append(collate(rows, Layout(pad_id=pad_id)))
     return out
 
@@ -209,7 +214,8 @@ def run_reference(args, world, rank):
     spec = with_labels(specs.preset(args.model))
     encoder = spec["arch"] == "encoder"
     batches = make_batches(0, args.warmup + args.steps, 4 if encoder else 1, spec["vocab"], args.seed,
-                           "von" if encoder else "choice", spec.get("pad_id", 0))
+                           "von" if encoder else "choice", spec.get("pad_id", 0),
+                           LENGTHS.get(args.model, "lognormal-9b"))
     times = []
     for j, b in enumerate(batches):
         _, _, per = von_cpu_sample(spec, b) if encoder else cpu_baseline_sample(spec, b, args.ref_layers)
@@ -222,8 +228,10 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": {"onejev-9b": WORKLOAD, "onejev16-9b": HYBRID_WORKLOAD,
-                                "von-base": VON_WORKLOAD}[args.model], "model": args.model,
+        "config": {"workload": {"onejev-9b": WORKLOAD, "onejev16-9b": HYBRID_WORKLOAD, "von-base": VON_WORKLOAD,
+                                "decider-2b": OTHER_WORKLOAD.format("Gemma-2B-shaped decider", "U[64,1024]"),
+                                "onejev-27b": OTHER_WORKLOAD.format("OneJev-27B-shaped", "U[512,8192]")}
+                   [args.model], "model": args.model,
                    "decisions_per_step": 4 if encoder else 1,
                    "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
@@ -254,10 +262,12 @@ def main():
                          "per state, rows of a state share the state prefix (prefix_len declared)")
     ap.add_argument("--fork", default="on", choices=["on", "off"],
                     help="compute shared prefixes once (on) or every row whole (off)")
-    ap.add_argument("--model", default="onejev-9b", choices=["onejev-9b", "onejev16-9b", "von-base"],
+    ap.add_argument("--model", default="onejev-9b",
+                    choices=["onejev-9b", "onejev16-9b", "von-base", "decider-2b", "onejev-27b"],
                     help="onejev-9b: the dense OneJev-9B shape (headline); onejev16-9b: the Qwen3.5-style hybrid "
                          "(gated delta nets + gated attention); von-base: the ModernBERT-base independent-options "
-                         "encoder")
+                         "encoder; decider-2b (lengths U[64,1024]) and onejev-27b (lengths U[512,8192]): the "
+                         "other decoder shapes")
     ap.add_argument("--gemm", default="2sm", choices=["2sm", "1sm"],
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
     args = ap.parse_args()
@@ -287,10 +297,13 @@ def main():
     n_batches = args.warmup + args.steps
     encoder = spec["arch"] == "encoder"
     batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed,
-                           "von" if encoder else args.workload, spec.get("pad_id", 0))
+                           "von" if encoder else args.workload, spec.get("pad_id", 0),
+                           LENGTHS.get(args.model, "lognormal-9b"))
+    max_len = max(int(b.real_len().max()) for b in batches)
     max_tokens = max(int(b.real_len().sum()) for b in batches)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
-                     max_seq=4096, attention=args.attention, fork=args.fork == "on", gemm=args.gemm)
+                     max_seq=max(4096, max_len), attention=args.attention, fork=args.fork == "on",
+                     gemm=args.gemm)
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
     width = eng.width if not encoder else max(b.k for b in batches)  # encoders: one logit per marker slot
@@ -466,7 +479,10 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
             "config": {"workload": {"onejev-9b": SHARED_WORKLOAD if shared else WORKLOAD,
-                                    "onejev16-9b": HYBRID_WORKLOAD, "von-base": VON_WORKLOAD}[args.model],
+                                    "onejev16-9b": HYBRID_WORKLOAD, "von-base": VON_WORKLOAD,
+                                    "decider-2b": OTHER_WORKLOAD.format("Gemma-2B-shaped decider", "U[64,1024]"),
+                                    "onejev-27b": OTHER_WORKLOAD.format("OneJev-27B-shaped", "U[512,8192]")}
+                       [args.model],
                        "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
