@@ -58,9 +58,10 @@ OTHER_WORKLOAD = "{} text decisions (all layers, synthetic weights), lengths {},
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
 # full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
-# launch had.  Weight re-reads dominate it, so it is reported as measured, not scaled.
-GATEUP_TRAFFIC_BYTES = 3.3236e9 + 0.8198e9
-GATEUP_TRAFFIC_TOKENS = 33763
+# launch had, per (model, GEMM kernel).  Operand re-reads dominate it, so it is reported as measured,
+# not scaled; other shapes report null.
+GATEUP_TRAFFIC = {("onejev-9b", "2sm"): (3.9676e9 + 0.8232e9, 33763),
+                  ("onejev-9b", "1sm"): (3.3236e9 + 0.8198e9, 33763)}
 
 
 def peaks():
@@ -270,6 +271,10 @@ def main():
                          "other decoder shapes")
     ap.add_argument("--gemm", default="2sm", choices=["2sm", "1sm"],
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
+    ap.add_argument("--gdn", default="chunk", choices=["chunk", "scan"],
+                    help="gated delta nets in 64-token chunks on the tensor cores (chunk) or token by token (scan)")
+    ap.add_argument("--raster-group", type=int, default=0,
+                    help="M tiles per GEMM raster group (0: the kernels' default)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -303,7 +308,7 @@ def main():
     max_tokens = max(int(b.real_len().sum()) for b in batches)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
                      max_seq=max(4096, max_len), attention=args.attention, fork=args.fork == "on",
-                     gemm=args.gemm)
+                     gemm=args.gemm, raster_group=args.raster_group, gdn=args.gdn)
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
     width = eng.width if not encoder else max(b.k for b in batches)  # encoders: one logit per marker slot
@@ -390,11 +395,13 @@ def main():
     achieved = gu_flops / (gu_launch_ms / 1e3) / 1e12
     gemm_ms = acc_ms[:4].sum() / prof_steps
     gemm_tf = acc_fl[:4].sum() / (acc_ms[:4].sum() / 1e3) / 1e12
+    traffic, traffic_tokens = GATEUP_TRAFFIC.get((args.model, args.gemm), (None, None))
     roofline = {
-        "kernel": "gemm_tcgen05_kernel<256,gated> (gate/up projection)",
+        "kernel": ("gemm2_tcgen05_kernel<gated> (gate/up projection, CTA pairs)" if args.gemm == "2sm"
+                   else "gemm_tcgen05_kernel<256,gated> (gate/up projection)"),
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": f"{pk_kind} bf16_tflops_sustained (dense fp16 and bf16 share the tensor-core rate)",
-        "traffic": GATEUP_TRAFFIC_BYTES, "traffic_tokens": GATEUP_TRAFFIC_TOKENS,
+        "traffic": traffic, "traffic_tokens": traffic_tokens,
         "algorithmic_bytes_per_launch": 2.0 * tokens_per_step * (spec["hidden"] + 2 * spec["ffn"])
         + 2.0 * 2 * spec["ffn"] * spec["hidden"],
         "flops_per_launch": gu_flops, "launch_ms": gu_launch_ms,
@@ -485,6 +492,8 @@ def main():
                        [args.model],
                        "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
+                       "raster_group": args.raster_group or "default",
+                       **({"gdn": args.gdn} if specs.is_hybrid(spec) else {}),
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,
                        "computed_tokens_last_step": int(computed_tokens),
                        "parallelism": f"replicas x{world} (one full-weight replica per GPU, no collectives)",

@@ -126,8 +126,14 @@ class DecoderOracle:
     cache_layers=False regenerates each layer's weights when it is used and
     drops them afterwards, so a 40-layer 9B model runs in ~2 GB of host memory."""
 
-    def __init__(self, spec: dict, layers: int | None = None, cache_layers: bool = True):
+    def __init__(self, spec: dict, layers: int | None = None, cache_layers: bool = True, store16: bool = False):
+        """store16 (hybrid stacks): round every activation the GPU path keeps in
+        16 bits to fp16 where it is stored (norm outputs, projection outputs,
+        q/k/v after their norms, mixer outputs, the MLP activation); the
+        residual stream stays fp32.  It measures what fp16 storage alone does to
+        the outputs, as a yardstick for the GPU's deviation from fp32."""
         self.spec = spec
+        self.store16 = store16
         self.ckpt = FastCheckpoint(spec)
         self.cache_layers = cache_layers
         self.n_layers = spec["layers"] if layers is None else layers
@@ -192,42 +198,43 @@ class DecoderOracle:
         w = self.layer(i)
         n = h.shape[0]
         eps = s["rms_eps"]
-        x = rmsnorm(h, w["input_layernorm.weight"], eps, True)
+        st = (lambda t: t.astype(np.float16).astype(np.float32)) if self.store16 else (lambda t: t)
+        x = st(rmsnorm(h, w["input_layernorm.weight"], eps, True))
         if s["layer_types"][i] == "full_attention":
             hd, nq, nkv = s["head_dim"], s["heads"], s["kv_heads"]
             qg = (x @ w["self_attn.q_proj.weight"].T).reshape(n, nq, 2 * hd)
-            q, gate = qg[..., :hd], qg[..., hd:].reshape(n, nq * hd)
+            q, gate = qg[..., :hd], st(qg[..., hd:].reshape(n, nq * hd))
             k = (x @ w["self_attn.k_proj.weight"].T).reshape(n, nkv, hd)
-            v = (x @ w["self_attn.v_proj.weight"].T).reshape(n, nkv, hd)
+            v = st((x @ w["self_attn.v_proj.weight"].T).reshape(n, nkv, hd))
             q = rmsnorm(q, w["self_attn.q_norm.weight"], eps, True)
             k = rmsnorm(k, w["self_attn.k_norm.weight"], eps, True)
             rd = cos.shape[-1]
-            q = np.concatenate([apply_rope(q[..., :rd], cos, sin), q[..., rd:]], axis=-1)
-            k = np.concatenate([apply_rope(k[..., :rd], cos, sin), k[..., rd:]], axis=-1)
-            a = attention(q, k, v, causal=True).reshape(n, nq * hd) * sigmoid(gate)
+            q = st(np.concatenate([apply_rope(q[..., :rd], cos, sin), q[..., rd:]], axis=-1))
+            k = st(np.concatenate([apply_rope(k[..., :rd], cos, sin), k[..., rd:]], axis=-1))
+            a = st(attention(q, k, v, causal=True).reshape(n, nq * hd) * sigmoid(gate))
             h = h + a @ w["self_attn.o_proj.weight"].T
         else:
             lk, lv, dk, dv = s["lin_k_heads"], s["lin_v_heads"], s["lin_k_dim"], s["lin_v_dim"]
             kd, vd = lk * dk, lv * dv
             p = "linear_attn."
-            mixed = x @ w[p + "in_proj_qkv.weight"].T
-            z = (x @ w[p + "in_proj_z.weight"].T).reshape(n, lv, dv)
-            b = x @ w[p + "in_proj_b.weight"].T
-            a = x @ w[p + "in_proj_a.weight"].T
+            mixed = st(x @ w[p + "in_proj_qkv.weight"].T)
+            z = st((x @ w[p + "in_proj_z.weight"].T).reshape(n, lv, dv))
+            b = st(x @ w[p + "in_proj_b.weight"].T)
+            a = st(x @ w[p + "in_proj_a.weight"].T)
             conv = causal_conv_silu(mixed, w[p + "conv1d.weight"][:, 0, :])
             q = conv[:, :kd].reshape(n, lk, dk)
             k = conv[:, kd:2 * kd].reshape(n, lk, dk)
-            v = conv[:, 2 * kd:].reshape(n, lv, dv)
+            v = st(conv[:, 2 * kd:].reshape(n, lv, dv))
             beta = sigmoid(b)
             g = (-np.exp(w[p + "A_log"]) * softplus(a + w[p + "dt_bias"])).astype(np.float32)
             rep = lv // lk
-            q = l2norm(np.repeat(q, rep, axis=1)) * np.float32(dk ** -0.5)
-            k = l2norm(np.repeat(k, rep, axis=1))
+            q = st(l2norm(np.repeat(q, rep, axis=1)) * np.float32(dk ** -0.5))
+            k = st(l2norm(np.repeat(k, rep, axis=1)))
             o = gated_delta_rule(q, k, v, g, beta)
-            o = rmsnorm(o, w[p + "norm.weight"], eps, False) * silu(z)
+            o = st(rmsnorm(o, w[p + "norm.weight"], eps, False) * silu(z))
             h = h + o.reshape(n, vd) @ w[p + "out_proj.weight"].T
-        x = rmsnorm(h, w["post_attention_layernorm.weight"], eps, True)
-        act = silu(x @ w["mlp.gate_proj.weight"].T) * (x @ w["mlp.up_proj.weight"].T)
+        x = st(rmsnorm(h, w["post_attention_layernorm.weight"], eps, True))
+        act = st(silu(x @ w["mlp.gate_proj.weight"].T) * (x @ w["mlp.up_proj.weight"].T))
         h = h + act @ w["mlp.down_proj.weight"].T
         return h.astype(np.float32)
 

@@ -59,7 +59,7 @@ def test_hybrid_9b_shape_vs_oracle():
     try:
         got = logprobs(eng, batch)
         st = eng.last_stats()
-        assert st["kernel_launches"][7] == 2 * 3  # conv + scan for each gated-delta-net layer
+        assert st["kernel_launches"][7] == 2 * 3  # conv + recurrence for each gated-delta-net layer
     finally:
         eng.close()
     check_vs_oracle(got, DecoderOracle(spec).infer(batch), batch.nopts)
@@ -87,6 +87,30 @@ def test_hybrid_ending_in_linear_layer_bf16_and_pruning():
     assert np.abs(c - b)[live].max() <= 1e-1  # bf16 rounding only
 
 
+def test_gdn_chunked_form_matches_token_scan_and_oracle():
+    """The 64-token chunked (tensor-core) recurrence against the token-by-token
+    one and the oracle, on lengths at and around the chunk edges."""
+    spec = hybrid(4)
+    rng = np.random.default_rng(63)
+    rows = decoder_rows(rng, 8, spec["vocab"], lengths="fixed:8")
+    for r, n in zip(rows, (1, 2, 63, 64, 65, 128, 129, 700)):
+        r.ids = rng.integers(3, spec["vocab"], size=n).tolist()
+        r.markers = [n - 1]
+    batch = collate(rows, Layout(pad_id=0))
+    kw = dict(max_tokens=8192, max_rows=16, max_seq=2048)
+    chunk = B200Engine(spec, gdn="chunk", **kw)
+    scan = B200Engine(spec, gdn="scan", **kw)
+    try:
+        a, b = logprobs(chunk, batch), logprobs(scan, batch)
+    finally:
+        chunk.close()
+        scan.close()
+    live = a > -1e4
+    assert np.array_equal(live, b > -1e4)
+    assert np.abs(a - b)[live].max() <= 1e-2
+    check_vs_oracle(a, DecoderOracle(spec).infer(batch), batch.nopts)
+
+
 def test_hybrid_chunking_is_bit_exact():
     spec = hybrid(4)
     batch = batch_of(spec, 5, 7, 800)
@@ -102,7 +126,13 @@ def test_hybrid_chunking_is_bit_exact():
 
 
 def test_hybrid_full_depth_vs_oracle():
-    """All 32 layers (24 gated delta nets, 8 gated attentions) of the 9B shape."""
+    """All 32 layers (24 gated delta nets, 8 gated attentions) of the 9B shape.
+
+    At this depth fp16 activation storage by itself moves these log-probs by up
+    to ~4e-2 (the oracle with every 16-bit store of the GPU path emulated,
+    `store16`), so each row is held to the 2e-2 tolerance beyond that row's own
+    storage deviation; decisions must match wherever the fp32 top-2 margin
+    exceeds 2e-2."""
     spec = with_labels(specs.preset("onejev16-9b", seed=62))
     rng = np.random.default_rng(62)
     rows = decoder_rows(rng, 3, spec["vocab"], lengths="fixed:8")
@@ -115,7 +145,17 @@ def test_hybrid_full_depth_vs_oracle():
         got = logprobs(eng, batch)
     finally:
         eng.close()
-    check_vs_oracle(got, DecoderOracle(spec, cache_layers=False).infer(batch), batch.nopts)
+    lp32 = option_logprobs(DecoderOracle(spec, cache_layers=False).infer(batch), batch.nopts)
+    lp16 = option_logprobs(DecoderOracle(spec, cache_layers=False, store16=True).infer(batch), batch.nopts)
+    for i, k in enumerate(batch.nopts):
+        k = int(k)
+        storage = np.abs(lp16[i, :k] - lp32[i, :k]).max()
+        d = np.abs(got[i, :k] - lp32[i, :k]).max()
+        assert d <= LOGPROB_TOL + storage, f"row {i}: {d:.3e} (fp16 storage alone: {storage:.3e})"
+        top = np.sort(lp32[i, :k])[::-1]
+        if top[0] - top[1] > LOGPROB_TOL:
+            assert np.argmax(got[i, :k]) == np.argmax(lp32[i, :k]), f"row {i}: decision differs"
+        assert np.all(got[i, k:] == -1e4)
 
 
 @pytest.mark.parametrize("vl", [False, True])

@@ -46,7 +46,7 @@ struct GdnParams {
   const int4* segs;        // packed sequences {start, len, col0, src_row}
 };
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // One token per CTA (256 threads = 8 warps); warp w handles heads w, w + 8, ...
 // of the 2*lk + lv conv heads (q heads, then k heads, then v heads), 4
@@ -229,6 +229,446 @@ __global__ void __launch_bounds__(256, 1) gdn_scan_kernel(GdnParams p) {
     const float rstd = rsqrtf(ss / 128.0f + p.eps);
     out[row(len - 1) * p.ld_out + head * 128 + col] =
         Elem<T>::from(o_prev * rstd * w_norm * silu_f(Elem<T>::to(z_prev)));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chunked form of the same recurrence on the tensor cores (mma.sync m16n8k16,
+// fp32 accumulate), chunks of C = 64 tokens.  For a chunk entered with state
+// S0, let G_t be the inclusive sum of g from the chunk start to token t.
+// Unrolling the per-token rule inside the chunk gives, for the deltas
+// d_t = (v_t - k_t^T S_{t-1}) b_t of all its tokens at once,
+//     (I + A) D = R,   R = diag(b) (V - diag(e^G) K S0),
+//     A[t,s] = b_t e^(G_t - G_s) (k_t . k_s)   for s < t   (0 otherwise);
+// then
+//     O  = diag(e^G) Q S0 + P D,   P[t,s] = e^(G_t - G_s) (q_t . k_s), s <= t,
+//     S1 = e^(G_C) S0 + (diag(e^(G_C - G)) K)^T D.
+// Every exponent is <= 0 (g <= 0 and s <= t), so nothing overflows.  Tokens
+// past the sequence end enter as k = q = v = 0, g = b = 0 and drop out.
+//
+// (I + A) D = R is solved by 16-row blocks: the four diagonal blocks are
+// inverted in fp32 by forward substitution (one warp each), then for block
+// rows i = 0..3,  D_i = (I + A_ii)^-1 (R_i - sum_{k<i} A_ik D_k),  all on the
+// tensor cores.  The value columns are independent, so warp w carries its own
+// 16 columns through the four block rows with no cross-warp dependency.
+//
+// One (sequence, value head) per CTA of 8 warps, chunks in order.  The state
+// stays in fp32 registers across chunks (warp w holds key rows 16w..16w+15,
+// all 128 value columns, as mma accumulators) with a 16-bit copy in shared
+// memory for the K S0 / Q S0 products.  K, Q, V and the gates of chunk i + 1
+// and z of chunk i load (cp.async) while chunk i computes.
+// ---------------------------------------------------------------------------
+struct GdnChunkConfig {
+  static constexpr int C = 64;    // tokens per chunk
+  static constexpr int D = 128;   // key = value head dim
+  static constexpr int TILE = C * D * 2;          // one [64][128] 16-bit tile
+  static constexpr int KQV = 3 * TILE;            // K, Q, V of one chunk (two buffers)
+  static constexpr int OFF_Z = 2 * KQV;           // z of the current chunk
+  static constexpr int OFF_S = OFF_Z + TILE;      // [128][128] 16-bit state copy
+  static constexpr int OFF_R = OFF_S + 2 * TILE;
+  static constexpr int OFF_D = OFF_R + TILE;
+  static constexpr int OFF_P = OFF_D + TILE;      // [64][64] 16-bit
+  static constexpr int OFF_A = OFF_P + C * C * 2; // [64][64] 16-bit, -A below the diagonal blocks
+  static constexpr int OFF_TII = OFF_A + C * C * 2;  // 4 x [16][16] 16-bit diagonal-block inverses
+  static constexpr int OFF_X = OFF_TII + 4 * 512;    // 8 warps x [16][16] 16-bit scratch
+  static constexpr int OFF_F32 = OFF_X + 8 * 512;
+  static constexpr int F32_ADIAG = 0;             // 4 x [16][17] fp32 diagonal blocks of A
+  static constexpr int F32_G = 4 * 16 * 17;       // [2][64] gates g (then G), by buffer
+  static constexpr int F32_B = F32_G + 2 * C;     // [2][64] beta
+  static constexpr int F32_RED = F32_B + 2 * C;   // [64][2] row sums of o^2
+  static constexpr int F32_COUNT = F32_RED + 2 * C;
+  static constexpr int SMEM_BYTES = OFF_F32 + F32_COUNT * 4;
+};
+
+// Byte offset of element (r, col) in a swizzled [rows][W] 16-bit tile.
+template <int W>
+__device__ __forceinline__ uint32_t gdn_elem(int r, int col) {
+  return static_cast<uint32_t>(r * W * 2 + ((((col >> 3) ^ (r & 7)) << 4) | ((col & 7) << 1)));
+}
+// Byte offset of 16-byte chunk c of row r in a swizzled [rows][W] 16-bit tile.
+template <int W>
+__device__ __forceinline__ uint32_t gdn_chunk16(int r, int c) {
+  return static_cast<uint32_t>(r * W * 2 + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool pred) {
+  const int n = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+
+template <class T>
+__global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnParams p) {
+  using Cfg = GdnChunkConfig;
+  constexpr int C = Cfg::C, D = Cfg::D;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t base = smem_u32(smem);
+  const uint32_t sZ = base + Cfg::OFF_Z, sS = base + Cfg::OFF_S, sR = base + Cfg::OFF_R, sD = base + Cfg::OFF_D;
+  const uint32_t sP = base + Cfg::OFF_P, sA = base + Cfg::OFF_A, sTii = base + Cfg::OFF_TII;
+  float* f32 = reinterpret_cast<float*>(smem + Cfg::OFF_F32);
+  float* sAd = f32 + Cfg::F32_ADIAG;
+  float* sRed = f32 + Cfg::F32_RED;
+
+  const int4 sg = p.segs[blockIdx.x];
+  const int start = sg.x, len = sg.y;
+  if (len <= 0) return;
+  const int head = blockIdx.y;
+  const int kh = head / (p.lv / p.lk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wr = warp & 3;
+  const T* qkv = static_cast<const T*>(p.qkv);
+  const T* proj = static_cast<const T*>(p.proj);
+  T* out = static_cast<T*>(p.out);
+  const int n_chunks = (len + C - 1) / C;
+
+  // K, Q, V rows of chunk ci (zero past the end) and its gates into buffer b.
+  auto load_chunk = [&](int ci, int b) {
+    const int c0 = ci * C, valid = min(C, len - c0);
+    for (int i = tid; i < 3 * C * (D / 8); i += 256) {
+      const int tile = i / (C * (D / 8)), r = (i >> 4) & (C - 1), c = i & 15;
+      const bool ok = r < valid;
+      const int col = tile == 0 ? p.kd + kh * D : (tile == 1 ? kh * D : 2 * p.kd + head * D);  // K, Q, V
+      cp_async16(base + b * Cfg::KQV + tile * Cfg::TILE + gdn_chunk16<D>(r, c),
+                 qkv + static_cast<size_t>(start + c0 + (ok ? r : 0)) * p.ld_qkv + col + c * 8, ok);
+    }
+    if (tid < 2 * C) {
+      const int t = tid & (C - 1);
+      const bool ok = t < valid;
+      const float* src = (tid < C ? p.g : p.beta) + static_cast<size_t>(start + c0 + (ok ? t : 0)) * p.lv + head;
+      cp_async4(smem_u32(f32 + (tid < C ? Cfg::F32_G : Cfg::F32_B) + b * C + t), src, ok);
+    }
+    cp_async_commit();
+  };
+  auto load_z = [&](int ci) {
+    const int c0 = ci * C, valid = min(C, len - c0);
+    for (int i = tid; i < C * (D / 8); i += 256) {
+      const int r = i >> 4, c = i & 15;
+      const bool ok = r < valid;
+      cp_async16(sZ + gdn_chunk16<D>(r, c),
+                 proj + static_cast<size_t>(start + c0 + (ok ? r : 0)) * p.ld_proj + p.col_z + head * D + c * 8, ok);
+    }
+    cp_async_commit();
+  };
+
+  // Fragment coordinates of the [64 x 128] products: rows r0.., columns c0n..
+  const int r0 = 16 * wr, c0n = 64 * (warp >> 2);
+  const int t0 = r0 + (lane >> 2);
+
+  float S[16][4];  // state rows 16*warp + lane/4 (+8), columns nb*8 + 2*(lane&3) (+1)
+#pragma unroll
+  for (int i = 0; i < 16; ++i) S[i][0] = S[i][1] = S[i][2] = S[i][3] = 0.0f;
+
+  load_chunk(0, 0);
+  float2 wn[8];  // gated-norm weights of this thread's output columns
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) wn[nb] = *reinterpret_cast<const float2*>(p.norm_w + c0n + nb * 8 + 2 * (lane & 3));
+  for (int ci = 0; ci < n_chunks; ++ci) {
+    const int c0 = ci * C;
+    const int valid = min(C, len - c0);
+    const bool first = ci == 0, last = ci + 1 == n_chunks;
+    const int buf = ci & 1;
+    const uint32_t sK = base + buf * Cfg::KQV, sQ = sK + Cfg::TILE, sV = sK + 2 * Cfg::TILE;
+    uint8_t* kbytes = smem + buf * Cfg::KQV;
+    float* sG = f32 + Cfg::F32_G + buf * C;
+    float* sB = f32 + Cfg::F32_B + buf * C;
+    __syncthreads();  // the previous chunk is done with z, the other K/Q/V buffer and the scratch
+    load_z(ci);
+    if (!last) {
+      load_chunk(ci + 1, buf ^ 1);
+      cp_async_wait<2>();
+    } else {
+      cp_async_wait<1>();
+    }
+    __syncthreads();
+    if (warp == 0) {  // inclusive prefix sum of g over the chunk (two tokens per lane)
+      const float a = sG[2 * lane], b = sG[2 * lane + 1];
+      float x = a + b;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      sG[2 * lane] = x - b;
+      sG[2 * lane + 1] = x;
+    }
+    __syncthreads();
+
+    // (1) warps 0-3: A = b_t e^(G_t-G_s) K K^T (s < t): diagonal blocks fp32,
+    // blocks left of them negated in 16 bits;  warps 4-7: P (s <= t), 16-bit.
+    // Key blocks right of the row block are zero and skipped.
+    {
+      const uint32_t sM = warp < 4 ? sK : sQ;
+      float acc[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t a[4];
+        ldmatrix_x4(sM + gdn_chunk16<D>(r0 + (lane & 15), ks * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nb2 = 0; nb2 < 4; ++nb2) {
+          if (nb2 > wr) continue;
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(sK + gdn_chunk16<D>(nb2 * 16 + (lane & 7) + ((lane >> 4) << 3), ks * 2 + ((lane >> 3) & 1)), b0,
+                      b1, b2, b3);
+          mma_16816<T>(acc[2 * nb2], a, b0, b1);
+          mma_16816<T>(acc[2 * nb2 + 1], a, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        if ((nb >> 1) > wr) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int t = t0 + 8 * h, s = nb * 8 + 2 * (lane & 3);
+          const float gt = sG[t];
+          if (warp < 4) {
+            const float bt = sB[t];
+            const float v0 = s < t ? bt * __expf(gt - sG[s]) * acc[nb][2 * h] : 0.0f;
+            const float v1 = s + 1 < t ? bt * __expf(gt - sG[s + 1]) * acc[nb][2 * h + 1] : 0.0f;
+            if ((nb >> 1) == wr) {
+              float* ad = sAd + wr * 272 + (t - r0) * 17 + (s - r0);
+              ad[0] = v0;
+              ad[1] = v1;
+            } else {
+              *reinterpret_cast<uint32_t*>(smem + Cfg::OFF_A + gdn_elem<C>(t, s)) = Elem<T>::pack2(-v0, -v1);
+            }
+          } else {
+            const float v0 = s <= t ? __expf(gt - sG[s]) * acc[nb][2 * h] : 0.0f;
+            const float v1 = s + 1 <= t ? __expf(gt - sG[s + 1]) * acc[nb][2 * h + 1] : 0.0f;
+            *reinterpret_cast<uint32_t*>(smem + Cfg::OFF_P + gdn_elem<C>(t, s)) = Elem<T>::pack2(v0, v1);
+          }
+        }
+      }
+    }
+
+    // (2) R = b (V - e^G K S0) -> sR;  O = e^G Q S0 kept in registers.
+    float o[8][4];
+    {
+      float ks_acc[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ks_acc[i][0] = ks_acc[i][1] = ks_acc[i][2] = ks_acc[i][3] = 0.0f;
+        o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+      }
+      if (!first) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          uint32_t aK[4], aQ[4];
+          const uint32_t off = gdn_chunk16<D>(r0 + (lane & 15), kk * 2 + (lane >> 4));
+          ldmatrix_x4(sK + off, aK[0], aK[1], aK[2], aK[3]);
+          ldmatrix_x4(sQ + off, aQ[0], aQ[1], aQ[2], aQ[3]);
+#pragma unroll
+          for (int nd2 = 0; nd2 < 4; ++nd2) {
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4_trans(sS + gdn_chunk16<D>(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3),
+                                                  (c0n >> 3) + nd2 * 2 + (lane >> 4)),
+                              b0, b1, b2, b3);
+            mma_16816<T>(ks_acc[2 * nd2], aK, b0, b1);
+            mma_16816<T>(ks_acc[2 * nd2 + 1], aK, b2, b3);
+            mma_16816<T>(o[2 * nd2], aQ, b0, b1);
+            mma_16816<T>(o[2 * nd2 + 1], aQ, b2, b3);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int t = t0 + 8 * h;
+        const float eg = __expf(sG[t]), bt = sB[t];
+#pragma unroll
+        for (int nb = 0; nb < 8; ++nb) {
+          const int col = c0n + nb * 8 + 2 * (lane & 3);
+          const uint32_t off = gdn_elem<D>(t, col);
+          const float2 v = Elem<T>::unpack2(*reinterpret_cast<const uint32_t*>(kbytes + 2 * Cfg::TILE + off));
+          *reinterpret_cast<uint32_t*>(smem + Cfg::OFF_R + off) =
+              Elem<T>::pack2(bt * (v.x - eg * ks_acc[nb][2 * h]), bt * (v.y - eg * ks_acc[nb][2 * h + 1]));
+          o[nb][2 * h] *= eg;
+          o[nb][2 * h + 1] *= eg;
+        }
+      }
+    }
+    __syncthreads();
+
+    // (3) Warps 0-3 invert diagonal block w of I + A (lane j: column j);
+    // warps 4-7 scale K rows by e^(G_C - G_t) for the state update.
+    if (warp < 4) {
+      if (lane < 16) {
+        const float* ad = sAd + warp * 272;
+        const int j = lane;
+        float x[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float a0 = i == j ? 1.0f : 0.0f, a1 = 0.0f;  // two chains: half the dependent FMA latency
+#pragma unroll
+          for (int m = 0; m + 1 < i; m += 2) {
+            a0 -= ad[i * 17 + m] * x[m];
+            a1 -= ad[i * 17 + m + 1] * x[m + 1];
+          }
+          if (i & 1) a0 -= ad[i * 17 + i - 1] * x[i - 1];
+          x[i] = a0 + a1;
+        }
+        T* tii = reinterpret_cast<T*>(smem + Cfg::OFF_TII + warp * 512);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tii[i * 16 + j] = Elem<T>::from(x[i]);
+      }
+    } else if (!last) {
+      const float gc = sG[C - 1];
+      for (int i = tid - 128; i < C * (D / 8); i += 128) {
+        const int r = i >> 4, c = i & 15;
+        const float f = __expf(gc - sG[r]);
+        uint4* q = reinterpret_cast<uint4*>(kbytes + gdn_chunk16<D>(r, c));
+        uint4 v = *q;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 x = Elem<T>::unpack2(w[e]);
+          w[e] = Elem<T>::pack2(x.x * f, x.y * f);
+        }
+        *q = v;
+      }
+    }
+    __syncthreads();
+
+    // (4) Block forward substitution for this warp's 16 value columns.
+    {
+      const int cw = 16 * warp;
+      uint8_t* xs = smem + Cfg::OFF_X + warp * 512;
+      const uint32_t sX = base + Cfg::OFF_X + warp * 512;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float acc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float2 r = Elem<T>::unpack2(*reinterpret_cast<const uint32_t*>(
+                smem + Cfg::OFF_R + gdn_elem<D>(16 * i + (lane >> 2) + 8 * h, cw + nt * 8 + 2 * (lane & 3))));
+            acc[nt][2 * h] = r.x;
+            acc[nt][2 * h + 1] = r.y;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          if (k >= i) continue;
+          uint32_t a[4], b0, b1, b2, b3;
+          ldmatrix_x4(sA + gdn_chunk16<C>(16 * i + (lane & 15), 2 * k + (lane >> 4)), a[0], a[1], a[2], a[3]);
+          ldmatrix_x4_trans(sD + gdn_chunk16<D>(16 * k + (lane & 7) + (((lane >> 3) & 1) << 3), (cw >> 3) + (lane >> 4)),
+                            b0, b1, b2, b3);
+          mma_16816<T>(acc[0], a, b0, b1);
+          mma_16816<T>(acc[1], a, b2, b3);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            *reinterpret_cast<uint32_t*>(xs + ((lane >> 2) + 8 * h) * 32 + (nt * 8 + 2 * (lane & 3)) * 2) =
+                Elem<T>::pack2(acc[nt][2 * h], acc[nt][2 * h + 1]);
+          }
+        }
+        __syncwarp();
+        uint32_t a[4], b0, b1, b2, b3;
+        ldmatrix_x4_trans(sX + ((lane & 7) + (((lane >> 3) & 1) << 3)) * 32 + (lane >> 4) * 16, b0, b1, b2, b3);
+        ldmatrix_x4(sTii + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, a[0], a[1], a[2], a[3]);
+        float d[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+        mma_16816<T>(d[0], a, b0, b1);
+        mma_16816<T>(d[1], a, b2, b3);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            *reinterpret_cast<uint32_t*>(
+                smem + Cfg::OFF_D + gdn_elem<D>(16 * i + (lane >> 2) + 8 * h, cw + nt * 8 + 2 * (lane & 3))) =
+                Elem<T>::pack2(d[nt][2 * h], d[nt][2 * h + 1]);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+
+    // (5a) O += P D (key blocks right of the row block are zero in P).
+#pragma unroll
+    for (int ks = 0; ks < C / 16; ++ks) {
+      if (ks > wr) continue;
+      uint32_t a[4];
+      ldmatrix_x4(sP + gdn_chunk16<C>(r0 + (lane & 15), ks * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+#pragma unroll
+      for (int nd2 = 0; nd2 < 4; ++nd2) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(sD + gdn_chunk16<D>(ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3),
+                                              (c0n >> 3) + nd2 * 2 + (lane >> 4)),
+                          b0, b1, b2, b3);
+        mma_16816<T>(o[2 * nd2], a, b0, b1);
+        mma_16816<T>(o[2 * nd2 + 1], a, b2, b3);
+      }
+    }
+
+    // (5b) S = e^(G_C) S + (e^(G_C - G) K)^T D; its 16-bit copy for the next chunk.
+    if (!last) {
+      const float ec = __expf(sG[C - 1]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        S[i][0] *= ec;
+        S[i][1] *= ec;
+        S[i][2] *= ec;
+        S[i][3] *= ec;
+      }
+      const int m0 = 16 * warp;
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        uint32_t a[4];
+        ldmatrix_x4_trans(sK + gdn_chunk16<D>(ks * 16 + (lane & 7) + ((lane >> 4) << 3), (m0 >> 3) + ((lane >> 3) & 1)),
+                          a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nd2 = 0; nd2 < 8; ++nd2) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(sD + gdn_chunk16<D>(ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), nd2 * 2 + (lane >> 4)),
+                            b0, b1, b2, b3);
+          mma_16816<T>(S[2 * nd2], a, b0, b1);
+          mma_16816<T>(S[2 * nd2 + 1], a, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = m0 + (lane >> 2) + 8 * h;
+#pragma unroll
+        for (int nb = 0; nb < 16; ++nb) {
+          const int col = nb * 8 + 2 * (lane & 3);
+          *reinterpret_cast<uint32_t*>(smem + Cfg::OFF_S + gdn_elem<D>(row, col)) =
+              Elem<T>::pack2(S[nb][2 * h], S[nb][2 * h + 1]);
+        }
+      }
+    }
+
+    // (5c) Gated RMSNorm over each token's 128 outputs (two warps per row).
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) ss += o[nb][2 * h] * o[nb][2 * h] + o[nb][2 * h + 1] * o[nb][2 * h + 1];
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      if ((lane & 3) == 0) sRed[(t0 + 8 * h) * 2 + (warp >> 2)] = ss;
+    }
+    if (!last) {
+      cp_async_wait<1>();  // z of this chunk (the next chunk's K, Q, V may still be in flight)
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = t0 + 8 * h;
+      if (t >= valid) continue;
+      const float rstd = rsqrtf((sRed[2 * t] + sRed[2 * t + 1]) * (1.0f / D) + p.eps);
+      T* orow = out + static_cast<size_t>(start + c0 + t) * p.ld_out + head * D;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        const int col = c0n + nb * 8 + 2 * (lane & 3);
+        const float2 z = Elem<T>::unpack2(*reinterpret_cast<const uint32_t*>(smem + Cfg::OFF_Z + gdn_elem<D>(t, col)));
+        *reinterpret_cast<uint32_t*>(orow + col) = Elem<T>::pack2(o[nb][2 * h] * rstd * wn[nb].x * silu_f(z.x),
+                                                                  o[nb][2 * h + 1] * rstd * wn[nb].y * silu_f(z.y));
+      }
+    }
   }
 }
 

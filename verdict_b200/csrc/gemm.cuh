@@ -47,8 +47,11 @@ struct EpiParams {
   int rot_dim;            // rotary width: the first rot_dim columns of a head (multiple of 64; 0 = head_dim)
 };
 
+// group_m: M tiles per raster group (tiles walk M fastest inside a group, so a
+// group's A rows stay in L2 while W streams past them once per group).
 struct GemmShape {
   int M, N, K;
+  int group_m;
 };
 
 __device__ __forceinline__ float apply_act(float x, int act) {
@@ -430,7 +433,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         int m, n;
-        tile_coords(tile, num_m, num_n, Cfg::GROUP_M, m, n);
+        tile_coords(tile, num_m, num_n, shape.group_m, m, n);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) goto producer_done;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
@@ -502,7 +505,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int m, n;
-      tile_coords(tile, num_m, num_n, Cfg::GROUP_M, m, n);
+      tile_coords(tile, num_m, num_n, shape.group_m, m, n);
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);

@@ -206,7 +206,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       uint32_t phase = 0;
       for (int tile = pair; tile < tiles; tile += pairs) {
         int m, n;
-        tile_coords(tile, num_m, num_n, Cfg::GROUP_M, m, n);
+        tile_coords(tile, num_m, num_n, shape.group_m, m, n);
         const int ya = m * 2 * BM + static_cast<int>(rank) * BM;
         const int yb = n * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -280,7 +280,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < tiles; tile += pairs) {
       int m, n;
-      tile_coords(tile, num_m, num_n, Cfg::GROUP_M, m, n);
+      tile_coords(tile, num_m, num_n, shape.group_m, m, n);
       if (!mbar_wait_cluster(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);

@@ -46,8 +46,9 @@ static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, const 
                               int* word, int sms) {
   const int tiles = ((M + 127) / 128) * (N / bn);
   const int grid = std::min(tiles, sms);
-  const GemmShape shape{M, N, K};
+  GemmShape shape{M, N, K, GemmConfig<256>::GROUP_M};
   const int pairs = bn == 256 ? gemm2_max_pairs(sms) : 0;
+  if (pairs > 0) shape.group_m = Gemm2Config::GROUP_M;
   if (pairs > 0) {
     const int grid2 = 2 * std::min(((M + 255) / 256) * (N / 256), pairs);
     gemm2_tcgen05_kernel<EPI, T><<<grid2, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, s>>>(a, w_half, c, shape,

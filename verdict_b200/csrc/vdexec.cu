@@ -597,6 +597,8 @@ struct Options {
   bool tc_attention = true;  // head_dim 128 causal attention on tcgen05 (else the mma.sync kernel)
   bool fork = true;          // shared-prefix rows: prefix computed once (host-memory decoder batches)
   bool gemm2 = true;         // 256-wide projections on CTA pairs (cta_group::2), else one CTA per tile
+  int raster_group = 0;      // M tiles per GEMM raster group; 0 = the kernel's default
+  bool gdn_chunk = true;     // gated delta nets in 64-token chunks on the tensor cores, else token by token
 };
 
 }  // namespace vd
@@ -1279,6 +1281,9 @@ static void init_kernel_attrs_t() {
   cuda_check(cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnTcConfig::SMEM_BYTES),
              "tcgen05 attention smem attribute");
+  cuda_check(cudaFuncSetAttribute(gdn_chunk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  GdnChunkConfig::SMEM_BYTES),
+             "chunked gated delta net smem attribute");
 }
 
 static void init_kernel_attrs() {
@@ -1307,9 +1312,10 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const int num_m = (M + 127) / 128;
   const int tiles = num_m * (L.n / L.bn);
   const int grid = std::min(tiles, H->num_sms);
-  const GemmShape shape{M, L.n, L.k};
+  GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
   if (L.bn == 256 && H->opt.gemm2 && H->gemm2_pairs > 0) {
+    if (H->opt.raster_group <= 0) shape.group_m = Gemm2Config::GROUP_M;
     const int pair_tiles = ((M + 255) / 256) * (L.n / 256);
     const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
     launch(H, kind, flops, [&] {
@@ -1654,6 +1660,15 @@ static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan
   g.eps = static_cast<float>(s.rms_eps);
   g.segs = reinterpret_cast<const int4*>(H->segs);
   launch(H, VD_K_GDN, 0.0, [&] { gdn_conv_prep_kernel<T, 4><<<ntok, 256, 0, H->stream>>>(g); });
+  if (H->opt.gdn_chunk) {
+    // per token and value head: K K^T and Q K^T rows (2 x 64 x 128), K S0 and
+    // Q S0 (2 x 128 x 128), T R and P D (2 x 64 x 128), the state update (128 x 128)
+    const double flops = 2.0 * ntok * s.lin_v_heads * (4.0 * 64 * 128 + 3.0 * 128 * 128);
+    launch(H, VD_K_GDN, flops, [&] {
+      gdn_chunk_kernel<T><<<dim3(P.n_seg, s.lin_v_heads), 256, GdnChunkConfig::SMEM_BYTES, H->stream>>>(g);
+    });
+    return;
+  }
   // per token and value head: decay + two rank-1 passes over the 128 x 128 state
   const double flops = 4.0 * ntok * s.lin_v_heads * s.lin_k_dim * s.lin_v_dim;
   launch(H, VD_K_GDN, flops, [&] {
@@ -2076,6 +2091,11 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       const std::string gm = o.string_or("gemm", "2sm");
       if (gm != "2sm" && gm != "1sm") fail(VD_EINVAL, "gemm must be \"2sm\" or \"1sm\"");
       H->opt.gemm2 = gm == "2sm";
+      H->opt.raster_group = static_cast<int>(o.integer_or("raster_group", 0));
+      const std::string gd = o.string_or("gdn", "chunk");
+      if (gd != "chunk" && gd != "scan") fail(VD_EINVAL, "gdn must be \"chunk\" or \"scan\"");
+      H->opt.gdn_chunk = gd == "chunk";
+      if (H->opt.raster_group < 0 || H->opt.raster_group > 4096) fail(VD_EINVAL, "raster_group must be in [0, 4096]");
       const std::string at = o.string_or("attention", "tc");
       if (at != "tc" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\" or \"mma\"");
       H->opt.tc_attention = at == "tc";

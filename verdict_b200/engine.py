@@ -73,7 +73,8 @@ class B200Engine(Engine):
     def __init__(self, spec, device: int = 0, *, max_tokens: int = 65536, max_rows: int = 512,
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
-                 prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm"):
+                 prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
+                 raster_group: int = 0, gdn: str = "chunk"):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory)."""
         self.lib = _abi.load()
@@ -90,7 +91,7 @@ class B200Engine(Engine):
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
                                attention=attention, prune_last_layer=prune_last_layer, fork=fork,
-                               gemm=gemm))
+                               gemm=gemm, raster_group=raster_group, gdn=gdn))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
         rc = self.lib.vd_open(model, device, opts.encode(), ctypes.byref(h), err, len(err))
