@@ -11,13 +11,15 @@
 //   y    = RMSNorm(o over the head) * w * silu(z)               (gated norm)
 //   out  = y @ W_out^T                          (GEMM, residual epilogue)
 //
-// gdn_conv_prep_kernel does the conv, the l2 norms and the gates for one token
-// per CTA; gdn_scan_kernel runs the recurrence for one (sequence, v head) per
-// CTA with two threads per state column (dk = dv = 128: 64 fp32 registers of
-// state per thread), k and q of the next token staged in shared memory while
-// the current one is consumed, and applies the gated norm of token t in step
-// t + 1 (the head's sum of squares needs the CTA-wide reduction that step's
-// barrier already provides).
+// gdn_conv_prep_kernel does the conv, the l2 norms and the gates (32-token
+// tiles, one conv head per warp).  The recurrence and the gated norm run in
+// gdn_chunk_kernel (64-token chunks on the tensor cores, the default) or in
+// gdn_scan_kernel (token by token: one (sequence, v head) per CTA with two
+// threads per state column (dk = dv = 128: 64 fp32 registers of state per
+// thread), k and q of the next token staged in shared memory while the
+// current one is consumed, and the gated norm of token t applied in step t + 1
+// (the head's sum of squares needs the CTA-wide reduction that step's barrier
+// already provides)).
 #pragma once
 
 #include "common.cuh"
@@ -48,53 +50,98 @@ struct GdnParams {
 
 __device__ __forceinline__ float silu_f(float x) { return x * __fdividef(1.0f, 1.0f + __expf(-x)); }
 
-// One token per CTA (256 threads = 8 warps); warp w handles heads w, w + 8, ...
-// of the 2*lk + lv conv heads (q heads, then k heads, then v heads), 4
-// channels per lane.  K is the conv width.
+// Tiles of GDN_CONV_TOKENS tokens; warp w of block row y owns conv head
+// 8y + w (q heads, then k heads, then v heads, 128 channels each, 4 per
+// lane), keeps its conv weights and the last K - 1 inputs in registers and
+// walks the tile's tokens in order, so every input row is read once.  The
+// history restarts at each sequence start (position 0) and, at the tile start,
+// is loaded for the tokens the position says are inside the sequence.  The
+// last block row computes the gates g and beta of the tile's tokens.
+constexpr int GDN_CONV_TOKENS = 32;
+
 template <class T, int K>
 __global__ void __launch_bounds__(256) gdn_conv_prep_kernel(GdnParams p) {
-  const int t = blockIdx.x;
-  if (t >= p.ntok) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pos = p.positions[t];
-  const T* proj = static_cast<const T*>(p.proj);
-  T* out = static_cast<T*>(p.qkv);
+  const int t_begin = blockIdx.x * GDN_CONV_TOKENS;
+  const int t_end = min(t_begin + GDN_CONV_TOKENS, p.ntok);
   const int heads = 2 * p.lk + p.lv;
-  for (int h = warp; h < heads; h += 8) {
-    const int c = h * 128 + lane * 4;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const float4* wr = reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(c) * K);
-    float w[4][K];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* proj = static_cast<const T*>(p.proj);
+  if (blockIdx.y == gridDim.y - 1) {  // gates
+    for (int i = threadIdx.x; i < GDN_CONV_TOKENS * p.lv; i += 256) {
+      const int t = t_begin + i / p.lv, h = i % p.lv;
+      if (t >= t_end) break;
+      const float a = Elem<T>::to(proj[static_cast<size_t>(t) * p.ld_proj + p.col_a + h]);
+      const float b = Elem<T>::to(proj[static_cast<size_t>(t) * p.ld_proj + p.col_b + h]);
+      const float x = a + p.dt_bias[h];
+      const float sp = x > 20.0f ? x : log1pf(__expf(x));  // softplus (threshold 20)
+      p.g[static_cast<size_t>(t) * p.lv + h] = -__expf(p.A_log[h]) * sp;
+      p.beta[static_cast<size_t>(t) * p.lv + h] = __fdividef(1.0f, 1.0f + __expf(-b));
+    }
+    return;
+  }
+  const int h = blockIdx.y * 8 + warp;
+  if (h >= heads) return;
+  const int c = h * 128 + lane * 4;
+  T* out = static_cast<T*>(p.qkv);
+  float w[4][K];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 4; ++i) {
+    const float4* wr = reinterpret_cast<const float4*>(p.conv_w + static_cast<size_t>(c + i) * K);
 #pragma unroll
-      for (int j = 0; j < K; j += 4) {
-        const float4 v = __ldg(wr + (i * K + j) / 4);
-        w[i][j] = v.x;
-        if (j + 1 < K) w[i][j + 1] = v.y;
-        if (j + 2 < K) w[i][j + 2] = v.z;
-        if (j + 3 < K) w[i][j + 3] = v.w;
+    for (int j = 0; j < K; j += 4) {
+      const float4 v = __ldg(wr + j / 4);
+      w[i][j] = v.x;
+      if (j + 1 < K) w[i][j + 1] = v.y;
+      if (j + 2 < K) w[i][j + 2] = v.z;
+      if (j + 3 < K) w[i][j + 3] = v.w;
+    }
+  }
+  const bool is_qk = h < 2 * p.lk;
+  const float scale = h < p.lk ? p.q_scale : 1.0f;
+  auto load4 = [&](int t, float (&x)[4]) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(proj + static_cast<size_t>(t) * p.ld_proj + c);
+    const float2 a = Elem<T>::unpack2(raw.x), b = Elem<T>::unpack2(raw.y);
+    x[0] = a.x;
+    x[1] = a.y;
+    x[2] = b.x;
+    x[3] = b.y;
+  };
+  // hist[j]: input of token t - 1 - j (0 outside the sequence)
+  float hist[K - 1][4];
+  {
+    const int pos0 = p.positions[t_begin];
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {
+      if (j < pos0) {
+        load4(t_begin - 1 - j, hist[j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hist[j][i] = 0.0f;
       }
     }
+  }
+  for (int t = t_begin; t < t_end; ++t) {
+    float x[4];
+    load4(t, x);
+    if (p.positions[t] == 0) {
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      const int back = K - 1 - j;  // tokens before t
-      if (back > pos) continue;    // before the sequence start: zero history
-      const uint2 raw = *reinterpret_cast<const uint2*>(proj + static_cast<size_t>(t - back) * p.ld_proj + c);
-      const float2 a = Elem<T>::unpack2(raw.x), b = Elem<T>::unpack2(raw.y);
-      acc[0] += w[0][j] * a.x;
-      acc[1] += w[1][j] * a.y;
-      acc[2] += w[2][j] * b.x;
-      acc[3] += w[3][j] * b.y;
+      for (int j = 0; j < K - 1; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hist[j][i] = 0.0f;
     }
+    float acc[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i] = silu_f(acc[i]);
-    if (h < 2 * p.lk) {  // q or k head: l2 norm over its 128 channels
+    for (int i = 0; i < 4; ++i) {
+      float a = w[i][K - 1] * x[i];
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) a += w[i][K - 2 - j] * hist[j][i];
+      acc[i] = silu_f(a);
+    }
+    if (is_qk) {  // l2 norm over the head's 128 channels
       float ss = acc[0] * acc[0] + acc[1] * acc[1] + acc[2] * acc[2] + acc[3] * acc[3];
 #pragma unroll
-      for (int s = 16; s > 0; s >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s);
-      float r = rsqrtf(ss + 1e-6f);
-      if (h < p.lk) r *= p.q_scale;
+      for (int sft = 16; sft > 0; sft >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, sft);
+      const float r = rsqrtf(ss + 1e-6f) * scale;
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[i] *= r;
     }
@@ -102,14 +149,12 @@ __global__ void __launch_bounds__(256) gdn_conv_prep_kernel(GdnParams p) {
     o.x = Elem<T>::pack2(acc[0], acc[1]);
     o.y = Elem<T>::pack2(acc[2], acc[3]);
     *reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * p.ld_qkv + c) = o;
-  }
-  for (int h = threadIdx.x; h < p.lv; h += 256) {
-    const float a = Elem<T>::to(proj[static_cast<size_t>(t) * p.ld_proj + p.col_a + h]);
-    const float b = Elem<T>::to(proj[static_cast<size_t>(t) * p.ld_proj + p.col_b + h]);
-    const float x = a + p.dt_bias[h];
-    const float sp = x > 20.0f ? x : log1pf(__expf(x));  // softplus (threshold 20)
-    p.g[static_cast<size_t>(t) * p.lv + h] = -__expf(p.A_log[h]) * sp;
-    p.beta[static_cast<size_t>(t) * p.lv + h] = 1.0f / (1.0f + __expf(-b));
+#pragma unroll
+    for (int j = K - 2; j > 0; --j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hist[j][i] = hist[j - 1][i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hist[0][i] = x[i];
   }
 }
 
@@ -308,10 +353,12 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnParams p) {
   float* sAd = f32 + Cfg::F32_ADIAG;
   float* sRed = f32 + Cfg::F32_RED;
 
-  const int4 sg = p.segs[blockIdx.x];
+  // blockIdx.x: value head (fastest, so the heads of the longest sequences,
+  // listed first, start first), blockIdx.y: sequence
+  const int4 sg = p.segs[blockIdx.y];
   const int start = sg.x, len = sg.y;
   if (len <= 0) return;
-  const int head = blockIdx.y;
+  const int head = blockIdx.x;
   const int kh = head / (p.lv / p.lk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int wr = warp & 3;

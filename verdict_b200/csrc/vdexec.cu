@@ -1574,6 +1574,12 @@ static ChunkPlan plan_chunk(vd_handle* H, const Chunk& c, bool causal, int tile_
   }
   cu[c.nb] = P.ntok;
   P.n_tiles = n;
+  // Gated-delta-net recurrences run one CTA per (sequence, head), as long as
+  // the sequence: longest first, so the last wave is not one long sequence.
+  // (Each entry carries its own start and source row; no kernel depends on
+  // the order.)
+  if (H->spec.any_linear())
+    std::stable_sort(segs, segs + P.n_seg, [](const PackSeg& a, const PackSeg& b) { return a.len > b.len; });
   // Longest work first: a causal tile costs ~ its last query row's keys.
   std::stable_sort(tiles, tiles + n, [causal, tile_rows](const AttnTile& a, const AttnTile& b) {
     const int wa = (causal ? std::min(a.seq_len, a.q_start + tile_rows) : a.seq_len) + a.pre_len;
@@ -1659,13 +1665,14 @@ static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan
   g.q_scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(s.lin_k_dim)));
   g.eps = static_cast<float>(s.rms_eps);
   g.segs = reinterpret_cast<const int4*>(H->segs);
-  launch(H, VD_K_GDN, 0.0, [&] { gdn_conv_prep_kernel<T, 4><<<ntok, 256, 0, H->stream>>>(g); });
+  const dim3 conv_grid((ntok + GDN_CONV_TOKENS - 1) / GDN_CONV_TOKENS, (2 * g.lk + g.lv + 7) / 8 + 1);
+  launch(H, VD_K_GDN, 0.0, [&] { gdn_conv_prep_kernel<T, 4><<<conv_grid, 256, 0, H->stream>>>(g); });
   if (H->opt.gdn_chunk) {
     // per token and value head: K K^T and Q K^T rows (2 x 64 x 128), K S0 and
     // Q S0 (2 x 128 x 128), T R and P D (2 x 64 x 128), the state update (128 x 128)
     const double flops = 2.0 * ntok * s.lin_v_heads * (4.0 * 64 * 128 + 3.0 * 128 * 128);
     launch(H, VD_K_GDN, flops, [&] {
-      gdn_chunk_kernel<T><<<dim3(P.n_seg, s.lin_v_heads), 256, GdnChunkConfig::SMEM_BYTES, H->stream>>>(g);
+      gdn_chunk_kernel<T><<<dim3(s.lin_v_heads, P.n_seg), 256, GdnChunkConfig::SMEM_BYTES, H->stream>>>(g);
     });
     return;
   }
