@@ -194,12 +194,12 @@ def test_gemm_rejects_bad_shapes():
     assert rc == _abi.VD_EINVAL and b"N % 128" in err.value
 
 
-@pytest.mark.parametrize("nq,nkv", [(32, 8), (4, 4), (40, 8)])
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 32, 8), (128, 4, 4), (128, 40, 8), (256, 8, 1), (256, 16, 4),
+                                       (256, 3, 3)])
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
-def test_attention_tc_varlen(nq, nkv, dt):
-    """The tcgen05 / TMEM attention kernel (head_dim 128, causal) vs torch fp32 SDPA."""
-    hd = 128
-    g = torch.Generator(device="cuda").manual_seed(nq * 7 + nkv)
+def test_attention_tc_varlen(hd, nq, nkv, dt):
+    """The tcgen05 / TMEM attention kernels (head_dim 128 and 256, causal) vs torch fp32 SDPA."""
+    g = torch.Generator(device="cuda").manual_seed(hd + nq * 7 + nkv)
     lens = [1, 127, 128, 129, 300, 17, 1000, 256, 2100]
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     T = int(cu[-1])

@@ -1,0 +1,324 @@
+// Causal varlen attention on the tcgen05 tensor cores for head_dim 256 (the
+// Gemma-2B decider and the Qwen3.5 hybrids' gated attention layers).
+//
+// One CTA = one 128-row query tile of one sequence for one query head; keys in
+// tiles of 64.  TMEM: two S/P buffers of 64 columns (S of tile j + 1 is computed
+// while the softmax warps work on tile j) and O, 128 rows x 256 fp32 columns.
+//   warp 0      : TMA producer of Q (once) and the K tiles (2-stage ring)
+//   warp 1      : TMEM allocator + MMA issuer (one lane):
+//                 S(0), S(1), then per tile j: O += P(j) V(j) (A = P from
+//                 TMEM, B = V MN-major), S(j + 2) into the buffer P(j) used
+//   warp 2      : TMA producer of the V tiles (2-stage ring; a K stage is
+//                 released once its S is computed, a V stage once its P V is)
+//   warps 3..6  : softmax, one query row per thread (TMEM lane quarter = warp
+//                 & 3): S from TMEM, running max with lazy rescaling (a row
+//                 keeps its max until a tile raises it by more than 8 in log2
+//                 units; a raise rescales O in TMEM after the previous P V has
+//                 completed), P packed to 16-bit pairs over S; at the end
+//                 O / l (times sigmoid(gate) for gated attention) to global.
+// Shared memory: Q 64 KB (four 128 x 64 swizzled atoms), K and V 2 x 32 KB
+// each.  Every mbarrier wait is bounded; on a timeout the CTA records an error
+// code, raises its abort flag and all roles leave their loops.
+#pragma once
+
+#include "attention_tc.cuh"
+
+namespace vd {
+
+struct AttnTc256Params {
+  void* out;                   // T [tokens, ld_out]
+  int ld_out;
+  const void* qkv;             // T [tokens, ld_qkv] (gate columns for gated attention)
+  int ld_qkv;
+  int q_col0, k_col0, v_col0;  // column offsets of the q / k / v blocks in qkv
+  int gate_col0;               // >= 0: output *= sigmoid(qkv[:, gate_col0 + head * 256 + c])
+  const AttnTile* tiles;       // 128-row query tiles
+  int group;                   // query heads per K/V head
+  float scale_log2;
+  int* err;
+};
+
+struct AttnTc256Config {
+  static constexpr int HD = 256, BM = 128, BN = 64;
+  static constexpr int Q_ATOM = BM * 64 * 2;    // [128 rows x 64 cols] 16-bit, 16 KB
+  static constexpr int KV_ATOM = BN * 64 * 2;   // [64 rows x 64 cols], 8 KB
+  static constexpr int Q_BYTES = 4 * Q_ATOM;    // 64 KB
+  static constexpr int KV_BYTES = 4 * KV_ATOM;  // 32 KB
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;
+  static constexpr int BAR_OFF = V_OFF + 2 * KV_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 256;
+  static constexpr int THREADS = 224;
+  static constexpr uint32_t TMEM_COLS = 512;  // S/P [0, 128), O [128, 384)
+  static constexpr float RESCALE_THRESHOLD = 8.0f;
+};
+
+template <class T>
+__global__ void __launch_bounds__(224, 1)
+    attention_tc256_kernel(const __grid_constant__ CUtensorMap tm_qkv64, AttnTc256Params p) {
+  using C = AttnTc256Config;
+  constexpr uint32_t FMT = Elem<T>::kUmmaFormat;
+  constexpr uint32_t IDESC_S = umma_idesc_f16kind(128, 64, FMT);                // A, B K-major
+  constexpr uint32_t IDESC_PV = umma_idesc_f16kind(128, 256, FMT) | (1u << 16);  // B (V) MN-major
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2] per stage
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* k_empty = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per S/P buffer
+  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* pv_done = bars + 13;  // one arrival per P V
+  uint64_t* o_final = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const AttnTile tile = p.tiles[blockIdx.x];
+  const int head = blockIdx.y;
+  const int kvh = head / p.group;
+  const int kv_end = min(tile.seq_len, tile.q_start + C::BM);
+  // Key tiles: first the shared prefix's (n_pre, unmasked but for its end),
+  // then the sequence's own (causal).
+  const int n_pre = (tile.pre_len + C::BN - 1) / C::BN;
+  const int n_kv = n_pre + (kv_end + C::BN - 1) / C::BN;
+  auto key_row = [&](int j) {
+    return j < n_pre ? tile.pre_start + j * C::BN : tile.seq_start + (j - n_pre) * C::BN;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(o_final, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv64);
+      const int qx = p.q_col0 + head * C::HD, kx = p.k_col0 + kvh * C::HD;
+      const int qy = tile.seq_start + tile.q_start;
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM, &tm_qkv64, q_full, qx + 64 * a, qy);
+        tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM + C::Q_ATOM / 2, &tm_qkv64, q_full, qx + 64 * a, qy + 64);
+      }
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tma_load_2d(smem + C::K_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &k_full[s], kx + 64 * a,
+                      key_row(j));
+      }
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {
+      const int vx = p.v_col0 + kvh * C::HD;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tma_load_2d(smem + C::V_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &v_full[s], vx + 64 * a,
+                      key_row(j));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(smem + C::Q_OFF);
+      // S(j) = Q K_j^T into S/P buffer j & 1; releases K stage j & 1 when done.
+      auto issue_s = [&](int j) {
+        const int b = j & 1;
+        const uint32_t k_addr = smem_u32(smem + C::K_OFF + b * C::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          umma_f16kind(tmem + b * 64, sw128_kmajor_desc(q_addr + (kk >> 2) * C::Q_ATOM + (kk & 3) * 32),
+                       sw128_kmajor_desc(k_addr + (kk >> 2) * C::KV_ATOM + (kk & 3) * 32), IDESC_S,
+                       kk != 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[b]);
+        umma_commit(&k_empty[b]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutFull);
+      for (int j = 0; ok && j < 2 && j < n_kv; ++j) {
+        if (!mbar_wait(&k_full[j], 0, abort_flag, p.err, kErrTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_s(j);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int b = j & 1, ph = (j >> 1) & 1;
+        if (!mbar_wait(&v_full[b], ph, abort_flag, p.err, kErrTimeoutFull)) break;
+        if (!mbar_wait(&p_full[b], ph, abort_flag, p.err, kErrTimeoutFull)) break;
+        tc_fence_after();
+        // O += P(j) V(j): A = P from TMEM (8 columns per 16 keys), B = V
+        // MN-major (64-dim atoms KV_ATOM apart), K advances 16 key rows = 2 KB.
+        const uint32_t v_addr = smem_u32(smem + C::V_OFF + b * C::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16kind_ts(tmem + 128, tmem + b * 64 + kk * 8, sw128_mnmajor_desc(v_addr + kk * 2048, C::KV_ATOM),
+                          IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[b]);
+        umma_commit(pv_done);
+        if (j + 1 == n_kv) umma_commit(o_final);
+        // S(j + 2) overwrites P(j) in TMEM; MMAs of one thread run in order.
+        if (j + 2 < n_kv) {
+          if (!mbar_wait(&k_full[b], ((j + 2) >> 1) & 1, abort_flag, p.err, kErrTimeoutFull)) break;
+          tc_fence_after();
+          issue_s(j + 2);
+        }
+      }
+    }
+  } else {
+    // Softmax warps 3..6: query row r of the tile, TMEM lane quarter warp & 3.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t o_tm = tmem + lane_base + 128;
+    const int q_row = tile.q_start + r;  // row inside the sequence
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int b = j & 1;
+      const uint32_t s_tm = tmem + lane_base + b * 64;
+      const bool in_pre = j < n_pre;
+      const int kv0 = (in_pre ? j : j - n_pre) * C::BN;  // key index inside its segment
+      const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
+      const int causal_row = in_pre ? 0x7fffffff : q_row;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool need_mask = kv0 + C::BN > seg_len || (!in_pre && kv0 + C::BN > tile.q_start);
+      uint32_t sr[64];
+      tmem_ld32_nowait(s_tm + 0, sr + 0);
+      tmem_ld32_nowait(s_tm + 32, sr + 32);
+      tmem_wait_ld();
+      float mx = -INFINITY;
+      if (need_mask) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int kv = kv0 + i;
+          if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(sr[i]));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+      }
+      const float m_tile = mx * p.scale_log2;
+      const bool raise = m_tile > m_run + C::RESCALE_THRESHOLD;
+      const bool warp_raise = __any_sync(0xffffffffu, raise);
+      const float m_new = raise ? m_tile : m_run;
+      const float alpha = raise ? fast_exp2(m_run - m_new) : 1.0f;
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float e0 = fast_exp2(__uint_as_float(sr[c * 32 + i]) * p.scale_log2 - m_new);
+          const float e1 = fast_exp2(__uint_as_float(sr[c * 32 + i + 1]) * p.scale_log2 - m_new);
+          rs += e0 + e1;
+          pk[i >> 1] = Elem<T>::pack2(e0, e1);
+        }
+        tmem_st16(s_tm + c * 16, pk);
+      }
+      // A raised max rescales the O rows accumulated so far, once P(j - 1) V
+      // has landed (P(j) V cannot start before this warp's p_full arrival).
+      if (warp_raise && j > 0) {
+        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float v[32];
+          tmem_load_f32x32(o_tm + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32f(o_tm + c * 32, v);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+    }
+    if (ok && mbar_wait(o_final, 0, abort_flag, p.err, kErrTimeoutAccFull)) {
+      tc_fence_after();
+      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      const size_t tok = static_cast<size_t>(tile.seq_start + q_row);
+      T* dst = static_cast<T*>(p.out) + tok * p.ld_out + head * C::HD;
+      const T* gate = p.gate_col0 >= 0 ? static_cast<const T*>(p.qkv) + tok * p.ld_qkv + p.gate_col0 + head * C::HD
+                                       : nullptr;
+      const bool live = q_row < tile.seq_len;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        float v[32];
+        tmem_load_f32x32(o_tm + c * 32, v);
+        if (live) {
+          if (gate != nullptr) {
+            const uint4* g4 = reinterpret_cast<const uint4*>(gate + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w = g4[q];
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 g = Elem<T>::unpack2(ws[e]);
+                v[q * 8 + 2 * e] *= inv * __fdividef(1.0f, 1.0f + __expf(-g.x));
+                v[q * 8 + 2 * e + 1] *= inv * __fdividef(1.0f, 1.0f + __expf(-g.y));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= inv;
+          }
+          store_x32<T>(dst + c * 32, v);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace vd

@@ -225,7 +225,8 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
                                        const int32_t* cu_seqlens_host, int64_t nseq, void* out, int64_t ld_out,
                                        void* stream, char* err, size_t errlen) {
   return guarded(nullptr, err, errlen, [&] {
-    if (head_dim != 128 || !causal) fail(VD_EINVAL, "the tcgen05 attention kernel is causal with head_dim 128");
+    if ((head_dim != 128 && head_dim != 256) || !causal)
+      fail(VD_EINVAL, "the tcgen05 attention kernels are causal with head_dim 128 or 256");
     if (heads < 1 || kv_heads < 1 || heads % kv_heads != 0) fail(VD_EINVAL, "heads must be a multiple of kv_heads");
     if (nseq < 1 || !cu_seqlens_host || !qkv || !out) fail(VD_EINVAL, "need at least one sequence and buffers");
     if (ld_qkv % 8 != 0 || q_col0 % 8 != 0 || k_col0 % 8 != 0 || v_col0 % 8 != 0 || ld_out % 8 != 0)
@@ -248,6 +249,30 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
     cuda_check(cudaMalloc(&d_tiles, tiles.size() * sizeof(AttnTile)), "tile table");
     std::unique_ptr<AttnTile, decltype(&cudaFree)> guard(d_tiles, &cudaFree);
     cuda_check(cudaMemcpy(d_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice), "tiles");
+    if (head_dim == 256) {
+      const CUtensorMap map64 = make_map(qkv, T, ld_qkv, 64, f16);
+      AttnTc256Params p;
+      p.out = out;
+      p.ld_out = static_cast<int>(ld_out);
+      p.qkv = qkv;
+      p.ld_qkv = static_cast<int>(ld_qkv);
+      p.q_col0 = static_cast<int>(q_col0);
+      p.k_col0 = static_cast<int>(k_col0);
+      p.v_col0 = static_cast<int>(v_col0);
+      p.gate_col0 = -1;
+      p.tiles = d_tiles;
+      p.group = heads / kv_heads;
+      p.scale_log2 = static_cast<float>(1.0 / std::sqrt(256.0) * 1.4426950408889634);
+      p.err = word;
+      dim3 grid(static_cast<unsigned>(tiles.size()), heads);
+      if (f16)
+        attention_tc256_kernel<__half><<<grid, AttnTc256Config::THREADS, AttnTc256Config::SMEM_BYTES, s>>>(map64, p);
+      else
+        attention_tc256_kernel<__nv_bfloat16>
+            <<<grid, AttnTc256Config::THREADS, AttnTc256Config::SMEM_BYTES, s>>>(map64, p);
+      ops_finish(s, word);
+      return;
+    }
     const CUtensorMap map = make_map(qkv, T, ld_qkv, 128, f16);
     AttnTcParams p;
     p.out = out;

@@ -36,6 +36,7 @@
 #include "vdexec.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "attention_tc256.cuh"
 #include "checkpoint.hpp"
 #include "common.cuh"
 #include "convert.cuh"
@@ -639,7 +640,7 @@ struct vd_handle {
   vd::PackSeg* segs = nullptr;  // packed sequences of a chunk (rows, shared prefixes, suffixes)
   vd::RowMap* rowmap = nullptr; // per decision: where its slot token is packed
   float2* rope = nullptr;
-  CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow, map_qkv;
+  CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow, map_qkv, map_qkv64;
   // last-layer slot rows (one per decision of a chunk)
   float* h_s = nullptr;
   void *xn_s = nullptr, *attn_s = nullptr, *act_s = nullptr;
@@ -1196,6 +1197,7 @@ static void alloc_workspace(vd_handle* H) {
   H->map_xn = make_map(H->xn, T, d, 128, f16);
   H->map_attn = make_map(H->attn, T, attw, 128, f16);
   H->map_qkv = make_map(H->qkv, T, qkvw, 128, f16);
+  H->map_qkv64 = make_map(H->qkv, T, qkvw, 64, f16);
   H->out_qkv = make_out_map(H->qkv, T, qkvw, false, f16);
   H->out_h = make_out_map(H->h, T, d, true);
   if (s.decoder()) {
@@ -1281,6 +1283,9 @@ static void init_kernel_attrs_t() {
   cuda_check(cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnTcConfig::SMEM_BYTES),
              "tcgen05 attention smem attribute");
+  cuda_check(cudaFuncSetAttribute(attention_tc256_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnTc256Config::SMEM_BYTES),
+             "tcgen05 head_dim-256 attention smem attribute");
   cuda_check(cudaFuncSetAttribute(gdn_chunk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   GdnChunkConfig::SMEM_BYTES),
              "chunked gated delta net smem attribute");
@@ -1346,14 +1351,15 @@ static EpiParams epi(const float* bias = nullptr, int act = kActNone) {
 
 static EpiParams epi_params_for(const float* bias, int act) { return epi(bias, act); }
 
-// The tcgen05 kernel covers causal head_dim 128 with 128-row query tiles; the
-// warp-level kernel takes the rest with 64-row tiles.
-static bool use_tc_attention(const vd_handle* H, int hd, bool causal) {
-  return H->opt.tc_attention && hd == 128 && causal;
+// The tcgen05 kernels cover causal head_dim 128 (ungated) and 256 (gated or
+// not) with 128-row query tiles; the warp-level kernel takes the rest with
+// 64-row tiles.
+static bool use_tc_attention(const vd_handle* H, int hd, bool causal, bool gated = false) {
+  return H->opt.tc_attention && causal && (hd == 256 || (hd == 128 && !gated));
 }
 
 static int attn_tile_rows(const vd_handle* H, int hd, bool causal, bool gated = false) {
-  return !gated && use_tc_attention(H, hd, causal) ? 128 : 64;
+  return use_tc_attention(H, hd, causal, gated) ? 128 : 64;
 }
 
 // gate_col0 >= 0: gated attention (the output is multiplied by the sigmoid of
@@ -1380,7 +1386,27 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
   dim3 grid(n_tiles, heads);
   if (!((hd == 64 && !causal) || (hd == 128 && causal) || (hd == 256 && causal)))
     fail(VD_ESPEC, "no attention kernel for this head size / mask");
-  if (gate_col0 < 0 && use_tc_attention(H, hd, causal)) {
+  if (hd == 256 && use_tc_attention(H, hd, causal, gate_col0 >= 0)) {
+    AttnTc256Params tp;
+    tp.out = H->attn;
+    tp.ld_out = ld_out;
+    tp.qkv = H->qkv;
+    tp.ld_qkv = ld_qkv;
+    tp.q_col0 = q0;
+    tp.k_col0 = k0;
+    tp.v_col0 = v0;
+    tp.gate_col0 = gate_col0;
+    tp.tiles = H->tiles;
+    tp.group = group;
+    tp.scale_log2 = p.scale_log2;
+    tp.err = H->d_err;
+    launch(H, VD_K_ATTN, flops, [&] {
+      attention_tc256_kernel<T><<<grid, AttnTc256Config::THREADS, AttnTc256Config::SMEM_BYTES, H->stream>>>(
+          H->map_qkv64, tp);
+    });
+    return;
+  }
+  if (use_tc_attention(H, hd, causal, gate_col0 >= 0)) {
     AttnTcParams tp;
     tp.out = H->attn;
     tp.ld_out = ld_out;
