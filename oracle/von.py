@@ -79,8 +79,13 @@ def masked_attention(q, k, v, allowed):
 
 
 class VonOracle:
-    def __init__(self, spec: dict):
+    def __init__(self, spec: dict, store16: bool = False):
+        """store16: round every activation the GPU path keeps in 16 bits (norm
+        outputs, q/k after RoPE, v, the attention output, the GeGLU product) to
+        fp16 where it is stored; the residual stream stays fp32.  It measures
+        what fp16 storage alone does to the logits."""
         self.spec = spec
+        self.store16 = store16
         self.ckpt = FastCheckpoint(spec)
         self.w = {name: self.ckpt.get(name) for name in self.ckpt.names()
                   if not name.endswith("tok_embeddings.weight")}
@@ -100,17 +105,18 @@ class VonOracle:
         uniq, inv = np.unique(ids, return_inverse=True)
         emb = self.ckpt.get("encoder.embeddings.tok_embeddings.weight", rows=uniq)[inv]
         h = layernorm(emb, w["encoder.embeddings.norm.weight"], zero, eps)
+        st = (lambda t: t.astype(np.float16).astype(np.float32)) if self.store16 else (lambda t: t)
         for i, kind in enumerate(s["layer_types"]):
             p = f"encoder.layers.{i}."
-            x = h if i == 0 else layernorm(h, w[p + "attn_norm.weight"], zero, eps)
+            x = st(h if i == 0 else layernorm(h, w[p + "attn_norm.weight"], zero, eps))
             qkv = (x @ w[p + "attn.Wqkv.weight"].T).reshape(n, 3, heads, hd)
             cos, sin = tabs[kind]
-            q, k = apply_rope(qkv[:, 0], cos, sin), apply_rope(qkv[:, 1], cos, sin)
-            a = masked_attention(q, k, qkv[:, 2], full if kind == "full_attention" else sliding)
+            q, k = st(apply_rope(qkv[:, 0], cos, sin)), st(apply_rope(qkv[:, 1], cos, sin))
+            a = st(masked_attention(q, k, st(qkv[:, 2]), full if kind == "full_attention" else sliding))
             h = h + a.reshape(n, d) @ w[p + "attn.Wo.weight"].T
-            x = layernorm(h, w[p + "mlp_norm.weight"], zero, eps)
+            x = st(layernorm(h, w[p + "mlp_norm.weight"], zero, eps))
             inp, gate = np.split(x @ w[p + "mlp.Wi.weight"].T, 2, axis=-1)
-            h = (h + (gelu_erf(inp) * gate) @ w[p + "mlp.Wo.weight"].T).astype(np.float32)
+            h = (h + st(gelu_erf(inp) * gate) @ w[p + "mlp.Wo.weight"].T).astype(np.float32)
         return layernorm(h, w["encoder.final_norm.weight"], zero, eps)
 
     def score(self, rep: np.ndarray) -> np.ndarray:

@@ -68,10 +68,17 @@ def von_batch(spec, seed, n):
 
 
 def test_von_base_full_depth_vs_oracle():
-    """All 22 layers of the ModernBERT-base shape (7 global, 15 local)."""
+    """All 22 layers of the ModernBERT-base shape (7 global, 15 local).  At this
+    depth fp16 activation storage alone moves the logits by ~ENC_TOL (the
+    oracle with every 16-bit store of the GPU path emulated, `store16`), so the
+    bound is ENC_TOL beyond that storage deviation."""
     spec = specs.preset("von-base", seed=71)
     batch = von_batch(spec, 71, 6)
-    check(run(spec, batch), VonOracle(spec).infer(batch))
+    ref = VonOracle(spec).infer(batch)
+    ref16 = VonOracle(spec, store16=True).infer(batch)
+    live = ref > -1e4
+    storage = np.abs(ref16 - ref)[live].max() / max(1.0, float(np.abs(ref[live]).max()))
+    check(run(spec, batch), ref, ENC_TOL + storage)
 
 
 def test_von_chunking_is_bit_exact_and_windows_matter():

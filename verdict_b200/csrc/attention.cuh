@@ -120,6 +120,19 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
   float l_run[2] = {0.0f, 0.0f};
 
   const int q_row_a = tile.q_start + warp * 16 + (lane >> 2);  // rows of c0/c1; c2/c3 are +8
+  // Option id and position of this thread's two query rows (option masks only).
+  constexpr int kQDead = -2;  // row past the sequence end
+  int q_opt[2] = {kQDead, kQDead}, q_pos[2] = {0, 0};
+  if (p.opt_id != nullptr) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int qr = q_row_a + 8 * h;
+      if (qr < tile.seq_len) {
+        q_opt[h] = __ldg(p.opt_id + tile.seq_start + qr);
+        if (p.window > 0) q_pos[h] = __ldg(p.opt_pos + tile.seq_start + qr);
+      }
+    }
+  }
 
   for (int j = 0; j < n_kv; ++j) {
     const int buf = j & 1;
@@ -167,24 +180,30 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
     const bool need_mask = (kv0 + Cfg::BN > seg_len) || (CAUSAL && !in_pre && kv0 + Cfg::BN > tile.q_start) ||
                            p.opt_id != nullptr;
     if (need_mask && p.opt_id != nullptr) {
-      // Option masks (bidirectional encoders only: no prefix segment here).
+      // Option masks (bidirectional encoders only: no prefix segment here):
+      // each of this thread's 16 keys is looked up once per tile, its two
+      // query rows once per CTA.
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int kv = kv0 + nb * 8 + ((lane & 3) << 1) + (e & 1);
-          const int qr = q_row_a + ((e >> 1) << 3);
-          bool dead = kv >= seg_len || qr >= tile.seq_len;
-          if (!dead) {
-            const int kt = tile.seq_start + kv, qt = tile.seq_start + qr;
-            const int ok = __ldg(p.opt_id + kt), oq = __ldg(p.opt_id + qt);
-            dead = oq == -1 ? ok != -1 : (ok != -1 && ok != oq);
-            if (!dead && p.window > 0) {
-              const int d = __ldg(p.opt_pos + qt) - __ldg(p.opt_pos + kt);
-              dead = d > p.window || -d > p.window;
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int kv = kv0 + nb * 8 + ((lane & 3) << 1) + e2;
+          const bool kdead = kv >= seg_len;
+          const int kt = tile.seq_start + (kdead ? 0 : kv);
+          const int ok = kdead ? -1 : __ldg(p.opt_id + kt);
+          const int pk = (kdead || p.window <= 0) ? 0 : __ldg(p.opt_pos + kt);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            bool dead = kdead || q_opt[h] == kQDead;
+            if (!dead) {
+              dead = q_opt[h] == -1 ? ok != -1 : (ok != -1 && ok != q_opt[h]);
+              if (!dead && p.window > 0) {
+                const int d = q_pos[h] - pk;
+                dead = d > p.window || -d > p.window;
+              }
             }
+            if (dead) s[nb][2 * h + e2] = -INFINITY;
           }
-          if (dead) s[nb][e] = -INFINITY;
         }
       }
     } else if (need_mask) {

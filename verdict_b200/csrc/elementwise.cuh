@@ -147,6 +147,57 @@ __global__ void __launch_bounds__(NT)
   }
 }
 
+// The same LayerNorm with one warp per row for d = 128 * VPT (VPT float4 per
+// lane held in registers, shuffle reductions, no block barrier): 8 rows per
+// CTA of 256 threads.  The encoder widths (768: VPT 6) are far too narrow to
+// keep a 256-thread CTA per row busy.
+template <int VPT, class T>
+__global__ void __launch_bounds__(256)
+    layernorm_warp_kernel(float* __restrict__ x, int d, const float* __restrict__ w, const float* __restrict__ bvec,
+                          float eps, int inplace, T* __restrict__ out, int rows) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(r) * d);
+  float4 v[VPT];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    v[k] = xr[lane + 32 * k];
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(d);
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, e = v[k].w - mean;
+    ss += a * a + b * b + c * c + e * e;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = rsqrtf(ss / static_cast<float>(d) + eps);
+  const float4* wv = reinterpret_cast<const float4*>(w);
+  const float4* bv = reinterpret_cast<const float4*>(bvec);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * d);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = lane + 32 * k;
+    const float4 g = __ldg(wv + i), bb = __ldg(bv + i);
+    float4 y;
+    y.x = (v[k].x - mean) * rstd * g.x + bb.x;
+    y.y = (v[k].y - mean) * rstd * g.y + bb.y;
+    y.z = (v[k].z - mean) * rstd * g.z + bb.z;
+    y.w = (v[k].w - mean) * rstd * g.w + bb.w;
+    if (inplace) xr[i] = y;
+    uint2 pk;
+    pk.x = Elem<T>::pack2(y.x, y.y);
+    pk.y = Elem<T>::pack2(y.z, y.w);
+    o[i] = pk;
+  }
+}
+
 // Encoder embeddings: h = LN(word[tok] + pos[p] + type[0]); fp32 h and a 16-bit copy.
 template <int NT, class T>
 __global__ void __launch_bounds__(NT)

@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnParams p) {
   constexpr int C = Cfg::C, D = Cfg::D;
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
-  const uint32_t sZ = base + Cfg::OFF_Z, sS = base + Cfg::OFF_S, sR = base + Cfg::OFF_R, sD = base + Cfg::OFF_D;
+  const uint32_t sS = base + Cfg::OFF_S, sD = base + Cfg::OFF_D, sZ = base + Cfg::OFF_Z;
   const uint32_t sP = base + Cfg::OFF_P, sA = base + Cfg::OFF_A, sTii = base + Cfg::OFF_TII;
   float* f32 = reinterpret_cast<float*>(smem + Cfg::OFF_F32);
   float* sAd = f32 + Cfg::F32_ADIAG;
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnParams p) {
     const int valid = min(C, len - c0);
     const bool first = ci == 0, last = ci + 1 == n_chunks;
     const int buf = ci & 1;
-    const uint32_t sK = base + buf * Cfg::KQV, sQ = sK + Cfg::TILE, sV = sK + 2 * Cfg::TILE;
+    const uint32_t sK = base + buf * Cfg::KQV, sQ = sK + Cfg::TILE;  // V at sK + 2 * TILE, read by byte offset
     uint8_t* kbytes = smem + buf * Cfg::KQV;
     float* sG = f32 + Cfg::F32_G + buf * C;
     float* sB = f32 + Cfg::F32_B + buf * C;

@@ -1712,18 +1712,17 @@ static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan
 template <class T>
 static double decoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
-  const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads;
+  const int d = s.hidden, hd = s.head_dim, nq = s.heads;
   const ChunkPlan P = plan_chunk(H, c, true, attn_tile_rows(H, hd, true, s.hybrid()));
   const int ntok = P.ntok, n_tiles = P.n_tiles;
   pack(H, c, P, 0);
   const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
   launch(H, VD_K_OTHER, 0.0,
          [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h); });
-  const int qkvw = H->ld_qkv, qc = nq * hd, kc = nkv * hd;
+  const int qc = nq * hd;
   const float eps = static_cast<float>(s.rms_eps);
   const int pone = s.norm_plus_one ? 1 : 0;
   const double attn_flops = 4.0 * hd * nq * P.pairs;
-  (void)qkvw;
   for (int i = 0; i < s.layers; ++i) {
     const DecLayer& L = H->dec[i];
     launch(H, VD_K_NORM, 0.0, [&] {
@@ -1771,16 +1770,27 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   return ntok;
 }
 
+// LayerNorm of the ntok fp32 rows of h (16-bit copy to xn, fp32 in place when
+// `inplace`): one warp per row for the widths that fit its registers.
+template <class T>
+static void layernorm_rows(vd_handle* H, int d, const float* w, const float* b, float eps, int inplace, int ntok) {
+  launch(H, VD_K_NORM, 0.0, [&] {
+    T* xn = static_cast<T*>(H->xn);
+    const int blocks = (ntok + 7) / 8;
+    switch (d % 128 == 0 ? d / 128 : 0) {
+      case 4: layernorm_warp_kernel<4, T><<<blocks, 256, 0, H->stream>>>(H->h, d, w, b, eps, inplace, xn, ntok); break;
+      case 6: layernorm_warp_kernel<6, T><<<blocks, 256, 0, H->stream>>>(H->h, d, w, b, eps, inplace, xn, ntok); break;
+      case 8: layernorm_warp_kernel<8, T><<<blocks, 256, 0, H->stream>>>(H->h, d, w, b, eps, inplace, xn, ntok); break;
+      default: layernorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, w, b, eps, inplace, xn, ntok);
+    }
+  });
+}
+
 template <class T>
 static void enc_layer(vd_handle* H, const EncLayer& L, int ntok, int n_tiles, double attn_flops) {
   const int d = H->spec.hidden;
   const int nh = d / 64;
-  auto ln = [&](const float* w, const float* b, int inplace) {
-    launch(H, VD_K_NORM, 0.0, [&] {
-      layernorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, w, b, L.eps, inplace, static_cast<T*>(H->xn),
-                                                            ntok);
-    });
-  };
+  auto ln = [&](const float* w, const float* b, int inplace) { layernorm_rows<T>(H, d, w, b, L.eps, inplace, ntok); };
   if (L.pre_norm) ln(L.ln1_w, L.ln1_b, 0);
   gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, epi(L.qkv.b), H->out_qkv);
   attention<T>(H, attn_flops, n_tiles, nh, 64, false, 3 * d, 0, d, 2 * d, 1, d);
@@ -1809,12 +1819,7 @@ static double von_forward(vd_handle* H, const Chunk& c) {
                                                    H->von_opt, H->von_pos, H->d_err);
   });
   const float eps = static_cast<float>(s.ln_eps);
-  auto ln = [&](const float* w, int inplace) {
-    launch(H, VD_K_NORM, 0.0, [&] {
-      layernorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, w, H->zero_d, eps, inplace,
-                                                            static_cast<T*>(H->xn), ntok);
-    });
-  };
+  auto ln = [&](const float* w, int inplace) { layernorm_rows<T>(H, d, w, H->zero_d, eps, inplace, ntok); };
   launch(H, VD_K_OTHER, 0.0,
          [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, 1.0f, H->h); });
   ln(H->emb_ln_w, 1);  // the residual stream starts from the normalised embedding
