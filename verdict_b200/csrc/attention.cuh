@@ -78,7 +78,7 @@ __device__ __forceinline__ void load_tile_async(uint32_t s_base, const T* g, int
 }
 
 template <int HD, bool CAUSAL, class T>
-__global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
+__global__ void __launch_bounds__(128, HD == 64 ? 4 : 1) attention_varlen_kernel(AttnParams p) {
   using Cfg = AttnConfig<HD>;
   constexpr int NB = Cfg::BN / 8;   // n-blocks of S per warp (8)
   constexpr int ND = HD / 8;        // n-blocks of O per warp
@@ -121,8 +121,7 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
 
   const int q_row_a = tile.q_start + warp * 16 + (lane >> 2);  // rows of c0/c1; c2/c3 are +8
   // Option id and position of this thread's two query rows (option masks only).
-  constexpr int kQDead = -2;  // row past the sequence end
-  int q_opt[2] = {kQDead, kQDead}, q_pos[2] = {0, 0};
+  int q_opt[2] = {-1, -1}, q_pos[2] = {0, 0};
   if (p.opt_id != nullptr) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -180,29 +179,42 @@ __global__ void __launch_bounds__(128) attention_varlen_kernel(AttnParams p) {
     const bool need_mask = (kv0 + Cfg::BN > seg_len) || (CAUSAL && !in_pre && kv0 + Cfg::BN > tile.q_start) ||
                            p.opt_id != nullptr;
     if (need_mask && p.opt_id != nullptr) {
-      // Option masks (bidirectional encoders only: no prefix segment here):
-      // each of this thread's 16 keys is looked up once per tile, its two
-      // query rows once per CTA.
+      // Option masks (bidirectional encoders only: no prefix segment here).
+      // A key is visible iff it is a shared token or in the query's own option
+      // (for a shared query the two coincide), and in local layers within the
+      // window.  Keys past the sequence end carry an option code nothing
+      // matches.  Rows past the end are never stored, so they are not masked.
+      constexpr int kKeyDead = -3;
+      int kopt[NB][2], kpos[NB][2];
+      bool all_shared = true;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
         for (int e2 = 0; e2 < 2; ++e2) {
           const int kv = kv0 + nb * 8 + ((lane & 3) << 1) + e2;
-          const bool kdead = kv >= seg_len;
-          const int kt = tile.seq_start + (kdead ? 0 : kv);
-          const int ok = kdead ? -1 : __ldg(p.opt_id + kt);
-          const int pk = (kdead || p.window <= 0) ? 0 : __ldg(p.opt_pos + kt);
+          const bool in = kv < seg_len;
+          const int kt = tile.seq_start + (in ? kv : 0);
+          kopt[nb][e2] = in ? __ldg(p.opt_id + kt) : kKeyDead;
+          kpos[nb][e2] = (in && p.window > 0) ? __ldg(p.opt_pos + kt) : 0;
+          all_shared = all_shared && kopt[nb][e2] == -1;
+        }
+      }
+      // Global layers: a tile of shared keys is visible to every query row.
+      if (!(p.window <= 0 && __all_sync(0xffffffffu, all_shared))) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            bool dead = kdead || q_opt[h] == kQDead;
-            if (!dead) {
-              dead = q_opt[h] == -1 ? ok != -1 : (ok != -1 && ok != q_opt[h]);
-              if (!dead && p.window > 0) {
-                const int d = q_pos[h] - pk;
-                dead = d > p.window || -d > p.window;
+        for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int ko = kopt[nb][e2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              bool ok = ko == -1 || ko == q_opt[h];
+              if (p.window > 0) {
+                const int d = q_pos[h] - kpos[nb][e2];
+                ok = ok && d <= p.window && -d <= p.window;
               }
+              if (!ok) s[nb][2 * h + e2] = -INFINITY;
             }
-            if (dead) s[nb][2 * h + e2] = -INFINITY;
           }
         }
       }
