@@ -55,6 +55,10 @@ VON_WORKLOAD = ("ModernBERT-base-shaped independent-options decisions (22 layers
                 "vocab 50368, every 3rd layer global, the rest a 64-position window), option-masked attention; "
                 "[CLS] prefix U[16,200] [SEP] then 2-6 [MASK]-led options of U[1,12] tokens")
 OTHER_WORKLOAD = "{} text decisions (all layers, synthetic weights), lengths {}, 2-8 options"
+BERT_WORKLOAD = ("BERT-base-shaped marker-head encoder decisions (laya: 12 layers, d=768, 12 heads, GELU 3072, "
+                 "post-LN, vocab 30522, 2 head layers), lengths U[16,128], K=3 markers, ids U[1000,30522)")
+XLMR_WORKLOAD = ("XLM-R-base-shaped marker-head encoder decisions (laya-multilingual: 12 layers, d=768, 12 heads, "
+                 "GELU 3072, vocab 250002), lengths clip(lognormal(4.5,0.6),8,512), K~U{2..6}, ids U[5,250002)")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
 # full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
@@ -144,13 +148,29 @@ def whole_job_rate(decisions_per_rank: int, world: int, max_ms: float) -> float:
 
 
 LENGTHS = {"onejev-9b": "lognormal-9b", "onejev16-9b": "lognormal-9b", "decider-2b": "uniform-2b",
-           "onejev-27b": "uniform-27b"}
+           "onejev-27b": "uniform-27b", "laya-bert": "uniform-bert", "laya-xlmr": "lognormal-xlmr"}
+# Marker-head encoder rows: ([CLS], [SEP]) ids, lowest text id, longest row.
+MARKER_ROWS = {"uniform-bert": (101, 102, 1000, 510), "lognormal-xlmr": (0, 2, 5, 512)}
+
+
+def workload_of(spec, workload):
+    """Row generator of a model: independent options (von), marker head, or the decoder workloads."""
+    if spec["arch"] != "encoder":
+        return workload
+    return "von" if spec.get("family") == "independent_options" else "marker"
+
+
+def workload_text(model, shared=False):
+    return {"onejev-9b": SHARED_WORKLOAD if shared else WORKLOAD, "onejev16-9b": HYBRID_WORKLOAD,
+            "von-base": VON_WORKLOAD, "laya-bert": BERT_WORKLOAD, "laya-xlmr": XLMR_WORKLOAD,
+            "decider-2b": OTHER_WORKLOAD.format("Gemma-2B-shaped decider", "U[64,1024]"),
+            "onejev-27b": OTHER_WORKLOAD.format("OneJev-27B-shaped", "U[512,8192]")}[model]
 
 
 def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad_id=0, lengths="lognormal-9b"):
     """Each rank's own shard of the workload: batch j of rank r is seeded by
     (seed, r, j), so ranks never share a decision."""
-    from verdict_b200.batch import Layout, collate, decoder_rows, shared_prefix_rows, von_rows
+    from verdict_b200.batch import Layout, collate, decoder_rows, encoder_rows, shared_prefix_rows, von_rows
     out = []
     for j in range(n_batches):
         rng = np.random.default_rng([seed, rank, j])
@@ -158,9 +178,16 @@ def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad
             rows = shared_prefix_rows(rng, per_batch, vocab)
         elif workload == "von":
             rows = von_rows(rng, per_batch, vocab)
+        elif workload == "marker":
+            cls_id, sep_id, id_low, max_len = MARKER_ROWS[lengths]
+            rows = encoder_rows(rng, per_batch, vocab, lengths=lengths, cls_id=cls_id, sep_id=sep_id,
+                                id_low=id_low, max_len=max_len)
         else:
             rows = decoder_rows(rng, per_batch, vocab, lengths=lengths)
-        out.append(collate(rows, Layout(pad_id=pad_id)))
+        batch = collate(rows, Layout(pad_id=pad_id))
+        if workload == "marker":
+            batch.qtype[:] = rng.integers(0, 3, size=batch.b)
+        out.append(batch)
     return out
 
 
@@ -189,15 +216,20 @@ def cpu_baseline_sample(spec, batch, layers_timed):
     return 1.0 / per_decision, sample, per_decision
 
 
-def von_cpu_sample(spec, batch):
+def encoder_cpu_sample(spec, batch):
     """The oracle (fp32 numpy) on the batch's first 4 rows, all layers; decisions/s."""
+    from oracle.encoder import EncoderOracle
     from oracle.von import VonOracle
     from verdict_b200.batch import CollatedBatch
     n = min(4, batch.b)
     sub = CollatedBatch(batch.input_ids[:n * batch.l], batch.attention_mask[:n * batch.l],
                         batch.marker_pos[:n * batch.k], batch.marker_mask[:n * batch.k], batch.qtype[:n],
                         batch.nopts, n, batch.l, batch.k, batch.rows[:n])
-    orc = VonOracle(spec)
+    orc = VonOracle(spec) if spec.get("family") == "independent_options" else EncoderOracle(spec)
+    one = CollatedBatch(batch.input_ids[:batch.l], batch.attention_mask[:batch.l], batch.marker_pos[:batch.k],
+                        batch.marker_mask[:batch.k], batch.qtype[:1], batch.nopts, 1, batch.l, batch.k,
+                        batch.rows[:1])
+    orc.infer(one)  # generates the weights outside the timed region
     t0 = time.perf_counter()
     orc.infer(sub)
     dt = time.perf_counter() - t0
@@ -215,11 +247,11 @@ def run_reference(args, world, rank):
     spec = with_labels(specs.preset(args.model))
     encoder = spec["arch"] == "encoder"
     batches = make_batches(0, args.warmup + args.steps, 4 if encoder else 1, spec["vocab"], args.seed,
-                           "von" if encoder else "choice", spec.get("pad_id", 0),
+                           workload_of(spec, "choice"), spec.get("pad_id", 0),
                            LENGTHS.get(args.model, "lognormal-9b"))
     times = []
     for j, b in enumerate(batches):
-        _, _, per = von_cpu_sample(spec, b) if encoder else cpu_baseline_sample(spec, b, args.ref_layers)
+        _, _, per = encoder_cpu_sample(spec, b) if encoder else cpu_baseline_sample(spec, b, args.ref_layers)
         if j >= args.warmup:
             times.append(per)
     mean = float(np.mean(times))
@@ -229,10 +261,7 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": {"onejev-9b": WORKLOAD, "onejev16-9b": HYBRID_WORKLOAD, "von-base": VON_WORKLOAD,
-                                "decider-2b": OTHER_WORKLOAD.format("Gemma-2B-shaped decider", "U[64,1024]"),
-                                "onejev-27b": OTHER_WORKLOAD.format("OneJev-27B-shaped", "U[512,8192]")}
-                   [args.model], "model": args.model,
+        "config": {"workload": workload_text(args.model), "model": args.model,
                    "decisions_per_step": 4 if encoder else 1,
                    "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
@@ -256,18 +285,21 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2, help="layers timed per CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--attention", default="tc", choices=["tc", "mma"],
-                    help="head_dim-128 causal attention kernel: tcgen05 (tc) or warp-level mma.sync")
+    ap.add_argument("--attention", default="tc", choices=["tc", "tc2", "mma"],
+                    help="head_dim-128 causal attention kernel: tcgen05 with one query head per CTA (tc) or "
+                         "two (tc2), or warp-level mma.sync")
     ap.add_argument("--workload", default="choice", choices=["choice", "shared-prefix"],
                     help="choice: the OneJev-9B decision workload (headline); shared-prefix: 8 questions "
                          "per state, rows of a state share the state prefix (prefix_len declared)")
     ap.add_argument("--fork", default="on", choices=["on", "off"],
                     help="compute shared prefixes once (on) or every row whole (off)")
     ap.add_argument("--model", default="onejev-9b",
-                    choices=["onejev-9b", "onejev16-9b", "von-base", "decider-2b", "onejev-27b"],
+                    choices=["onejev-9b", "onejev16-9b", "von-base", "laya-bert", "laya-xlmr", "decider-2b",
+                             "onejev-27b"],
                     help="onejev-9b: the dense OneJev-9B shape (headline); onejev16-9b: the Qwen3.5-style hybrid "
                          "(gated delta nets + gated attention); von-base: the ModernBERT-base independent-options "
-                         "encoder; decider-2b (lengths U[64,1024]) and onejev-27b (lengths U[512,8192]): the "
+                         "encoder; laya-bert / laya-xlmr: the BERT-base / XLM-R-base marker-head encoders; "
+                         "decider-2b (lengths U[64,1024]) and onejev-27b (lengths U[512,8192]): the "
                          "other decoder shapes")
     ap.add_argument("--gemm", default="2sm", choices=["2sm", "1sm"],
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
@@ -302,7 +334,7 @@ def main():
     n_batches = args.warmup + args.steps
     encoder = spec["arch"] == "encoder"
     batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed,
-                           "von" if encoder else args.workload, spec.get("pad_id", 0),
+                           workload_of(spec, args.workload), spec.get("pad_id", 0),
                            LENGTHS.get(args.model, "lognormal-9b"))
     max_len = max(int(b.real_len().max()) for b in batches)
     max_tokens = max(int(b.real_len().sum()) for b in batches)
@@ -475,7 +507,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, sample, _ = (von_cpu_sample(spec, batches[0]) if encoder
+        v, sample, _ = (encoder_cpu_sample(spec, batches[0]) if encoder
                         else cpu_baseline_sample(spec, batches[0], args.ref_layers))
         cpu = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample}
 
@@ -485,11 +517,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded; random-init weights generated on device)",
-            "config": {"workload": {"onejev-9b": SHARED_WORKLOAD if shared else WORKLOAD,
-                                    "onejev16-9b": HYBRID_WORKLOAD, "von-base": VON_WORKLOAD,
-                                    "decider-2b": OTHER_WORKLOAD.format("Gemma-2B-shaped decider", "U[64,1024]"),
-                                    "onejev-27b": OTHER_WORKLOAD.format("OneJev-27B-shaped", "U[512,8192]")}
-                       [args.model],
+            "config": {"workload": workload_text(args.model, shared),
                        "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
                        "raster_group": args.raster_group or "default",

@@ -119,7 +119,7 @@ typedef struct vd_stats {
  *   src/tokenize.rs:96-171) and default to "family": "letter_readout".
  * opts_json: NULL or {"max_tokens": N, "max_rows": N, "max_seq": N,
  *   "max_markers": N, "output": "logprobs"|"logits", "act_dtype":
- *   "fp16"|"bf16", "attention": "tc"|"mma", "prune_last_layer": bool,
+ *   "fp16"|"bf16", "attention": "tc"|"tc2"|"mma", "prune_last_layer": bool,
  *   "fork": bool (default true: decoder rows that share a prefix — declared
  *   prefix_len, else a common prefix of >= 32 tokens — compute it once, as
  *   executor/torch_exec.py:1935-2022 does; planned on the host from the ids:

@@ -74,11 +74,10 @@ VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_
 
 /*
  * The same causal attention on the 5th-generation tensor cores (tcgen05 MMAs
- * with TMEM accumulators, TMA-fed), head_dim 128 (128-key tiles, two query
- * heads per CTA) or 256 (64-key tiles, one query head per CTA), 128-row query
- * tiles; the kernels the engine uses for decoders with those head sizes.  Same
- * arguments and result as vdk_attention; strides and column offsets multiples
- * of 8.
+ * with TMEM accumulators, TMA-fed), head_dim 128 or 256, one query head per
+ * CTA, 128-row query tiles and 64-key tiles; the kernel the engine uses for
+ * decoders with those head sizes.  Same arguments and result as
+ * vdk_attention; strides and column offsets multiples of 8.
  */
 VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0, int64_t v_col0,
                             int heads, int kv_heads, int head_dim, int dtype, int causal,

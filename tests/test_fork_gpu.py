@@ -110,7 +110,7 @@ def long_prefix_batch(vocab, seed, prefix_lens=(1500, 700), members=4, declared=
     return batch_of([rows[i] for i in order], [pl[i] for i in order], seed=seed)
 
 
-@pytest.mark.parametrize("attention", ["tc", "mma"])
+@pytest.mark.parametrize("attention", ["tc", "tc2", "mma"])
 @pytest.mark.parametrize("declared", [True, False])
 def test_long_shared_prefixes_hd128(attention, declared):
     spec = spec9b()

@@ -187,12 +187,14 @@ def test_encoder_full_depth_vs_oracle(preset, lengths):
         eng.close()
 
 
-def test_tensor_core_attention_matches_warp_level_attention():
-    """The engine's tcgen05 attention and its mma.sync attention give the same
-    decisions on the OneJev-9B shape (both against the oracle too)."""
+@pytest.mark.parametrize("mode", ["tc", "tc2"])
+def test_tensor_core_attention_matches_warp_level_attention(mode):
+    """The engine's tcgen05 attention (one query head per CTA: tc; two: tc2)
+    and its mma.sync attention give the same decisions on the OneJev-9B shape
+    (both against the oracle too)."""
     spec, batch = decoder_case("onejev-9b", 2, 6, seed=13, max_len=1500)
     ref = DecoderOracle(spec).infer(batch)
-    a = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, attention="tc")
+    a = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, attention=mode)
     b = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, attention="mma")
     try:
         la, lb = engine_logprobs(a, batch), engine_logprobs(b, batch)

@@ -1,9 +1,10 @@
-// Causal varlen attention on the tcgen05 tensor cores for head_dim 256 (the
-// Gemma-2B decider and the Qwen3.5 hybrids' gated attention layers).
+// Causal varlen attention on the tcgen05 tensor cores, one query head per CTA,
+// head_dim HD = 128 or 256 (256: the Gemma-2B decider and the Qwen3.5
+// hybrids' gated attention layers, where O alone fills 256 TMEM columns).
 //
 // One CTA = one 128-row query tile of one sequence for one query head; keys in
 // tiles of 64.  TMEM: two S/P buffers of 64 columns (S of tile j + 1 is computed
-// while the softmax warps work on tile j) and O, 128 rows x 256 fp32 columns.
+// while the softmax warps work on tile j) and O, 128 rows x HD fp32 columns.
 //   warp 0      : TMA producer of Q (once) and the K tiles (2-stage ring)
 //   warp 1      : TMEM allocator + MMA issuer (one lane):
 //                 S(0), S(1), then per tile j: O += P(j) V(j) (A = P from
@@ -16,51 +17,57 @@
 //                 units; a raise rescales O in TMEM after the previous P V has
 //                 completed), P packed to 16-bit pairs over S; at the end
 //                 O / l (times sigmoid(gate) for gated attention) to global.
-// Shared memory: Q 64 KB (four 128 x 64 swizzled atoms), K and V 2 x 32 KB
-// each.  Every mbarrier wait is bounded; on a timeout the CTA records an error
-// code, raises its abort flag and all roles leave their loops.
+// Shared memory: Q HD/64 swizzled 128 x 64 atoms (HD = 256: 64 KB), K and V
+// two stages of HD/64 64 x 64 atoms each (HD = 256: 2 x 32 KB each).  At HD =
+// 128 a CTA takes 96 KB and 256 TMEM columns, so two run per SM and one's
+// prologue and epilogue overlap the other's main loop.  Every mbarrier wait
+// is bounded; on a timeout the CTA records an error code, raises its abort
+// flag and all roles leave their loops.
 #pragma once
 
 #include "attention_tc.cuh"
 
 namespace vd {
 
-struct AttnTc256Params {
+struct AttnTcHeadParams {
   void* out;                   // T [tokens, ld_out]
   int ld_out;
   const void* qkv;             // T [tokens, ld_qkv] (gate columns for gated attention)
   int ld_qkv;
   int q_col0, k_col0, v_col0;  // column offsets of the q / k / v blocks in qkv
-  int gate_col0;               // >= 0: output *= sigmoid(qkv[:, gate_col0 + head * 256 + c])
+  int gate_col0;               // >= 0: output *= sigmoid(qkv[:, gate_col0 + head * HD + c])
   const AttnTile* tiles;       // 128-row query tiles
   int group;                   // query heads per K/V head
   float scale_log2;
   int* err;
 };
 
-struct AttnTc256Config {
-  static constexpr int HD = 256, BM = 128, BN = 64;
-  static constexpr int Q_ATOM = BM * 64 * 2;    // [128 rows x 64 cols] 16-bit, 16 KB
-  static constexpr int KV_ATOM = BN * 64 * 2;   // [64 rows x 64 cols], 8 KB
-  static constexpr int Q_BYTES = 4 * Q_ATOM;    // 64 KB
-  static constexpr int KV_BYTES = 4 * KV_ATOM;  // 32 KB
+template <int HD_>
+struct AttnTcHeadConfig {
+  static constexpr int HD = HD_, BM = 128, BN = 64;
+  static constexpr int ATOMS = HD / 64;             // 64-column swizzle atoms per row
+  static constexpr int Q_ATOM = BM * 64 * 2;        // [128 rows x 64 cols] 16-bit, 16 KB
+  static constexpr int KV_ATOM = BN * 64 * 2;       // [64 rows x 64 cols], 8 KB
+  static constexpr int Q_BYTES = ATOMS * Q_ATOM;
+  static constexpr int KV_BYTES = ATOMS * KV_ATOM;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * KV_BYTES;
   static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 256;
   static constexpr int THREADS = 224;
-  static constexpr uint32_t TMEM_COLS = 512;  // S/P [0, 128), O [128, 384)
+  static constexpr uint32_t TMEM_COLS = HD == 256 ? 512 : 256;  // S/P [0, 128), O [128, 128 + HD)
+  static constexpr int MIN_CTAS = HD == 128 ? 2 : 1;
   static constexpr float RESCALE_THRESHOLD = 8.0f;
 };
 
-template <class T>
-__global__ void __launch_bounds__(224, 1)
-    attention_tc256_kernel(const __grid_constant__ CUtensorMap tm_qkv64, AttnTc256Params p) {
-  using C = AttnTc256Config;
+template <int HD, class T>
+__global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
+    attention_tc_head_kernel(const __grid_constant__ CUtensorMap tm_qkv64, AttnTcHeadParams p) {
+  using C = AttnTcHeadConfig<HD>;
   constexpr uint32_t FMT = Elem<T>::kUmmaFormat;
   constexpr uint32_t IDESC_S = umma_idesc_f16kind(128, 64, FMT);                // A, B K-major
-  constexpr uint32_t IDESC_PV = umma_idesc_f16kind(128, 256, FMT) | (1u << 16);  // B (V) MN-major
+  constexpr uint32_t IDESC_PV = umma_idesc_f16kind(128, HD, FMT) | (1u << 16);   // B (V) MN-major
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -121,7 +128,7 @@ __global__ void __launch_bounds__(224, 1)
       const int qy = tile.seq_start + tile.q_start;
       mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
+      for (int a = 0; a < C::ATOMS; ++a) {
         tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM, &tm_qkv64, q_full, qx + 64 * a, qy);
         tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM + C::Q_ATOM / 2, &tm_qkv64, q_full, qx + 64 * a, qy + 64);
       }
@@ -130,7 +137,7 @@ __global__ void __launch_bounds__(224, 1)
         if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < C::ATOMS; ++a)
           tma_load_2d(smem + C::K_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &k_full[s], kx + 64 * a,
                       key_row(j));
       }
@@ -143,7 +150,7 @@ __global__ void __launch_bounds__(224, 1)
         if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < C::ATOMS; ++a)
           tma_load_2d(smem + C::V_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &v_full[s], vx + 64 * a,
                       key_row(j));
       }
@@ -156,7 +163,7 @@ __global__ void __launch_bounds__(224, 1)
         const int b = j & 1;
         const uint32_t k_addr = smem_u32(smem + C::K_OFF + b * C::KV_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
+        for (int kk = 0; kk < HD / 16; ++kk) {
           umma_f16kind(tmem + b * 64, sw128_kmajor_desc(q_addr + (kk >> 2) * C::Q_ATOM + (kk & 3) * 32),
                        sw128_kmajor_desc(k_addr + (kk >> 2) * C::KV_ATOM + (kk & 3) * 32), IDESC_S,
                        kk != 0 ? 1u : 0u);
@@ -261,7 +268,7 @@ __global__ void __launch_bounds__(224, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           float v[32];
           tmem_load_f32x32(o_tm + c * 32, v);
 #pragma unroll
@@ -285,7 +292,7 @@ __global__ void __launch_bounds__(224, 1)
                                        : nullptr;
       const bool live = q_row < tile.seq_len;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         float v[32];
         tmem_load_f32x32(o_tm + c * 32, v);
         if (live) {

@@ -299,6 +299,9 @@ __global__ void __launch_bounds__(NT)
   // last layer's O projection); otherwise h is the packed batch.
   const float* x = compact ? h + static_cast<size_t>(i) * d : h + static_cast<size_t>(rm.base + slot) * d;
   float ss = 0.0f;
+  // Unrolled so that several loads per thread are in flight: at small batch
+  // (one block per decision) the kernel is bound by DRAM latency, not bandwidth.
+#pragma unroll 4
   for (int j = threadIdx.x; j < d; j += NT) {
     const float v = x[j];
     xs[j] = v;
@@ -312,6 +315,7 @@ __global__ void __launch_bounds__(NT)
   for (int o = warp; o < n; o += NT / 32) {
     const float* hr = head + static_cast<size_t>(o) * d;
     float acc = 0.0f;
+#pragma unroll 8
     for (int j = lane * 4; j < d; j += 128) {
       const float4 a = *reinterpret_cast<const float4*>(xs + j);
       const float4 b = __ldg(reinterpret_cast<const float4*>(hr + j));

@@ -249,47 +249,33 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
     cuda_check(cudaMalloc(&d_tiles, tiles.size() * sizeof(AttnTile)), "tile table");
     std::unique_ptr<AttnTile, decltype(&cudaFree)> guard(d_tiles, &cudaFree);
     cuda_check(cudaMemcpy(d_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice), "tiles");
-    if (head_dim == 256) {
-      const CUtensorMap map64 = make_map(qkv, T, ld_qkv, 64, f16);
-      AttnTc256Params p;
-      p.out = out;
-      p.ld_out = static_cast<int>(ld_out);
-      p.qkv = qkv;
-      p.ld_qkv = static_cast<int>(ld_qkv);
-      p.q_col0 = static_cast<int>(q_col0);
-      p.k_col0 = static_cast<int>(k_col0);
-      p.v_col0 = static_cast<int>(v_col0);
-      p.gate_col0 = -1;
-      p.tiles = d_tiles;
-      p.group = heads / kv_heads;
-      p.scale_log2 = static_cast<float>(1.0 / std::sqrt(256.0) * 1.4426950408889634);
-      p.err = word;
-      dim3 grid(static_cast<unsigned>(tiles.size()), heads);
-      if (f16)
-        attention_tc256_kernel<__half><<<grid, AttnTc256Config::THREADS, AttnTc256Config::SMEM_BYTES, s>>>(map64, p);
-      else
-        attention_tc256_kernel<__nv_bfloat16>
-            <<<grid, AttnTc256Config::THREADS, AttnTc256Config::SMEM_BYTES, s>>>(map64, p);
-      ops_finish(s, word);
-      return;
-    }
-    const CUtensorMap map = make_map(qkv, T, ld_qkv, 128, f16);
-    AttnTcParams p;
+    const CUtensorMap map64 = make_map(qkv, T, ld_qkv, 64, f16);
+    AttnTcHeadParams p;
     p.out = out;
     p.ld_out = static_cast<int>(ld_out);
+    p.qkv = qkv;
+    p.ld_qkv = static_cast<int>(ld_qkv);
     p.q_col0 = static_cast<int>(q_col0);
     p.k_col0 = static_cast<int>(k_col0);
     p.v_col0 = static_cast<int>(v_col0);
+    p.gate_col0 = -1;
     p.tiles = d_tiles;
     p.group = heads / kv_heads;
-    p.pairs_per_kv = (p.group + 1) / 2;
-    p.scale_log2 = static_cast<float>(1.0 / std::sqrt(128.0) * 1.4426950408889634);
+    p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)) * 1.4426950408889634);
     p.err = word;
-    dim3 grid(static_cast<unsigned>(tiles.size()), kv_heads * p.pairs_per_kv);
-    if (f16)
-      attention_tc_kernel<__half><<<grid, AttnTcConfig::THREADS, AttnTcConfig::SMEM_BYTES, s>>>(map, p);
+    dim3 grid(static_cast<unsigned>(tiles.size()), heads);
+    if (head_dim == 256 && f16)
+      attention_tc_head_kernel<256, __half>
+          <<<grid, AttnTcHeadConfig<256>::THREADS, AttnTcHeadConfig<256>::SMEM_BYTES, s>>>(map64, p);
+    else if (head_dim == 256)
+      attention_tc_head_kernel<256, __nv_bfloat16>
+          <<<grid, AttnTcHeadConfig<256>::THREADS, AttnTcHeadConfig<256>::SMEM_BYTES, s>>>(map64, p);
+    else if (f16)
+      attention_tc_head_kernel<128, __half>
+          <<<grid, AttnTcHeadConfig<128>::THREADS, AttnTcHeadConfig<128>::SMEM_BYTES, s>>>(map64, p);
     else
-      attention_tc_kernel<__nv_bfloat16><<<grid, AttnTcConfig::THREADS, AttnTcConfig::SMEM_BYTES, s>>>(map, p);
+      attention_tc_head_kernel<128, __nv_bfloat16>
+          <<<grid, AttnTcHeadConfig<128>::THREADS, AttnTcHeadConfig<128>::SMEM_BYTES, s>>>(map64, p);
     ops_finish(s, word);
   });
 }

@@ -36,7 +36,7 @@
 #include "vdexec.h"
 #include "attention.cuh"
 #include "attention_tc.cuh"
-#include "attention_tc256.cuh"
+#include "attention_tc_head.cuh"
 #include "checkpoint.hpp"
 #include "common.cuh"
 #include "convert.cuh"
@@ -596,6 +596,7 @@ struct Options {
   bool f16 = true;  // activations and projection weights in fp16 (else bf16)
   bool prune_last_layer = true;  // last layer's O projection and MLP on the slot rows only
   bool tc_attention = true;  // head_dim 128 causal attention on tcgen05 (else the mma.sync kernel)
+  bool tc_head = true;       // head_dim 128 on the one-head-per-CTA tcgen05 kernel (else two heads per CTA)
   bool fork = true;          // shared-prefix rows: prefix computed once (host-memory decoder batches)
   bool gemm2 = true;         // 256-wide projections on CTA pairs (cta_group::2), else one CTA per tile
   int raster_group = 0;      // M tiles per GEMM raster group; 0 = the kernel's default
@@ -1283,9 +1284,12 @@ static void init_kernel_attrs_t() {
   cuda_check(cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnTcConfig::SMEM_BYTES),
              "tcgen05 attention smem attribute");
-  cuda_check(cudaFuncSetAttribute(attention_tc256_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  AttnTc256Config::SMEM_BYTES),
-             "tcgen05 head_dim-256 attention smem attribute");
+  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<128, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnTcHeadConfig<128>::SMEM_BYTES),
+             "tcgen05 one-head attention smem attribute");
+  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<256, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnTcHeadConfig<256>::SMEM_BYTES),
+             "tcgen05 one-head attention smem attribute");
   cuda_check(cudaFuncSetAttribute(gdn_chunk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   GdnChunkConfig::SMEM_BYTES),
              "chunked gated delta net smem attribute");
@@ -1351,11 +1355,11 @@ static EpiParams epi(const float* bias = nullptr, int act = kActNone) {
 
 static EpiParams epi_params_for(const float* bias, int act) { return epi(bias, act); }
 
-// The tcgen05 kernels cover causal head_dim 128 (ungated) and 256 (gated or
-// not) with 128-row query tiles; the warp-level kernel takes the rest with
-// 64-row tiles.
+// The tcgen05 kernels cover causal head_dim 128 and 256 with 128-row query
+// tiles (gated head_dim 128 only on the one-head kernel); the warp-level kernel
+// takes the rest with 64-row tiles.
 static bool use_tc_attention(const vd_handle* H, int hd, bool causal, bool gated = false) {
-  return H->opt.tc_attention && causal && (hd == 256 || (hd == 128 && !gated));
+  return H->opt.tc_attention && causal && (hd == 256 || (hd == 128 && (!gated || H->opt.tc_head)));
 }
 
 static int attn_tile_rows(const vd_handle* H, int hd, bool causal, bool gated = false) {
@@ -1386,8 +1390,8 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
   dim3 grid(n_tiles, heads);
   if (!((hd == 64 && !causal) || (hd == 128 && causal) || (hd == 256 && causal)))
     fail(VD_ESPEC, "no attention kernel for this head size / mask");
-  if (hd == 256 && use_tc_attention(H, hd, causal, gate_col0 >= 0)) {
-    AttnTc256Params tp;
+  if ((hd == 256 || H->opt.tc_head) && use_tc_attention(H, hd, causal, gate_col0 >= 0)) {
+    AttnTcHeadParams tp;
     tp.out = H->attn;
     tp.ld_out = ld_out;
     tp.qkv = H->qkv;
@@ -1401,8 +1405,12 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
     tp.scale_log2 = p.scale_log2;
     tp.err = H->d_err;
     launch(H, VD_K_ATTN, flops, [&] {
-      attention_tc256_kernel<T><<<grid, AttnTc256Config::THREADS, AttnTc256Config::SMEM_BYTES, H->stream>>>(
-          H->map_qkv64, tp);
+      if (hd == 256)
+        attention_tc_head_kernel<256, T>
+            <<<grid, AttnTcHeadConfig<256>::THREADS, AttnTcHeadConfig<256>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+      else
+        attention_tc_head_kernel<128, T>
+            <<<grid, AttnTcHeadConfig<128>::THREADS, AttnTcHeadConfig<128>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
     });
     return;
   }
@@ -2135,8 +2143,9 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.gdn_chunk = gd == "chunk";
       if (H->opt.raster_group < 0 || H->opt.raster_group > 4096) fail(VD_EINVAL, "raster_group must be in [0, 4096]");
       const std::string at = o.string_or("attention", "tc");
-      if (at != "tc" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\" or \"mma\"");
-      H->opt.tc_attention = at == "tc";
+      if (at != "tc" && at != "tc2" && at != "mma") fail(VD_EINVAL, "attention must be \"tc\", \"tc2\" or \"mma\"");
+      H->opt.tc_attention = at != "mma";
+      H->opt.tc_head = at == "tc";
       const std::string dt = o.string_or("act_dtype", "fp16");
       if (dt != "fp16" && dt != "bf16") fail(VD_EINVAL, "act_dtype must be \"fp16\" or \"bf16\"");
       H->opt.f16 = dt == "fp16";
