@@ -231,6 +231,97 @@ __global__ void __launch_bounds__(NT)
   }
 }
 
+// The same embedding LayerNorm with one warp per token for d = 128 * VPT: the
+// three bf16 rows are summed in registers, reduced with shuffles and written
+// once (h fp32, out 16-bit); 8 tokens per CTA of 256 threads.
+template <int VPT, class T>
+__global__ void __launch_bounds__(256)
+    embed_ln_warp_kernel(const int* __restrict__ tokens, const int* __restrict__ positions, int n_tokens,
+                         const __nv_bfloat16* __restrict__ word, const __nv_bfloat16* __restrict__ pos_emb,
+                         const __nv_bfloat16* __restrict__ type0, int d, const float* __restrict__ w,
+                         const float* __restrict__ bvec, float eps, float* __restrict__ h, T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= n_tokens) return;
+  const uint2* a = reinterpret_cast<const uint2*>(word + static_cast<size_t>(tokens[t]) * d);
+  const uint2* p = reinterpret_cast<const uint2*>(pos_emb + static_cast<size_t>(positions[t]) * d);
+  const uint2* c = reinterpret_cast<const uint2*>(type0);
+  float4 v[VPT];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = lane + 32 * k;
+    const uint2 x = __ldg(a + i), y = __ldg(p + i), z = __ldg(c + i);
+    const float2 x0 = unpack_bf16x2(x.x), x1 = unpack_bf16x2(x.y);
+    const float2 y0 = unpack_bf16x2(y.x), y1 = unpack_bf16x2(y.y);
+    const float2 z0 = unpack_bf16x2(z.x), z1 = unpack_bf16x2(z.y);
+    v[k] = make_float4(x0.x + y0.x + z0.x, x0.y + y0.y + z0.y, x1.x + y1.x + z1.x, x1.y + y1.y + z1.y);
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(d);
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const float e0 = v[k].x - mean, e1 = v[k].y - mean, e2 = v[k].z - mean, e3 = v[k].w - mean;
+    ss += e0 * e0 + e1 * e1 + e2 * e2 + e3 * e3;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = rsqrtf(ss / static_cast<float>(d) + eps);
+  const float4* wv = reinterpret_cast<const float4*>(w);
+  const float4* bv = reinterpret_cast<const float4*>(bvec);
+  float4* hr = reinterpret_cast<float4*>(h + static_cast<size_t>(t) * d);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * d);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = lane + 32 * k;
+    const float4 g = __ldg(wv + i), bb = __ldg(bv + i);
+    float4 y;
+    y.x = (v[k].x - mean) * rstd * g.x + bb.x;
+    y.y = (v[k].y - mean) * rstd * g.y + bb.y;
+    y.z = (v[k].z - mean) * rstd * g.z + bb.z;
+    y.w = (v[k].w - mean) * rstd * g.w + bb.w;
+    hr[i] = y;
+    uint2 pk;
+    pk.x = Elem<T>::pack2(y.x, y.y);
+    pk.y = Elem<T>::pack2(y.z, y.w);
+    o[i] = pk;
+  }
+}
+
+// The question-type add below with one warp per token (d = 128 * VPT), 8
+// tokens per CTA: one float4 of h and four bf16 of the table per lane and step.
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    add_type_warp_kernel(float* __restrict__ h, int T, int d, const int* __restrict__ seq_id,
+                         const int64_t* __restrict__ qtype, const __nv_bfloat16* __restrict__ table, int n_types,
+                         int* err) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  int64_t q = qtype ? qtype[seq_id[t]] : 0;
+  if (q < 0 || q >= n_types) {
+    if (lane == 0) record_error(err, kErrTokenRange);
+    q = 0;
+  }
+  const uint2* e = reinterpret_cast<const uint2*>(table + static_cast<size_t>(q) * d);
+  float4* hr = reinterpret_cast<float4*>(h + static_cast<size_t>(t) * d);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = lane + 32 * k;
+    float4 v = hr[i];
+    const uint2 x = __ldg(e + i);
+    const float2 x0 = unpack_bf16x2(x.x), x1 = unpack_bf16x2(x.y);
+    v.x += x0.x;
+    v.y += x0.y;
+    v.z += x1.x;
+    v.w += x1.y;
+    hr[i] = v;
+  }
+}
+
 // h[t, :] += table[qtype[seq_id[t]], :] (the decision head's question-type embedding).
 __global__ void add_type_kernel(float* __restrict__ h, int T, int d, const int* __restrict__ seq_id,
                                 const int64_t* __restrict__ qtype, const __nv_bfloat16* __restrict__ table,

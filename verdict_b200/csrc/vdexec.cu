@@ -1880,15 +1880,48 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
   const int pos_offset = s.style == "xlmr" ? s.pad_id + 1 : 0;
   if (P.max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
   pack(H, c, P, pos_offset);
+  const int vpt = d % 128 == 0 ? d / 128 : 0;  // warp-per-token kernels for d = 512, 768, 1024
   launch(H, VD_K_OTHER, 0.0, [&] {
-    embed_ln_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed, H->pos_emb,
-                                                         H->type_emb0, d, H->emb_ln_w, H->emb_ln_b,
-                                                         static_cast<float>(s.ln_eps), H->h, static_cast<T*>(H->xn));
+    const float eps = static_cast<float>(s.ln_eps);
+    T* xn = static_cast<T*>(H->xn);
+    const int blocks = (ntok + 7) / 8;
+    switch (vpt) {
+      case 4:
+        embed_ln_warp_kernel<4, T><<<blocks, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed,
+                                                                  H->pos_emb, H->type_emb0, d, H->emb_ln_w,
+                                                                  H->emb_ln_b, eps, H->h, xn);
+        break;
+      case 6:
+        embed_ln_warp_kernel<6, T><<<blocks, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed,
+                                                                  H->pos_emb, H->type_emb0, d, H->emb_ln_w,
+                                                                  H->emb_ln_b, eps, H->h, xn);
+        break;
+      case 8:
+        embed_ln_warp_kernel<8, T><<<blocks, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed,
+                                                                  H->pos_emb, H->type_emb0, d, H->emb_ln_w,
+                                                                  H->emb_ln_b, eps, H->h, xn);
+        break;
+      default:
+        embed_ln_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->tokens, H->positions, ntok, H->embed, H->pos_emb,
+                                                             H->type_emb0, d, H->emb_ln_w, H->emb_ln_b, eps, H->h,
+                                                             xn);
+    }
   });
   const double attn_flops = 4.0 * d * P.pairs;
   for (const EncLayer& L : H->enc) enc_layer<T>(H, L, ntok, n_tiles, attn_flops);
   launch(H, VD_K_OTHER, 0.0, [&] {
-    add_type_kernel<<<ntok, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3, H->d_err);
+    const int blocks = (ntok + 7) / 8;
+    if (vpt == 4)
+      add_type_warp_kernel<4><<<blocks, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3,
+                                                             H->d_err);
+    else if (vpt == 6)
+      add_type_warp_kernel<6><<<blocks, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3,
+                                                             H->d_err);
+    else if (vpt == 8)
+      add_type_warp_kernel<8><<<blocks, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3,
+                                                             H->d_err);
+    else
+      add_type_kernel<<<ntok, 256, 0, H->stream>>>(H->h, ntok, d, H->seq_id, c.qtype, H->qtype_emb, 3, H->d_err);
   });
   for (const EncLayer& L : H->head) enc_layer<T>(H, L, ntok, n_tiles, attn_flops);
   const int nm = static_cast<int>(c.nb * c.k);
