@@ -73,10 +73,11 @@ VD_API int vdk_attention(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_
                          int64_t nseq, void* out, int64_t ld_out, void* stream, char* err, size_t errlen);
 
 /*
- * The same causal attention on the 5th-generation tensor cores (tcgen05 MMAs
- * with TMEM accumulators, TMA-fed), head_dim 128 or 256, one query head per
- * CTA, 128-row query tiles and 64-key tiles; the kernel the engine uses for
- * decoders with those head sizes.  Same arguments and result as
+ * The same attention on the 5th-generation tensor cores (tcgen05 MMAs with
+ * TMEM accumulators, TMA-fed), causal with head_dim 128 or 256 or
+ * bidirectional with head_dim 64, one query head per CTA, 128-row query tiles
+ * and 64-key tiles; the kernel the engine uses for decoders with those head
+ * sizes and for the marker-head encoders.  Same arguments and result as
  * vdk_attention; strides and column offsets multiples of 8.
  */
 VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t q_col0, int64_t k_col0, int64_t v_col0,

@@ -195,10 +195,12 @@ def test_gemm_rejects_bad_shapes():
 
 
 @pytest.mark.parametrize("hd,nq,nkv", [(128, 32, 8), (128, 4, 4), (128, 40, 8), (256, 8, 1), (256, 16, 4),
-                                       (256, 3, 3)])
+                                       (256, 3, 3), (64, 12, 12), (64, 16, 4)])
 @pytest.mark.parametrize("dt", ["fp16", "bf16"])
 def test_attention_tc_varlen(hd, nq, nkv, dt):
-    """The tcgen05 / TMEM attention kernels (head_dim 128 and 256, causal) vs torch fp32 SDPA."""
+    """The tcgen05 / TMEM attention kernel (head_dim 128 and 256 causal, 64
+    bidirectional) vs torch fp32 SDPA."""
+    causal = hd != 64
     g = torch.Generator(device="cuda").manual_seed(hd + nq * 7 + nkv)
     lens = [1, 127, 128, 129, 300, 17, 1000, 256, 2100]
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
@@ -207,9 +209,9 @@ def test_attention_tc_varlen(hd, nq, nkv, dt):
     qkv = rand16(dt, T, width, gen=g)
     out = torch.zeros(T, nq * hd, device="cuda", dtype=DTYPES[dt][0])
     q0, k0, v0 = 0, nq * hd, (nq + nkv) * hd
-    run(lib().vdk_attention_tc, P(qkv), width, q0, k0, v0, nq, nkv, hd, DTYPES[dt][1], 1,
+    run(lib().vdk_attention_tc, P(qkv), width, q0, k0, v0, nq, nkv, hd, DTYPES[dt][1], int(causal),
         ctypes.c_void_p(cu.ctypes.data), len(lens), P(out), nq * hd)
-    ref = attention_ref(qkv, cu.tolist(), nq, nkv, hd, q0, k0, v0, True)
+    ref = attention_ref(qkv, cu.tolist(), nq, nkv, hd, q0, k0, v0, causal)
     # P enters the P.V product in the 16-bit type; with bf16 (8-bit mantissa)
     # and up to 2100 keys a few outputs drift just past 2e-2, hence 3e-2.
     close16(out, ref, rel=2e-2 if dt == "fp16" else 3e-2)

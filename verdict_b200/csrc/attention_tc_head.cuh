@@ -1,6 +1,8 @@
-// Causal varlen attention on the tcgen05 tensor cores, one query head per CTA,
-// head_dim HD = 128 or 256 (256: the Gemma-2B decider and the Qwen3.5
-// hybrids' gated attention layers, where O alone fills 256 TMEM columns).
+// Varlen attention on the tcgen05 tensor cores, one query head per CTA:
+// causal with head_dim HD = 128 or 256 (256: the Gemma-2B decider and the
+// Qwen3.5 hybrids' gated attention layers, where O alone fills 256 TMEM
+// columns), or bidirectional (CAUSAL = false) with HD = 64 for the marker-head
+// encoders (every key of the sequence, no option masks).
 //
 // One CTA = one 128-row query tile of one sequence for one query head; keys in
 // tiles of 64.  TMEM: two S/P buffers of 64 columns (S of tile j + 1 is computed
@@ -19,8 +21,9 @@
 //                 O / l (times sigmoid(gate) for gated attention) to global.
 // Shared memory: Q HD/64 swizzled 128 x 64 atoms (HD = 256: 64 KB), K and V
 // two stages of HD/64 64 x 64 atoms each (HD = 256: 2 x 32 KB each).  At HD =
-// 128 a CTA takes 96 KB and 256 TMEM columns, so two run per SM and one's
-// prologue and epilogue overlap the other's main loop.  Every mbarrier wait
+// 128 a CTA takes 96 KB and 256 TMEM columns (at HD = 64, 48 KB and 256
+// columns), so two run per SM and one's prologue and epilogue overlap the
+// other's main loop.  Every mbarrier wait
 // is bounded; on a timeout the CTA records an error code, raises its abort
 // flag and all roles leave their loops.
 #pragma once
@@ -57,11 +60,11 @@ struct AttnTcHeadConfig {
   static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 256;
   static constexpr int THREADS = 224;
   static constexpr uint32_t TMEM_COLS = HD == 256 ? 512 : 256;  // S/P [0, 128), O [128, 128 + HD)
-  static constexpr int MIN_CTAS = HD == 128 ? 2 : 1;
+  static constexpr int MIN_CTAS = HD == 256 ? 1 : 2;
   static constexpr float RESCALE_THRESHOLD = 8.0f;
 };
 
-template <int HD, class T>
+template <int HD, class T, bool CAUSAL = true>
 __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
     attention_tc_head_kernel(const __grid_constant__ CUtensorMap tm_qkv64, AttnTcHeadParams p) {
   using C = AttnTcHeadConfig<HD>;
@@ -88,9 +91,9 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
   const AttnTile tile = p.tiles[blockIdx.x];
   const int head = blockIdx.y;
   const int kvh = head / p.group;
-  const int kv_end = min(tile.seq_len, tile.q_start + C::BM);
+  const int kv_end = CAUSAL ? min(tile.seq_len, tile.q_start + C::BM) : tile.seq_len;
   // Key tiles: first the shared prefix's (n_pre, unmasked but for its end),
-  // then the sequence's own (causal).
+  // then the sequence's own (causal, or all of them).
   const int n_pre = (tile.pre_len + C::BN - 1) / C::BN;
   const int n_kv = n_pre + (kv_end + C::BN - 1) / C::BN;
   auto key_row = [&](int j) {
@@ -218,13 +221,13 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
       const bool in_pre = j < n_pre;
       const int kv0 = (in_pre ? j : j - n_pre) * C::BN;  // key index inside its segment
       const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
-      const int causal_row = in_pre ? 0x7fffffff : q_row;
+      const int causal_row = (in_pre || !CAUSAL) ? 0x7fffffff : q_row;
       if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool need_mask = kv0 + C::BN > seg_len || (!in_pre && kv0 + C::BN > tile.q_start);
+      const bool need_mask = kv0 + C::BN > seg_len || (CAUSAL && !in_pre && kv0 + C::BN > tile.q_start);
       uint32_t sr[64];
       tmem_ld32_nowait(s_tm + 0, sr + 0);
       tmem_ld32_nowait(s_tm + 32, sr + 32);

@@ -225,8 +225,8 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
                                        const int32_t* cu_seqlens_host, int64_t nseq, void* out, int64_t ld_out,
                                        void* stream, char* err, size_t errlen) {
   return guarded(nullptr, err, errlen, [&] {
-    if ((head_dim != 128 && head_dim != 256) || !causal)
-      fail(VD_EINVAL, "the tcgen05 attention kernels are causal with head_dim 128 or 256");
+    if (!((head_dim == 128 || head_dim == 256) && causal) && !(head_dim == 64 && !causal))
+      fail(VD_EINVAL, "the tcgen05 attention kernels are causal with head_dim 128 or 256, or bidirectional with 64");
     if (heads < 1 || kv_heads < 1 || heads % kv_heads != 0) fail(VD_EINVAL, "heads must be a multiple of kv_heads");
     if (nseq < 1 || !cu_seqlens_host || !qkv || !out) fail(VD_EINVAL, "need at least one sequence and buffers");
     if (ld_qkv % 8 != 0 || q_col0 % 8 != 0 || k_col0 % 8 != 0 || v_col0 % 8 != 0 || ld_out % 8 != 0)
@@ -264,7 +264,13 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
     p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)) * 1.4426950408889634);
     p.err = word;
     dim3 grid(static_cast<unsigned>(tiles.size()), heads);
-    if (head_dim == 256 && f16)
+    if (head_dim == 64 && f16)
+      attention_tc_head_kernel<64, __half, false>
+          <<<grid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, s>>>(map64, p);
+    else if (head_dim == 64)
+      attention_tc_head_kernel<64, __nv_bfloat16, false>
+          <<<grid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, s>>>(map64, p);
+    else if (head_dim == 256 && f16)
       attention_tc_head_kernel<256, __half>
           <<<grid, AttnTcHeadConfig<256>::THREADS, AttnTcHeadConfig<256>::SMEM_BYTES, s>>>(map64, p);
     else if (head_dim == 256)

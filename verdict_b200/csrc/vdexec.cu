@@ -1290,6 +1290,9 @@ static void init_kernel_attrs_t() {
   cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<256, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnTcHeadConfig<256>::SMEM_BYTES),
              "tcgen05 one-head attention smem attribute");
+  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<64, T, false>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcHeadConfig<64>::SMEM_BYTES),
+             "tcgen05 one-head attention smem attribute");
   cuda_check(cudaFuncSetAttribute(gdn_chunk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   GdnChunkConfig::SMEM_BYTES),
              "chunked gated delta net smem attribute");
@@ -1324,8 +1327,27 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
   if (L.bn == 256 && H->opt.gemm2 && H->gemm2_pairs > 0) {
-    if (H->opt.raster_group <= 0) shape.group_m = Gemm2Config::GROUP_M;
     const int pair_tiles = ((M + 255) / 256) * (L.n / 256);
+    // A GEMM of a wave or two of CTA pairs (short batches, the encoders' 768-
+    // wide projections) leaves SMs idle; as 128 x 128 tiles on single CTAs
+    // (the W map with 128-row boxes) it spreads over all SMs.  A 128 x 128
+    // tile runs well below half a pair tile's rate, so this is taken only
+    // when it needs at most half the pair kernel's per-SM tile rounds (a pair
+    // tile is two 128 x 128 tiles per SM).
+    if constexpr (EPI == kEpiStore || EPI == kEpiResidual) {
+      const int64_t t128 = static_cast<int64_t>(num_m) * (L.n / 128);
+      const int64_t rounds2 = 2 * ((pair_tiles + H->gemm2_pairs - 1) / H->gemm2_pairs);
+      const int64_t rounds1 = (t128 + H->num_sms - 1) / H->num_sms;
+      if (2 * rounds1 <= rounds2) {
+        const int grid1 = static_cast<int>(std::min<int64_t>(t128, H->num_sms));
+        launch(H, kind, flops, [&] {
+          gemm_tcgen05_kernel<128, EPI, T><<<grid1, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
+                                             H->stream>>>(a, L.map_half, c, shape, ep, H->d_err);
+        });
+        return;
+      }
+    }
+    if (H->opt.raster_group <= 0) shape.group_m = Gemm2Config::GROUP_M;
     const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
     launch(H, kind, flops, [&] {
       gemm2_tcgen05_kernel<EPI, T><<<grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, H->stream>>>(
@@ -1390,6 +1412,29 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
   dim3 grid(n_tiles, heads);
   if (!((hd == 64 && !causal) || (hd == 128 && causal) || (hd == 256 && causal)))
     fail(VD_ESPEC, "no attention kernel for this head size / mask");
+  if (hd == 64 && !causal && opt_id == nullptr && window == 0 && gate_col0 < 0 && H->opt.tc_attention) {
+    // Marker-head encoders: bidirectional head_dim 64 on the tensor cores
+    // (128-row query tiles, planned by encoder_forward).  The option-masked
+    // ModernBERT attention stays on the warp-level kernel.
+    AttnTcHeadParams tp;
+    tp.out = H->attn;
+    tp.ld_out = ld_out;
+    tp.qkv = H->qkv;
+    tp.ld_qkv = ld_qkv;
+    tp.q_col0 = q0;
+    tp.k_col0 = k0;
+    tp.v_col0 = v0;
+    tp.gate_col0 = -1;
+    tp.tiles = H->tiles;
+    tp.group = group;
+    tp.scale_log2 = p.scale_log2;
+    tp.err = H->d_err;
+    launch(H, VD_K_ATTN, flops, [&] {
+      attention_tc_head_kernel<64, T, false>
+          <<<grid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+    });
+    return;
+  }
   if ((hd == 256 || H->opt.tc_head) && use_tc_attention(H, hd, causal, gate_col0 >= 0)) {
     AttnTcHeadParams tp;
     tp.out = H->attn;
@@ -1875,7 +1920,9 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
   const ModelSpec& s = H->spec;
   if (s.von()) return von_forward<T>(H, c);
   const int d = s.hidden;
-  const ChunkPlan P = plan_chunk(H, c, false, 64);
+  // Query tiles of 128 rows for the tcgen05 attention (head_dim 64, see
+  // attention()), 64 for the warp-level kernel.
+  const ChunkPlan P = plan_chunk(H, c, false, H->opt.tc_attention ? 128 : 64);
   const int ntok = P.ntok, n_tiles = P.n_tiles;
   const int pos_offset = s.style == "xlmr" ? s.pad_id + 1 : 0;
   if (P.max_len + pos_offset > s.max_pos) fail(VD_EINVAL, "a row is longer than the model's position table");
