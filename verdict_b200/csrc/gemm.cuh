@@ -54,9 +54,31 @@ struct GemmShape {
   int group_m;
 };
 
+// GELU in its exact form, x * Phi(x), Phi the standard normal CDF, with erf
+// from Abramowitz & Stegun, Handbook of Mathematical Functions, formula
+// 7.1.26 (|error| <= 1.5e-7 for z >= 0):
+//   erf(z) = 1 - q(z),  q(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^(-z^2),
+//   t = 1 / (1 + p z).
+// q is the tail 1 - erf(|z|) itself, so Phi(x) = q / 2 for x < 0 and
+// 1 - q / 2 otherwise come out without cancellation.  One reciprocal and one
+// exp2 on the special-function unit plus a handful of FMAs per element: the
+// encoders' up projections (K = 768) are bound by this epilogue.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.4426950408889634f));
+  const float q = poly * t * e;
+  return x * (x < 0.0f ? 0.5f * q : fmaf(-0.5f, q, 1.0f));
+}
+
 __device__ __forceinline__ float apply_act(float x, int act) {
   switch (act) {
-    case kActGeluErf: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    case kActGeluErf: return gelu_erf(x);
     case kActGeluTanh: {
       const float c = 0.7978845608028654f;  // sqrt(2/pi)
       return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
