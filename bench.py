@@ -493,6 +493,7 @@ def main():
         e0.record(stream)
         h2d = d2h = 0
         host_ms, fwd_ms, enq_ms, call_ms = [], [], [], []
+        parts = {"prep_ms": [], "upload_ms": [], "download_ms": [], "finish_ms": []}
         for i in range(args.steps):
             t0 = time.perf_counter()
             bi, bo = step_host(args.warmup + i)
@@ -501,6 +502,8 @@ def main():
             fwd_ms.append(st["forward_ms"])
             enq_ms.append(st["enqueue_ms"])
             call_ms.append(st["host_ms"])
+            for key, acc in parts.items():
+                acc.append(st[key])
             h2d += bi
             d2h += bo
         e1.record(stream)
@@ -510,6 +513,7 @@ def main():
         e2e = {"value": whole_job_rate(args.batch * args.steps, world, e2e_ms), "unit": UNIT,
                "host_ms_per_call": float(np.mean(host_ms)), "device_forward_ms_per_call": float(np.mean(fwd_ms)),
                "library_call_ms": float(np.mean(call_ms)), "enqueue_ms_per_call": float(np.mean(enq_ms)),
+               "call_breakdown_ms": {key: float(np.mean(acc)) for key, acc in parts.items()},
                "clocks": e2e_clk, "h2d_bytes_per_step": h2d // args.steps,
                "d2h_bytes_per_step": d2h // args.steps}
 

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VDEXEC_ABI_VERSION 1
+#define VDEXEC_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define VD_API __attribute__((visibility("default")))
@@ -103,6 +103,14 @@ typedef struct vd_stats {
   int64_t fork_groups;
   int64_t fork_rows;
   int64_t shared_tokens;
+  /* vd_infer on host memory: host time before the forward's first event
+   * (validation, staging, uploads enqueued) and after its last launch
+   * (download, synchronisation, error check); device time of the uploads
+   * before the forward and of the download after it. */
+  double prep_ms;
+  double finish_ms;
+  double upload_ms;
+  double download_ms;
 } vd_stats;
 
 /*

@@ -169,7 +169,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(lib, s), f"{s} declared in include/ but not exported"
         assert s in _abi.SIGNATURES, f"{s} has no ctypes signature"
-    assert lib.vd_abi_version() == 1
+    assert lib.vd_abi_version() == 2
 
 
 def test_open_without_gpu_fails_cleanly():

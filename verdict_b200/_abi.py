@@ -38,6 +38,8 @@ class VdStats(ctypes.Structure):
         ("kernel_flops", ctypes.c_double * 8),
         ("host_ms", ctypes.c_double), ("enqueue_ms", ctypes.c_double),
         ("fork_groups", ctypes.c_int64), ("fork_rows", ctypes.c_int64), ("shared_tokens", ctypes.c_int64),
+        ("prep_ms", ctypes.c_double), ("finish_ms", ctypes.c_double), ("upload_ms", ctypes.c_double),
+        ("download_ms", ctypes.c_double),
     ]
 
 

@@ -670,6 +670,7 @@ struct vd_handle {
   int slot = 0;
   size_t pinned_bytes = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev_user = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;  // host-memory calls: before the uploads, after the download
   vd_stats stats{};
   int64_t launches = 0;
   // per-kernel event timing (vd_set_profiling)
@@ -1246,6 +1247,8 @@ static void alloc_workspace(vd_handle* H) {
   }
   cuda_check(cudaEventCreate(&H->ev0), "event");
   cuda_check(cudaEventCreate(&H->ev1), "event");
+  cuda_check(cudaEventCreate(&H->ev_in), "event");
+  cuda_check(cudaEventCreate(&H->ev_out), "event");
   cuda_check(cudaEventCreateWithFlags(&H->ev_user, cudaEventDisableTiming), "event");
 }
 
@@ -2299,6 +2302,7 @@ extern "C" VD_API int vd_infer(vd_handle* h, const vd_batch* batch, float* logit
     cudaStream_t s = h->stream;
     cuda_check(cudaStreamSynchronize(s), "synchronize");  // staging buffers may be regrown
     ensure_host_inputs(h, n_ids, n_m, b, b * out_width);
+    cuda_check(cudaEventRecord(h->ev_in, s), "event");
     cuda_check(cudaMemcpyAsync(h->in_ids, batch->input_ids, n_ids * 8, cudaMemcpyHostToDevice, s), "upload ids");
     cuda_check(cudaMemcpyAsync(h->in_mpos, batch->marker_pos, n_m * 8, cudaMemcpyHostToDevice, s), "upload markers");
     if (batch->marker_mask)
@@ -2307,11 +2311,20 @@ extern "C" VD_API int vd_infer(vd_handle* h, const vd_batch* batch, float* logit
       cuda_check(cudaMemcpyAsync(h->in_nopts, batch->nopts, b * 8, cudaMemcpyHostToDevice, s), "upload nopts");
     if (batch->qtype)
       cuda_check(cudaMemcpyAsync(h->in_qtype, batch->qtype, b * 8, cudaMemcpyHostToDevice, s), "upload qtype");
+    const double prep_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_call).count();
     run_batch(h, batch, h->in_ids, h->in_mpos, batch->marker_mask ? h->in_mmask : nullptr,
               batch->nopts ? h->in_nopts : nullptr, batch->qtype ? h->in_qtype : nullptr, h->out_dev, out_width);
+    const auto t_launched = std::chrono::steady_clock::now();
     cuda_check(cudaMemcpyAsync(logits_out, h->out_dev, b * out_width * sizeof(float), cudaMemcpyDeviceToHost, s),
                "download logits");
+    cuda_check(cudaEventRecord(h->ev_out, s), "event");
     check_device_error(h);
+    float up = 0, down = 0;
+    if (cudaEventElapsedTime(&up, h->ev_in, h->ev0) == cudaSuccess) h->stats.upload_ms = up;
+    if (cudaEventElapsedTime(&down, h->ev1, h->ev_out) == cudaSuccess) h->stats.download_ms = down;
+    h->stats.prep_ms = prep_ms;
+    h->stats.finish_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_launched).count();
   });
 }
 
@@ -2418,6 +2431,8 @@ extern "C" VD_API void vd_close(vd_handle* h) {
       }
       if (h->ev0) cudaEventDestroy(h->ev0);
       if (h->ev1) cudaEventDestroy(h->ev1);
+      if (h->ev_in) cudaEventDestroy(h->ev_in);
+      if (h->ev_out) cudaEventDestroy(h->ev_out);
       if (h->ev_user) cudaEventDestroy(h->ev_user);
       for (cudaEvent_t e : h->prof_pool) cudaEventDestroy(e);
       if (h->stream) cudaStreamDestroy(h->stream);
