@@ -52,6 +52,28 @@ def test_workload_generators_follow_the_benchmark_shapes():
         assert 2 <= len(r.markers) <= 6
 
 
+def test_bench_marker_head_workloads():
+    """bench.py's marker-head encoder batches: BERT rows U[16,128] with 3
+    markers and text ids >= 1000, XLM-R rows <= 512 with 2-6 markers; every
+    row gets a question type in [0, 3); models route to their row builders."""
+    import sys
+    sys.path.insert(0, REPO)
+    import bench
+    bert = bench.make_batches(0, 2, 32, 30522, 7, "marker", 0, "uniform-bert")
+    for b in bert:
+        assert b.b == 32 and b.k == 3 and 0 <= b.qtype.min() and b.qtype.max() < 3
+        for i, r in enumerate(b.rows):
+            ids = b.input_ids[i * b.l:i * b.l + r.real_len]
+            assert 16 <= r.real_len <= 128 and ids[0] == 101 and ids[-1] == 102
+            text = ids[(ids != 101) & (ids != 102)]
+            assert text.min() >= 1000
+    xlmr = bench.make_batches(0, 1, 64, 250002, 7, "marker", 1, "lognormal-xlmr")[0]
+    assert xlmr.l <= 512 and 2 <= xlmr.k <= 6
+    assert bench.workload_of(specs.preset("laya-xlmr"), "choice") == "marker"
+    assert bench.workload_of(specs.preset("von-base"), "choice") == "von"
+    assert bench.workload_of(specs.preset("onejev-9b"), "shared-prefix") == "shared-prefix"
+
+
 # --- synthetic checkpoints ------------------------------------------------------
 
 def test_bf16_round_ties_to_even():
