@@ -194,6 +194,38 @@ def test_library_exports_every_declared_symbol():
     assert lib.vd_abi_version() == 2
 
 
+def test_headers_compile_as_c_and_match_the_python_mirror(tmp_path):
+    """include/*.h are plain C, and vd_batch / vd_stats have the layout the
+    ctypes mirror (verdict_b200/_abi.py) assumes: size and every field offset."""
+    import shutil
+    import subprocess
+    from verdict_b200 import _abi
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "vdexec.h"', '#include "vdexec_kernels.h"',
+             'int main(void) {']
+    for cname, mirror in (("vd_batch", _abi.VdBatch), ("vd_stats", _abi.VdStats)):
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in mirror._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ['  printf("VD_K_COUNT %d\\n", (int)VD_K_COUNT);', '  return 0;', '}']
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        *key, value = line.split()
+        got[" ".join(key)] = int(value)
+    for cname, mirror in (("vd_batch", _abi.VdBatch), ("vd_stats", _abi.VdStats)):
+        assert got[f"{cname} size"] == ctypes.sizeof(mirror), cname
+        for field, _ in mirror._fields_:
+            assert got[f"{cname} {field}"] == getattr(mirror, field).offset, (cname, field)
+    assert got["VD_K_COUNT"] == len(_abi.KERNEL_CLASSES)
+
+
 def test_open_without_gpu_fails_cleanly():
     import torch
     if torch.cuda.is_available():
