@@ -187,6 +187,33 @@ def test_encoder_full_depth_vs_oracle(preset, lengths):
         eng.close()
 
 
+@pytest.mark.parametrize("preset,lengths", [("laya-bert", "uniform-bert"), ("laya-xlmr", "lognormal-xlmr")])
+def test_encoder_tensor_core_attention_matches_warp_level_attention(preset, lengths):
+    """Marker-head encoders: the bidirectional head_dim-64 tcgen05 attention
+    (default, 128-row query tiles) and the warp-level kernel (`attention:
+    "mma"`, 64-row tiles) give the same scorer logits, both near the oracle."""
+    spec = specs.preset(preset, layers=3, seed=43)
+    rng = np.random.default_rng(43)
+    cls_id, sep_id = (101, 102) if preset == "laya-bert" else (0, 2)
+    rows = encoder_rows(rng, 12, spec["vocab"], lengths=lengths, cls_id=cls_id, sep_id=sep_id, id_low=5,
+                        max_len=spec["max_pos"] - 2)
+    batch = collate(rows, Layout(pad_id=spec["pad_id"]))
+    batch.qtype[:] = rng.integers(0, 3, size=batch.b)
+    ref = EncoderOracle(spec).infer(batch)
+    live = ref > -1e4
+    scale = max(1.0, float(np.abs(ref[live]).max()))
+    got = {}
+    for mode in ("tc", "mma"):
+        eng = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=512, attention=mode)
+        try:
+            got[mode] = engine_logprobs(eng, batch)
+        finally:
+            eng.close()
+        assert np.all(got[mode][~live] == -1e4)
+        assert np.abs(got[mode][live] - ref[live]).max() / scale <= ENC_TOL
+    assert np.abs(got["tc"][live] - got["mma"][live]).max() / scale <= ENC_TOL
+
+
 @pytest.mark.parametrize("mode", ["tc", "tc2"])
 def test_tensor_core_attention_matches_warp_level_attention(mode):
     """The engine's tcgen05 attention (one query head per CTA: tc; two: tc2)
