@@ -19,11 +19,16 @@ Printed JSON (rank 0, one line):
   roofline  the gate/up projection GEMM (tcgen05, the largest kernel): its
          algorithmic FLOPs per launch / its mean launch time from events around
          each launch, against the measured sustained dense 16-bit tensor peak
-  dtype  fp16: activations and projection weights in fp16 (the bf16 checkpoint
-         values are exact in fp16), fp32 accumulation and fp32 residual stream
+  dtype  fp16 (default): activations and projection weights in fp16 (the bf16
+         checkpoint values are exact in fp16), fp32 accumulation and fp32
+         residual stream; --act-dtype bf16 keeps them in bf16
+  sweep  the same workload at 1, 8 and 256 decisions per step (one GPU):
+         decisions/s, mean and p99 step time, SM clock
   cpu_baseline  the CPU oracle (fp32 numpy restatement of the reference's CPU
-         executor path) on a bounded sample, on this host's cores
---impl reference runs that CPU implementation as the reference arm.
+         executor path) on a bounded sample of the workload's decisions, every
+         layer timed, on all of this host's cores
+--impl reference runs that CPU implementation as the reference arm: one
+decision of the workload per step through every layer (nothing extrapolated).
 """
 
 from __future__ import annotations
@@ -34,6 +39,13 @@ import os
 import subprocess
 import sys
 import time
+
+if "reference" in sys.argv[1:]:
+    # The reference arm runs on the host cores: torchrun sets OMP_NUM_THREADS=1,
+    # and BLAS / OpenMP read these variables when they load (before numpy).
+    _cores = str(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count())
+    for _var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_var] = _cores
 
 import numpy as np
 
@@ -147,6 +159,9 @@ def whole_job_rate(decisions_per_rank: int, world: int, max_ms: float) -> float:
     return decisions_per_rank * world / (max_ms / 1e3)
 
 
+# Concurrency sweep: (decisions per step, timed steps), each after 3 warm-up steps.
+SWEEP = ((1, 16), (8, 8), (256, 3))
+
 LENGTHS = {"onejev-9b": "lognormal-9b", "onejev16-9b": "lognormal-9b", "decider-2b": "uniform-2b",
            "onejev-27b": "uniform-27b", "laya-bert": "uniform-bert", "laya-xlmr": "lognormal-xlmr"}
 # Marker-head encoder rows: ([CLS], [SEP]) ids, lowest text id, longest row.
@@ -191,29 +206,93 @@ def make_batches(rank, n_batches, per_batch, vocab, seed, workload="choice", pad
     return out
 
 
-def cpu_baseline_sample(spec, batch, layers_timed):
-    """Time the oracle (fp32 numpy) on one decision through `layers_timed` of the
-    model's layers and scale to the full depth; returns (decisions/s, sample text)."""
+def host_threads():
+    """Set up the CPU legs: BLAS / OpenMP threads on every core this process may
+    run on, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1), and
+    glibc malloc keeping freed blocks (the forward's large temporaries are then
+    reused instead of faulted in afresh each time, as torch's CPU allocator
+    does).  Returns the thread count the BLAS library reports afterwards."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    try:
+        import ctypes
+        libc = ctypes.CDLL("libc.so.6")
+        libc.mallopt(-3, 1 << 30)      # M_MMAP_THRESHOLD: heap, not mmap, up to 1 GiB
+        libc.mallopt(-1, 2 ** 31 - 1)  # M_TRIM_THRESHOLD: keep freed memory
+    except Exception:
+        pass
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=n)
+        blas = [i["num_threads"] for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(blas[0]) if blas else n
+    except Exception:
+        return n
+
+
+def decoder_cpu_times(spec, seqs):
+    """Seconds of the oracle's full-depth fp32 forward + readout per decision
+    (every layer, nothing scaled).  Layer-major, as a batch runs through a
+    model: each layer's weights are generated once (untimed; the reference
+    holds them in memory) and each decision's pass through that layer is timed
+    on its own.  `seqs`: [(token ids, nopts)], slot = last token."""
     from oracle.decoder import DecoderOracle, rmsnorm
-    orc = DecoderOracle(spec, layers=layers_timed, cache_layers=True)
-    n = int(batch.rows[0].real_len)
-    ids = batch.input_ids[:n]
-    for i in range(layers_timed):
-        orc.layer(i)  # generate weights outside the timed region
-    t0 = time.perf_counter()
-    cos, sin = orc.rope(n)
-    h = orc.embed(ids)
-    t1 = time.perf_counter()
-    for i in range(layers_timed):
-        h = orc.layer_forward(i, h, cos, sin)
-    t2 = time.perf_counter()
-    hs = rmsnorm(h[-1:], orc.final_norm, spec["rms_eps"], spec["norm_plus_one"])
-    _ = hs @ orc.head_w[: int(batch.nopts[0])].T
-    t3 = time.perf_counter()
-    per_decision = (t1 - t0) + (t2 - t1) * spec["layers"] / layers_timed + (t3 - t2)
-    sample = (f"1 decision of {n} tokens; {layers_timed} of {spec['layers']} layers timed and scaled "
-              f"to full depth (embed + readout timed once)")
-    return 1.0 / per_decision, sample, per_decision
+    orc = DecoderOracle(spec, cache_layers=False)
+    times = np.zeros(len(seqs))
+    hs, tabs = [], []
+    for j, (ids, _) in enumerate(seqs):
+        h = orc.embed(np.asarray(ids, dtype=np.int64))  # embedding rows (generated untimed)
+        t0 = time.perf_counter()
+        tabs.append(orc.rope(len(ids)))
+        hs.append(h.copy())
+        times[j] += time.perf_counter() - t0
+    for layer in range(spec["layers"]):
+        orc._layers[layer] = orc.layer(layer)
+        for j in range(len(seqs)):
+            t0 = time.perf_counter()
+            hs[j] = orc.layer_forward(layer, hs[j], *tabs[j])
+            times[j] += time.perf_counter() - t0
+        del orc._layers[layer]
+    for j, (_, nopts) in enumerate(seqs):
+        t0 = time.perf_counter()
+        hn = rmsnorm(hs[j][-1:], orc.final_norm, spec["rms_eps"], spec["norm_plus_one"])
+        logits = hn[0] @ orc.head_w[:int(nopts)].T
+        z = logits - logits.max()
+        _ = z - np.log(np.exp(z).sum())
+        times[j] += time.perf_counter() - t0
+    return times
+
+
+def decoder_cpu_sample(batches, n):
+    """The first n decisions of the workload's batches (row order), for the CPU legs."""
+    out = []
+    for b in batches:
+        for i in range(b.b):
+            out.append((b.input_ids[i * b.l:i * b.l + int(b.rows[i].real_len)], int(b.nopts[i])))
+            if len(out) == n:
+                return out
+    return out
+
+
+def cpu_baseline_decoder(spec, batches, budget_s=20.0):
+    """The CPU baseline of the repo's own bench line: the oracle on decisions of
+    the same workload, all layers, on this host's cores.  Takes the first
+    decisions of the timed batches until their tokens add up to about
+    `budget_s` of CPU work (at least 2 decisions; the first one absorbs the
+    first use of each layer's weights and is not counted)."""
+    tok_per_s = 515.0 / 8.0  # rough fp32 throughput of 16 cores on the 9B shape, for sizing only
+    seqs, tokens = [], 0
+    for ids, nopts in decoder_cpu_sample(batches, 1 << 30):
+        seqs.append((ids, nopts))
+        tokens += len(ids)
+        if len(seqs) >= 3 and tokens * spec["layers"] / 40.0 >= budget_s * tok_per_s:
+            break
+    threads = host_threads()
+    t = decoder_cpu_times(spec, seqs)[1:]
+    toks = [len(ids) for ids, _ in seqs[1:]]
+    sample = (f"{len(t)} decisions of the workload (first rows of the timed batches, {int(np.sum(toks))} tokens, "
+              f"lengths {min(toks)}-{max(toks)}), every one of the {spec['layers']} layers timed, nothing scaled; "
+              "one more decision run first, untimed")
+    return len(t) / float(np.sum(t)), sample, float(np.mean(t)), threads
 
 
 def encoder_cpu_sample(spec, batch):
@@ -237,38 +316,50 @@ def encoder_cpu_sample(spec, batch):
 
 
 def run_reference(args, world, rank):
-    """The reference arm: the CPU path of the reference executor (fp32), as the
-    oracle port, on this host's cores; rank 0 only."""
+    """The reference arm: the reference executor's CPU path (fp32), as the
+    oracle port, on all of this host's cores; rank 0 only.  A decoder step is
+    one decision of the workload through every layer (no extrapolation), an
+    encoder step four decisions."""
     if rank != 0:
         return
-    import torch  # noqa: F401  (thread settings only)
     from verdict_b200 import spec as specs
     from verdict_b200.synth import with_labels
     spec = with_labels(specs.preset(args.model))
     encoder = spec["arch"] == "encoder"
-    batches = make_batches(0, args.warmup + args.steps, 4 if encoder else 1, spec["vocab"], args.seed,
-                           workload_of(spec, "choice"), spec.get("pad_id", 0),
-                           LENGTHS.get(args.model, "lognormal-9b"))
-    times = []
-    for j, b in enumerate(batches):
-        _, _, per = encoder_cpu_sample(spec, b) if encoder else cpu_baseline_sample(spec, b, args.ref_layers)
-        if j >= args.warmup:
-            times.append(per)
+    threads = host_threads()
+    t_start = time.perf_counter()
+    if encoder:
+        batches = make_batches(0, args.warmup + args.steps, 4, spec["vocab"], args.seed,
+                               workload_of(spec, "choice"), spec.get("pad_id", 0),
+                               LENGTHS.get(args.model, "lognormal-9b"))
+        per = [encoder_cpu_sample(spec, b)[2] * 4 for b in batches]
+        per_step = 4
+        sample = "per step 4 decisions of the workload, all layers"
+    else:
+        # Steps take the workload's own decisions in order (the repo arm's
+        # batches, seeded identically), one per step.
+        batches = make_batches(0, 1, max(args.batch, args.warmup + args.steps), spec["vocab"], args.seed,
+                               workload_of(spec, "choice"), spec.get("pad_id", 0),
+                               LENGTHS.get(args.model, "lognormal-9b"))
+        seqs = decoder_cpu_sample(batches, args.warmup + args.steps)
+        per = list(decoder_cpu_times(spec, seqs))
+        per_step = 1
+        toks = [len(ids) for ids, _ in seqs[args.warmup:]]
+        sample = (f"per step 1 decision of the workload through all {spec['layers']} layers (nothing scaled); "
+                  f"timed decisions {int(np.sum(toks))} tokens, lengths {min(toks)}-{max(toks)}")
+    times = per[args.warmup:]
     mean = float(np.mean(times))
-    value = 1.0 / mean
-    cores = os.cpu_count()
+    value = per_step / mean
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
+        "p99_ms": float(np.percentile(times, 99)) * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
         "config": {"workload": workload_text(args.model), "model": args.model,
-                   "decisions_per_step": 4 if encoder else 1,
-                   "parallelism": "host cores"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": ("per step 4 decisions, all layers" if encoder else
-                                    f"per step 1 decision; {args.ref_layers} of {spec['layers']} layers timed "
-                                    "and scaled")},
+                   "decisions_per_step": per_step, "parallelism": f"host cores ({threads} BLAS threads)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "timed_s": float(np.sum(times)), "run_s": time.perf_counter() - t_start,
     }
     print(json.dumps(line), flush=True)
 
@@ -282,7 +373,6 @@ def main():
     ap.add_argument("--batch", type=int, default=64, help="decisions per step (concurrency)")
     ap.add_argument("--layers", type=int, default=None, help="override depth (default: full 40)")
     ap.add_argument("--seed", type=int, default=20261201)
-    ap.add_argument("--ref-layers", type=int, default=2, help="layers timed per CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--attention", default="tc", choices=["tc", "tc2", "mma"],
@@ -305,6 +395,11 @@ def main():
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
     ap.add_argument("--gdn", default="chunk", choices=["chunk", "scan"],
                     help="gated delta nets in 64-token chunks on the tensor cores (chunk) or token by token (scan)")
+    ap.add_argument("--act-dtype", default="fp16", choices=["fp16", "bf16"],
+                    help="16-bit element type of activations and projection weights (fp32 accumulation and "
+                         "residual stream either way)")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false",
+                    help="skip the concurrency sweep (decoders: 1, 8 and 256 decisions per step)")
     ap.add_argument("--raster-group", type=int, default=0,
                     help="M tiles per GEMM raster group (0: the kernels' default)")
     args = ap.parse_args()
@@ -336,11 +431,21 @@ def main():
     batches = make_batches(rank, n_batches, args.batch, spec["vocab"], args.seed,
                            workload_of(spec, args.workload), spec.get("pad_id", 0),
                            LENGTHS.get(args.model, "lognormal-9b"))
-    max_len = max(int(b.real_len().max()) for b in batches)
-    max_tokens = max(int(b.real_len().sum()) for b in batches)
-    eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(args.batch, 8),
+    # Concurrency sweep (decoders, one GPU): other batch sizes of the same
+    # workload, timed after the headline, each from its own seeded batches.
+    sweep_sets = {}
+    if args.sweep and not encoder and world == 1 and args.workload == "choice":
+        for c, steps in SWEEP:
+            sweep_sets[c] = make_batches(rank, 3 + steps, c, spec["vocab"], args.seed + 1000 + c,
+                                         workload_of(spec, args.workload), spec.get("pad_id", 0),
+                                         LENGTHS.get(args.model, "lognormal-9b"))
+    every = batches + [b for bs in sweep_sets.values() for b in bs]
+    max_len = max(int(b.real_len().max()) for b in every)
+    max_tokens = max(int(b.real_len().sum()) for b in every)
+    max_batch = max(b.b for b in every)
+    eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(max_batch, 8),
                      max_seq=max(4096, max_len), attention=args.attention, fork=args.fork == "on",
-                     gemm=args.gemm, raster_group=args.raster_group, gdn=args.gdn)
+                     gemm=args.gemm, raster_group=args.raster_group, gdn=args.gdn, act_dtype=args.act_dtype)
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
     width = eng.width if not encoder else max(b.k for b in batches)  # encoders: one logit per marker slot
@@ -517,17 +622,54 @@ def main():
                "clocks": e2e_clk, "h2d_bytes_per_step": h2d // args.steps,
                "d2h_bytes_per_step": d2h // args.steps}
 
+    sweep = None
+    if sweep_sets:
+        sweep = {}
+        for c, bs in sweep_sets.items():
+            dv = [{k: torch.from_numpy(np.ascontiguousarray(v)).to(f"cuda:{local}") for k, v in dict(
+                input_ids=b.input_ids, marker_pos=b.marker_pos, marker_mask=b.marker_mask.astype(np.uint8),
+                nopts=b.nopts, qtype=b.qtype).items()} for b in bs]
+            o = torch.empty(c, width, device=f"cuda:{local}", dtype=torch.float32)
+
+            def run_c(j, bs=bs, dv=dv, o=o):
+                b = bs[j]
+                eng.infer_device(b.b, b.l, b.k, {k: v.data_ptr() for k, v in dv[j].items()}, b.real_len(),
+                                 o.data_ptr(), width)
+
+            for j in range(3):
+                run_c(j)
+            eng.sync()
+            ck = Clocks(local)
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * (len(bs) - 3))]
+            with torch.cuda.stream(stream):
+                for i in range(len(bs) - 3):
+                    ev[2 * i].record(stream)
+                    run_c(3 + i)
+                    ev[2 * i + 1].record(stream)
+            eng.sync()
+            cl = ck.stop()
+            ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(len(bs) - 3)]
+            sweep[f"c{c}"] = {"decisions_per_step": c, "steps": len(ms), "warmup": 3,
+                              "value": c * len(ms) / (ev[0].elapsed_time(ev[-1]) / 1e3), "unit": UNIT,
+                              "ms_per_step": float(np.mean(ms)), "p99_ms": float(np.percentile(ms, 99)),
+                              "ms_per_decision": float(np.mean(ms)) / c,
+                              "mean_tokens_per_step": float(np.mean([b.real_len().sum() for b in bs[3:]])),
+                              "sm_mhz": cl.get("sm_mhz"), "reasons": cl.get("reasons")}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, sample, _ = (encoder_cpu_sample(spec, batches[0]) if encoder
-                        else cpu_baseline_sample(spec, batches[0], args.ref_layers))
-        cpu = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+        if encoder:
+            threads = host_threads()
+            v, sample, _ = encoder_cpu_sample(spec, batches[0])
+        else:
+            v, sample, _, threads = cpu_baseline_decoder(spec, batches[args.warmup:])
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "p99_ms": p99_ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.act_dtype,
             "data": "synthetic (seeded; random-init weights generated on device)",
             "config": {"workload": workload_text(args.model, shared),
                        "model": args.model,
@@ -541,7 +683,7 @@ def main():
                               "leg does not flush)" if encoder else
                               "no flush: each step streams every layer's weights (GBs) and the activations, far "
                               "above the 126 MB L2")},
-            "e2e": e2e, "gpu_launches": int(launches), "clocks": clk, "roofline": roofline,
+            "e2e": e2e, "gpu_launches": int(launches), "clocks": clk, "roofline": roofline, "sweep": sweep,
             "kernels": kern, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

@@ -122,7 +122,9 @@ def make_cases():
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {os.path.basename(__file__)} <path of the reference checkout>")
+    ref_root = sys.argv[1]
     ex = load_executor(ref_root)
     out = {}
     meta = []

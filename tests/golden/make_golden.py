@@ -227,7 +227,9 @@ def encoder_case(ref_root, name, spec, seed):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {os.path.basename(__file__)} <path of the reference checkout>")
+    ref_root = sys.argv[1]
     ex = load_module("torch_exec", os.path.join(ref_root, "executor", "torch_exec.py"))
 
     qwen = specs.preset("onejev-9b", hidden=256, layers=2, heads=4, kv_heads=2, head_dim=128,

@@ -180,3 +180,77 @@ def test_device_resident_batches_fork_when_they_declare_prefixes():
                 assert np.abs(got - host)[live].max() <= FORK_TOL
     finally:
         eng.close()
+
+
+def letter_branches_batch(vocab, seed, chat=72, states=(700, 350, 1200), questions=3):
+    """Rows as letter_branches renders them (`build_row`,
+    src/family/letter_branches.rs:89-121): one chat/system prompt shared by
+    every row, then the state, then the question; the declared prefix_len is
+    chat + state.  Without it the 32-token common-prefix key would put every
+    row in one group that forks only the chat prompt."""
+    rng = np.random.default_rng(seed)
+    head = rng.integers(3, vocab, size=chat).tolist()
+    rows, pl = [], []
+    for n in states:
+        pre = head + rng.integers(3, vocab, size=n).tolist()
+        for _ in range(questions):
+            rows.append(pre + rng.integers(3, vocab, size=int(rng.integers(30, 120))).tolist())
+            pl.append(len(pre))
+    order = rng.permutation(len(rows))
+    return batch_of([rows[i] for i in order], [pl[i] for i in order], seed=seed)
+
+
+def vd_infer_raw(eng, batch, with_prefix_len):
+    """vd_infer through ctypes exactly as the Rust binding calls it: host
+    buffers, RowMeta's real_len / real_k / prefix_len passed as arrays."""
+    import ctypes
+    from verdict_b200 import _abi
+    ids = np.ascontiguousarray(batch.input_ids, dtype=np.int64)
+    amask = np.ascontiguousarray(batch.attention_mask, dtype=np.int64)
+    mpos = np.ascontiguousarray(batch.marker_pos, dtype=np.int64)
+    mmask = np.ascontiguousarray(batch.marker_mask, dtype=np.uint8)
+    qtype = np.ascontiguousarray(batch.qtype, dtype=np.int64)
+    nopts = np.ascontiguousarray(batch.nopts, dtype=np.int64)
+    real_len = np.array([r.real_len for r in batch.rows], dtype=np.int64)
+    real_k = np.array([r.real_k for r in batch.rows], dtype=np.int64)
+    prefix_len = np.array([r.prefix_len for r in batch.rows], dtype=np.int64)
+    st = _abi.VdBatch()
+    st.b, st.l, st.k, st.memory = batch.b, batch.l, batch.k, _abi.VD_MEM_HOST
+    for name, a in (("input_ids", ids), ("attention_mask", amask), ("marker_pos", mpos), ("marker_mask", mmask),
+                    ("qtype", qtype), ("nopts", nopts), ("real_len", real_len), ("real_k", real_k)):
+        setattr(st, name, ctypes.c_void_p(a.ctypes.data))
+    st.prefix_len = ctypes.c_void_p(prefix_len.ctypes.data) if with_prefix_len else None
+    out = np.empty((batch.b, eng.width), dtype=np.float32)
+    err = ctypes.create_string_buffer(1024)
+    rc = eng.lib.vd_infer(eng.h, ctypes.byref(st), ctypes.c_void_p(out.ctypes.data), eng.width, err, len(err))
+    _abi.check(rc, err)
+    return out.astype(np.float64), eng.last_stats()
+
+
+def test_rust_binding_passes_declared_prefixes():
+    """The C ABI called as the Rust `Engine` binding calls it forms the
+    reference's declared-prefix groups (one per state) when prefix_len is
+    passed, and the common-prefix groups when it is not; both give the
+    whole-row answer."""
+    spec = spec9b()
+    batch = letter_branches_batch(spec["vocab"], 12)
+    ids = batch.input_ids.reshape(batch.b, batch.l)
+    slot = batch.marker_pos.reshape(batch.b, batch.k)[:, 0]
+    declared = fork.plan(ids, batch.real_len(), slot, batch.prefix_len(), single=False)
+    undeclared = fork.plan(ids, batch.real_len(), slot, None, single=False)
+    assert len(declared) == 3 and len(undeclared) == 1 and undeclared[0][1] == 72
+    on = B200Engine(spec, max_tokens=16384, max_rows=64, max_seq=4096)
+    off = B200Engine(spec, max_tokens=16384, max_rows=64, max_seq=4096, fork=False)
+    try:
+        whole, _ = vd_infer_raw(off, batch, True)
+        for with_pl, groups in ((True, declared), (False, undeclared)):
+            got, st = vd_infer_raw(on, batch, with_pl)
+            assert st["fork_groups"] == len(groups)
+            assert st["fork_rows"] == sum(len(m) for m, _ in groups)
+            assert st["shared_tokens"] == sum(n * (len(m) - 1) for m, n in groups)
+            live = whole > -1e4
+            assert np.all(got[~live] == -1e4)
+            assert np.abs(got - whole)[live].max() <= FORK_TOL
+    finally:
+        on.close()
+        off.close()

@@ -215,3 +215,23 @@ def test_attention_tc_varlen(hd, nq, nkv, dt):
     # P enters the P.V product in the 16-bit type; with bf16 (8-bit mantissa)
     # and up to 2100 keys a few outputs drift just past 2e-2, hence 3e-2.
     close16(out, ref, rel=2e-2 if dt == "fp16" else 3e-2)
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 40, 8), (256, 8, 1)])
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_attention_tc_long_keys(hd, nq, nkv, dt):
+    """Rows of 8,192 keys (the 27B shape's longest prompts) on the tcgen05
+    kernel vs torch fp32 SDPA: the running max / rescale path over 128 key
+    tiles and the 16-bit P at that depth."""
+    g = torch.Generator(device="cuda").manual_seed(8192 + hd)
+    lens = [8192, 4100, 3]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    width = (nq + 2 * nkv) * hd
+    qkv = rand16(dt, T, width, gen=g)
+    out = torch.zeros(T, nq * hd, device="cuda", dtype=DTYPES[dt][0])
+    q0, k0, v0 = 0, nq * hd, (nq + nkv) * hd
+    run(lib().vdk_attention_tc, P(qkv), width, q0, k0, v0, nq, nkv, hd, DTYPES[dt][1], 1,
+        ctypes.c_void_p(cu.ctypes.data), len(lens), P(out), nq * hd)
+    ref = attention_ref(qkv, cu.tolist(), nq, nkv, hd, q0, k0, v0, True)
+    close16(out, ref, rel=2e-2 if dt == "fp16" else 3e-2)

@@ -144,7 +144,8 @@ def test_decoder_shapes_vs_oracle(preset, layers, n_rows, max_len):
         eng.close()
 
 
-@pytest.mark.parametrize("preset,lens", [("onejev-9b", (48, 130, 300)), ("decider-2b", (64, 257, 700))])
+@pytest.mark.parametrize("preset,lens", [("onejev-9b", (48, 130, 300)), ("decider-2b", (64, 257, 700)),
+                                         ("onejev-9b", (515, 1200)), ("decider-2b", (1024,))])
 def test_decoder_full_depth_vs_oracle(preset, lens):
     """All layers of the benchmark shapes (40 for OneJev-9B, 18 for the 2B
     decider) against the fp32 oracle, which regenerates each layer's weights
@@ -157,6 +158,49 @@ def test_decoder_full_depth_vs_oracle(preset, lens):
         r.markers = [n - 1]
     batch = collate(rows, Layout(pad_id=0))
     eng = B200Engine(spec, max_tokens=4096, max_rows=8, max_seq=2048)
+    try:
+        got = engine_logprobs(eng, batch)
+    finally:
+        eng.close()
+    ref = DecoderOracle(spec, cache_layers=False).infer(batch)
+    assert_decoder_parity(got, ref, batch.nopts)
+
+
+def fixed_rows(spec, seed, lens):
+    rng = np.random.default_rng(seed)
+    rows = decoder_rows(rng, len(lens), spec["vocab"], lengths="fixed:8")
+    for r, n in zip(rows, lens):
+        r.ids = rng.integers(3, spec["vocab"], size=n).tolist()
+        r.markers = [n - 1]
+    return collate(rows, Layout(pad_id=0))
+
+
+@pytest.mark.parametrize("preset,layers,lens", [
+    ("onejev-9b", 2, (2048, 3000, 4096)),   # the 9B length mix's upper end (clip at 4096)
+    ("onejev-27b", 2, (4096, 8192, 600)),   # the 27B mix's longest prompts (U[512, 8192])
+    ("decider-2b", 2, (1024, 777)),         # the 2B mix's longest prompt (U[64, 1024])
+])
+def test_decoder_long_rows_vs_oracle(preset, layers, lens):
+    """Rows at the configs' maximum lengths in one packed batch: the RoPE
+    table, the attention tile tables and the 16-bit softmax path at 4k-8k
+    positions against the fp32 oracle."""
+    spec = with_labels(specs.preset(preset, layers=layers, seed=83))
+    batch = fixed_rows(spec, 83, lens)
+    ref = DecoderOracle(spec).infer(batch)
+    eng = B200Engine(spec, max_tokens=sum(lens) + 128, max_rows=8, max_seq=8192)
+    try:
+        got = engine_logprobs(eng, batch)
+        assert_decoder_parity(got, ref, batch.nopts)
+    finally:
+        eng.close()
+
+
+def test_27b_full_depth_vs_oracle():
+    """All 64 layers of the 27B shape (54 GB of 16-bit weights on the GPU;
+    the oracle regenerates each layer on the host as it goes)."""
+    spec = with_labels(specs.preset("onejev-27b", seed=79))
+    batch = fixed_rows(spec, 79, (40, 150, 420))
+    eng = B200Engine(spec, max_tokens=2048, max_rows=8, max_seq=2048)
     try:
         got = engine_logprobs(eng, batch)
     finally:

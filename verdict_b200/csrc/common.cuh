@@ -28,6 +28,7 @@ enum DeviceError : int {
   kErrTimeoutAccEmpty = 4,  // MMA warp waited too long for a drained accumulator
   kErrTokenRange = 10,      // a token id outside [0, vocab)
   kErrSlotRange = 11,       // a slot / marker position outside its row
+  kErrNonFinite = 12,       // inf / NaN in a slot or marker hidden state or an output logit
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -117,20 +118,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false when the
-// CTA was aborted or the wait timed out (the error is then recorded).
+// CTA was aborted or the wait timed out after limit_ns (the error is then
+// recorded); limit_ns = 0 means VD_WAIT_TIMEOUT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+                                          int* err, int code, uint64_t limit_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t limit = limit_ns ? limit_ns : VD_WAIT_TIMEOUT_NS;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > VD_WAIT_TIMEOUT_NS) {
+    if (globaltimer() - t0 > limit) {
       *abort_flag = 1;
       record_error(err, code);
       return false;
     }
   }
+}
+
+// Bounded wait that ignores the abort flag: an aborting thread uses it to let
+// its own asynchronous work (tensor-core ops, copies) finish before the CTA
+// frees the resources that work writes to.  False when limit_ns passed first.
+__device__ __forceinline__ bool mbar_wait_own(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t limit = limit_ns ? limit_ns : VD_WAIT_TIMEOUT_NS;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > limit) return false;
+  return true;
 }
 
 // ---------------------------------------------------------------------------

@@ -364,7 +364,10 @@ __global__ void gather_slot_rows_kernel(const RowMap* __restrict__ rows, const i
 // Decoder readout, one CTA per row: final RMSNorm of the slot token's hidden
 // state, dot products with the first n option-label rows of the LM head (fp32,
 // as `hs[slot].float() @ head_w.T`), then either the log-softmax restricted to
-// the n options or the raw logits; columns >= n are -1e4.
+// the n options or the raw logits; columns >= n are -1e4.  An inf or NaN in the
+// slot's hidden state or in a logit (a 16-bit activation that overflowed on the
+// way, which poisons every later token of its row) is reported as
+// kErrNonFinite, so the batch fails instead of returning meaningless scores.
 template <int NT>
 __global__ void __launch_bounds__(NT)
     readout_kernel(const float* __restrict__ h, int d, const RowMap* __restrict__ rows,
@@ -390,6 +393,7 @@ __global__ void __launch_bounds__(NT)
   // last layer's O projection); otherwise h is the packed batch.
   const float* x = compact ? h + static_cast<size_t>(i) * d : h + static_cast<size_t>(rm.base + slot) * d;
   float ss = 0.0f;
+  bool finite = true;
   // Unrolled so that several loads per thread are in flight: at small batch
   // (one block per decision) the kernel is bound by DRAM latency, not bandwidth.
 #pragma unroll 4
@@ -397,7 +401,9 @@ __global__ void __launch_bounds__(NT)
     const float v = x[j];
     xs[j] = v;
     ss += v * v;
+    finite &= isfinite(v);
   }
+  if (!__syncthreads_and(finite) && threadIdx.x == 0) record_error(err, kErrNonFinite);
   const float rstd = rsqrtf(block_sum<NT>(ss, red) / static_cast<float>(d) + eps);
   const float add = plus_one ? 1.0f : 0.0f;
   for (int j = threadIdx.x; j < d; j += NT) xs[j] = xs[j] * rstd * (norm_w[j] + add);
@@ -414,7 +420,10 @@ __global__ void __launch_bounds__(NT)
     }
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-    if (lane == 0) lg[o] = acc;
+    if (lane == 0) {
+      lg[o] = acc;
+      if (!isfinite(acc)) record_error(err, kErrNonFinite);
+    }
   }
   __syncthreads();
   float shift = 0.0f;
@@ -524,11 +533,12 @@ __global__ void __launch_bounds__(NT)
 
 // Final scorer projection Linear(d, 1) on the GELU'd rows, then the marker mask:
 // out[i, j] = y[i*k + j] . w + b for live markers, -1e4 otherwise; columns
-// j >= k of a wider output are -1e4.
+// j >= k of a wider output are -1e4.  A non-finite live logit (an activation
+// that overflowed its 16-bit range upstream) is reported as kErrNonFinite.
 template <class T>
 __global__ void marker_score_kernel(const T* __restrict__ y, int d, const float* __restrict__ w,
                                     const float* __restrict__ bias, const uint8_t* __restrict__ marker_mask, int b,
-                                    int k, float* __restrict__ out, int width) {
+                                    int k, float* __restrict__ out, int width, int* err) {
   const int i = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int j = warp; j < width; j += nw) {
@@ -539,6 +549,7 @@ __global__ void marker_score_kernel(const T* __restrict__ y, int d, const float*
 #pragma unroll
       for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
       acc += bias[0];
+      if (lane == 0 && !isfinite(acc)) record_error(err, kErrNonFinite);
     } else {
       acc = kSentinel;
     }

@@ -49,9 +49,15 @@ struct EpiParams {
 
 // group_m: M tiles per raster group (tiles walk M fastest inside a group, so a
 // group's A rows stay in L2 while W streams past them once per group).
+// wait_ns: limit of every barrier wait (0: VD_WAIT_TIMEOUT_NS).  stall_after
+// (one-CTA kernel, failure-path tests only; 0 = off): the producer stops after
+// issuing this many k-blocks, so the MMA warp's wait for the next stage runs
+// out and the launch ends through its abort path with kErrTimeoutFull.
 struct GemmShape {
   int M, N, K;
   int group_m;
+  uint64_t wait_ns;
+  int stall_after;
 };
 
 // GELU in its exact form, x * Phi(x), Phi the standard normal CDF, with erf
@@ -415,7 +421,9 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* mma_drained = acc_empty + 3;  // the MMA warp's own ops, on its abort path
   uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
+  const uint64_t wait_ns = shape.wait_ns;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -429,6 +437,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       mbar_init(&acc_full[j], 1);
       mbar_init(&acc_empty[j], Cfg::EPI_WARPS);  // one arrival per epilogue warp
     }
+    mbar_init(mma_drained, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -453,11 +462,14 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       tma_prefetch_desc(&tmC);
       int stage = 0;
       uint32_t phase = 0;
+      int issued = 0;
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
         int m, n;
         tile_coords(tile, num_m, num_n, shape.group_m, m, n);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) goto producer_done;
+          if (shape.stall_after > 0 && issued == shape.stall_after) goto producer_drain;
+          ++issued;
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, wait_ns)) goto producer_done;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * BK, m * BM);
           tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * BK, n * BN);
@@ -467,10 +479,11 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
           }
         }
       }
+    producer_drain:
       // Drain: wait until the MMA warp released every stage we filled, so no TMA
       // write can land after the CTA exits.
       for (int i = 0; i < STAGES; ++i) {
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) break;
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, wait_ns)) break;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
@@ -484,13 +497,16 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      bool ok = true;
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutAccEmpty)) break;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutAccEmpty, wait_ns)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrTimeoutFull)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrTimeoutFull, wait_ns)) {
             ok = false;
             break;
           }
@@ -515,6 +531,12 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
           acc_phase ^= 1;
         }
       }
+      if (!ok) {
+        // Aborted: let the MMAs this thread already issued finish (bounded)
+        // before the CTA frees the tensor memory they write.
+        umma_commit(mma_drained);
+        mbar_wait_own(mma_drained, 0, wait_ns);
+      }
     }
   } else {
     // Epilogue warps 2..9: warp w drains TMEM lanes 32*(w%4).. (the quarter it
@@ -528,7 +550,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       int m, n;
       tile_coords(tile, num_m, num_n, shape.group_m, m, n);
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull)) break;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull, wait_ns)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row = m * BM + row_in_tile;

@@ -66,13 +66,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                                  int code) {
+                                                  int code, uint64_t limit_ns = 0) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t limit = limit_ns ? limit_ns : VD_WAIT_TIMEOUT_NS;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > VD_WAIT_TIMEOUT_NS) {
+    if (globaltimer() - t0 > limit) {
       *abort_flag = 1;
       record_error(err, code);
       return false;
@@ -210,7 +211,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
         const int ya = m * 2 * BM + static_cast<int>(rank) * BM;
         const int yb = n * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) goto producer_done;
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, shape.wait_ns)) goto producer_done;
           if (leader) mbar_arrive_expect_tx(&full[stage], Cfg::PAIR_STAGE_BYTES);
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
           tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * BK, ya);
@@ -224,7 +225,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       // Drain: every stage this CTA filled has been consumed by the pair's MMAs
       // (the leader's commit arrives here too) before the CTA may exit.
       for (int i = 0; i < STAGES; ++i) {
-        if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty)) break;
+        if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, shape.wait_ns)) break;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
@@ -239,12 +240,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int tile = pair; tile < tiles; tile += pairs) {
-        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutAccEmpty)) break;
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutAccEmpty, shape.wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait_cluster(&full[stage], phase, abort_flag, err, kErrTimeoutFull)) {
+          if (!mbar_wait_cluster(&full[stage], phase, abort_flag, err, kErrTimeoutFull, shape.wait_ns)) {
             ok = false;
             break;
           }
@@ -281,7 +282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
     for (int tile = pair; tile < tiles; tile += pairs) {
       int m, n;
       tile_coords(tile, num_m, num_n, shape.group_m, m, n);
-      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull)) break;
+      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull, shape.wait_ns)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row0 = m * 2 * BM + static_cast<int>(rank) * BM;

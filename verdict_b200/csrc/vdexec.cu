@@ -601,6 +601,8 @@ struct Options {
   bool gemm2 = true;         // 256-wide projections on CTA pairs (cta_group::2), else one CTA per tile
   int raster_group = 0;      // M tiles per GEMM raster group; 0 = the kernel's default
   bool gdn_chunk = true;     // gated delta nets in 64-token chunks on the tensor cores, else token by token
+  uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
+  int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
 
 }  // namespace vd
@@ -673,6 +675,7 @@ struct vd_handle {
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;  // host-memory calls: before the uploads, after the download
   vd_stats stats{};
   int64_t launches = 0;
+  bool stall_pending = false;  // opt.debug_stall: not yet applied in this call
   // per-kernel event timing (vd_set_profiling)
   bool profiling = false;
   struct ProfRec {
@@ -1327,8 +1330,16 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const int num_m = (M + 127) / 128;
   const int tiles = num_m * (L.n / L.bn);
   const int grid = std::min(tiles, H->num_sms);
-  GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M};
+  GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M,
+                  H->opt.wait_ns, 0};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
+  // Failure-path tests: the first one-CTA GEMM of the call stalls its producer.
+  auto stall_one_cta = [&] {
+    if (H->stall_pending) {
+      shape.stall_after = H->opt.debug_stall;
+      H->stall_pending = false;
+    }
+  };
   if (L.bn == 256 && H->opt.gemm2 && H->gemm2_pairs > 0) {
     const int pair_tiles = ((M + 255) / 256) * (L.n / 256);
     // A GEMM of a wave or two of CTA pairs (short batches, the encoders' 768-
@@ -1343,6 +1354,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
       const int64_t rounds1 = (t128 + H->num_sms - 1) / H->num_sms;
       if (2 * rounds1 <= rounds2) {
         const int grid1 = static_cast<int>(std::min<int64_t>(t128, H->num_sms));
+        stall_one_cta();
         launch(H, kind, flops, [&] {
           gemm_tcgen05_kernel<128, EPI, T><<<grid1, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
                                              H->stream>>>(a, L.map_half, c, shape, ep, H->d_err);
@@ -1358,6 +1370,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
     });
     return;
   }
+  stall_one_cta();
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
       gemm_tcgen05_kernel<256, EPI, T>
@@ -1913,7 +1926,7 @@ static double von_forward(vd_handle* H, const Chunk& c) {
   launch(H, VD_K_OTHER, 0.0, [&] {
     marker_score_kernel<T><<<c.nb, 256, 0, H->stream>>>(static_cast<const T*>(H->mhid), d, H->sc_w3, H->sc_b3,
                                                         c.mmask, c.nb, static_cast<int>(c.k), c.out,
-                                                        static_cast<int>(c.width));
+                                                        static_cast<int>(c.width), H->d_err);
   });
   return ntok;
 }
@@ -1989,7 +2002,8 @@ static double encoder_forward(vd_handle* H, const Chunk& c) {
   launch(H, VD_K_OTHER, 0.0, [&] {
     marker_score_kernel<T><<<c.nb, 256, 0, H->stream>>>(static_cast<const T*>(H->mhid), d, H->sc_w3, H->sc_b3,
                                                         c.mmask, c.nb,
-                                                     static_cast<int>(c.k), c.out, static_cast<int>(c.width));
+                                                     static_cast<int>(c.k), c.out, static_cast<int>(c.width),
+                                                     H->d_err);
   });
   return ntok;
 }
@@ -2072,6 +2086,7 @@ static void run_batch(vd_handle* H, const vd_batch* b, const int64_t* ids, const
   const auto t_enqueue = std::chrono::steady_clock::now();
   H->stats = vd_stats{};
   H->launches = 0;
+  H->stall_pending = H->opt.debug_stall > 0;
   cuda_check(cudaEventRecord(H->ev0, H->stream), "event");
   int64_t r0 = 0, chunks = 0, tokens = 0;
   while (r0 < b->b) {
@@ -2129,6 +2144,12 @@ static void check_device_error(vd_handle* H) {
     cuda_check(cudaStreamSynchronize(H->stream), "synchronize");
     if (e == kErrTokenRange) fail(VD_EDEVICE, "a token id or qtype is outside the model's range");
     if (e == kErrSlotRange) fail(VD_EDEVICE, "a slot / marker position lies outside its row");
+    if (e == kErrNonFinite)
+      fail(VD_EDEVICE, std::string("non-finite values (inf / NaN) reached a slot or marker hidden state: an "
+                                   "activation overflowed its 16-bit range") +
+                           (H->opt.f16 ? "; fp16 activations stop at 65504, reopen the model with "
+                                         "\"act_dtype\": \"bf16\" (fp32's exponent range)"
+                                       : ""));
     H->healthy = false;
     H->dead_reason = "a kernel pipeline timed out (device error " + std::to_string(e) + ")";
     fail(VD_ECUDA, H->dead_reason);
@@ -2232,6 +2253,12 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       const std::string dt = o.string_or("act_dtype", "fp16");
       if (dt != "fp16" && dt != "bf16") fail(VD_EINVAL, "act_dtype must be \"fp16\" or \"bf16\"");
       H->opt.f16 = dt == "fp16";
+      const long long wait_us = o.integer_or("wait_limit_us", 0);
+      if (wait_us < 0 || wait_us > 60000000) fail(VD_EINVAL, "wait_limit_us must be in [0, 6e7]");
+      H->opt.wait_ns = static_cast<uint64_t>(wait_us) * 1000ull;
+      const long long stall = o.integer_or("debug_stall_gemm", 0);
+      if (stall < 0 || stall > 1000000) fail(VD_EINVAL, "debug_stall_gemm must be in [0, 1e6]");
+      H->opt.debug_stall = static_cast<int>(stall);
     }
     if (H->opt.max_tokens < 128 || H->opt.max_rows < 1 || H->opt.max_seq < 1)
       fail(VD_EINVAL, "max_tokens must be >= 128 and max_rows, max_seq >= 1");
@@ -2448,8 +2475,8 @@ extern "C" VD_API void vd_close(vd_handle* h) {
 // vdk_attention_noalloc: the varlen attention kernel with its tile table in a
 // fixed device array instead of memory allocated per call.
 //
-// The attention kernel needs one 16-byte work descriptor per 64-row query tile
-// (AttnTile).  vdk_attention allocates that table on every call; this variant
+// The attention kernel needs one 32-byte work descriptor per 64-row query tile
+// (AttnTile, eight ints).  vdk_attention allocates that table on every call; this variant
 // keeps it in g_noalloc_tiles below, a file-scope device array that exists on
 // every GPU that loads the library until the process exits.  The host side
 // builds the table in a static host array and copies it over, so the call

@@ -74,9 +74,12 @@ class B200Engine(Engine):
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
                  prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
-                 raster_group: int = 0, gdn: str = "chunk"):
+                 raster_group: int = 0, gdn: str = "chunk", wait_limit_us: int = 0, debug_stall_gemm: int = 0):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
-        relative "checkpoint" path is taken from that directory)."""
+        relative "checkpoint" path is taken from that directory).
+        `wait_limit_us`: limit of the GEMM kernels' pipeline waits (0: 2 s);
+        `debug_stall_gemm` (failure-path tests only): the first one-CTA GEMM of
+        every call stops loading after that many k-blocks, so its wait runs out."""
         self.lib = _abi.load()
         if isinstance(spec, (str, os.PathLike)):
             model = os.fspath(spec).encode()
@@ -91,7 +94,8 @@ class B200Engine(Engine):
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
                                attention=attention, prune_last_layer=prune_last_layer, fork=fork,
-                               gemm=gemm, raster_group=raster_group, gdn=gdn))
+                               gemm=gemm, raster_group=raster_group, gdn=gdn, wait_limit_us=wait_limit_us,
+                               debug_stall_gemm=debug_stall_gemm))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
         rc = self.lib.vd_open(model, device, opts.encode(), ctypes.byref(h), err, len(err))
