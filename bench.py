@@ -395,6 +395,9 @@ def main():
                     help="256-wide projections on CTA pairs (2sm) or one CTA per tile (1sm)")
     ap.add_argument("--gdn", default="chunk", choices=["chunk", "scan"],
                     help="gated delta nets in 64-token chunks on the tensor cores (chunk) or token by token (scan)")
+    ap.add_argument("--norm", default="fused", choices=["fused", "separate"],
+                    help="decoders' RMSNorm fused into the residual GEMMs and the projections (fused) or a kernel "
+                         "of its own (separate)")
     ap.add_argument("--act-dtype", default="fp16", choices=["fp16", "bf16"],
                     help="16-bit element type of activations and projection weights (fp32 accumulation and "
                          "residual stream either way)")
@@ -445,7 +448,8 @@ def main():
     max_batch = max(b.b for b in every)
     eng = B200Engine(spec, device=local, max_tokens=max(max_tokens, 4096), max_rows=max(max_batch, 8),
                      max_seq=max(4096, max_len), attention=args.attention, fork=args.fork == "on",
-                     gemm=args.gemm, raster_group=args.raster_group, gdn=args.gdn, act_dtype=args.act_dtype)
+                     gemm=args.gemm, raster_group=args.raster_group, gdn=args.gdn, act_dtype=args.act_dtype,
+                     norm=args.norm)
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
     width = eng.width if not encoder else max(b.k for b in batches)  # encoders: one logit per marker slot
@@ -674,6 +678,7 @@ def main():
             "config": {"workload": workload_text(args.model, shared),
                        "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
+                       "norm": args.norm,
                        "raster_group": args.raster_group or "default",
                        **({"gdn": args.gdn} if specs.is_hybrid(spec) else {}),
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,

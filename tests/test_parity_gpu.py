@@ -277,6 +277,26 @@ def test_tensor_core_attention_matches_warp_level_attention(mode):
         b.close()
 
 
+@pytest.mark.parametrize("preset,act_dtype", [("onejev-9b", "fp16"), ("onejev-9b", "bf16"), ("decider-2b", "fp16")])
+def test_fused_rmsnorm_matches_separate_rmsnorm(preset, act_dtype):
+    """RMSNorm fused into the residual GEMMs (row statistics, 16-bit copy of
+    the residual) and into the consuming projections (gains folded into W, row
+    factor in the epilogue) against the standalone norm kernel: the same
+    decisions, both near the oracle."""
+    spec, batch = decoder_case(preset, 3, 6, seed=19, max_len=1200)
+    ref = DecoderOracle(spec).infer(batch)
+    got = {}
+    for norm in ("fused", "separate"):
+        eng = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, norm=norm, act_dtype=act_dtype)
+        try:
+            got[norm] = engine_logprobs(eng, batch)
+        finally:
+            eng.close()
+        if act_dtype == "fp16":
+            assert_decoder_parity(got[norm], ref, batch.nopts)
+    assert np.abs(got["fused"] - got["separate"]).max() <= (1e-2 if act_dtype == "fp16" else LOGPROB_TOL)
+
+
 def test_last_layer_on_slot_rows_is_bit_exact():
     """Running the last layer's O projection and MLP on the slot rows only
     changes no bit of the result (each row's arithmetic is the same)."""

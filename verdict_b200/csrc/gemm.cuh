@@ -23,13 +23,24 @@
 //   kEpiQKRope    : per attention head of the tile: optional bias, optional
 //                   q/k RMSNorm over the head, rotary embedding for q and k
 //                   heads; v heads are stored as they are.
+//   kEpiResidualNorm : the residual add that feeds an RMSNorm (decoders' O /
+//                   out_proj and down projections): res_f32 += acc + bias,
+//                   then from the new residual row a 16-bit copy times
+//                   `prescale` (the next projection's A operand) and the sum of
+//                   squares of each 64-column block (its RMS statistics).
+// RMSNorm fused into the consuming projection: RMSNorm(h) W^T = rstd (h (W g)^T)
+// with the gains g folded into W at load, so a consumer reads A = the producer's
+// copy of h and multiplies each accumulator row by rstd / prescale (row factor,
+// from the producer's block sums) before its own epilogue.
 #pragma once
 
 #include "common.cuh"
 
 namespace vd {
 
-enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiGated = 2, kEpiQKRope = 3 };
+enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiGated = 2, kEpiQKRope = 3, kEpiResidualNorm = 4 };
+
+constexpr int kNormBlock = 64;  // columns per partial sum of squares of the fused RMSNorm
 enum ActKind : int { kActNone = 0, kActGeluErf = 1, kActGeluTanh = 2, kActRelu = 3, kActSilu = 4 };
 
 struct EpiParams {
@@ -45,7 +56,42 @@ struct EpiParams {
   const int* positions;   // [M] token position inside its sequence
   const float2* rope;     // [max_pos][rot_dim/2] (cos, sin)
   int rot_dim;            // rotary width: the first rot_dim columns of a head (multiple of 64; 0 = head_dim)
+  // kEpiResidualNorm: the residual (fp32 [M, N], row stride N) updated in place,
+  // the 16-bit copy of the new rows times `prescale` ([M, N]) and the block
+  // sums of squares ([M, N / kNormBlock]).
+  float* res;
+  void* xcopy;
+  float prescale;
+  float* ss_out;
+  // Fused RMSNorm of the A rows (store, gated and QK-rope epilogues): row
+  // factor rsqrt(sum(ss_in[m, :]) * ss_inv_n + ss_eps) * ss_post, applied to
+  // the accumulators first; ss_in == null: none.
+  const float* ss_in;
+  int ss_slots;
+  float ss_inv_n, ss_eps, ss_post;
 };
+
+// The fused RMSNorm's factor for accumulator row `row`: the block sums are added
+// in a fixed order, so the result does not depend on how rows were tiled.
+__device__ __forceinline__ float row_factor(const EpiParams& p, int row, bool row_ok) {
+  if (p.ss_in == nullptr || !row_ok) return 1.0f;
+  const float4* b = reinterpret_cast<const float4*>(p.ss_in + static_cast<size_t>(row) * p.ss_slots);
+  float ss = 0.0f;
+#pragma unroll 4
+  for (int i = 0; i < p.ss_slots / 4; ++i) {
+    const float4 t = __ldg(b + i);
+    ss += t.x;
+    ss += t.y;
+    ss += t.z;
+    ss += t.w;
+  }
+  return rsqrtf(ss * p.ss_inv_n + p.ss_eps) * p.ss_post;
+}
+
+__device__ __forceinline__ void scale32(float (&v)[32], float f) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] *= f;
+}
 
 // group_m: M tiles per raster group (tiles walk M fastest inside a group, so a
 // group's A rows stay in L2 while W streams past them once per group).
@@ -198,7 +244,8 @@ __device__ __forceinline__ void out_chunk_add32(EpiOut& o, const float (&v)[32],
 // head itself, so the two warps sharing a head need no exchange.
 template <int HD, class T>
 __device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row, bool row_ok, int col0,
-                                              const EpiParams& p, const float* gain, int u_begin, int u_end) {
+                                              const EpiParams& p, const float* gain, int u_begin, int u_end,
+                                              float f) {
   const int rot = p.rot_dim ? p.rot_dim : HD;
   const int R = rot / 2;            // rotary half-width (columns)
   const int pairs = R / 32;         // rotary work units
@@ -209,6 +256,7 @@ __device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row
     for (int c = 0; c < HD / 32; ++c) {
       float v[32];
       tmem_load_f32x32(tbase + c * 32, v);
+      scale32(v, f);
       add_bias32(v, p.bias, col0 + c * 32);
 #pragma unroll
       for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
@@ -237,6 +285,8 @@ __device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row
       float x1[32], x2[32];
       tmem_load_f32x32(tbase + c * 32, x1);
       tmem_load_f32x32(tbase + R + c * 32, x2);
+      scale32(x1, f);
+      scale32(x2, f);
       add_bias32(x1, p.bias, col0 + c * 32);
       add_bias32(x2, p.bias, col0 + R + c * 32);
       scale(x1, c * 32);
@@ -256,6 +306,7 @@ __device__ __forceinline__ void epi_head_rope(EpiOut& o, uint32_t tbase, int row
       const int c = rot / 32 + (u - pairs);  // a chunk past the rotary columns
       float x[32];
       tmem_load_f32x32(tbase + c * 32, x);
+      scale32(x, f);
       add_bias32(x, p.bias, col0 + c * 32);
       scale(x, c * 32);
       out_chunk16<T>(o, x, col0 + c * 32);
@@ -282,11 +333,12 @@ __device__ __forceinline__ void head_units(const EpiParams& p, int half, int& be
 // Plain store of 32-column chunks [c_begin, c_end) starting at column col0.
 template <class T>
 __device__ __forceinline__ void epi_store_chunks(EpiOut& o, uint32_t tbase, int col0, const EpiParams& p,
-                                                 int c_begin, int c_end) {
+                                                 int c_begin, int c_end, float f = 1.0f) {
 #pragma unroll 1
   for (int c = c_begin; c < c_end; ++c) {
     float v[32];
     tmem_load_f32x32(tbase + c * 32, v);
+    scale32(v, f);
     add_bias32(v, p.bias, col0 + c * 32);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = apply_act(v[j], p.act);
@@ -302,7 +354,7 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
                                               const EpiParams& p) {
   constexpr int CH = BN / 32;  // 32-column chunks per tile
   if constexpr (EPI == kEpiStore) {
-    epi_store_chunks<T>(o, taddr, n0, p, half * CH / 2, (half + 1) * CH / 2);
+    epi_store_chunks<T>(o, taddr, n0, p, half * CH / 2, (half + 1) * CH / 2, row_factor(p, row, row_ok));
   } else if constexpr (EPI == kEpiResidual) {
 #pragma unroll 1
     for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
@@ -311,16 +363,54 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
       add_bias32(v, p.bias, n0 + c * 32);
       out_chunk_add32(o, v, n0 + c * 32);
     }
+  } else if constexpr (EPI == kEpiResidualNorm) {
+    // This thread owns row `row`, columns [n0 + 32 c, +32) for the chunks of
+    // its half (an even number of chunks: whole 64-column blocks).  Plain
+    // loads and stores: each thread moves whole 128-byte lines of its row.
+    static_assert((CH / 2) % 2 == 0, "a warp's columns must cover whole 64-column blocks");
+    const int N = p.ss_slots * kNormBlock;
+    float ss = 0.0f;
+#pragma unroll 1
+    for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
+      float v[32];
+      tmem_load_f32x32(taddr + c * 32, v);
+      add_bias32(v, p.bias, n0 + c * 32);
+      if (row_ok) {
+        const size_t off = static_cast<size_t>(row) * N + n0 + c * 32;
+        float4* hr = reinterpret_cast<float4*>(p.res + off);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 a = hr[q];
+          v[4 * q + 0] += a.x;
+          v[4 * q + 1] += a.y;
+          v[4 * q + 2] += a.z;
+          v[4 * q + 3] += a.w;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) hr[q] = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+        float sc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc[j] = v[j] * p.prescale;
+        store_x32<T>(static_cast<T*>(p.xcopy) + off, sc);
+        if (c & 1) {
+          p.ss_out[static_cast<size_t>(row) * p.ss_slots + (n0 + c * 32) / kNormBlock] = ss;
+          ss = 0.0f;
+        }
+      }
+    }
   } else if constexpr (EPI == kEpiGated) {
     constexpr int HALF = BN / 2;         // output columns of the tile
     constexpr int OC = HALF / 32;        // output chunks
+    const float f = row_factor(p, row, row_ok);
 #pragma unroll 1
     for (int c = half * OC / 2; c < (half + 1) * OC / 2; ++c) {
       float g[32], u[32];
       tmem_load_f32x32(taddr + c * 32, g);
       tmem_load_f32x32(taddr + HALF + c * 32, u);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) g[j] = apply_act(g[j], p.act) * u[j];
+      for (int j = 0; j < 32; ++j) g[j] = apply_act(g[j] * f, p.act) * (u[j] * f);
       out_chunk16<T>(o, g, n0 / 2 + c * 32);
     }
   } else if constexpr (EPI == kEpiQKRope) {
@@ -329,6 +419,7 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
     // rotary chunk pairs.  head_dim 256 (one head per 256-wide tile): the warps
     // split its four chunk pairs.
     // Columns past the q and k blocks (v, and a hybrid's output gate) are stored as they are.
+    const float f = row_factor(p, row, row_ok);
     if (p.head_dim == 64) {
       // head_dim 64 (ModernBERT): BN / 64 heads per tile, each warp half of them;
       // one rotary pair per head (columns [0, 32) with [32, 64)).
@@ -339,9 +430,9 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
         const int col0 = n0 + h * 64;
         const uint32_t tb = taddr + h * 64;
         if (col0 < p.q_cols + p.k_cols)
-          epi_head_rope<64, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, 0, 1);
+          epi_head_rope<64, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, 0, 1, f);
         else
-          epi_store_chunks<T>(o, tb, col0, p, 0, 2);
+          epi_store_chunks<T>(o, tb, col0, p, 0, 2, f);
       }
     } else if (p.head_dim == 128) {
       constexpr int HEADS = BN / 128;
@@ -356,16 +447,16 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
         head_units<128>(p, half, ub, ue);
       }
       if (col0 < p.q_cols + p.k_cols)
-        epi_head_rope<128, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, ub, ue);
+        epi_head_rope<128, T>(o, tb, row, row_ok, col0, p, col0 < p.q_cols ? p.q_norm : p.k_norm, ub, ue, f);
       else
-        epi_store_chunks<T>(o, tb, col0, p, HEADS == 2 ? 0 : 2 * half, HEADS == 2 ? 4 : 2 * half + 2);
+        epi_store_chunks<T>(o, tb, col0, p, HEADS == 2 ? 0 : 2 * half, HEADS == 2 ? 4 : 2 * half + 2, f);
     } else if constexpr (BN == 256) {
       if (n0 < p.q_cols + p.k_cols) {
         int ub = 0, ue = 0;
         head_units<256>(p, half, ub, ue);
-        epi_head_rope<256, T>(o, taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, ub, ue);
+        epi_head_rope<256, T>(o, taddr, row, row_ok, n0, p, n0 < p.q_cols ? p.q_norm : p.k_norm, ub, ue, f);
       } else {
-        epi_store_chunks<T>(o, taddr, n0, p, 4 * half, 4 * half + 4);
+        epi_store_chunks<T>(o, taddr, n0, p, 4 * half, 4 * half + 4, f);
       }
     }
   }

@@ -58,6 +58,12 @@ struct VdError {
 
 [[noreturn]] static void fail(int code, const std::string& msg) { throw VdError{code, msg}; }
 
+// Fused RMSNorm with fp16 activations: the 16-bit copy of the residual rows is
+// stored times 2^-6, so rows up to 4.2e6 in magnitude stay inside fp16's range
+// while values down to 2^-8 remain normal numbers (the row factor undoes it
+// exactly).  bf16 has fp32's exponent range and stores the rows as they are.
+constexpr float kNormPrescale16 = 1.0f / 64.0f;
+
 static void cuda_check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) fail(VD_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -601,6 +607,7 @@ struct Options {
   bool gemm2 = true;         // 256-wide projections on CTA pairs (cta_group::2), else one CTA per tile
   int raster_group = 0;      // M tiles per GEMM raster group; 0 = the kernel's default
   bool gdn_chunk = true;     // gated delta nets in 64-token chunks on the tensor cores, else token by token
+  bool fuse_norm = true;     // decoders: RMSNorm fused into the residual GEMMs and the projections that read it
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
@@ -644,6 +651,9 @@ struct vd_handle {
   vd::RowMap* rowmap = nullptr; // per decision: where its slot token is packed
   float2* rope = nullptr;
   CUtensorMap map_xn, map_attn, map_act, map_act2, map_mrow, map_qkv, map_qkv64;
+  // fused RMSNorm: block sums of squares of the residual rows ([rows, d / 64]),
+  // two for the main rows (attention / MLP input), one for the slot rows
+  float *ss_a = nullptr, *ss_b = nullptr, *ss_s = nullptr;
   // last-layer slot rows (one per decision of a chunk)
   float* h_s = nullptr;
   void *xn_s = nullptr, *attn_s = nullptr, *act_s = nullptr;
@@ -887,6 +897,18 @@ static void init_linear(vd_handle* H, Linear& L, int n, int k, bool bias, int bn
 
 static float2* upload_rope(vd_handle* H, int rot, double theta);
 
+// Fused RMSNorm: the norm's gains g (as stored: w, applied as w + add) folded
+// into the columns of the projection that reads the normalised rows.
+static void fold_gains(vd_handle* H, Linear& L, const float* g) {
+  const float add = H->spec.norm_plus_one ? 1.0f : 0.0f;
+  const int64_t n = static_cast<int64_t>(L.n) * L.k;
+  if (H->opt.f16)
+    scale_cols_kernel<__half><<<grid_for(n), 256, 0, H->stream>>>(static_cast<__half*>(L.w), L.n, L.k, g, add);
+  else
+    scale_cols_kernel<__nv_bfloat16><<<grid_for(n), 256, 0, H->stream>>>(static_cast<__nv_bfloat16*>(L.w), L.n,
+                                                                          L.k, g, add);
+}
+
 static void load_decoder(vd_handle* H) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads, f = s.ffn;
@@ -932,6 +954,10 @@ static void load_decoder(vd_handle* H) {
       fill_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
       init_linear(H, L.down, d, f, false);
       fill_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
+      if (H->opt.fuse_norm) {
+        fold_gains(H, L.qkv, L.in_norm);
+        fold_gains(H, L.gu, L.post_norm);
+      }
       continue;
     }
     init_linear(H, L.qkv, s.qkv_width(), d, s.qkv_bias, bn_qkv);
@@ -962,6 +988,10 @@ static void load_decoder(vd_handle* H) {
     fill_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
     init_linear(H, L.down, d, f, false);
     fill_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
+    if (H->opt.fuse_norm) {
+      fold_gains(H, L.qkv, L.in_norm);
+      fold_gains(H, L.gu, L.post_norm);
+    }
   }
   H->final_norm = dalloc<float>(H, d);
   fill_f32(H, H->final_norm, "model.norm.weight", d, n_scale, n_off);
@@ -1216,6 +1246,10 @@ static void alloc_workspace(vd_handle* H) {
     H->map_act_s = make_map(H->act_s, R, s.ffn, 128, f16);
     H->out_act_s = make_out_map(H->act_s, R, s.ffn, false, f16);
     H->out_h_s = make_out_map(H->h_s, R, d, true);
+    if (d % kNormBlock != 0) fail(VD_ESPEC, "hidden size must be a multiple of 64");
+    H->ss_a = dalloc<float>(H, T * (d / kNormBlock));
+    H->ss_b = dalloc<float>(H, T * (d / kNormBlock));
+    H->ss_s = dalloc<float>(H, R * (d / kNormBlock));
   }
   H->map_act = make_map(H->act, T, s.ffn, 128, f16);
   H->out_act = make_out_map(H->act, T, s.ffn, false, f16);
@@ -1280,8 +1314,11 @@ static void init_kernel_attrs_t() {
   set_gemm_attr<256, kEpiGated, T>();
   set_gemm_attr<256, kEpiQKRope, T>();
   set_gemm_attr<128, kEpiQKRope, T>();
+  set_gemm_attr<256, kEpiResidualNorm, T>();
+  set_gemm_attr<128, kEpiResidualNorm, T>();
   for (auto f : {gemm2_tcgen05_kernel<kEpiStore, T>, gemm2_tcgen05_kernel<kEpiResidual, T>,
-                 gemm2_tcgen05_kernel<kEpiGated, T>, gemm2_tcgen05_kernel<kEpiQKRope, T>})
+                 gemm2_tcgen05_kernel<kEpiGated, T>, gemm2_tcgen05_kernel<kEpiQKRope, T>,
+                 gemm2_tcgen05_kernel<kEpiResidualNorm, T>})
     cuda_check(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Config::SMEM_BYTES),
                "two-CTA gemm smem attribute");
   set_attn_attr<64, false, T>();
@@ -1348,7 +1385,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
     // tile runs well below half a pair tile's rate, so this is taken only
     // when it needs at most half the pair kernel's per-SM tile rounds (a pair
     // tile is two 128 x 128 tiles per SM).
-    if constexpr (EPI == kEpiStore || EPI == kEpiResidual) {
+    if constexpr (EPI == kEpiStore || EPI == kEpiResidual || EPI == kEpiResidualNorm) {
       const int64_t t128 = static_cast<int64_t>(num_m) * (L.n / 128);
       const int64_t rounds2 = 2 * ((pair_tiles + H->gemm2_pairs - 1) / H->gemm2_pairs);
       const int64_t rounds1 = (t128 + H->num_sms - 1) / H->num_sms;
@@ -1709,10 +1746,12 @@ static void pack(vd_handle* H, const Chunk& c, const ChunkPlan& P, int pos_offse
 // RoPE in the epilogue; a hybrid's output-gate columns pass through), then
 // varlen causal attention (gated in a hybrid) into H->attn.
 template <class T>
-static void full_attention_mixer(vd_handle* H, const DecLayer& L, int ntok, int n_tiles, double attn_flops) {
+static void full_attention_mixer(vd_handle* H, const DecLayer& L, int ntok, int n_tiles, double attn_flops,
+                                 const EpiParams& norm_in) {
   const ModelSpec& s = H->spec;
   const int hd = s.head_dim, nq = s.heads, nkv = s.kv_heads, qc = nq * hd, kc = nkv * hd;
-  EpiParams q = epi(L.qkv.b);
+  EpiParams q = norm_in;
+  q.bias = L.qkv.b;
   q.q_norm = L.q_norm;
   q.k_norm = L.k_norm;
   q.q_cols = qc;
@@ -1732,9 +1771,9 @@ static void full_attention_mixer(vd_handle* H, const DecLayer& L, int ntok, int 
 // l2 norms + gates into H->qkv / gdn_g / gdn_beta, then the recurrence with the
 // gated norm into H->attn (one CTA per sequence and value head).
 template <class T>
-static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan& P) {
+static void gdn_mixer(vd_handle* H, const DecLayer& L, int ntok, const ChunkPlan& P, const EpiParams& norm_in) {
   const ModelSpec& s = H->spec;
-  gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, epi(), H->out_proj);
+  gemm<kEpiStore, T>(H, VD_K_QKV, H->map_xn, L.qkv, ntok, norm_in, H->out_proj);
   GdnParams g{};
   g.proj = H->proj;
   g.ld_proj = s.gdn_proj();
@@ -1786,21 +1825,54 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   const int ntok = P.ntok, n_tiles = P.n_tiles;
   pack(H, c, P, 0);
   const float escale = s.embed_scale ? static_cast<float>(std::pow(static_cast<double>(d), 0.5)) : 1.0f;
-  launch(H, VD_K_OTHER, 0.0,
-         [&] { embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h); });
   const int qc = nq * hd;
   const float eps = static_cast<float>(s.rms_eps);
   const int pone = s.norm_plus_one ? 1 : 0;
   const double attn_flops = 4.0 * hd * nq * P.pairs;
+  // Fused RMSNorm (default): every residual add that feeds a norm (embedding,
+  // O / out_proj, down) also writes the 16-bit copy of the new rows and their
+  // block sums of squares; the projection reading them (QKV / in_proj, gate/up)
+  // applies the row factor.  ss_a feeds the attention input, ss_b the MLP input.
+  const bool fused = H->opt.fuse_norm;
+  const float pre = H->opt.f16 ? kNormPrescale16 : 1.0f;
+  const int slots = d / kNormBlock;
+  auto produce = [&](float* res, void* copy, float* ss) {
+    EpiParams p = epi();
+    p.res = res;
+    p.xcopy = copy;
+    p.prescale = pre;
+    p.ss_out = ss;
+    p.ss_slots = slots;
+    return p;
+  };
+  auto consume = [&](EpiParams p, const float* ss) {
+    if (!fused) return p;
+    p.ss_in = ss;
+    p.ss_slots = slots;
+    p.ss_inv_n = 1.0f / static_cast<float>(d);
+    p.ss_eps = eps;
+    p.ss_post = 1.0f / pre;
+    return p;
+  };
+  auto separate_norm = [&](const float* x, const float* g, void* out, int rows) {
+    launch(H, VD_K_NORM, 0.0, [&] {
+      rmsnorm_kernel<256, T><<<rows, 256, 0, H->stream>>>(x, d, g, pone, eps, static_cast<T*>(out), rows);
+    });
+  };
+  launch(H, VD_K_OTHER, 0.0, [&] {
+    if (fused)
+      embed_norm_kernel<T><<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, pre, H->h,
+                                                        static_cast<T*>(H->xn), H->ss_a);
+    else
+      embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h);
+  });
   for (int i = 0; i < s.layers; ++i) {
     const DecLayer& L = H->dec[i];
-    launch(H, VD_K_NORM, 0.0, [&] {
-      rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.in_norm, pone, eps, static_cast<T*>(H->xn), ntok);
-    });
+    if (!fused) separate_norm(H->h, L.in_norm, H->xn, ntok);
     if (L.linear) {
-      gdn_mixer<T>(H, L, ntok, P);
+      gdn_mixer<T>(H, L, ntok, P, consume(epi(), H->ss_a));
     } else {
-      full_attention_mixer<T>(H, L, ntok, n_tiles, attn_flops);
+      full_attention_mixer<T>(H, L, ntok, n_tiles, attn_flops, consume(epi(), H->ss_a));
     }
     const bool last = i + 1 == s.layers;
     if (last && H->opt.prune_last_layer) {
@@ -1811,22 +1883,30 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
                                                                  static_cast<const T*>(H->attn), qc, H->h, d,
                                                                  static_cast<T*>(H->attn_s), H->h_s, H->d_err);
       });
-      gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(), H->out_h_s);
-      launch(H, VD_K_NORM, 0.0, [&] {
-        rmsnorm_kernel<256, T><<<c.nb, 256, 0, H->stream>>>(H->h_s, d, L.post_norm, pone, eps,
-                                                            static_cast<T*>(H->xn_s), c.nb);
-      });
-      gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn_s, L.gu, c.nb, epi(nullptr, s.act), H->out_act_s);
+      if (fused) {
+        gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, produce(H->h_s, H->xn_s, H->ss_s),
+                                  H->out_h_s);
+      } else {
+        gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(), H->out_h_s);
+        separate_norm(H->h_s, L.post_norm, H->xn_s, c.nb);
+      }
+      gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn_s, L.gu, c.nb, consume(epi(nullptr, s.act), H->ss_s),
+                         H->out_act_s);
       gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act_s, L.down, c.nb, epi(), H->out_h_s);
       continue;
     }
-    gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(), H->out_h);
-    launch(H, VD_K_NORM, 0.0, [&] {
-      rmsnorm_kernel<256, T><<<ntok, 256, 0, H->stream>>>(H->h, d, L.post_norm, pone, eps, static_cast<T*>(H->xn),
-                                                          ntok);
-    });
-    gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, epi(nullptr, s.act), H->out_act);
-    gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(), H->out_h);
+    if (fused) {
+      gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn, L.o, ntok, produce(H->h, H->xn, H->ss_b), H->out_h);
+    } else {
+      gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(), H->out_h);
+      separate_norm(H->h, L.post_norm, H->xn, ntok);
+    }
+    gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, consume(epi(nullptr, s.act), H->ss_b), H->out_act);
+    // The last layer's down projection feeds only the readout's final norm.
+    if (fused && !last)
+      gemm<kEpiResidualNorm, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, produce(H->h, H->xn, H->ss_a), H->out_h);
+    else
+      gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(), H->out_h);
   }
   const bool compact = H->opt.prune_last_layer;
   const size_t smem = sizeof(float) * (d + H->n_labels);
@@ -2253,6 +2333,9 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       const std::string dt = o.string_or("act_dtype", "fp16");
       if (dt != "fp16" && dt != "bf16") fail(VD_EINVAL, "act_dtype must be \"fp16\" or \"bf16\"");
       H->opt.f16 = dt == "fp16";
+      const std::string nm = o.string_or("norm", "fused");
+      if (nm != "fused" && nm != "separate") fail(VD_EINVAL, "norm must be \"fused\" or \"separate\"");
+      H->opt.fuse_norm = nm == "fused";
       const long long wait_us = o.integer_or("wait_limit_us", 0);
       if (wait_us < 0 || wait_us > 60000000) fail(VD_EINVAL, "wait_limit_us must be in [0, 6e7]");
       H->opt.wait_ns = static_cast<uint64_t>(wait_us) * 1000ull;

@@ -74,9 +74,13 @@ class B200Engine(Engine):
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
                  prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
-                 raster_group: int = 0, gdn: str = "chunk", wait_limit_us: int = 0, debug_stall_gemm: int = 0):
+                 raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", wait_limit_us: int = 0,
+                 debug_stall_gemm: int = 0):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory).
+        `norm` (decoders): "fused" folds each RMSNorm into the residual GEMM that
+        produces its input and the projection that reads it; "separate" runs it
+        as its own kernel.
         `wait_limit_us`: limit of the GEMM kernels' pipeline waits (0: 2 s);
         `debug_stall_gemm` (failure-path tests only): the first one-CTA GEMM of
         every call stops loading after that many k-blocks, so its wait runs out."""
@@ -94,7 +98,8 @@ class B200Engine(Engine):
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
                                attention=attention, prune_last_layer=prune_last_layer, fork=fork,
-                               gemm=gemm, raster_group=raster_group, gdn=gdn, wait_limit_us=wait_limit_us,
+                               gemm=gemm, raster_group=raster_group, gdn=gdn, norm=norm,
+                               wait_limit_us=wait_limit_us,
                                debug_stall_gemm=debug_stall_gemm))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
