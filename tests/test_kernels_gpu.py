@@ -234,4 +234,16 @@ def test_attention_tc_long_keys(hd, nq, nkv, dt):
     run(lib().vdk_attention_tc, P(qkv), width, q0, k0, v0, nq, nkv, hd, DTYPES[dt][1], 1,
         ctypes.c_void_p(cu.ctypes.data), len(lens), P(out), nq * hd)
     ref = attention_ref(qkv, cu.tolist(), nq, nkv, hd, q0, k0, v0, True)
-    close16(out, ref, rel=2e-2 if dt == "fp16" else 3e-2)
+    # P enters P.V rounded to the 16-bit type (2^-9 relative for bf16, 2^-12
+    # for fp16), so an output's error scales with sum_j p_j |v_j|, not with
+    # |output|: where the terms cancel (short rows, |o| ~ 0) the relative bound
+    # alone is too tight.  sum_j p_j |v_j| is the attention of |v|.
+    qkv_abs = qkv.clone()
+    qkv_abs[:, v0:v0 + nkv * hd] = qkv_abs[:, v0:v0 + nkv * hd].abs()
+    mass = attention_ref(qkv_abs, cu.tolist(), nq, nkv, hd, q0, k0, v0, True)
+    eps = 2.0 ** -9 if dt == "bf16" else 2.0 ** -12
+    got = out.float()
+    rms = ref.pow(2).mean().sqrt().item()
+    bound = 2e-2 * ref.abs() + 2e-2 * rms + 4 * eps * mass + 1e-6
+    bad = ((got - ref).abs() > bound).sum().item()
+    assert bad == 0, f"{bad} of {ref.numel()} outside tolerance; max err {(got - ref).abs().max().item():.3e}"

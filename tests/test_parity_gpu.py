@@ -285,24 +285,34 @@ def test_fused_rmsnorm_matches_separate_rmsnorm(preset, act_dtype):
     decisions, both near the oracle."""
     spec, batch = decoder_case(preset, 3, 6, seed=19, max_len=1200)
     ref = DecoderOracle(spec).infer(batch)
-    got = {}
+    ref_lp = option_logprobs(ref, batch.nopts)
+    live = ref_lp > -1e4
+    got, dev = {}, {}
     for norm in ("fused", "separate"):
         eng = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, norm=norm, act_dtype=act_dtype)
         try:
             got[norm] = engine_logprobs(eng, batch)
         finally:
             eng.close()
+        dev[norm] = np.abs(got[norm] - ref_lp)[live].max()
         if act_dtype == "fp16":
             assert_decoder_parity(got[norm], ref, batch.nopts)
-    assert np.abs(got["fused"] - got["separate"]).max() <= (1e-2 if act_dtype == "fp16" else LOGPROB_TOL)
+    if act_dtype == "fp16":
+        assert np.abs(got["fused"] - got["separate"]).max() <= 1e-2
+    else:
+        # bf16 activations are ~3e-2 from fp32 at this depth either way (8
+        # mantissa bits); fusing must not make that worse.
+        assert dev["fused"] <= 1.25 * dev["separate"] + 5e-3, dev
 
 
 def test_last_layer_on_slot_rows_is_bit_exact():
     """Running the last layer's O projection and MLP on the slot rows only
     changes no bit of the result (each row's arithmetic is the same)."""
     spec, batch = decoder_case("onejev-9b", 2, 5, seed=17, max_len=900)
-    full = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, prune_last_layer=False)
-    pruned = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096)
+    # split_k off: with it, batches of <= 1024 rows (here the slot rows) sum
+    # K in split order, which is exact to tolerance but not to the bit.
+    full = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, prune_last_layer=False, split_k=False)
+    pruned = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, split_k=False)
     try:
         np.testing.assert_array_equal(engine_logprobs(full, batch), engine_logprobs(pruned, batch))
     finally:
@@ -314,8 +324,8 @@ def test_chunking_and_batching_are_bit_exact():
     """Rows are independent: splitting a batch by rows (small workspace) or
     running rows alone gives the same bits as one packed forward."""
     spec, batch = decoder_case("onejev-9b", 2, 5, seed=7, max_len=900)
-    big = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096)
-    small = B200Engine(spec, max_tokens=1024, max_rows=2, max_seq=1024)
+    big = B200Engine(spec, max_tokens=8192, max_rows=64, max_seq=4096, split_k=False)
+    small = B200Engine(spec, max_tokens=1024, max_rows=2, max_seq=1024, split_k=False)
     try:
         a = engine_logprobs(big, batch)
         b = engine_logprobs(small, batch)
@@ -324,6 +334,27 @@ def test_chunking_and_batching_are_bit_exact():
     finally:
         big.close()
         small.close()
+
+
+@pytest.mark.parametrize("preset,n_rows,max_len", [("onejev-9b", 1, 700), ("onejev-9b", 2, 520),
+                                                   ("decider-2b", 1, 900), ("onejev-27b", 1, 600)])
+def test_split_k_small_batches_vs_oracle(preset, n_rows, max_len):
+    """Small batches (<= 1024 tokens) run their projections with K split over
+    CTAs (fixed-order reduction of the partial tiles): against the oracle and
+    within rounding of the same engine without the split."""
+    spec, batch = decoder_case(preset, 2, n_rows, seed=23, max_len=max_len)
+    ref = DecoderOracle(spec).infer(batch)
+    got = {}
+    for split in (True, False):
+        eng = B200Engine(spec, max_tokens=4096, max_rows=8, max_seq=2048, split_k=split)
+        try:
+            got[split] = engine_logprobs(eng, batch)
+            again = engine_logprobs(eng, batch)
+            np.testing.assert_array_equal(got[split], again)  # run to run: the same bits
+        finally:
+            eng.close()
+        assert_decoder_parity(got[split], ref, batch.nopts)
+    assert np.abs(got[True] - got[False]).max() <= 5e-3
 
 
 def test_edge_lengths_vs_oracle():

@@ -79,13 +79,14 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int T, const __nv_b
 
 // Decoder embedding that starts the fused-RMSNorm chain (one 128-thread block
 // per token): h[t, :] = emb[tokens[t], :] * scale (fp32 residual stream), the
-// 16-bit copy xcopy[t, :] = T(h[t, :] * prescale) that the first QKV GEMM reads
-// as its A operand, and ss[t, b] = the sum of squares of h[t, 64b .. 64b + 63]
-// (the block sums the GEMM's row factor adds up).  d % 64 == 0.
+// 16-bit copy xcopy[t, :] = T(h[t, :] * (g + add) * prescale) that the first
+// QKV GEMM reads as its A operand (g: the first layer's input-norm gains), and
+// ss[t, b] = the sum of squares of h[t, 64b .. 64b + 63] (the block sums the
+// GEMM's row factor adds up).  d % 64 == 0.
 template <class T>
 __global__ void embed_norm_kernel(const int* __restrict__ tokens, int n_tok, const __nv_bfloat16* __restrict__ emb,
-                                  int d, float scale, float prescale, float* __restrict__ h, T* __restrict__ xcopy,
-                                  float* __restrict__ ss) {
+                                  int d, float scale, const float* __restrict__ g, float add, float prescale,
+                                  float* __restrict__ h, T* __restrict__ xcopy, float* __restrict__ ss) {
   const int t = blockIdx.x;
   if (t >= n_tok) return;
   const uint4* src = reinterpret_cast<const uint4*>(emb + static_cast<size_t>(tokens[t]) * d);
@@ -103,11 +104,13 @@ __global__ void embed_norm_kernel(const int* __restrict__ tokens, int n_tok, con
       v[4] = c.x * scale, v[5] = c.y * scale, v[6] = e.x * scale, v[7] = e.y * scale;
       dst[2 * i] = make_float4(v[0], v[1], v[2], v[3]);
       dst[2 * i + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(g) + 2 * i);
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(g) + 2 * i + 1);
       uint4 o;
-      o.x = Elem<T>::pack2(v[0] * prescale, v[1] * prescale);
-      o.y = Elem<T>::pack2(v[2] * prescale, v[3] * prescale);
-      o.z = Elem<T>::pack2(v[4] * prescale, v[5] * prescale);
-      o.w = Elem<T>::pack2(v[6] * prescale, v[7] * prescale);
+      o.x = Elem<T>::pack2(v[0] * ((g0.x + add) * prescale), v[1] * ((g0.y + add) * prescale));
+      o.y = Elem<T>::pack2(v[2] * ((g0.z + add) * prescale), v[3] * ((g0.w + add) * prescale));
+      o.z = Elem<T>::pack2(v[4] * ((g1.x + add) * prescale), v[5] * ((g1.y + add) * prescale));
+      o.w = Elem<T>::pack2(v[6] * ((g1.z + add) * prescale), v[7] * ((g1.w + add) * prescale));
       cp[i] = o;
     }
     float q = 0.0f;
@@ -118,17 +121,6 @@ __global__ void embed_norm_kernel(const int* __restrict__ tokens, int n_tok, con
     q += __shfl_xor_sync(0xffffffffu, q, 4);
     if (ok && (i & 7) == 0) ss[static_cast<size_t>(t) * (d / 64) + i / 8] = q;
   }
-}
-
-// Folds RMSNorm gains into the columns of a projection weight [rows, cols]:
-// w[r, c] = T(w[r, c] * (g[c] + add)), add = 1 for (1 + w) gains.
-template <class T>
-__global__ void scale_cols_kernel(T* __restrict__ w, int64_t rows, int64_t cols, const float* __restrict__ g,
-                                  float add) {
-  const int64_t n = rows * cols;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    w[i] = Elem<T>::from(Elem<T>::to(w[i]) * (g[i % cols] + add));
 }
 
 // RMSNorm of fp32 rows -> 16-bit T: out = T(x * rsqrt(mean(x^2) + eps) * g),

@@ -25,13 +25,15 @@
 //                   heads; v heads are stored as they are.
 //   kEpiResidualNorm : the residual add that feeds an RMSNorm (decoders' O /
 //                   out_proj and down projections): res_f32 += acc + bias,
-//                   then from the new residual row a 16-bit copy times
-//                   `prescale` (the next projection's A operand) and the sum of
-//                   squares of each 64-column block (its RMS statistics).
-// RMSNorm fused into the consuming projection: RMSNorm(h) W^T = rstd (h (W g)^T)
-// with the gains g folded into W at load, so a consumer reads A = the producer's
-// copy of h and multiplies each accumulator row by rstd / prescale (row factor,
-// from the producer's block sums) before its own epilogue.
+//                   then from the new residual row h a 16-bit copy of
+//                   h * g * prescale (g: the following norm's gains; the next
+//                   projection's A operand) and the sum of squares of each
+//                   64-column block of h (its RMS statistics).
+// RMSNorm fused into the consuming projection: RMSNorm(h) W^T = rstd ((h g) W^T),
+// so a consumer reads A = the producer's copy and multiplies each accumulator
+// row by rstd / prescale (row factor, from the producer's block sums) before its
+// own epilogue.  One 16-bit rounding of h g, as the standalone norm rounds its
+// output once; the weights are used as loaded.
 #pragma once
 
 #include "common.cuh"
@@ -63,6 +65,8 @@ struct EpiParams {
   void* xcopy;
   float prescale;
   float* ss_out;
+  const float* norm_gain;  // [N] gains of the following RMSNorm, applied as norm_gain + norm_add
+  float norm_add;
   // Fused RMSNorm of the A rows (store, gated and QK-rope epilogues): row
   // factor rsqrt(sum(ss_in[m, :]) * ss_inv_n + ss_eps) * ss_post, applied to
   // the accumulators first; ss_in == null: none.
@@ -99,11 +103,21 @@ __device__ __forceinline__ void scale32(float (&v)[32], float f) {
 // (one-CTA kernel, failure-path tests only; 0 = off): the producer stops after
 // issuing this many k-blocks, so the MMA warp's wait for the next stage runs
 // out and the launch ends through its abort path with kErrTimeoutFull.
+// splits > 1 (one-CTA kernel, small batches): K is split over `splits` work
+// units per output tile; each unit writes its fp32 partial tile to
+// part[split][m_pad][N], and the unit that finishes last (per-tile arrival
+// counters, left at zero) adds the partials in split order into its
+// accumulator and runs the epilogue, so the result does not depend on which
+// unit finished when.
 struct GemmShape {
   int M, N, K;
   int group_m;
   uint64_t wait_ns;
   int stall_after;
+  int splits;
+  int m_pad;
+  float* part;
+  int* counters;
 };
 
 // GELU in its exact form, x * Phi(x), Phi the standard normal CDF, with erf
@@ -391,8 +405,15 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
 #pragma unroll
         for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
         float sc[32];
+        const float4* g4 = reinterpret_cast<const float4*>(p.norm_gain + n0 + c * 32);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sc[j] = v[j] * p.prescale;
+        for (int q = 0; q < 8; ++q) {
+          const float4 g = __ldg(g4 + q);
+          sc[4 * q + 0] = v[4 * q + 0] * ((g.x + p.norm_add) * p.prescale);
+          sc[4 * q + 1] = v[4 * q + 1] * ((g.y + p.norm_add) * p.prescale);
+          sc[4 * q + 2] = v[4 * q + 2] * ((g.z + p.norm_add) * p.prescale);
+          sc[4 * q + 3] = v[4 * q + 3] * ((g.w + p.norm_add) * p.prescale);
+        }
         store_x32<T>(static_cast<T*>(p.xcopy) + off, sc);
         if (c & 1) {
           p.ss_out[static_cast<size_t>(row) * p.ss_slots + (n0 + c * 32) / kNormBlock] = ss;
@@ -462,6 +483,80 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
   }
 }
 
+// Split-K fixup of one work unit, run by the 8 epilogue warps (threads 64..319,
+// named barrier 1).  Each thread owns accumulator row `row` (padded tile row)
+// and the columns of its `half`.  The unit's partial goes to part[ks]; the
+// tile's arrival counter says whether all splits have landed; the last unit
+// adds part[0..splits) in order into its TMEM accumulator and returns true
+// (the caller then runs the epilogue on it), the others return false.
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Named barrier 1 over the epilogue warps that also ANDs a warp-uniform flag.
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, 256, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
+template <int BN>
+__device__ __forceinline__ bool split_fixup(uint32_t taddr, const GemmShape& sh, int tile, int ks, int row, int col0,
+                                            int half, volatile int* last_flag) {
+  constexpr int CH = BN / 32;
+  const size_t plane = static_cast<size_t>(sh.m_pad) * sh.N;
+  float* mine = sh.part + ks * plane + static_cast<size_t>(row) * sh.N + col0;
+#pragma unroll 1
+  for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
+    float v[32];
+    tmem_load_f32x32(taddr + c * 32, v);
+    float4* d = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+  __threadfence();  // this thread's partial is visible before the arrival below
+  epi_bar_sync();
+  if (threadIdx.x == 64) {
+    const int before = atomicAdd(sh.counters + tile, 1);
+    const bool last = before == sh.splits - 1;
+    if (last) sh.counters[tile] = 0;  // every unit of the tile has arrived: ready for the next launch
+    *last_flag = last ? 1 : 0;
+  }
+  epi_bar_sync();
+  if (!*last_flag) return false;
+  __threadfence();
+  const float* rowp = sh.part + static_cast<size_t>(row) * sh.N + col0;
+#pragma unroll 1
+  for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+#pragma unroll 1
+    for (int k = 0; k < sh.splits; ++k) {
+      const float4* s4 = reinterpret_cast<const float4*>(rowp + k * plane + c * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 t = __ldcg(s4 + q);
+        v[4 * q + 0] += t.x;
+        v[4 * q + 1] += t.y;
+        v[4 * q + 2] += t.z;
+        v[4 * q + 3] += t.w;
+      }
+    }
+    tmem_st32f(taddr + c * 32, v);
+  }
+  tmem_wait_st();
+  // Both warps of a lane quarter read the whole tile row in some epilogues.
+  tc_fence_before();
+  epi_bar_sync();
+  tc_fence_after();
+  return true;
+}
+
 template <int BN>
 struct GemmConfig {
   static constexpr int BM = 128;
@@ -513,6 +608,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* mma_drained = acc_empty + 3;  // the MMA warp's own ops, on its abort path
+  volatile int* split_last = reinterpret_cast<volatile int*>(acc_empty + 4);  // split-K: this unit finishes the tile
   uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
   const uint64_t wait_ns = shape.wait_ns;
 
@@ -545,6 +641,13 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
   const int num_n = shape.N / BN;
   const int tiles = num_m * num_n;
   const int kblocks = shape.K / BK;
+  const int splits = shape.splits > 1 ? shape.splits : 1;
+  const int units = tiles * splits;  // unit u: tile u / splits, K range u % splits
+  auto k_range = [&](int u, int& kb0, int& kb1) {
+    const int ks = u % splits;
+    kb0 = static_cast<int>(static_cast<int64_t>(ks) * kblocks / splits);
+    kb1 = static_cast<int>(static_cast<int64_t>(ks + 1) * kblocks / splits);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -554,10 +657,11 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        int m, n;
-        tile_coords(tile, num_m, num_n, shape.group_m, m, n);
-        for (int kb = 0; kb < kblocks; ++kb) {
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        int m, n, kb0, kb1;
+        tile_coords(u / splits, num_m, num_n, shape.group_m, m, n);
+        k_range(u, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (shape.stall_after > 0 && issued == shape.stall_after) goto producer_drain;
           ++issued;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, wait_ns)) goto producer_done;
@@ -589,14 +693,16 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        int kb0, kb1;
+        k_range(u, kb0, kb1);
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrTimeoutAccEmpty, wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrTimeoutFull, wait_ns)) {
             ok = false;
             break;
@@ -607,7 +713,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             umma_f16kind(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32), IDESC,
-                      (kb | k) != 0 ? 1u : 0u);
+                      (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -638,15 +744,22 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     EpiOut o{epi_stage + (warp - 2) * Cfg::EPI_STAGE_BYTES, &tmC, 0, lane, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int tile = u / splits;
       int m, n;
       tile_coords(tile, num_m, num_n, shape.group_m, m, n);
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull, wait_ns)) break;
+      bool got = mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrTimeoutAccFull, wait_ns);
+      // The split fixup synchronises the 8 epilogue warps, so they must agree
+      // on going on (one giving up on an abort while another saw the
+      // accumulator land would leave the other at a barrier).
+      if (splits > 1) got = epi_bar_and(__all_sync(0xffffffffu, got));
+      if (!got) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row = m * BM + row_in_tile;
       o.y = m * BM + lane_group * 32;
-      gemm_epilogue<BN, EPI, T>(o, taddr, row, row < shape.M, n * BN, half, ep);
+      if (splits == 1 || split_fixup<BN>(taddr, shape, tile, u % splits, row, n * BN, half, split_last))
+        gemm_epilogue<BN, EPI, T>(o, taddr, row, row < shape.M, n * BN, half, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);

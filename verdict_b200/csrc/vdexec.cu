@@ -58,11 +58,35 @@ struct VdError {
 
 [[noreturn]] static void fail(int code, const std::string& msg) { throw VdError{code, msg}; }
 
-// Fused RMSNorm with fp16 activations: the 16-bit copy of the residual rows is
-// stored times 2^-6, so rows up to 4.2e6 in magnitude stay inside fp16's range
-// while values down to 2^-8 remain normal numbers (the row factor undoes it
-// exactly).  bf16 has fp32's exponent range and stores the rows as they are.
+// Fused RMSNorm with fp16 activations: the 16-bit copy of the residual rows
+// (times the norm's gains) is stored times 2^-6, so rows up to 4.2e6 in
+// magnitude stay inside fp16's range while values down to 2^-8 remain normal
+// numbers (the row factor undoes it exactly).  bf16 has fp32's exponent range
+// and stores the rows as they are.
 constexpr float kNormPrescale16 = 1.0f / 64.0f;
+
+// Small batches (M <= kSplitMaxM rows) run their projections as 128-row tiles
+// on one CTA each, with K split over work units when that fills the SMs better
+// (a 515-token decision has 5 row tiles: 80 tiles for a 4096-wide output on 148
+// SMs).  The partial tiles live in a workspace of kSplitPartElems floats.
+constexpr int kSplitMaxM = 1024;
+constexpr int64_t kSplitPartElems = int64_t(64) << 20;  // 256 MB
+
+// Splits of K (k-blocks of 64) for `tiles` output tiles on `sms` SMs: the
+// fewest rounds of the longest unit, a split costing about two k-blocks of
+// partial-tile traffic; 1 = no split.
+static int choose_splits(int tiles, int kblocks, int sms, int max_splits) {
+  double best = std::ceil(static_cast<double>(tiles) / sms) * kblocks;
+  int pick = 1;
+  for (int S = 2; S <= max_splits && kblocks / S >= 4; ++S) {
+    const double t = std::ceil(static_cast<double>(tiles) * S / sms) * std::ceil(static_cast<double>(kblocks) / S) + 2.0;
+    if (t < 0.95 * best) {
+      best = t;
+      pick = S;
+    }
+  }
+  return pick;
+}
 
 static void cuda_check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) fail(VD_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -608,6 +632,7 @@ struct Options {
   int raster_group = 0;      // M tiles per GEMM raster group; 0 = the kernel's default
   bool gdn_chunk = true;     // gated delta nets in 64-token chunks on the tensor cores, else token by token
   bool fuse_norm = true;     // decoders: RMSNorm fused into the residual GEMMs and the projections that read it
+  bool split_k = true;       // small batches: K split over CTAs where that fills the SMs better
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
@@ -654,6 +679,11 @@ struct vd_handle {
   // fused RMSNorm: block sums of squares of the residual rows ([rows, d / 64]),
   // two for the main rows (attention / MLP input), one for the slot rows
   float *ss_a = nullptr, *ss_b = nullptr, *ss_s = nullptr;
+  // split-K partial tiles and per-tile arrival counters (small batches)
+  float* split_part = nullptr;
+  int64_t split_part_elems = 0;
+  int* split_cnt = nullptr;
+  int64_t split_cnt_n = 0;
   // last-layer slot rows (one per decision of a chunk)
   float* h_s = nullptr;
   void *xn_s = nullptr, *attn_s = nullptr, *act_s = nullptr;
@@ -897,18 +927,6 @@ static void init_linear(vd_handle* H, Linear& L, int n, int k, bool bias, int bn
 
 static float2* upload_rope(vd_handle* H, int rot, double theta);
 
-// Fused RMSNorm: the norm's gains g (as stored: w, applied as w + add) folded
-// into the columns of the projection that reads the normalised rows.
-static void fold_gains(vd_handle* H, Linear& L, const float* g) {
-  const float add = H->spec.norm_plus_one ? 1.0f : 0.0f;
-  const int64_t n = static_cast<int64_t>(L.n) * L.k;
-  if (H->opt.f16)
-    scale_cols_kernel<__half><<<grid_for(n), 256, 0, H->stream>>>(static_cast<__half*>(L.w), L.n, L.k, g, add);
-  else
-    scale_cols_kernel<__nv_bfloat16><<<grid_for(n), 256, 0, H->stream>>>(static_cast<__nv_bfloat16*>(L.w), L.n,
-                                                                          L.k, g, add);
-}
-
 static void load_decoder(vd_handle* H) {
   const ModelSpec& s = H->spec;
   const int d = s.hidden, hd = s.head_dim, nq = s.heads, nkv = s.kv_heads, f = s.ffn;
@@ -954,10 +972,6 @@ static void load_decoder(vd_handle* H) {
       fill_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
       init_linear(H, L.down, d, f, false);
       fill_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
-      if (H->opt.fuse_norm) {
-        fold_gains(H, L.qkv, L.in_norm);
-        fold_gains(H, L.gu, L.post_norm);
-      }
       continue;
     }
     init_linear(H, L.qkv, s.qkv_width(), d, s.qkv_bias, bn_qkv);
@@ -988,10 +1002,6 @@ static void load_decoder(vd_handle* H) {
     fill_lin(H, L.gu.w, p + "mlp.up_proj.weight", f, d, lin, 0.0f, 128, 256, 128);
     init_linear(H, L.down, d, f, false);
     fill_lin(H, L.down.w, p + "mlp.down_proj.weight", d, f, lin, 0.0f);
-    if (H->opt.fuse_norm) {
-      fold_gains(H, L.qkv, L.in_norm);
-      fold_gains(H, L.gu, L.post_norm);
-    }
   }
   H->final_norm = dalloc<float>(H, d);
   fill_f32(H, H->final_norm, "model.norm.weight", d, n_scale, n_off);
@@ -1253,6 +1263,16 @@ static void alloc_workspace(vd_handle* H) {
   }
   H->map_act = make_map(H->act, T, s.ffn, 128, f16);
   H->out_act = make_out_map(H->act, T, s.ffn, false, f16);
+  if (o.split_k) {
+    // Widest projection of the model: the fused gate/up (2 ffn), QKV, or hidden.
+    const int64_t max_n = std::max<int64_t>({2 * static_cast<int64_t>(std::max(s.ffn, 4 * d)), qkvw, d,
+                                              s.decoder() && s.any_linear() ? s.gdn_proj() : 0});
+    H->split_part_elems = kSplitPartElems;
+    H->split_part = dalloc<float>(H, H->split_part_elems);
+    H->split_cnt_n = (kSplitMaxM / 128) * ((max_n + 127) / 128);
+    H->split_cnt = dalloc<int>(H, H->split_cnt_n);
+    cuda_check(cudaMemset(H->split_cnt, 0, sizeof(int) * H->split_cnt_n), "clear split-K counters");
+  }
   if (s.decoder() && s.any_linear()) {
     // gated-delta-net in_proj output and per-(token, v head) gates
     H->proj = dalloc<uint16_t>(H, T * s.gdn_proj());
@@ -1368,7 +1388,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const int tiles = num_m * (L.n / L.bn);
   const int grid = std::min(tiles, H->num_sms);
   GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M,
-                  H->opt.wait_ns, 0};
+                  H->opt.wait_ns, 0, 1, 0, nullptr, nullptr};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
   // Failure-path tests: the first one-CTA GEMM of the call stalls its producer.
   auto stall_one_cta = [&] {
@@ -1377,6 +1397,32 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
       H->stall_pending = false;
     }
   };
+  if (H->split_part && M <= kSplitMaxM) {
+    const int m_pad = num_m * 128;
+    const int64_t plane = static_cast<int64_t>(m_pad) * L.n;
+    const int max_s = static_cast<int>(std::min<int64_t>(8, H->split_part_elems / plane));
+    const int S = tiles <= H->split_cnt_n ? choose_splits(tiles, L.k / 64, H->num_sms, max_s) : 1;
+    if (S > 1) {
+      shape.splits = S;
+      shape.m_pad = m_pad;
+      shape.part = H->split_part;
+      shape.counters = H->split_cnt;
+      const int grid_s = std::min(tiles * S, H->num_sms);
+      stall_one_cta();
+      launch(H, kind, flops, [&] {
+        if (L.bn == 256) {
+          gemm_tcgen05_kernel<256, EPI, T><<<grid_s, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES,
+                                              H->stream>>>(a, L.map, c, shape, ep, H->d_err);
+        } else {
+          if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
+          else
+            gemm_tcgen05_kernel<128, EPI, T><<<grid_s, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
+                                                H->stream>>>(a, L.map, c, shape, ep, H->d_err);
+        }
+      });
+      return;
+    }
+  }
   if (L.bn == 256 && H->opt.gemm2 && H->gemm2_pairs > 0) {
     const int pair_tiles = ((M + 255) / 256) * (L.n / 256);
     // A GEMM of a wave or two of CTA pairs (short batches, the encoders' 768-
@@ -1836,13 +1882,16 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   const bool fused = H->opt.fuse_norm;
   const float pre = H->opt.f16 ? kNormPrescale16 : 1.0f;
   const int slots = d / kNormBlock;
-  auto produce = [&](float* res, void* copy, float* ss) {
+  const float gadd = s.norm_plus_one ? 1.0f : 0.0f;
+  auto produce = [&](float* res, void* copy, float* ss, const float* next_gain) {
     EpiParams p = epi();
     p.res = res;
     p.xcopy = copy;
     p.prescale = pre;
     p.ss_out = ss;
     p.ss_slots = slots;
+    p.norm_gain = next_gain;
+    p.norm_add = gadd;
     return p;
   };
   auto consume = [&](EpiParams p, const float* ss) {
@@ -1861,8 +1910,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   };
   launch(H, VD_K_OTHER, 0.0, [&] {
     if (fused)
-      embed_norm_kernel<T><<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, pre, H->h,
-                                                        static_cast<T*>(H->xn), H->ss_a);
+      embed_norm_kernel<T><<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->dec[0].in_norm,
+                                                        gadd, pre, H->h, static_cast<T*>(H->xn), H->ss_a);
     else
       embed_kernel<<<ntok, 128, 0, H->stream>>>(H->tokens, ntok, H->embed, d, escale, H->h);
   });
@@ -1884,8 +1933,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
                                                                  static_cast<T*>(H->attn_s), H->h_s, H->d_err);
       });
       if (fused) {
-        gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, produce(H->h_s, H->xn_s, H->ss_s),
-                                  H->out_h_s);
+        gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb,
+                                  produce(H->h_s, H->xn_s, H->ss_s, L.post_norm), H->out_h_s);
       } else {
         gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(), H->out_h_s);
         separate_norm(H->h_s, L.post_norm, H->xn_s, c.nb);
@@ -1896,7 +1945,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
       continue;
     }
     if (fused) {
-      gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn, L.o, ntok, produce(H->h, H->xn, H->ss_b), H->out_h);
+      gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn, L.o, ntok, produce(H->h, H->xn, H->ss_b, L.post_norm),
+                                H->out_h);
     } else {
       gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(), H->out_h);
       separate_norm(H->h, L.post_norm, H->xn, ntok);
@@ -1904,7 +1954,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, consume(epi(nullptr, s.act), H->ss_b), H->out_act);
     // The last layer's down projection feeds only the readout's final norm.
     if (fused && !last)
-      gemm<kEpiResidualNorm, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, produce(H->h, H->xn, H->ss_a), H->out_h);
+      gemm<kEpiResidualNorm, T>(H, VD_K_DOWN, H->map_act, L.down, ntok,
+                                produce(H->h, H->xn, H->ss_a, H->dec[i + 1].in_norm), H->out_h);
     else
       gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(), H->out_h);
   }
@@ -2336,6 +2387,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       const std::string nm = o.string_or("norm", "fused");
       if (nm != "fused" && nm != "separate") fail(VD_EINVAL, "norm must be \"fused\" or \"separate\"");
       H->opt.fuse_norm = nm == "fused";
+      H->opt.split_k = o.boolean_or("split_k", true);
       const long long wait_us = o.integer_or("wait_limit_us", 0);
       if (wait_us < 0 || wait_us > 60000000) fail(VD_EINVAL, "wait_limit_us must be in [0, 6e7]");
       H->opt.wait_ns = static_cast<uint64_t>(wait_us) * 1000ull;

@@ -74,13 +74,16 @@ class B200Engine(Engine):
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
                  prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
-                 raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", wait_limit_us: int = 0,
-                 debug_stall_gemm: int = 0):
+                 raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", split_k: bool = True,
+                 wait_limit_us: int = 0, debug_stall_gemm: int = 0):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory).
         `norm` (decoders): "fused" folds each RMSNorm into the residual GEMM that
         produces its input and the projection that reads it; "separate" runs it
         as its own kernel.
+        `split_k`: batches of up to 1024 tokens split K over CTAs where that
+        fills the GPU better (partials added in a fixed order: the same bits on
+        every run, within rounding of the unsplit sum).
         `wait_limit_us`: limit of the GEMM kernels' pipeline waits (0: 2 s);
         `debug_stall_gemm` (failure-path tests only): the first one-CTA GEMM of
         every call stops loading after that many k-blocks, so its wait runs out."""
@@ -98,7 +101,7 @@ class B200Engine(Engine):
         opts = json.dumps(dict(max_tokens=max_tokens, max_rows=max_rows, max_seq=max_seq,
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
                                attention=attention, prune_last_layer=prune_last_layer, fork=fork,
-                               gemm=gemm, raster_group=raster_group, gdn=gdn, norm=norm,
+                               gemm=gemm, raster_group=raster_group, gdn=gdn, norm=norm, split_k=split_k,
                                wait_limit_us=wait_limit_us,
                                debug_stall_gemm=debug_stall_gemm))
         err = ctypes.create_string_buffer(1024)
