@@ -305,6 +305,28 @@ def test_fused_rmsnorm_matches_separate_rmsnorm(preset, act_dtype):
         assert dev["fused"] <= 1.25 * dev["separate"] + 5e-3, dev
 
 
+@pytest.mark.parametrize("preset,lengths", [("onejev-9b", None), ("decider-2b", None), ("laya-xlmr", "lognormal-xlmr")])
+def test_persistent_attention_is_bit_exact(preset, lengths):
+    """The tcgen05 attention with CTAs looping over work items (default) and
+    with one CTA per item run the same arithmetic per item: the same bits."""
+    if lengths is None:
+        spec, batch = decoder_case(preset, 2, 7, seed=29, max_len=1500)
+    else:
+        spec = specs.preset(preset, layers=2, seed=29)
+        rng = np.random.default_rng(29)
+        rows = encoder_rows(rng, 40, spec["vocab"], lengths=lengths, cls_id=0, sep_id=2, id_low=5,
+                            max_len=spec["max_pos"] - 2)
+        batch = collate(rows, Layout(pad_id=spec["pad_id"]))
+    got = []
+    for persistent in (True, False):
+        eng = B200Engine(spec, max_tokens=16384, max_rows=64, max_seq=4096, attention_persistent=persistent)
+        try:
+            got.append(engine_logprobs(eng, batch))
+        finally:
+            eng.close()
+    np.testing.assert_array_equal(got[0], got[1])
+
+
 def test_last_layer_on_slot_rows_is_bit_exact():
     """Running the last layer's O projection and MLP on the slot rows only
     changes no bit of the result (each row's arithmetic is the same)."""

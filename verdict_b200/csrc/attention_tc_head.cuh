@@ -4,9 +4,15 @@
 // columns), or bidirectional (CAUSAL = false) with HD = 64 for the marker-head
 // encoders (every key of the sequence, no option masks).
 //
-// One CTA = one 128-row query tile of one sequence for one query head; keys in
-// tiles of 64.  TMEM: two S/P buffers of 64 columns (S of tile j + 1 is computed
-// while the softmax warps work on tile j) and O, 128 rows x HD fp32 columns.
+// Work item = one 128-row query tile of one sequence for one query head; keys
+// in tiles of 64.  A CTA runs items blockIdx.x, blockIdx.x + gridDim.x, ...
+// (persistent when the grid is smaller than the item count): its barriers and
+// tensor memory are set up once, and the next item's Q load and first two S
+// MMAs run while the softmax warps drain the previous item's O.  Items are
+// tile-major, head-minor over a tile table sorted by work, so the query heads
+// of one K/V head read the same K/V tiles at about the same time.  TMEM: two
+// S/P buffers of 64 columns (S of tile j + 1 is computed while the softmax
+// warps work on tile j) and O, 128 rows x HD fp32 columns.
 //   warp 0      : TMA producer of Q (once) and the K tiles (2-stage ring)
 //   warp 1      : TMEM allocator + MMA issuer (one lane):
 //                 S(0), S(1), then per tile j: O += P(j) V(j) (A = P from
@@ -40,6 +46,7 @@ struct AttnTcHeadParams {
   int q_col0, k_col0, v_col0;  // column offsets of the q / k / v blocks in qkv
   int gate_col0;               // >= 0: output *= sigmoid(qkv[:, gate_col0 + head * HD + c])
   const AttnTile* tiles;       // 128-row query tiles
+  int n_tiles, heads;          // work items: n_tiles * heads, item = tile * heads + head
   int group;                   // query heads per K/V head
   float scale_log2;
   int* err;
@@ -83,21 +90,35 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
   uint64_t* s_full = bars + 9;    // [2] per S/P buffer
   uint64_t* p_full = bars + 11;   // [2]
   uint64_t* pv_done = bars + 13;  // one arrival per P V
-  uint64_t* o_final = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* o_final = bars + 14;  // an item's last P V has landed in O
+  uint64_t* q_free = bars + 15;   // an item's last S has read Q: the next Q may load
+  uint64_t* o_free = bars + 16;   // the softmax warps have drained O: the next P V may overwrite it
+  uint64_t* mma_drained = bars + 17;  // the MMA warp's own ops, on its abort path
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const AttnTile tile = p.tiles[blockIdx.x];
-  const int head = blockIdx.y;
-  const int kvh = head / p.group;
-  const int kv_end = CAUSAL ? min(tile.seq_len, tile.q_start + C::BM) : tile.seq_len;
-  // Key tiles: first the shared prefix's (n_pre, unmasked but for its end),
-  // then the sequence's own (causal, or all of them).
-  const int n_pre = (tile.pre_len + C::BN - 1) / C::BN;
-  const int n_kv = n_pre + (kv_end + C::BN - 1) / C::BN;
-  auto key_row = [&](int j) {
-    return j < n_pre ? tile.pre_start + j * C::BN : tile.seq_start + (j - n_pre) * C::BN;
+  const int n_items = p.n_tiles * p.heads;
+
+  // Geometry of work item `it`: key tiles first of the shared prefix
+  // (n_pre, unmasked but for its end), then of the sequence itself (causal,
+  // or all of them).
+  struct Item {
+    AttnTile tile;
+    int head, kvh, n_pre, n_kv;
+  };
+  auto item_at = [&](int it) {
+    Item w;
+    w.tile = p.tiles[it / p.heads];
+    w.head = it - (it / p.heads) * p.heads;
+    w.kvh = w.head / p.group;
+    const int kv_end = CAUSAL ? min(w.tile.seq_len, w.tile.q_start + C::BM) : w.tile.seq_len;
+    w.n_pre = (w.tile.pre_len + C::BN - 1) / C::BN;
+    w.n_kv = w.n_pre + (kv_end + C::BN - 1) / C::BN;
+    return w;
+  };
+  auto key_row = [&](const Item& w, int j) {
+    return j < w.n_pre ? w.tile.pre_start + j * C::BN : w.tile.seq_start + (j - w.n_pre) * C::BN;
   };
 
   if (threadIdx.x == 0) {
@@ -112,6 +133,9 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
     }
     mbar_init(pv_done, 1);
     mbar_init(o_final, 1);
+    mbar_init(q_free, 1);
+    mbar_init(o_free, 4);
+    mbar_init(mma_drained, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -124,46 +148,67 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Key tiles are counted over all of this CTA's items (g): K / V stage and
+  // S / P buffer g & 1, phase (g >> 1) & 1.  Items are counted by qi.
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_qkv64);
-      const int qx = p.q_col0 + head * C::HD, kx = p.k_col0 + kvh * C::HD;
-      const int qy = tile.seq_start + tile.q_start;
-      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      uint32_t g = 0, qi = 0;
+      for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++qi) {
+        const Item w = item_at(it);
+        if (qi > 0 && !mbar_wait(q_free, (qi - 1) & 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
+        const int qx = p.q_col0 + w.head * C::HD, kx = p.k_col0 + w.kvh * C::HD;
+        const int qy = w.tile.seq_start + w.tile.q_start;
+        mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
-      for (int a = 0; a < C::ATOMS; ++a) {
-        tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM, &tm_qkv64, q_full, qx + 64 * a, qy);
-        tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM + C::Q_ATOM / 2, &tm_qkv64, q_full, qx + 64 * a, qy + 64);
-      }
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
+        for (int a = 0; a < C::ATOMS; ++a) {
+          tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM, &tm_qkv64, q_full, qx + 64 * a, qy);
+          tma_load_2d(smem + C::Q_OFF + a * C::Q_ATOM + C::Q_ATOM / 2, &tm_qkv64, q_full, qx + 64 * a, qy + 64);
+        }
+        bool ok = true;
+        for (int j = 0; j < w.n_kv; ++j, ++g) {
+          const int s = g & 1;
+          if (!mbar_wait(&k_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[s], C::KV_BYTES);
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_2d(smem + C::K_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &k_full[s], kx + 64 * a,
-                      key_row(j));
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_2d(smem + C::K_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &k_full[s], kx + 64 * a,
+                        key_row(w, j));
+        }
+        if (!ok) break;
       }
     }
   } else if (warp == 2) {
     if (lane == 0) {
-      const int vx = p.v_col0 + kvh * C::HD;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
+      uint32_t g = 0;
+      for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const Item w = item_at(it);
+        const int vx = p.v_col0 + w.kvh * C::HD;
+        bool ok = true;
+        for (int j = 0; j < w.n_kv; ++j, ++g) {
+          const int s = g & 1;
+          if (!mbar_wait(&v_empty[s], ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[s], C::KV_BYTES);
 #pragma unroll
-        for (int a = 0; a < C::ATOMS; ++a)
-          tma_load_2d(smem + C::V_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &v_full[s], vx + 64 * a,
-                      key_row(j));
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_2d(smem + C::V_OFF + s * C::KV_BYTES + a * C::KV_ATOM, &tm_qkv64, &v_full[s], vx + 64 * a,
+                        key_row(w, j));
+        }
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(smem + C::Q_OFF);
-      // S(j) = Q K_j^T into S/P buffer j & 1; releases K stage j & 1 when done.
-      auto issue_s = [&](int j) {
-        const int b = j & 1;
+      // S(g) = Q K_g^T into S/P buffer g & 1; releases K stage g & 1 when done.
+      auto issue_s = [&](uint32_t g) {
+        const int b = g & 1;
         const uint32_t k_addr = smem_u32(smem + C::K_OFF + b * C::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -174,36 +219,58 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
         umma_commit(&s_full[b]);
         umma_commit(&k_empty[b]);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutFull);
-      for (int j = 0; ok && j < 2 && j < n_kv; ++j) {
-        if (!mbar_wait(&k_full[j], 0, abort_flag, p.err, kErrTimeoutFull)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_s(j);
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int b = j & 1, ph = (j >> 1) & 1;
-        if (!mbar_wait(&v_full[b], ph, abort_flag, p.err, kErrTimeoutFull)) break;
-        if (!mbar_wait(&p_full[b], ph, abort_flag, p.err, kErrTimeoutFull)) break;
-        tc_fence_after();
-        // O += P(j) V(j): A = P from TMEM (8 columns per 16 keys), B = V
-        // MN-major (64-dim atoms KV_ATOM apart), K advances 16 key rows = 2 KB.
-        const uint32_t v_addr = smem_u32(smem + C::V_OFF + b * C::KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16kind_ts(tmem + 128, tmem + b * 64 + kk * 8, sw128_mnmajor_desc(v_addr + kk * 2048, C::KV_ATOM),
-                          IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&v_empty[b]);
-        umma_commit(pv_done);
-        if (j + 1 == n_kv) umma_commit(o_final);
-        // S(j + 2) overwrites P(j) in TMEM; MMAs of one thread run in order.
-        if (j + 2 < n_kv) {
-          if (!mbar_wait(&k_full[b], ((j + 2) >> 1) & 1, abort_flag, p.err, kErrTimeoutFull)) break;
+      uint32_t g = 0, qi = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++qi) {
+        const Item w = item_at(it);
+        ok = mbar_wait(q_full, qi & 1, abort_flag, p.err, kErrTimeoutFull);
+        for (int j = 0; ok && j < 2 && j < w.n_kv; ++j) {
+          if (!mbar_wait(&k_full[(g + j) & 1], ((g + j) >> 1) & 1, abort_flag, p.err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_s(j + 2);
+          issue_s(g + j);
         }
+        if (ok && w.n_kv <= 2) umma_commit(q_free);  // every S of the item issued: Q may be replaced
+        for (int j = 0; ok && j < w.n_kv; ++j) {
+          const uint32_t gj = g + j;
+          const int b = gj & 1, ph = (gj >> 1) & 1;
+          if (!mbar_wait(&v_full[b], ph, abort_flag, p.err, kErrTimeoutFull) ||
+              !mbar_wait(&p_full[b], ph, abort_flag, p.err, kErrTimeoutFull) ||
+              (j == 0 && qi > 0 && !mbar_wait(o_free, (qi - 1) & 1, abort_flag, p.err, kErrTimeoutAccEmpty))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // O += P(j) V(j): A = P from TMEM (8 columns per 16 keys), B = V
+          // MN-major (64-dim atoms KV_ATOM apart), K advances 16 key rows = 2 KB.
+          const uint32_t v_addr = smem_u32(smem + C::V_OFF + b * C::KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16kind_ts(tmem + 128, tmem + b * 64 + kk * 8, sw128_mnmajor_desc(v_addr + kk * 2048, C::KV_ATOM),
+                            IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&v_empty[b]);
+          umma_commit(pv_done);
+          if (j + 1 == w.n_kv) umma_commit(o_final);
+          // S(j + 2) overwrites P(j) in TMEM; MMAs of one thread run in order.
+          if (j + 2 < w.n_kv) {
+            if (!mbar_wait(&k_full[b], ((gj + 2) >> 1) & 1, abort_flag, p.err, kErrTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(gj + 2);
+            if (j + 3 == w.n_kv) umma_commit(q_free);
+          }
+        }
+        g += w.n_kv;
+      }
+      if (!ok) {
+        // Aborted: the MMAs already issued finish (bounded) before the CTA
+        // frees the tensor memory they write.
+        umma_commit(mma_drained);
+        mbar_wait_own(mma_drained, 0, 0);
       }
     }
   } else {
@@ -212,87 +279,96 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t o_tm = tmem + lane_base + 128;
-    const int q_row = tile.q_start + r;  // row inside the sequence
-    float m_run = -INFINITY, l_run = 0.0f;
+    uint32_t g = 0, qi = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int b = j & 1;
-      const uint32_t s_tm = tmem + lane_base + b * 64;
-      const bool in_pre = j < n_pre;
-      const int kv0 = (in_pre ? j : j - n_pre) * C::BN;  // key index inside its segment
-      const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
-      const int causal_row = (in_pre || !CAUSAL) ? 0x7fffffff : q_row;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool need_mask = kv0 + C::BN > seg_len || (CAUSAL && !in_pre && kv0 + C::BN > tile.q_start);
-      uint32_t sr[64];
-      tmem_ld32_nowait(s_tm + 0, sr + 0);
-      tmem_ld32_nowait(s_tm + 32, sr + 32);
-      tmem_wait_ld();
-      float mx = -INFINITY;
-      if (need_mask) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int kv = kv0 + i;
-          if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(sr[i]));
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-      }
-      const float m_tile = mx * p.scale_log2;
-      const bool raise = m_tile > m_run + C::RESCALE_THRESHOLD;
-      const bool warp_raise = __any_sync(0xffffffffu, raise);
-      const float m_new = raise ? m_tile : m_run;
-      const float alpha = raise ? fast_exp2(m_run - m_new) : 1.0f;
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float e0 = fast_exp2(__uint_as_float(sr[c * 32 + i]) * p.scale_log2 - m_new);
-          const float e1 = fast_exp2(__uint_as_float(sr[c * 32 + i + 1]) * p.scale_log2 - m_new);
-          rs += e0 + e1;
-          pk[i >> 1] = Elem<T>::pack2(e0, e1);
-        }
-        tmem_st16(s_tm + c * 16, pk);
-      }
-      // A raised max rescales the O rows accumulated so far, once P(j - 1) V
-      // has landed (P(j) V cannot start before this warp's p_full arrival).
-      if (warp_raise && j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++qi) {
+      const Item w = item_at(it);
+      const AttnTile& tile = w.tile;
+      const int q_row = tile.q_start + r;  // row inside the sequence
+      float m_run = -INFINITY, l_run = 0.0f;
+      for (int j = 0; j < w.n_kv; ++j) {
+        const uint32_t gj = g + j;
+        const int b = gj & 1;
+        const uint32_t s_tm = tmem + lane_base + b * 64;
+        const bool in_pre = j < w.n_pre;
+        const int kv0 = (in_pre ? j : j - w.n_pre) * C::BN;  // key index inside its segment
+        const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
+        const int causal_row = (in_pre || !CAUSAL) ? 0x7fffffff : q_row;
+        if (!mbar_wait(&s_full[b], (gj >> 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          float v[32];
-          tmem_load_f32x32(o_tm + c * 32, v);
+        const bool need_mask = kv0 + C::BN > seg_len || (CAUSAL && !in_pre && kv0 + C::BN > tile.q_start);
+        uint32_t sr[64];
+        tmem_ld32_nowait(s_tm + 0, sr + 0);
+        tmem_ld32_nowait(s_tm + 32, sr + 32);
+        tmem_wait_ld();
+        float mx = -INFINITY;
+        if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32f(o_tm + c * 32, v);
+          for (int i = 0; i < 64; ++i) {
+            const int kv = kv0 + i;
+            if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
+            mx = fmaxf(mx, __uint_as_float(sr[i]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
         }
+        const float m_tile = mx * p.scale_log2;
+        const bool raise = m_tile > m_run + C::RESCALE_THRESHOLD;
+        const bool warp_raise = __any_sync(0xffffffffu, raise);
+        const float m_new = raise ? m_tile : m_run;
+        const float alpha = raise ? fast_exp2(m_run - m_new) : 1.0f;
+        float rs = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float e0 = fast_exp2(__uint_as_float(sr[c * 32 + i]) * p.scale_log2 - m_new);
+            const float e1 = fast_exp2(__uint_as_float(sr[c * 32 + i + 1]) * p.scale_log2 - m_new);
+            rs += e0 + e1;
+            pk[i >> 1] = Elem<T>::pack2(e0, e1);
+          }
+          tmem_st16(s_tm + c * 16, pk);
+        }
+        // A raised max rescales the O rows accumulated so far, once P(j - 1) V
+        // has landed (P(j) V cannot start before this warp's p_full arrival).
+        if (warp_raise && j > 0) {
+          if (!mbar_wait(pv_done, (gj - 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            float v[32];
+            tmem_load_f32x32(o_tm + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tmem_st32f(o_tm + c * 32, v);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
+        l_run = l_run * alpha + rs;
+        m_run = m_new;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-    }
-    if (ok && mbar_wait(o_final, 0, abort_flag, p.err, kErrTimeoutAccFull)) {
+      if (!ok || !mbar_wait(o_final, qi & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
       const size_t tok = static_cast<size_t>(tile.seq_start + q_row);
-      T* dst = static_cast<T*>(p.out) + tok * p.ld_out + head * C::HD;
-      const T* gate = p.gate_col0 >= 0 ? static_cast<const T*>(p.qkv) + tok * p.ld_qkv + p.gate_col0 + head * C::HD
-                                       : nullptr;
+      T* dst = static_cast<T*>(p.out) + tok * p.ld_out + w.head * C::HD;
+      const T* gate = p.gate_col0 >= 0
+                          ? static_cast<const T*>(p.qkv) + tok * p.ld_qkv + p.gate_col0 + w.head * C::HD
+                          : nullptr;
       const bool live = q_row < tile.seq_len;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
@@ -303,13 +379,13 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
             const uint4* g4 = reinterpret_cast<const uint4*>(gate + c * 32);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const uint4 w = g4[q];
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+              const uint4 gw = g4[q];
+              const uint32_t ws[4] = {gw.x, gw.y, gw.z, gw.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float2 g = Elem<T>::unpack2(ws[e]);
-                v[q * 8 + 2 * e] *= inv * __fdividef(1.0f, 1.0f + __expf(-g.x));
-                v[q * 8 + 2 * e + 1] *= inv * __fdividef(1.0f, 1.0f + __expf(-g.y));
+                const float2 gg = Elem<T>::unpack2(ws[e]);
+                v[q * 8 + 2 * e] *= inv * __fdividef(1.0f, 1.0f + __expf(-gg.x));
+                v[q * 8 + 2 * e + 1] *= inv * __fdividef(1.0f, 1.0f + __expf(-gg.y));
               }
             }
           } else {
@@ -319,6 +395,11 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
           store_x32<T>(dst + c * 32, v);
         }
       }
+      // O may now be overwritten by the next item's first P V.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
+      g += w.n_kv;
     }
   }
 

@@ -58,11 +58,9 @@ struct EpiParams {
   const int* positions;   // [M] token position inside its sequence
   const float2* rope;     // [max_pos][rot_dim/2] (cos, sin)
   int rot_dim;            // rotary width: the first rot_dim columns of a head (multiple of 64; 0 = head_dim)
-  // kEpiResidualNorm: the residual (fp32 [M, N], row stride N) updated in place,
-  // the 16-bit copy of the new rows times `prescale` ([M, N]) and the block
-  // sums of squares ([M, N / kNormBlock]).
-  float* res;
-  void* xcopy;
+  // kEpiResidualNorm: the residual (the fp32 output map, updated in place), the
+  // 16-bit copy of the new rows times the gains and `prescale` (the second
+  // output map) and the block sums of squares ([M, N / kNormBlock]).
   float prescale;
   float* ss_out;
   const float* norm_gain;  // [N] gains of the following RMSNorm, applied as norm_gain + norm_add
@@ -206,6 +204,13 @@ struct EpiOut {
   int y;                   // first output row of this warp's 32 rows
   int lane;
   int n16;                 // 16-bit chunks issued so far (selects the staging half)
+  // kEpiResidualNorm: the 16-bit copy's map, this warp's TMA-load barrier and
+  // its phase, the wait limit and the error word
+  const CUtensorMap* map2;
+  uint64_t* ld_bar;
+  uint32_t ld_phase;
+  uint64_t wait_ns;
+  int* err;
 };
 
 // One 32x32 chunk of 16-bit outputs at column x.
@@ -379,46 +384,77 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
     }
   } else if constexpr (EPI == kEpiResidualNorm) {
     // This thread owns row `row`, columns [n0 + 32 c, +32) for the chunks of
-    // its half (an even number of chunks: whole 64-column blocks).  Plain
-    // loads and stores: each thread moves whole 128-byte lines of its row.
+    // its half (an even number of chunks: whole 64-column blocks).  Per chunk
+    // the warp's 32 x 32 block of the residual comes in by TMA into the
+    // staging buffer (the 128-byte-swizzled layout the fp32 TMA store uses),
+    // each thread adds its row, and the new block leaves by TMA store; the
+    // 16-bit copy follows through the same buffer.
     static_assert((CH / 2) % 2 == 0, "a warp's columns must cover whole 64-column blocks");
-    const int N = p.ss_slots * kNormBlock;
     float ss = 0.0f;
+    const int r = o.lane;
 #pragma unroll 1
     for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
+      const int x = n0 + c * 32;
+      // The stage is free once the previous chunk's stores have read it.
+      if (o.lane == 0) {
+        bulk_wait_read<0>();
+        mbar_arrive_expect_tx(o.ld_bar, 32 * 32 * 4);
+        tma_load_2d(o.stage, o.map, o.ld_bar, x, o.y);
+      }
       float v[32];
       tmem_load_f32x32(taddr + c * 32, v);
-      add_bias32(v, p.bias, n0 + c * 32);
-      if (row_ok) {
-        const size_t off = static_cast<size_t>(row) * N + n0 + c * 32;
-        float4* hr = reinterpret_cast<float4*>(p.res + off);
+      add_bias32(v, p.bias, x);
+      // Our own load: wait for it even on an abort (it writes the stage).
+      if (!mbar_wait_own(o.ld_bar, o.ld_phase, o.wait_ns)) record_error(o.err, kErrTimeoutFull);
+      o.ld_phase ^= 1;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 a = hr[q];
-          v[4 * q + 0] += a.x;
-          v[4 * q + 1] += a.y;
-          v[4 * q + 2] += a.z;
-          v[4 * q + 3] += a.w;
-        }
+      for (int q = 0; q < 8; ++q) {
+        float4* a = reinterpret_cast<float4*>(o.stage + r * 128 + ((q ^ (r & 7)) << 4));
+        const float4 h = *a;
+        v[4 * q + 0] += h.x;
+        v[4 * q + 1] += h.y;
+        v[4 * q + 2] += h.z;
+        v[4 * q + 3] += h.w;
+        *a = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+      fence_proxy_async_smem_gemm();
+      __syncwarp();
+      if (o.lane == 0) {
+        tma_store_2d(o.map, o.stage, x, o.y);
+        bulk_commit();
+      }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) hr[q] = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+      const float4* g4 = reinterpret_cast<const float4*>(p.norm_gain + x);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
-        float sc[32];
-        const float4* g4 = reinterpret_cast<const float4*>(p.norm_gain + n0 + c * 32);
+      for (int q = 0; q < 8; ++q) {
+        const float4 g = __ldg(g4 + q);
+        v[4 * q + 0] *= (g.x + p.norm_add) * p.prescale;
+        v[4 * q + 1] *= (g.y + p.norm_add) * p.prescale;
+        v[4 * q + 2] *= (g.z + p.norm_add) * p.prescale;
+        v[4 * q + 3] *= (g.w + p.norm_add) * p.prescale;
+      }
+      // 16-bit copy: the first 2 KB of the stage once the fp32 store has read it.
+      if (o.lane == 0) bulk_wait_read<0>();
+      __syncwarp();
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 g = __ldg(g4 + q);
-          sc[4 * q + 0] = v[4 * q + 0] * ((g.x + p.norm_add) * p.prescale);
-          sc[4 * q + 1] = v[4 * q + 1] * ((g.y + p.norm_add) * p.prescale);
-          sc[4 * q + 2] = v[4 * q + 2] * ((g.z + p.norm_add) * p.prescale);
-          sc[4 * q + 3] = v[4 * q + 3] * ((g.w + p.norm_add) * p.prescale);
-        }
-        store_x32<T>(static_cast<T*>(p.xcopy) + off, sc);
-        if (c & 1) {
-          p.ss_out[static_cast<size_t>(row) * p.ss_slots + (n0 + c * 32) / kNormBlock] = ss;
-          ss = 0.0f;
-        }
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = Elem<T>::pack2(v[q * 8 + 0], v[q * 8 + 1]);
+        w.y = Elem<T>::pack2(v[q * 8 + 2], v[q * 8 + 3]);
+        w.z = Elem<T>::pack2(v[q * 8 + 4], v[q * 8 + 5]);
+        w.w = Elem<T>::pack2(v[q * 8 + 6], v[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(o.stage + r * 64 + ((q ^ ((r >> 1) & 3)) << 4)) = w;
+      }
+      fence_proxy_async_smem_gemm();
+      __syncwarp();
+      if (o.lane == 0) {
+        tma_store_2d(o.map2, o.stage, x, o.y);
+        bulk_commit();
+      }
+      if ((c & 1) && row_ok) {
+        p.ss_out[static_cast<size_t>(row) * p.ss_slots + x / kNormBlock] = ss;
+        ss = 0.0f;
       }
     }
   } else if constexpr (EPI == kEpiGated) {
@@ -592,7 +628,8 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
 template <int BN, int EPI, class T>
 __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, GemmShape shape, EpiParams ep, int* err) {
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                        GemmShape shape, EpiParams ep, int* err) {
   using Cfg = GemmConfig<BN>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = umma_idesc_f16kind(BM, BN, Elem<T>::kUmmaFormat);
@@ -609,6 +646,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* mma_drained = acc_empty + 3;  // the MMA warp's own ops, on its abort path
   volatile int* split_last = reinterpret_cast<volatile int*>(acc_empty + 4);  // split-K: this unit finishes the tile
+  uint64_t* epi_ld = acc_empty + 5;  // [EPI_WARPS] TMA loads of the residual (kEpiResidualNorm)
   uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
   const uint64_t wait_ns = shape.wait_ns;
 
@@ -625,6 +663,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       mbar_init(&acc_empty[j], Cfg::EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(mma_drained, 1);
+    for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(&epi_ld[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -654,6 +693,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
       tma_prefetch_desc(&tmC);
+      if constexpr (EPI == kEpiResidualNorm) tma_prefetch_desc(&tmD);
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
@@ -741,7 +781,8 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
     const int lane_group = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = lane_group * 32 + lane;
-    EpiOut o{epi_stage + (warp - 2) * Cfg::EPI_STAGE_BYTES, &tmC, 0, lane, 0};
+    EpiOut o{epi_stage + (warp - 2) * Cfg::EPI_STAGE_BYTES, &tmC, 0, lane, 0, &tmD, &epi_ld[warp - 2], 0u,
+             wait_ns, err};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {

@@ -148,7 +148,8 @@ struct Gemm2Config {
 template <int EPI, class T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS, 1)
     gemm2_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmC, GemmShape shape, EpiParams ep, int* err) {
+                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                         GemmShape shape, EpiParams ep, int* err) {
   using Cfg = Gemm2Config;
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = umma_idesc_f16kind(2 * BM, BN, Elem<T>::kUmmaFormat);
@@ -163,6 +164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* epi_ld = acc_empty + 3;  // [EPI_WARPS] TMA loads of the residual (kEpiResidualNorm)
   uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
@@ -179,6 +181,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       mbar_init(&acc_full[j], 1);
       mbar_init(&acc_empty[j], 2 * Cfg::EPI_WARPS);  // epilogue warps of both CTAs (leader's copy is used)
     }
+    for (int w = 0; w < Cfg::EPI_WARPS; ++w) mbar_init(&epi_ld[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -203,6 +206,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
       tma_prefetch_desc(&tmC);
+      if constexpr (EPI == kEpiResidualNorm) tma_prefetch_desc(&tmD);
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = pair; tile < tiles; tile += pairs) {
@@ -276,7 +280,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
     const int lane_group = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = lane_group * 32 + lane;
-    EpiOut o{epi_stage + (warp - 2) * Cfg::EPI_STAGE_BYTES, &tmC, 0, lane, 0};
+    EpiOut o{epi_stage + (warp - 2) * Cfg::EPI_STAGE_BYTES, &tmC, 0, lane, 0, &tmD, &epi_ld[warp - 2], 0u,
+             shape.wait_ns, err};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < tiles; tile += pairs) {

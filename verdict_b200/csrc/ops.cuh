@@ -51,12 +51,12 @@ static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, const 
   if (pairs > 0) shape.group_m = Gemm2Config::GROUP_M;
   if (pairs > 0) {
     const int grid2 = 2 * std::min(((M + 255) / 256) * (N / 256), pairs);
-    gemm2_tcgen05_kernel<EPI, T><<<grid2, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, s>>>(a, w_half, c, shape,
+    gemm2_tcgen05_kernel<EPI, T><<<grid2, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, s>>>(a, w_half, c, c, shape,
                                                                                              ep, word);
   } else if (bn == 256)
-    gemm_tcgen05_kernel<256, EPI, T><<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, c, shape, ep, word);
+    gemm_tcgen05_kernel<256, EPI, T><<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, s>>>(a, w, c, c, shape, ep, word);
   else if constexpr (EPI != kEpiGated)
-    gemm_tcgen05_kernel<128, EPI, T><<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, c, shape, ep, word);
+    gemm_tcgen05_kernel<128, EPI, T><<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, s>>>(a, w, c, c, shape, ep, word);
   else
     fail(VD_EINVAL, "gated GEMM needs N % 256 == 0");
 }
@@ -243,6 +243,13 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
       for (int q = 0; q < len; q += 128) tiles.push_back(AttnTile{start, len, q, 0, 0, {0, 0, 0}});
     }
     if (tiles.empty()) return;
+    // Most work first (a causal tile's keys end at its last query row), so the
+    // persistent CTAs end together.
+    std::stable_sort(tiles.begin(), tiles.end(), [causal](const AttnTile& a, const AttnTile& b) {
+      const int wa = causal ? std::min(a.seq_len, a.q_start + 128) : a.seq_len;
+      const int wb = causal ? std::min(b.seq_len, b.q_start + 128) : b.seq_len;
+      return wa > wb;
+    });
     const int64_t T = cu_seqlens_host[nseq];
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     AttnTile* d_tiles = nullptr;
@@ -260,10 +267,14 @@ extern "C" VD_API int vdk_attention_tc(const void* qkv, int64_t ld_qkv, int64_t 
     p.v_col0 = static_cast<int>(v_col0);
     p.gate_col0 = -1;
     p.tiles = d_tiles;
+    p.n_tiles = static_cast<int>(tiles.size());
+    p.heads = heads;
     p.group = heads / kv_heads;
     p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(head_dim)) * 1.4426950408889634);
     p.err = word;
-    dim3 grid(static_cast<unsigned>(tiles.size()), heads);
+    // Persistent: as many CTAs as run at once (two per SM; one at head_dim 256).
+    const int items = p.n_tiles * heads;
+    const dim3 grid(static_cast<unsigned>(std::min(items, (head_dim == 256 ? 1 : 2) * device_sms())));
     if (head_dim == 64 && f16)
       attention_tc_head_kernel<64, __half, false>
           <<<grid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, s>>>(map64, p);

@@ -633,6 +633,7 @@ struct Options {
   bool gdn_chunk = true;     // gated delta nets in 64-token chunks on the tensor cores, else token by token
   bool fuse_norm = true;     // decoders: RMSNorm fused into the residual GEMMs and the projections that read it
   bool split_k = true;       // small batches: K split over CTAs where that fills the SMs better
+  bool attn_persistent = true;  // one-head tcgen05 attention: CTAs loop over work items
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
@@ -690,6 +691,7 @@ struct vd_handle {
   CUtensorMap map_xn_s, map_attn_s, map_act_s;
   // GEMM output maps (epilogue TMA stores / reduce-adds)
   CUtensorMap out_qkv, out_act, out_act2, out_h, out_h_s, out_act_s, out_mhid;
+  CUtensorMap out_xn, out_xn_s;  // 16-bit residual copies written by the fused-norm epilogue
   // gated-delta-net workspace (hybrid stacks)
   int ld_qkv = 0;        // row stride of qkv (elements)
   // independent-options encoders: per-token option and option-invariant
@@ -1256,6 +1258,8 @@ static void alloc_workspace(vd_handle* H) {
     H->map_act_s = make_map(H->act_s, R, s.ffn, 128, f16);
     H->out_act_s = make_out_map(H->act_s, R, s.ffn, false, f16);
     H->out_h_s = make_out_map(H->h_s, R, d, true);
+    H->out_xn = make_out_map(H->xn, T, d, false, f16);
+    H->out_xn_s = make_out_map(H->xn_s, R, d, false, f16);
     if (d % kNormBlock != 0) fail(VD_ESPEC, "hidden size must be a multiple of 64");
     H->ss_a = dalloc<float>(H, T * (d / kNormBlock));
     H->ss_b = dalloc<float>(H, T * (d / kNormBlock));
@@ -1380,10 +1384,13 @@ static int gemm2_max_pairs(int num_sms) {
   return n;
 }
 
+// c: the output map; c2: the second output of kEpiResidualNorm (the 16-bit copy).
 template <int EPI, class T>
 static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, int M, const EpiParams& ep,
-                 const CUtensorMap& c) {
+                 const CUtensorMap& c, const CUtensorMap* c2 = nullptr) {
   if (M <= 0) return;
+  if (EPI == kEpiResidualNorm && c2 == nullptr) fail(VD_EINVAL, "residual-norm GEMM needs the copy's map");
+  const CUtensorMap& d = c2 ? *c2 : c;
   const int num_m = (M + 127) / 128;
   const int tiles = num_m * (L.n / L.bn);
   const int grid = std::min(tiles, H->num_sms);
@@ -1412,12 +1419,12 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
       launch(H, kind, flops, [&] {
         if (L.bn == 256) {
           gemm_tcgen05_kernel<256, EPI, T><<<grid_s, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES,
-                                              H->stream>>>(a, L.map, c, shape, ep, H->d_err);
+                                              H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
         } else {
           if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
           else
             gemm_tcgen05_kernel<128, EPI, T><<<grid_s, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
-                                                H->stream>>>(a, L.map, c, shape, ep, H->d_err);
+                                                H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
         }
       });
       return;
@@ -1440,7 +1447,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
         stall_one_cta();
         launch(H, kind, flops, [&] {
           gemm_tcgen05_kernel<128, EPI, T><<<grid1, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
-                                             H->stream>>>(a, L.map_half, c, shape, ep, H->d_err);
+                                             H->stream>>>(a, L.map_half, c, d, shape, ep, H->d_err);
         });
         return;
       }
@@ -1449,7 +1456,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
     const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
     launch(H, kind, flops, [&] {
       gemm2_tcgen05_kernel<EPI, T><<<grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, H->stream>>>(
-          a, L.map_half, c, shape, ep, H->d_err);
+          a, L.map_half, c, d, shape, ep, H->d_err);
     });
     return;
   }
@@ -1457,12 +1464,12 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
       gemm_tcgen05_kernel<256, EPI, T>
-          <<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, c, shape, ep, H->d_err);
+          <<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
     } else {
       if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
       else
         gemm_tcgen05_kernel<128, EPI, T>
-            <<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, c, shape, ep, H->d_err);
+            <<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
     }
   });
 }
@@ -1485,6 +1492,12 @@ static bool use_tc_attention(const vd_handle* H, int hd, bool causal, bool gated
 
 static int attn_tile_rows(const vd_handle* H, int hd, bool causal, bool gated = false) {
   return use_tc_attention(H, hd, causal, gated) ? 128 : 64;
+}
+
+// CTAs of the one-head tcgen05 attention for `items` work items: as many as
+// run at once (persistent, each looping over items), or one per item.
+static int attn_head_grid(const vd_handle* H, int items, int ctas_per_sm) {
+  return H->opt.attn_persistent ? std::max(1, std::min(items, ctas_per_sm * H->num_sms)) : std::max(1, items);
 }
 
 // gate_col0 >= 0: gated attention (the output is multiplied by the sigmoid of
@@ -1525,12 +1538,15 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
     tp.v_col0 = v0;
     tp.gate_col0 = -1;
     tp.tiles = H->tiles;
+    tp.n_tiles = n_tiles;
+    tp.heads = heads;
     tp.group = group;
     tp.scale_log2 = p.scale_log2;
     tp.err = H->d_err;
+    const dim3 pgrid(attn_head_grid(H, n_tiles * heads, AttnTcHeadConfig<64>::MIN_CTAS));
     launch(H, VD_K_ATTN, flops, [&] {
       attention_tc_head_kernel<64, T, false>
-          <<<grid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+          <<<pgrid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
     });
     return;
   }
@@ -1545,16 +1561,20 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
     tp.v_col0 = v0;
     tp.gate_col0 = gate_col0;
     tp.tiles = H->tiles;
+    tp.n_tiles = n_tiles;
+    tp.heads = heads;
     tp.group = group;
     tp.scale_log2 = p.scale_log2;
     tp.err = H->d_err;
     launch(H, VD_K_ATTN, flops, [&] {
       if (hd == 256)
         attention_tc_head_kernel<256, T>
-            <<<grid, AttnTcHeadConfig<256>::THREADS, AttnTcHeadConfig<256>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+            <<<attn_head_grid(H, n_tiles * heads, AttnTcHeadConfig<256>::MIN_CTAS), AttnTcHeadConfig<256>::THREADS,
+               AttnTcHeadConfig<256>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
       else
         attention_tc_head_kernel<128, T>
-            <<<grid, AttnTcHeadConfig<128>::THREADS, AttnTcHeadConfig<128>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+            <<<attn_head_grid(H, n_tiles * heads, AttnTcHeadConfig<128>::MIN_CTAS), AttnTcHeadConfig<128>::THREADS,
+               AttnTcHeadConfig<128>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
     });
     return;
   }
@@ -1883,10 +1903,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
   const float pre = H->opt.f16 ? kNormPrescale16 : 1.0f;
   const int slots = d / kNormBlock;
   const float gadd = s.norm_plus_one ? 1.0f : 0.0f;
-  auto produce = [&](float* res, void* copy, float* ss, const float* next_gain) {
+  auto produce = [&](float* ss, const float* next_gain) {
     EpiParams p = epi();
-    p.res = res;
-    p.xcopy = copy;
     p.prescale = pre;
     p.ss_out = ss;
     p.ss_slots = slots;
@@ -1933,8 +1951,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
                                                                  static_cast<T*>(H->attn_s), H->h_s, H->d_err);
       });
       if (fused) {
-        gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb,
-                                  produce(H->h_s, H->xn_s, H->ss_s, L.post_norm), H->out_h_s);
+        gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, produce(H->ss_s, L.post_norm), H->out_h_s,
+                                  &H->out_xn_s);
       } else {
         gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn_s, L.o, c.nb, epi(), H->out_h_s);
         separate_norm(H->h_s, L.post_norm, H->xn_s, c.nb);
@@ -1945,8 +1963,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
       continue;
     }
     if (fused) {
-      gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn, L.o, ntok, produce(H->h, H->xn, H->ss_b, L.post_norm),
-                                H->out_h);
+      gemm<kEpiResidualNorm, T>(H, VD_K_O, H->map_attn, L.o, ntok, produce(H->ss_b, L.post_norm), H->out_h,
+                                &H->out_xn);
     } else {
       gemm<kEpiResidual, T>(H, VD_K_O, H->map_attn, L.o, ntok, epi(), H->out_h);
       separate_norm(H->h, L.post_norm, H->xn, ntok);
@@ -1954,8 +1972,8 @@ static double decoder_forward(vd_handle* H, const Chunk& c) {
     gemm<kEpiGated, T>(H, VD_K_GATEUP, H->map_xn, L.gu, ntok, consume(epi(nullptr, s.act), H->ss_b), H->out_act);
     // The last layer's down projection feeds only the readout's final norm.
     if (fused && !last)
-      gemm<kEpiResidualNorm, T>(H, VD_K_DOWN, H->map_act, L.down, ntok,
-                                produce(H->h, H->xn, H->ss_a, H->dec[i + 1].in_norm), H->out_h);
+      gemm<kEpiResidualNorm, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, produce(H->ss_a, H->dec[i + 1].in_norm),
+                                H->out_h, &H->out_xn);
     else
       gemm<kEpiResidual, T>(H, VD_K_DOWN, H->map_act, L.down, ntok, epi(), H->out_h);
   }
@@ -2388,6 +2406,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       if (nm != "fused" && nm != "separate") fail(VD_EINVAL, "norm must be \"fused\" or \"separate\"");
       H->opt.fuse_norm = nm == "fused";
       H->opt.split_k = o.boolean_or("split_k", true);
+      H->opt.attn_persistent = o.boolean_or("attention_persistent", true);
       const long long wait_us = o.integer_or("wait_limit_us", 0);
       if (wait_us < 0 || wait_us > 60000000) fail(VD_EINVAL, "wait_limit_us must be in [0, 6e7]");
       H->opt.wait_ns = static_cast<uint64_t>(wait_us) * 1000ull;

@@ -75,7 +75,7 @@ class B200Engine(Engine):
                  act_dtype: str = "fp16", attention: str = "tc",
                  prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
                  raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", split_k: bool = True,
-                 wait_limit_us: int = 0, debug_stall_gemm: int = 0):
+                 attention_persistent: bool = True, wait_limit_us: int = 0, debug_stall_gemm: int = 0):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory).
         `norm` (decoders): "fused" folds each RMSNorm into the residual GEMM that
@@ -84,6 +84,8 @@ class B200Engine(Engine):
         `split_k`: batches of up to 1024 tokens split K over CTAs where that
         fills the GPU better (partials added in a fixed order: the same bits on
         every run, within rounding of the unsplit sum).
+        `attention_persistent`: the tcgen05 attention's CTAs loop over work
+        items (query tile x head) instead of one CTA per item.
         `wait_limit_us`: limit of the GEMM kernels' pipeline waits (0: 2 s);
         `debug_stall_gemm` (failure-path tests only): the first one-CTA GEMM of
         every call stops loading after that many k-blocks, so its wait runs out."""
@@ -102,6 +104,7 @@ class B200Engine(Engine):
                                max_markers=max_markers, output=output, act_dtype=act_dtype,
                                attention=attention, prune_last_layer=prune_last_layer, fork=fork,
                                gemm=gemm, raster_group=raster_group, gdn=gdn, norm=norm, split_k=split_k,
+                               attention_persistent=attention_persistent,
                                wait_limit_us=wait_limit_us,
                                debug_stall_gemm=debug_stall_gemm))
         err = ctypes.create_string_buffer(1024)
