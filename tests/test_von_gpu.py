@@ -84,8 +84,10 @@ def test_von_base_full_depth_vs_oracle():
 def test_von_chunking_is_bit_exact_and_windows_matter():
     spec = specs.preset("von-base", layers=6, seed=72)
     batch = von_batch(spec, 72, 9)
-    a = run(spec, batch)
-    b = run(spec, batch, max_tokens=512, max_rows=2)
+    # split_k off: small chunks would otherwise sum K in split order (exact to
+    # rounding, not to the bit).
+    a = run(spec, batch, split_k=False)
+    b = run(spec, batch, max_tokens=512, max_rows=2, split_k=False)
     np.testing.assert_array_equal(a, b)
     wide = run(dict(spec, sliding_window=4096), batch)  # a window covering every row: all layers global
     assert np.abs(wide - a)[a > -1e4].max() > 1e-4

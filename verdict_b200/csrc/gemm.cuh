@@ -103,17 +103,16 @@ __device__ __forceinline__ void scale32(float (&v)[32], float f) {
 // out and the launch ends through its abort path with kErrTimeoutFull.
 // splits > 1 (one-CTA kernel, small batches): K is split over `splits` work
 // units per output tile; each unit writes its fp32 partial tile to
-// part[split][m_pad][N], and the unit that finishes last (per-tile arrival
-// counters, left at zero) adds the partials in split order into its
-// accumulator and runs the epilogue, so the result does not depend on which
-// unit finished when.
+// part[split] (tiles * 128 * BN floats per split), and the unit that finishes
+// last (per-tile arrival counters, left at zero) adds the partials in split
+// order into its accumulator and runs the epilogue, so the result does not
+// depend on which unit finished when.
 struct GemmShape {
   int M, N, K;
   int group_m;
   uint64_t wait_ns;
   int stall_after;
   int splits;
-  int m_pad;
   float* part;
   int* counters;
 };
@@ -520,11 +519,15 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
 }
 
 // Split-K fixup of one work unit, run by the 8 epilogue warps (threads 64..319,
-// named barrier 1).  Each thread owns accumulator row `row` (padded tile row)
-// and the columns of its `half`.  The unit's partial goes to part[ks]; the
-// tile's arrival counter says whether all splits have landed; the last unit
-// adds part[0..splits) in order into its TMEM accumulator and returns true
-// (the caller then runs the epilogue on it), the others return false.
+// named barrier 1).  Each thread owns accumulator row `row_in_tile` of the
+// tile and the columns of its `half`.  The unit's partial tile goes to
+// part[split] in a layout private to this fixup, chosen so that every warp
+// access is one contiguous 128-byte line: epilogue warp slot w (TMEM lane
+// quarter w & 3, column half w >> 2) stores its 32 x 32 chunk c as
+// [column][row].  The tile's arrival counter says whether all splits have
+// landed; the last unit adds part[0..splits) in order into its TMEM
+// accumulator and returns true (the caller then runs the epilogue on it), the
+// others return false.
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 // Named barrier 1 over the epilogue warps that also ANDs a warp-uniform flag.
 __device__ __forceinline__ bool epi_bar_and(bool v) {
@@ -541,18 +544,21 @@ __device__ __forceinline__ bool epi_bar_and(bool v) {
 }
 
 template <int BN>
-__device__ __forceinline__ bool split_fixup(uint32_t taddr, const GemmShape& sh, int tile, int ks, int row, int col0,
-                                            int half, volatile int* last_flag) {
+__device__ __forceinline__ bool split_fixup(uint32_t taddr, const GemmShape& sh, int tile, int ks, int slot,
+                                            int half, int lane, volatile int* last_flag) {
   constexpr int CH = BN / 32;
-  const size_t plane = static_cast<size_t>(sh.m_pad) * sh.N;
-  float* mine = sh.part + ks * plane + static_cast<size_t>(row) * sh.N + col0;
+  constexpr int TILE_FLOATS = 128 * BN;
+  const int tiles = ((sh.M + 127) / 128) * (sh.N / BN);
+  const size_t plane = static_cast<size_t>(tiles) * TILE_FLOATS;
+  // This warp's chunks: slot-major, then chunk, then [column][row] inside.
+  const size_t base = static_cast<size_t>(tile) * TILE_FLOATS + static_cast<size_t>(slot) * (CH / 2) * 1024;
+  float* mine = sh.part + ks * plane + base;
 #pragma unroll 1
-  for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
+  for (int c = 0; c < CH / 2; ++c) {
     float v[32];
-    tmem_load_f32x32(taddr + c * 32, v);
-    float4* d = reinterpret_cast<float4*>(mine + c * 32);
+    tmem_load_f32x32(taddr + (half * CH / 2 + c) * 32, v);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    for (int j = 0; j < 32; ++j) mine[c * 1024 + j * 32 + lane] = v[j];
   }
   __threadfence();  // this thread's partial is visible before the arrival below
   epi_bar_sync();
@@ -565,25 +571,19 @@ __device__ __forceinline__ bool split_fixup(uint32_t taddr, const GemmShape& sh,
   epi_bar_sync();
   if (!*last_flag) return false;
   __threadfence();
-  const float* rowp = sh.part + static_cast<size_t>(row) * sh.N + col0;
+  const float* all = sh.part + base;
 #pragma unroll 1
-  for (int c = half * CH / 2; c < (half + 1) * CH / 2; ++c) {
+  for (int c = 0; c < CH / 2; ++c) {
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+    for (int j = 0; j < 32; ++j) v[j] = __ldcg(all + c * 1024 + j * 32 + lane);
 #pragma unroll 1
-    for (int k = 0; k < sh.splits; ++k) {
-      const float4* s4 = reinterpret_cast<const float4*>(rowp + k * plane + c * 32);
+    for (int k = 1; k < sh.splits; ++k) {
+      const float* pk = all + k * plane + c * 1024;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 t = __ldcg(s4 + q);
-        v[4 * q + 0] += t.x;
-        v[4 * q + 1] += t.y;
-        v[4 * q + 2] += t.z;
-        v[4 * q + 3] += t.w;
-      }
+      for (int j = 0; j < 32; ++j) v[j] += __ldcg(pk + j * 32 + lane);
     }
-    tmem_st32f(taddr + c * 32, v);
+    tmem_st32f(taddr + (half * CH / 2 + c) * 32, v);
   }
   tmem_wait_st();
   // Both warps of a lane quarter read the whole tile row in some epilogues.
@@ -799,7 +799,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(lane_group * 32) << 16);
       const int row = m * BM + row_in_tile;
       o.y = m * BM + lane_group * 32;
-      if (splits == 1 || split_fixup<BN>(taddr, shape, tile, u % splits, row, n * BN, half, split_last))
+      if (splits == 1 || split_fixup<BN>(taddr, shape, tile, u % splits, warp - 2, half, lane, split_last))
         gemm_epilogue<BN, EPI, T>(o, taddr, row, row < shape.M, n * BN, half, ep);
       tc_fence_before();
       __syncwarp();

@@ -1395,7 +1395,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const int tiles = num_m * (L.n / L.bn);
   const int grid = std::min(tiles, H->num_sms);
   GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M,
-                  H->opt.wait_ns, 0, 1, 0, nullptr, nullptr};
+                  H->opt.wait_ns, 0, 1, nullptr, nullptr};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
   // Failure-path tests: the first one-CTA GEMM of the call stalls its producer.
   auto stall_one_cta = [&] {
@@ -1411,7 +1411,6 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
     const int S = tiles <= H->split_cnt_n ? choose_splits(tiles, L.k / 64, H->num_sms, max_s) : 1;
     if (S > 1) {
       shape.splits = S;
-      shape.m_pad = m_pad;
       shape.part = H->split_part;
       shape.counters = H->split_cnt;
       const int grid_s = std::min(tiles * S, H->num_sms);
