@@ -400,7 +400,7 @@ def main():
                          "of its own (separate)")
     ap.add_argument("--attn-persistent", default="on", choices=["on", "off"],
                     help="tcgen05 attention: CTAs loop over work items (on) or one CTA per item (off)")
-    ap.add_argument("--split-k", default="on", choices=["on", "off"],
+    ap.add_argument("--split-k", default="off", choices=["on", "off"],
                     help="batches of <= 1024 tokens: split K over CTAs where that fills the GPU better")
     ap.add_argument("--act-dtype", default="fp16", choices=["fp16", "bf16"],
                     help="16-bit element type of activations and projection weights (fp32 accumulation and "

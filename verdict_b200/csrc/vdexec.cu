@@ -632,7 +632,7 @@ struct Options {
   int raster_group = 0;      // M tiles per GEMM raster group; 0 = the kernel's default
   bool gdn_chunk = true;     // gated delta nets in 64-token chunks on the tensor cores, else token by token
   bool fuse_norm = true;     // decoders: RMSNorm fused into the residual GEMMs and the projections that read it
-  bool split_k = true;       // small batches: K split over CTAs where that fills the SMs better
+  bool split_k = false;      // small batches: K split over CTAs where that fills the SMs better (measured slower)
   bool attn_persistent = true;  // one-head tcgen05 attention: CTAs loop over work items
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
@@ -2404,7 +2404,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       const std::string nm = o.string_or("norm", "fused");
       if (nm != "fused" && nm != "separate") fail(VD_EINVAL, "norm must be \"fused\" or \"separate\"");
       H->opt.fuse_norm = nm == "fused";
-      H->opt.split_k = o.boolean_or("split_k", true);
+      H->opt.split_k = o.boolean_or("split_k", false);
       H->opt.attn_persistent = o.boolean_or("attention_persistent", true);
       const long long wait_us = o.integer_or("wait_limit_us", 0);
       if (wait_us < 0 || wait_us > 60000000) fail(VD_EINVAL, "wait_limit_us must be in [0, 6e7]");

@@ -74,16 +74,18 @@ class B200Engine(Engine):
                  max_seq: int = 8192, max_markers: int = 16384, output: str = "logprobs",
                  act_dtype: str = "fp16", attention: str = "tc",
                  prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
-                 raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", split_k: bool = True,
+                 raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", split_k: bool = False,
                  attention_persistent: bool = True, wait_limit_us: int = 0, debug_stall_gemm: int = 0):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory).
         `norm` (decoders): "fused" folds each RMSNorm into the residual GEMM that
         produces its input and the projection that reads it; "separate" runs it
         as its own kernel.
-        `split_k`: batches of up to 1024 tokens split K over CTAs where that
-        fills the GPU better (partials added in a fixed order: the same bits on
-        every run, within rounding of the unsplit sum).
+        `split_k` (off by default: measured slower at the 9B shapes, the
+        partial tiles' round trip through memory outweighing the fuller
+        waves): batches of up to 1024 tokens split K over CTAs (partials added
+        in a fixed order: the same bits on every run, within rounding of the
+        unsplit sum).
         `attention_persistent`: the tcgen05 attention's CTAs loop over work
         items (query tile x head) instead of one CTA per item.
         `wait_limit_us`: limit of the GEMM kernels' pipeline waits (0: 2 s);
