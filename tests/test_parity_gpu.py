@@ -327,6 +327,39 @@ def test_persistent_attention_is_bit_exact(preset, lengths):
     np.testing.assert_array_equal(got[0], got[1])
 
 
+@pytest.mark.parametrize("preset", ["onejev-9b", "decider-2b", "laya-xlmr"])
+def test_attention_two_softmax_threads_per_row(preset):
+    """The tcgen05 attention with two softmax threads per query row (each
+    half of a key tile, row maxima exchanged through shared memory) against
+    the oracle and the one-thread-per-row kernel."""
+    if preset == "laya-xlmr":
+        spec = specs.preset(preset, layers=3, seed=31)
+        rng = np.random.default_rng(31)
+        rows = encoder_rows(rng, 24, spec["vocab"], lengths="lognormal-xlmr", cls_id=0, sep_id=2, id_low=5,
+                            max_len=spec["max_pos"] - 2)
+        batch = collate(rows, Layout(pad_id=spec["pad_id"]))
+        batch.qtype[:] = rng.integers(0, 3, size=batch.b)
+        ref = EncoderOracle(spec).infer(batch)
+    else:
+        spec, batch = decoder_case(preset, 2, 7, seed=31, max_len=1500)
+        ref = DecoderOracle(spec).infer(batch)
+    got = {}
+    for spr in (1, 2):
+        eng = B200Engine(spec, max_tokens=16384, max_rows=64, max_seq=4096, attention_threads_per_row=spr)
+        try:
+            got[spr] = engine_logprobs(eng, batch)
+        finally:
+            eng.close()
+        if preset == "laya-xlmr":
+            live = ref > -1e4
+            assert np.all(got[spr][~live] == -1e4)
+            assert np.abs(got[spr][live] - ref[live]).max() / max(1.0, float(np.abs(ref[live]).max())) <= ENC_TOL
+        else:
+            assert_decoder_parity(got[spr], ref, batch.nopts)
+    live = got[1] > -1e4
+    assert np.abs(got[1] - got[2])[live].max() <= 5e-3
+
+
 def test_last_layer_on_slot_rows_is_bit_exact():
     """Running the last layer's O projection and MLP on the slot rows only
     changes no bit of the result (each row's arithmetic is the same)."""

@@ -52,9 +52,13 @@ struct AttnTcHeadParams {
   int* err;
 };
 
-template <int HD_>
+// SPR: softmax threads per query row (1: four softmax warps, a thread holds its
+// row's 64 scores of a key tile; 2: eight softmax warps, two per TMEM lane
+// quarter, each holding 32 of the 64 scores and half of O's columns, the row
+// max exchanged through shared memory).
+template <int HD_, int SPR_ = 1>
 struct AttnTcHeadConfig {
-  static constexpr int HD = HD_, BM = 128, BN = 64;
+  static constexpr int HD = HD_, BM = 128, BN = 64, SPR = SPR_;
   static constexpr int ATOMS = HD / 64;             // 64-column swizzle atoms per row
   static constexpr int Q_ATOM = BM * 64 * 2;        // [128 rows x 64 cols] 16-bit, 16 KB
   static constexpr int KV_ATOM = BN * 64 * 2;       // [64 rows x 64 cols], 8 KB
@@ -64,17 +68,35 @@ struct AttnTcHeadConfig {
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * KV_BYTES;
-  static constexpr int SMEM_BYTES = 1024 + BAR_OFF + 256;
-  static constexpr int THREADS = 224;
+  // SPR = 2 exchange: [3][4 quarters][32 rows][2 parts] floats; regions 0 and 1
+  // carry the row maxima of even and odd key tiles, region 2 the row sums.
+  static constexpr int XCH_OFF = BAR_OFF + 256;
+  static constexpr int SMEM_BYTES = 1024 + XCH_OFF + (SPR == 2 ? 3 * 4 * 32 * 2 * 4 : 0);
+  static constexpr int THREADS = 96 + 128 * SPR;
   static constexpr uint32_t TMEM_COLS = HD == 256 ? 512 : 256;  // S/P [0, 128), O [128, 128 + HD)
   static constexpr int MIN_CTAS = HD == 256 ? 1 : 2;
   static constexpr float RESCALE_THRESHOLD = 8.0f;
 };
 
-template <int HD, class T, bool CAUSAL = true>
-__global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
+// Named barrier (ids 2..5, one per TMEM lane quarter) over the two softmax
+// warps of a row pair, ANDing a warp-uniform flag.
+__device__ __forceinline__ bool pair_bar_and(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %2, 0;\n\t"
+      "bar.red.and.pred p, %1, 64, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
+template <int HD, class T, bool CAUSAL = true, int SPR = 1>
+__global__ void __launch_bounds__(AttnTcHeadConfig<HD, SPR>::THREADS, AttnTcHeadConfig<HD, SPR>::MIN_CTAS)
     attention_tc_head_kernel(const __grid_constant__ CUtensorMap tm_qkv64, AttnTcHeadParams p) {
-  using C = AttnTcHeadConfig<HD>;
+  using C = AttnTcHeadConfig<HD, SPR>;
   constexpr uint32_t FMT = Elem<T>::kUmmaFormat;
   constexpr uint32_t IDESC_S = umma_idesc_f16kind(128, 64, FMT);                // A, B K-major
   constexpr uint32_t IDESC_PV = umma_idesc_f16kind(128, HD, FMT) | (1u << 16);   // B (V) MN-major
@@ -129,12 +151,12 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 4 * SPR);
     }
     mbar_init(pv_done, 1);
     mbar_init(o_final, 1);
     mbar_init(q_free, 1);
-    mbar_init(o_free, 4);
+    mbar_init(o_free, 4 * SPR);
     mbar_init(mma_drained, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -274,11 +296,18 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
       }
     }
   } else {
-    // Softmax warps 3..6: query row r of the tile, TMEM lane quarter warp & 3.
+    // Softmax warps 3 .. 3 + 4 SPR - 1: query row r of the tile (TMEM lane
+    // quarter warp & 3); with SPR = 2 the warp's `part` (0 or 1) selects key
+    // columns [32 part, +32) of each S tile and O columns [part HD/2, +HD/2).
+    constexpr int KC = C::BN / SPR;  // scores per thread and key tile
+    constexpr int OC = HD / SPR;     // O columns per thread
     const int quarter = warp & 3;
+    const int part = SPR == 2 ? (warp - 3) >> 2 : 0;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t o_tm = tmem + lane_base + 128;
+    const uint32_t o_tm = tmem + lane_base + 128 + part * OC;
+    float* xch = reinterpret_cast<float*>(smem + C::XCH_OFF);  // SPR = 2 exchange
+    const int bar_id = 2 + quarter;
     uint32_t g = 0, qi = 0;
     bool ok = true;
     for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++qi) {
@@ -291,30 +320,43 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
         const int b = gj & 1;
         const uint32_t s_tm = tmem + lane_base + b * 64;
         const bool in_pre = j < w.n_pre;
-        const int kv0 = (in_pre ? j : j - w.n_pre) * C::BN;  // key index inside its segment
+        const int kv0 = (in_pre ? j : j - w.n_pre) * C::BN + part * KC;  // first key of this thread's columns
         const int seg_len = in_pre ? tile.pre_len : tile.seq_len;
         const int causal_row = (in_pre || !CAUSAL) ? 0x7fffffff : q_row;
-        if (!mbar_wait(&s_full[b], (gj >> 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+        bool got = mbar_wait(&s_full[b], (gj >> 1) & 1, abort_flag, p.err, kErrTimeoutAccFull);
+        float mx = -INFINITY;
+        uint32_t sr[KC];
+        if (got) {
+          tc_fence_after();
+          const bool need_mask = kv0 + KC > seg_len || (CAUSAL && !in_pre && kv0 + KC > tile.q_start);
+#pragma unroll
+          for (int c = 0; c < KC / 32; ++c) tmem_ld32_nowait(s_tm + part * KC + c * 32, sr + c * 32);
+          tmem_wait_ld();
+          if (need_mask) {
+#pragma unroll
+            for (int i = 0; i < KC; ++i) {
+              const int kv = kv0 + i;
+              if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
+              mx = fmaxf(mx, __uint_as_float(sr[i]));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < KC; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+          }
+        }
+        if constexpr (SPR == 2) {
+          // The pair agrees on going on (a barrier must not wait for a warp
+          // that left) and swaps its halves' maxima; the exchange slot
+          // alternates with the tile so a partner still reading never sees
+          // the next tile's value.
+          float* slot = xch + (((gj & 1) * 4 + quarter) * 32 + lane) * 2;
+          slot[part] = mx;
+          got = pair_bar_and(bar_id, __all_sync(0xffffffffu, got));
+          mx = fmaxf(mx, slot[part ^ 1]);
+        }
+        if (!got) {
           ok = false;
           break;
-        }
-        tc_fence_after();
-        const bool need_mask = kv0 + C::BN > seg_len || (CAUSAL && !in_pre && kv0 + C::BN > tile.q_start);
-        uint32_t sr[64];
-        tmem_ld32_nowait(s_tm + 0, sr + 0);
-        tmem_ld32_nowait(s_tm + 32, sr + 32);
-        tmem_wait_ld();
-        float mx = -INFINITY;
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const int kv = kv0 + i;
-            if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(sr[i]));
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
         }
         const float m_tile = mx * p.scale_log2;
         const bool raise = m_tile > m_run + C::RESCALE_THRESHOLD;
@@ -323,7 +365,7 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
         const float alpha = raise ? fast_exp2(m_run - m_new) : 1.0f;
         float rs = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < KC / 32; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
@@ -332,18 +374,20 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
             rs += e0 + e1;
             pk[i >> 1] = Elem<T>::pack2(e0, e1);
           }
-          tmem_st16(s_tm + c * 16, pk);
+          tmem_st16(s_tm + part * (KC / 2) + c * 16, pk);
         }
         // A raised max rescales the O rows accumulated so far, once P(j - 1) V
         // has landed (P(j) V cannot start before this warp's p_full arrival).
         if (warp_raise && j > 0) {
-          if (!mbar_wait(pv_done, (gj - 1) & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+          bool done = mbar_wait(pv_done, (gj - 1) & 1, abort_flag, p.err, kErrTimeoutAccFull);
+          if constexpr (SPR == 2) done = pair_bar_and(bar_id, __all_sync(0xffffffffu, done));
+          if (!done) {
             ok = false;
             break;
           }
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < HD / 32; ++c) {
+          for (int c = 0; c < OC / 32; ++c) {
             float v[32];
             tmem_load_f32x32(o_tm + c * 32, v);
 #pragma unroll
@@ -358,20 +402,31 @@ __global__ void __launch_bounds__(224, AttnTcHeadConfig<HD>::MIN_CTAS)
         l_run = l_run * alpha + rs;
         m_run = m_new;
       }
-      if (!ok || !mbar_wait(o_final, qi & 1, abort_flag, p.err, kErrTimeoutAccFull)) {
+      if (!ok) break;
+      bool fin = mbar_wait(o_final, qi & 1, abort_flag, p.err, kErrTimeoutAccFull);
+      float l_tot = l_run;
+      if constexpr (SPR == 2) {
+        // Region 2: the next use of this slot is the next item's sum, with at
+        // least one max exchange (a barrier) in between.
+        float* slot = xch + ((2 * 4 + quarter) * 32 + lane) * 2;
+        slot[part] = l_run;
+        fin = pair_bar_and(bar_id, __all_sync(0xffffffffu, fin));
+        l_tot += slot[part ^ 1];
+      }
+      if (!fin) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
       const size_t tok = static_cast<size_t>(tile.seq_start + q_row);
-      T* dst = static_cast<T*>(p.out) + tok * p.ld_out + w.head * C::HD;
+      T* dst = static_cast<T*>(p.out) + tok * p.ld_out + w.head * C::HD + part * OC;
       const T* gate = p.gate_col0 >= 0
-                          ? static_cast<const T*>(p.qkv) + tok * p.ld_qkv + p.gate_col0 + w.head * C::HD
+                          ? static_cast<const T*>(p.qkv) + tok * p.ld_qkv + p.gate_col0 + w.head * C::HD + part * OC
                           : nullptr;
       const bool live = q_row < tile.seq_len;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < OC / 32; ++c) {
         float v[32];
         tmem_load_f32x32(o_tm + c * 32, v);
         if (live) {

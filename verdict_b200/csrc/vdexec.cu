@@ -634,6 +634,7 @@ struct Options {
   bool fuse_norm = true;     // decoders: RMSNorm fused into the residual GEMMs and the projections that read it
   bool split_k = false;      // small batches: K split over CTAs where that fills the SMs better (measured slower)
   bool attn_persistent = true;  // one-head tcgen05 attention: CTAs loop over work items
+  int attn_spr = 1;             // one-head tcgen05 attention: softmax threads per query row (1 or 2)
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
@@ -1329,6 +1330,13 @@ static void set_attn_attr() {
              "attention smem attribute");
 }
 
+template <int HD, class T, bool C, int SPR>
+static void set_attn_head_attr() {
+  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<HD, T, C, SPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnTcHeadConfig<HD, SPR>::SMEM_BYTES),
+             "tcgen05 one-head attention smem attribute");
+}
+
 template <class T>
 static void init_kernel_attrs_t() {
   set_gemm_attr<256, kEpiStore, T>();
@@ -1351,15 +1359,12 @@ static void init_kernel_attrs_t() {
   cuda_check(cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnTcConfig::SMEM_BYTES),
              "tcgen05 attention smem attribute");
-  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<128, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  AttnTcHeadConfig<128>::SMEM_BYTES),
-             "tcgen05 one-head attention smem attribute");
-  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<256, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  AttnTcHeadConfig<256>::SMEM_BYTES),
-             "tcgen05 one-head attention smem attribute");
-  cuda_check(cudaFuncSetAttribute(attention_tc_head_kernel<64, T, false>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcHeadConfig<64>::SMEM_BYTES),
-             "tcgen05 one-head attention smem attribute");
+  set_attn_head_attr<128, T, true, 1>();
+  set_attn_head_attr<256, T, true, 1>();
+  set_attn_head_attr<64, T, false, 1>();
+  set_attn_head_attr<128, T, true, 2>();
+  set_attn_head_attr<256, T, true, 2>();
+  set_attn_head_attr<64, T, false, 2>();
   cuda_check(cudaFuncSetAttribute(gdn_chunk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   GdnChunkConfig::SMEM_BYTES),
              "chunked gated delta net smem attribute");
@@ -1499,6 +1504,13 @@ static int attn_head_grid(const vd_handle* H, int items, int ctas_per_sm) {
   return H->opt.attn_persistent ? std::max(1, std::min(items, ctas_per_sm * H->num_sms)) : std::max(1, items);
 }
 
+template <int HD, class T, bool CAUSAL, int SPR>
+static void launch_attn_head(vd_handle* H, const AttnTcHeadParams& tp, int items) {
+  using C = AttnTcHeadConfig<HD, SPR>;
+  attention_tc_head_kernel<HD, T, CAUSAL, SPR>
+      <<<attn_head_grid(H, items, C::MIN_CTAS), C::THREADS, C::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+}
+
 // gate_col0 >= 0: gated attention (the output is multiplied by the sigmoid of
 // the gate columns of qkv), served by the warp-level kernel.
 template <class T>
@@ -1542,10 +1554,9 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
     tp.group = group;
     tp.scale_log2 = p.scale_log2;
     tp.err = H->d_err;
-    const dim3 pgrid(attn_head_grid(H, n_tiles * heads, AttnTcHeadConfig<64>::MIN_CTAS));
     launch(H, VD_K_ATTN, flops, [&] {
-      attention_tc_head_kernel<64, T, false>
-          <<<pgrid, AttnTcHeadConfig<64>::THREADS, AttnTcHeadConfig<64>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+      if (H->opt.attn_spr == 2) launch_attn_head<64, T, false, 2>(H, tp, n_tiles * heads);
+      else launch_attn_head<64, T, false, 1>(H, tp, n_tiles * heads);
     });
     return;
   }
@@ -1566,14 +1577,14 @@ static void attention(vd_handle* H, double flops, int n_tiles, int heads, int hd
     tp.scale_log2 = p.scale_log2;
     tp.err = H->d_err;
     launch(H, VD_K_ATTN, flops, [&] {
-      if (hd == 256)
-        attention_tc_head_kernel<256, T>
-            <<<attn_head_grid(H, n_tiles * heads, AttnTcHeadConfig<256>::MIN_CTAS), AttnTcHeadConfig<256>::THREADS,
-               AttnTcHeadConfig<256>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
-      else
-        attention_tc_head_kernel<128, T>
-            <<<attn_head_grid(H, n_tiles * heads, AttnTcHeadConfig<128>::MIN_CTAS), AttnTcHeadConfig<128>::THREADS,
-               AttnTcHeadConfig<128>::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+      const int items = n_tiles * heads;
+      if (hd == 256) {
+        if (H->opt.attn_spr == 2) launch_attn_head<256, T, true, 2>(H, tp, items);
+        else launch_attn_head<256, T, true, 1>(H, tp, items);
+      } else {
+        if (H->opt.attn_spr == 2) launch_attn_head<128, T, true, 2>(H, tp, items);
+        else launch_attn_head<128, T, true, 1>(H, tp, items);
+      }
     });
     return;
   }
@@ -2406,6 +2417,8 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.fuse_norm = nm == "fused";
       H->opt.split_k = o.boolean_or("split_k", false);
       H->opt.attn_persistent = o.boolean_or("attention_persistent", true);
+      H->opt.attn_spr = static_cast<int>(o.integer_or("attention_threads_per_row", 1));
+      if (H->opt.attn_spr != 1 && H->opt.attn_spr != 2) fail(VD_EINVAL, "attention_threads_per_row must be 1 or 2");
       const long long wait_us = o.integer_or("wait_limit_us", 0);
       if (wait_us < 0 || wait_us > 60000000) fail(VD_EINVAL, "wait_limit_us must be in [0, 6e7]");
       H->opt.wait_ns = static_cast<uint64_t>(wait_us) * 1000ull;
