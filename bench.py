@@ -72,12 +72,11 @@ BERT_WORKLOAD = ("BERT-base-shaped marker-head encoder decisions (laya: 12 layer
 XLMR_WORKLOAD = ("XLM-R-base-shaped marker-head encoder decisions (laya-multilingual: 12 layers, d=768, 12 heads, "
                  "GELU 3072, vocab 250002), lengths clip(lognormal(4.5,0.6),8,512), K~U{2..6}, ids U[5,250002)")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from a
-# full-size, one-pass ncu capture of this bench's first timed gate/up launch, and the token count that
-# launch had, per (model, GEMM kernel).  Operand re-reads dominate it, so it is reported as measured,
-# not scaled; other shapes report null.
-GATEUP_TRAFFIC = {("onejev-9b", "2sm"): (3.9676e9 + 0.8232e9, 33763),
-                  ("onejev-9b", "1sm"): (3.3236e9 + 0.8198e9, 33763)}
+# DRAM traffic of one gate/up GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu
+# capture of a small case (`--layers 2 --batch 32`, layer 0 of the second warm-up batch) and the
+# tokens that launch had, per (model, GEMM kernel); the bench scales it to its own launch by tokens.
+# Weight re-streaming grows a little faster than the tokens, so the scaled figure is a lower estimate.
+GATEUP_TRAFFIC = {("onejev-9b", "2sm"): (1.2605e9 + 0.3454e9, 14316)}
 
 
 def peaks():
@@ -548,14 +547,18 @@ def main():
     achieved = gu_flops / (gu_launch_ms / 1e3) / 1e12
     gemm_ms = acc_ms[:4].sum() / prof_steps
     gemm_tf = acc_fl[:4].sum() / (acc_ms[:4].sum() / 1e3) / 1e12
-    traffic, traffic_tokens = GATEUP_TRAFFIC.get((args.model, args.gemm), (None, None))
+    cap_bytes, cap_tokens = GATEUP_TRAFFIC.get((args.model, args.gemm), (None, None))
+    traffic = cap_bytes * tokens_per_step / cap_tokens if cap_bytes and not encoder else None
     roofline = {
         "kernel": ("gemm2_tcgen05_kernel<store> (FFN up projection with GELU, CTA pairs)" if encoder else
                    "gemm2_tcgen05_kernel<gated> (gate/up projection, CTA pairs)" if args.gemm == "2sm"
                    else "gemm_tcgen05_kernel<256,gated> (gate/up projection)"),
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
         "peak_source": f"{pk_kind} bf16_tflops_sustained (dense fp16 and bf16 share the tensor-core rate)",
-        "traffic": traffic, "traffic_tokens": traffic_tokens,
+        "traffic": traffic,
+        "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of a {cap_tokens}-token gate/up launch "
+                           f"({cap_bytes / 1e9:.3f} GB), scaled by tokens to this launch; a lower estimate (weights "
+                           "re-streamed once per 4,096-row raster group)") if traffic else None,
         # 16-bit A rows in, the ffn-wide output (act(g)*u, or act(x W) for the
         # encoders' up projection) out, and W once (2 ffn rows when gated).
         "algorithmic_bytes_per_launch": 2.0 * tokens_per_step * (spec["hidden"] + spec["ffn"])
