@@ -24,6 +24,9 @@ Printed JSON (rank 0, one line):
          residual stream; --act-dtype bf16 keeps them in bf16
   sweep  the same workload at 1, 8 and 256 decisions per step (one GPU):
          decisions/s, mean and p99 step time, SM clock
+  models the other presets' workloads on the same GPU (decider-2b batch 64,
+         onejev-27b batch 8 (~35k tokens), laya-xlmr batch 128, laya-bert batch
+         32): decisions/s, step time, p99
   cpu_baseline  the CPU oracle (fp32 numpy restatement of the reference's CPU
          executor path) on a bounded sample of the workload's decisions, every
          layer timed, on all of this host's cores
@@ -314,6 +317,64 @@ def encoder_cpu_sample(spec, batch):
     return n / dt, f"{n} rows, all {spec['layers']} layers", dt / n
 
 
+# Other model shapes measured in the same run (one GPU): (preset, decisions per step, timed steps).
+EXTRA_MODELS = (("decider-2b", 64, 5), ("onejev-27b", 8, 3), ("laya-xlmr", 128, 10), ("laya-bert", 32, 10))
+
+
+def other_model(model, per_step, steps, warmup, seed, local):
+    """decisions/s of another preset's workload on this GPU (device-resident
+    inputs, CUDA events; encoder steps after a 256 MB L2 flush, outside their
+    events), with the step time, p99, tokens per step and SM clock."""
+    import torch
+    from verdict_b200 import spec as specs
+    from verdict_b200.engine import B200Engine
+    from verdict_b200.synth import with_labels
+    spec = with_labels(specs.preset(model))
+    encoder = spec["arch"] == "encoder"
+    batches = make_batches(0, warmup + steps, per_step, spec["vocab"], seed + 7, workload_of(spec, "choice"),
+                           spec.get("pad_id", 0), LENGTHS.get(model, "lognormal-9b"))
+    eng = B200Engine(spec, device=local, max_tokens=max(4096, max(int(b.real_len().sum()) for b in batches)),
+                     max_rows=max(per_step, 8), max_seq=max(4096, max(int(b.real_len().max()) for b in batches)))
+    try:
+        width = eng.width if not encoder else max(b.k for b in batches)
+        dev = [{k: torch.from_numpy(np.ascontiguousarray(v)).to(f"cuda:{local}") for k, v in dict(
+            input_ids=b.input_ids, marker_pos=b.marker_pos, marker_mask=b.marker_mask.astype(np.uint8),
+            nopts=b.nopts, qtype=b.qtype).items()} for b in batches]
+        out = torch.empty(per_step, width, device=f"cuda:{local}", dtype=torch.float32)
+        stream = torch.cuda.ExternalStream(eng.stream())
+
+        def run(j):
+            b = batches[j]
+            eng.infer_device(b.b, b.l, b.k, {k: v.data_ptr() for k, v in dev[j].items()}, b.real_len(),
+                             out.data_ptr(), width)
+
+        for j in range(warmup):
+            run(j)
+        eng.sync()
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}") if encoder else None
+        ck = Clocks(local)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps)]
+        with torch.cuda.stream(stream):
+            for i in range(steps):
+                if flush is not None:
+                    flush.fill_(i & 0xFF)
+                ev[2 * i].record(stream)
+                run(warmup + i)
+                ev[2 * i + 1].record(stream)
+        eng.sync()
+        cl = ck.stop()
+        ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps)]
+        total = float(np.sum(ms)) if encoder else ev[0].elapsed_time(ev[-1])
+        return {"workload": workload_text(model), "decisions_per_step": per_step, "steps": steps, "warmup": warmup,
+                "value": per_step * steps / (total / 1e3), "unit": UNIT, "ms_per_step": total / steps,
+                "p99_ms": float(np.percentile(ms, 99)),
+                "mean_tokens_per_step": float(np.mean([b.real_len().sum() for b in batches[warmup:]])),
+                "sm_mhz": cl.get("sm_mhz"), "reasons": cl.get("reasons"),
+                "l2": "flushed before each step" if encoder else "not flushed (steps stream GBs of weights)"}
+    finally:
+        eng.close()
+
+
 def run_reference(args, world, rank):
     """The reference arm: the reference executor's CPU path (fp32), as the
     oracle port, on all of this host's cores; rank 0 only.  A decoder step is
@@ -406,6 +467,8 @@ def main():
     ap.add_argument("--act-dtype", default="fp16", choices=["fp16", "bf16"],
                     help="16-bit element type of activations and projection weights (fp32 accumulation and "
                          "residual stream either way)")
+    ap.add_argument("--no-extra-models", dest="extra_models", action="store_false",
+                    help="skip the other presets' lines (decider-2b, onejev-27b, laya-xlmr, laya-bert; one GPU)")
     ap.add_argument("--no-sweep", dest="sweep", action="store_false",
                     help="skip the concurrency sweep (decoders: 1, 8 and 256 decisions per step)")
     ap.add_argument("--raster-group", type=int, default=0,
@@ -670,6 +733,11 @@ def main():
                               "mean_tokens_per_step": float(np.mean([b.real_len().sum() for b in bs[3:]])),
                               "sm_mhz": cl.get("sm_mhz"), "reasons": cl.get("reasons")}
 
+    eng.close()
+    models = None
+    if args.extra_models and world == 1 and args.model == "onejev-9b" and args.workload == "choice":
+        models = {m: other_model(m, per_step, n, 3, args.seed, local) for m, per_step, n in EXTRA_MODELS}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if encoder:
@@ -700,10 +768,10 @@ def main():
                               "no flush: each step streams every layer's weights (GBs) and the activations, far "
                               "above the 126 MB L2")},
             "e2e": e2e, "gpu_launches": int(launches), "clocks": clk, "roofline": roofline, "sweep": sweep,
+            "models": models,
             "kernels": kern, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
