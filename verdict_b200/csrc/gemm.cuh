@@ -115,6 +115,7 @@ struct GemmShape {
   int splits;
   float* part;
   int* counters;
+  int l2_hints;  // pair kernel: L2 evict-last for A, evict-first for W loads
 };
 
 // GELU in its exact form, x * Phi(x), Phi the standard normal CDF, with erf

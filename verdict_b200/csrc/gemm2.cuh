@@ -92,6 +92,27 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// The same load with an L2 eviction-priority hint (a createpolicy value).
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                      int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
@@ -207,6 +228,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       tma_prefetch_desc(&tmB);
       tma_prefetch_desc(&tmC);
       if constexpr (EPI == kEpiResidualNorm) tma_prefetch_desc(&tmD);
+      const uint64_t pol_keep = l2_policy_evict_last(), pol_stream = l2_policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = pair; tile < tiles; tile += pairs) {
@@ -218,8 +240,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, shape.wait_ns)) goto producer_done;
           if (leader) mbar_arrive_expect_tx(&full[stage], Cfg::PAIR_STAGE_BYTES);
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * BK, ya);
-          tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb);
+          if (shape.l2_hints) {
+            // A rows are reused by every N tile of the raster group (long reuse
+            // distance): keep them; W tiles are used by the group's M tiles at
+            // about the same time and then not again for a while.
+            tma_load_2d_pair_hint(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * BK, ya, pol_keep);
+            tma_load_2d_pair_hint(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb, pol_stream);
+          } else {
+            tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * BK, ya);
+            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;

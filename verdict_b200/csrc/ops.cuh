@@ -46,7 +46,7 @@ static void ops_gemm_launch_t(const CUtensorMap& a, const CUtensorMap& w, const 
                               int* word, int sms) {
   const int tiles = ((M + 127) / 128) * (N / bn);
   const int grid = std::min(tiles, sms);
-  GemmShape shape{M, N, K, GemmConfig<256>::GROUP_M, 0, 0, 1, nullptr, nullptr};
+  GemmShape shape{M, N, K, GemmConfig<256>::GROUP_M, 0, 0, 1, nullptr, nullptr, 0};
   const int pairs = bn == 256 ? gemm2_max_pairs(sms) : 0;
   if (pairs > 0) shape.group_m = Gemm2Config::GROUP_M;
   if (pairs > 0) {

@@ -635,6 +635,7 @@ struct Options {
   bool split_k = false;      // small batches: K split over CTAs where that fills the SMs better (measured slower)
   bool attn_persistent = true;  // one-head tcgen05 attention: CTAs loop over work items
   int attn_spr = 1;             // one-head tcgen05 attention: softmax threads per query row (1 or 2)
+  bool l2_hints = false;        // pair GEMM: L2 eviction hints on its TMA loads
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
@@ -1400,7 +1401,7 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
   const int tiles = num_m * (L.n / L.bn);
   const int grid = std::min(tiles, H->num_sms);
   GemmShape shape{M, L.n, L.k, H->opt.raster_group > 0 ? H->opt.raster_group : GemmConfig<256>::GROUP_M,
-                  H->opt.wait_ns, 0, 1, nullptr, nullptr};
+                  H->opt.wait_ns, 0, 1, nullptr, nullptr, H->opt.l2_hints ? 1 : 0};
   const double flops = 2.0 * M * static_cast<double>(L.n) * L.k;
   // Failure-path tests: the first one-CTA GEMM of the call stalls its producer.
   auto stall_one_cta = [&] {
@@ -2417,6 +2418,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.fuse_norm = nm == "fused";
       H->opt.split_k = o.boolean_or("split_k", false);
       H->opt.attn_persistent = o.boolean_or("attention_persistent", true);
+      H->opt.l2_hints = o.boolean_or("l2_hints", false);
       H->opt.attn_spr = static_cast<int>(o.integer_or("attention_threads_per_row", 1));
       if (H->opt.attn_spr != 1 && H->opt.attn_spr != 2) fail(VD_EINVAL, "attention_threads_per_row must be 1 or 2");
       const long long wait_us = o.integer_or("wait_limit_us", 0);
