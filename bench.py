@@ -22,11 +22,11 @@ Printed JSON (rank 0, one line):
   dtype  fp16 (default): activations and projection weights in fp16 (the bf16
          checkpoint values are exact in fp16), fp32 accumulation and fp32
          residual stream; --act-dtype bf16 keeps them in bf16
-  sweep  the same workload at 1, 8 and 256 decisions per step (one GPU):
-         decisions/s, mean and p99 step time, SM clock
-  models the other presets' workloads on the same GPU (decider-2b batch 64,
-         onejev-27b batch 8 (~35k tokens), laya-xlmr batch 128, laya-bert batch
-         32): decisions/s, step time, p99
+  sweep  the same workload at 1, 8 and 256 decisions per step per GPU:
+         whole-job decisions/s (slowest rank), mean and p99 step time, SM clock
+  models the other presets' workloads, each rank its own shard (decider-2b
+         batch 64, onejev-27b batch 8 (~35k tokens), laya-xlmr batch 128,
+         laya-bert batch 32 per GPU): whole-job decisions/s, step time, p99
   cpu_baseline  the CPU oracle (fp32 numpy restatement of the reference's CPU
          executor path) on a bounded sample of the workload's decisions, every
          layer timed, on all of this host's cores
@@ -321,17 +321,19 @@ def encoder_cpu_sample(spec, batch):
 EXTRA_MODELS = (("decider-2b", 64, 5), ("onejev-27b", 8, 3), ("laya-xlmr", 128, 10), ("laya-bert", 32, 10))
 
 
-def other_model(model, per_step, steps, warmup, seed, local):
-    """decisions/s of another preset's workload on this GPU (device-resident
-    inputs, CUDA events; encoder steps after a 256 MB L2 flush, outside their
-    events), with the step time, p99, tokens per step and SM clock."""
+def other_model(model, per_step, steps, warmup, seed, local, rank, world, barrier, reduce_max):
+    """decisions/s of another preset's workload over all ranks (each its own
+    shard of `per_step` decisions per step on its GPU; device-resident inputs,
+    CUDA events, the slowest rank's time; encoder steps after a 256 MB L2
+    flush, outside their events), with the step time, p99, tokens per step and
+    this GPU's SM clock."""
     import torch
     from verdict_b200 import spec as specs
     from verdict_b200.engine import B200Engine
     from verdict_b200.synth import with_labels
     spec = with_labels(specs.preset(model))
     encoder = spec["arch"] == "encoder"
-    batches = make_batches(0, warmup + steps, per_step, spec["vocab"], seed + 7, workload_of(spec, "choice"),
+    batches = make_batches(rank, warmup + steps, per_step, spec["vocab"], seed + 7, workload_of(spec, "choice"),
                            spec.get("pad_id", 0), LENGTHS.get(model, "lognormal-9b"))
     eng = B200Engine(spec, device=local, max_tokens=max(4096, max(int(b.real_len().sum()) for b in batches)),
                      max_rows=max(per_step, 8), max_seq=max(4096, max(int(b.real_len().max()) for b in batches)))
@@ -362,13 +364,14 @@ def other_model(model, per_step, steps, warmup, seed, local):
                 run(warmup + i)
                 ev[2 * i + 1].record(stream)
         eng.sync()
+        barrier()
         cl = ck.stop()
         ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps)]
-        total = float(np.sum(ms)) if encoder else ev[0].elapsed_time(ev[-1])
-        return {"workload": workload_text(model), "decisions_per_step": per_step, "steps": steps, "warmup": warmup,
-                "value": per_step * steps / (total / 1e3), "unit": UNIT, "ms_per_step": total / steps,
-                "p99_ms": float(np.percentile(ms, 99)),
-                "mean_tokens_per_step": float(np.mean([b.real_len().sum() for b in batches[warmup:]])),
+        total = reduce_max(float(np.sum(ms)) if encoder else ev[0].elapsed_time(ev[-1]))
+        return {"workload": workload_text(model), "decisions_per_step_per_gpu": per_step, "steps": steps,
+                "warmup": warmup, "value": whole_job_rate(per_step * steps, world, total), "unit": UNIT,
+                "ms_per_step": total / steps, "p99_ms": reduce_max(float(np.percentile(ms, 99))),
+                "mean_tokens_per_step_per_gpu": float(np.mean([b.real_len().sum() for b in batches[warmup:]])),
                 "sm_mhz": cl.get("sm_mhz"), "reasons": cl.get("reasons"),
                 "l2": "flushed before each step" if encoder else "not flushed (steps stream GBs of weights)"}
     finally:
@@ -470,9 +473,9 @@ def main():
                     help="16-bit element type of activations and projection weights (fp32 accumulation and "
                          "residual stream either way)")
     ap.add_argument("--no-extra-models", dest="extra_models", action="store_false",
-                    help="skip the other presets' lines (decider-2b, onejev-27b, laya-xlmr, laya-bert; one GPU)")
+                    help="skip the other presets' lines (decider-2b, onejev-27b, laya-xlmr, laya-bert)")
     ap.add_argument("--no-sweep", dest="sweep", action="store_false",
-                    help="skip the concurrency sweep (decoders: 1, 8 and 256 decisions per step)")
+                    help="skip the concurrency sweep (decoders: 1, 8 and 256 decisions per step per GPU)")
     ap.add_argument("--raster-group", type=int, default=0,
                     help="M tiles per GEMM raster group (0: the kernels' default)")
     args = ap.parse_args()
@@ -507,7 +510,7 @@ def main():
     # Concurrency sweep (decoders, one GPU): other batch sizes of the same
     # workload, timed after the headline, each from its own seeded batches.
     sweep_sets = {}
-    if args.sweep and not encoder and world == 1 and args.workload == "choice":
+    if args.sweep and not encoder and args.workload == "choice":
         for c, steps in SWEEP:
             sweep_sets[c] = make_batches(rank, 3 + steps, c, spec["vocab"], args.seed + 1000 + c,
                                          workload_of(spec, args.workload), spec.get("pad_id", 0),
@@ -727,19 +730,22 @@ def main():
                     run_c(3 + i)
                     ev[2 * i + 1].record(stream)
             eng.sync()
+            barrier()
             cl = ck.stop()
             ms = [ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(len(bs) - 3)]
-            sweep[f"c{c}"] = {"decisions_per_step": c, "steps": len(ms), "warmup": 3,
-                              "value": c * len(ms) / (ev[0].elapsed_time(ev[-1]) / 1e3), "unit": UNIT,
-                              "ms_per_step": float(np.mean(ms)), "p99_ms": float(np.percentile(ms, 99)),
-                              "ms_per_decision": float(np.mean(ms)) / c,
-                              "mean_tokens_per_step": float(np.mean([b.real_len().sum() for b in bs[3:]])),
+            span = reduce_max(ev[0].elapsed_time(ev[-1]))
+            sweep[f"c{c}"] = {"decisions_per_step_per_gpu": c, "steps": len(ms), "warmup": 3,
+                              "value": whole_job_rate(c * len(ms), world, span), "unit": UNIT,
+                              "ms_per_step": span / len(ms), "p99_ms": reduce_max(float(np.percentile(ms, 99))),
+                              "ms_per_decision": span / len(ms) / c,
+                              "mean_tokens_per_step_per_gpu": float(np.mean([b.real_len().sum() for b in bs[3:]])),
                               "sm_mhz": cl.get("sm_mhz"), "reasons": cl.get("reasons")}
 
     eng.close()
     models = None
-    if args.extra_models and world == 1 and args.model == "onejev-9b" and args.workload == "choice":
-        models = {m: other_model(m, per_step, n, 3, args.seed, local) for m, per_step, n in EXTRA_MODELS}
+    if args.extra_models and args.model == "onejev-9b" and args.workload == "choice":
+        models = {m: other_model(m, per_step, n, 3, args.seed, local, rank, world, barrier, reduce_max)
+                  for m, per_step, n in EXTRA_MODELS}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
