@@ -360,6 +360,34 @@ def test_attention_two_softmax_threads_per_row(preset):
     assert np.abs(got[1] - got[2])[live].max() <= 5e-3
 
 
+@pytest.mark.parametrize("act_dtype", ["fp16", "bf16"])
+def test_results_do_not_depend_on_earlier_batches(act_dtype):
+    """A smaller batch after a larger one: the rows between the two batches'
+    token counts hold the earlier batch's data, and the last GEMM tile and the
+    masked keys of attention read them as padding.  They must not leak into
+    the answer (or grow into inf over 40 layers): the same bits as a fresh
+    handle, at full depth."""
+    spec = with_labels(specs.preset("onejev-9b", seed=37))
+    big = fixed_rows(spec, 37, (2100, 1700, 900, 333))
+    small = fixed_rows(spec, 38, (300, 129))
+    kw = dict(max_tokens=8192, max_rows=8, max_seq=4096, act_dtype=act_dtype)
+    eng = B200Engine(spec, **kw)
+    try:
+        engine_logprobs(eng, big)
+        after = engine_logprobs(eng, small)
+        engine_logprobs(eng, big)
+        again = engine_logprobs(eng, small)
+    finally:
+        eng.close()
+    fresh = B200Engine(spec, **kw)
+    try:
+        first = engine_logprobs(fresh, small)
+    finally:
+        fresh.close()
+    np.testing.assert_array_equal(after, first)
+    np.testing.assert_array_equal(again, first)
+
+
 def test_last_layer_on_slot_rows_is_bit_exact():
     """Running the last layer's O projection and MLP on the slot rows only
     changes no bit of the result (each row's arithmetic is the same)."""

@@ -407,14 +407,19 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
       // Our own load: wait for it even on an abort (it writes the stage).
       if (!mbar_wait_own(o.ld_bar, o.ld_phase, o.wait_ns)) record_error(o.err, kErrTimeoutFull);
       o.ld_phase ^= 1;
+      // Rows past M (the padding of the last tile, which the box store covers)
+      // keep their residual and get a zero copy: their accumulators come from
+      // stale A rows, and without a norm they would grow layer after layer
+      // into the keys that attention masks (0 * inf = NaN).
+      const float keep = row_ok ? 1.0f : 0.0f;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float4* a = reinterpret_cast<float4*>(o.stage + r * 128 + ((q ^ (r & 7)) << 4));
         const float4 h = *a;
-        v[4 * q + 0] += h.x;
-        v[4 * q + 1] += h.y;
-        v[4 * q + 2] += h.z;
-        v[4 * q + 3] += h.w;
+        v[4 * q + 0] = row_ok ? v[4 * q + 0] + h.x : h.x;
+        v[4 * q + 1] = row_ok ? v[4 * q + 1] + h.y : h.y;
+        v[4 * q + 2] = row_ok ? v[4 * q + 2] + h.z : h.z;
+        v[4 * q + 3] = row_ok ? v[4 * q + 3] + h.w : h.w;
         *a = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       }
       fence_proxy_async_smem_gemm();
@@ -426,13 +431,14 @@ __device__ __forceinline__ void gemm_epilogue(EpiOut& o, uint32_t taddr, int row
 #pragma unroll
       for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
       const float4* g4 = reinterpret_cast<const float4*>(p.norm_gain + x);
+      const float pre = p.prescale * keep;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 g = __ldg(g4 + q);
-        v[4 * q + 0] *= (g.x + p.norm_add) * p.prescale;
-        v[4 * q + 1] *= (g.y + p.norm_add) * p.prescale;
-        v[4 * q + 2] *= (g.z + p.norm_add) * p.prescale;
-        v[4 * q + 3] *= (g.w + p.norm_add) * p.prescale;
+        v[4 * q + 0] *= (g.x + p.norm_add) * pre;
+        v[4 * q + 1] *= (g.y + p.norm_add) * pre;
+        v[4 * q + 2] *= (g.z + p.norm_add) * pre;
+        v[4 * q + 3] *= (g.w + p.norm_add) * pre;
       }
       // 16-bit copy: the first 2 KB of the stage once the fp32 store has read it.
       if (o.lane == 0) bulk_wait_read<0>();

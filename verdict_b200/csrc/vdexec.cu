@@ -1231,6 +1231,12 @@ static void alloc_workspace(vd_handle* H) {
   cuda_check(cudaMemset(H->qkv, 0, static_cast<size_t>(T) * qkvw * 2), "clear qkv workspace");
   H->attn = dalloc<uint16_t>(H, T * attw);
   H->act = dalloc<uint16_t>(H, T * actw);
+  // Rows past a batch's tokens are read as padding by the GEMMs (the last
+  // tile) and attention (masked keys): start them at zero, never garbage.
+  cuda_check(cudaMemset(H->h, 0, static_cast<size_t>(T) * d * 4), "clear residual workspace");
+  cuda_check(cudaMemset(H->xn, 0, static_cast<size_t>(T) * d * 2), "clear normalised-input workspace");
+  cuda_check(cudaMemset(H->attn, 0, static_cast<size_t>(T) * attw * 2), "clear attention workspace");
+  cuda_check(cudaMemset(H->act, 0, static_cast<size_t>(T) * actw * 2), "clear activation workspace");
   H->tokens = dalloc<int>(H, T);
   H->positions = dalloc<int>(H, T);
   H->seq_id = dalloc<int>(H, T);
@@ -1255,6 +1261,10 @@ static void alloc_workspace(vd_handle* H) {
     H->xn_s = dalloc<uint16_t>(H, R * d);
     H->attn_s = dalloc<uint16_t>(H, R * attw);
     H->act_s = dalloc<uint16_t>(H, R * s.ffn);
+    cuda_check(cudaMemset(H->h_s, 0, static_cast<size_t>(R) * d * 4), "clear slot-row workspace");
+    cuda_check(cudaMemset(H->xn_s, 0, static_cast<size_t>(R) * d * 2), "clear slot-row workspace");
+    cuda_check(cudaMemset(H->attn_s, 0, static_cast<size_t>(R) * attw * 2), "clear slot-row workspace");
+    cuda_check(cudaMemset(H->act_s, 0, static_cast<size_t>(R) * s.ffn * 2), "clear slot-row workspace");
     H->map_xn_s = make_map(H->xn_s, R, d, 128, f16);
     H->map_attn_s = make_map(H->attn_s, R, attw, 128, f16);
     H->map_act_s = make_map(H->act_s, R, s.ffn, 128, f16);
