@@ -1,7 +1,8 @@
 """CPU oracle for the decision-model forward — TEST INFRASTRUCTURE ONLY.
 
 Only `tests/`, `__graft_entry__.smoke()` and the CPU-baseline leg of `bench.py`
-may import this package, and only as the checker or the timed CPU baseline.
+may import this package, and only as the reference answer the tests compare
+with or as the timed CPU baseline.
 Nothing on the product path (the `verdict_b200` package and its CUDA library)
 imports, links or calls it.
 

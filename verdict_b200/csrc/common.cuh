@@ -148,7 +148,7 @@ __device__ __forceinline__ bool mbar_wait_own(uint64_t* bar, uint32_t parity, ui
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled bulk tensor copies; no cluster multicast anywhere in this build)
+// TMA (tiled bulk tensor copies; no cluster multicast on any load in this library)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

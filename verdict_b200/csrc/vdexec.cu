@@ -2453,7 +2453,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
     cuda_check(cudaSetDevice(device), "cudaSetDevice");
     cudaDeviceProp prop;
     cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
-    if (prop.major != 10) fail(VD_ECUDA, std::string("this build targets sm_100a (B200); device is ") + prop.name);
+    if (prop.major != 10) fail(VD_ECUDA, std::string("this library targets sm_100a (B200); device is ") + prop.name);
     H->num_sms = prop.multiProcessorCount;
     cuda_check(cudaStreamCreateWithFlags(&H->stream, cudaStreamNonBlocking), "stream");
     init_kernel_attrs();

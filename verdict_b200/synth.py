@@ -1,6 +1,6 @@
 """Deterministic synthetic checkpoints and seeded synthetic decision workloads.
 
-No weights ship with this build, so every model is random-initialised from a seed.
+No weights ship with this package, so every model is random-initialised from a seed.
 The generator is counter-based: element `i` of tensor `name` is a pure function of
 (seed, name, i).  The C library evaluates the same function on the GPU
 (`csrc/synth.cuh`), the numpy code below evaluates it on the host, and both
