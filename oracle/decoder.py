@@ -127,9 +127,9 @@ class DecoderOracle:
     drops them afterwards, so a 40-layer 9B model runs in ~2 GB of host memory."""
 
     def __init__(self, spec: dict, layers: int | None = None, cache_layers: bool = True, store16: bool = False):
-        """store16 (hybrid stacks): round every activation the GPU path keeps in
-        16 bits to fp16 where it is stored (norm outputs, projection outputs,
-        q/k/v after their norms, mixer outputs, the MLP activation); the
+        """store16: round every activation the GPU path keeps in 16 bits to fp16
+        where it is stored (norm outputs, projection outputs, q/k/v after their
+        norms and rotary embedding, mixer outputs, the MLP activation); the
         residual stream stays fp32.  It measures what fp16 storage alone does to
         the outputs, as a yardstick for the GPU's deviation from fp32."""
         self.spec = spec
@@ -250,7 +250,8 @@ class DecoderOracle:
         w = self.layer(i)
         hd, nq, nkv = s["head_dim"], s["heads"], s["kv_heads"]
         n = h.shape[0]
-        x = rmsnorm(h, w["input_layernorm.weight"], s["rms_eps"], s["norm_plus_one"])
+        st = (lambda t: t.astype(np.float16).astype(np.float32)) if self.store16 else (lambda t: t)
+        x = st(rmsnorm(h, w["input_layernorm.weight"], s["rms_eps"], s["norm_plus_one"]))
         q = x @ w["self_attn.q_proj.weight"].T
         k = x @ w["self_attn.k_proj.weight"].T
         v = x @ w["self_attn.v_proj.weight"].T
@@ -264,15 +265,15 @@ class DecoderOracle:
         if s["qk_norm"]:
             q = rmsnorm(q, w["self_attn.q_norm.weight"], s["rms_eps"], s["norm_plus_one"])
             k = rmsnorm(k, w["self_attn.k_norm.weight"], s["rms_eps"], s["norm_plus_one"])
-        q = apply_rope(q, cos, sin)
-        k = apply_rope(k, cos, sin)
-        a = attention(q, k, v, causal=True).reshape(n, nq * hd)
+        q = st(apply_rope(q, cos, sin))
+        k = st(apply_rope(k, cos, sin))
+        a = st(attention(q, k, st(v), causal=True).reshape(n, nq * hd))
         h = h + a @ w["self_attn.o_proj.weight"].T
-        x = rmsnorm(h, w["post_attention_layernorm.weight"], s["rms_eps"], s["norm_plus_one"])
+        x = st(rmsnorm(h, w["post_attention_layernorm.weight"], s["rms_eps"], s["norm_plus_one"]))
         g = x @ w["mlp.gate_proj.weight"].T
         u = x @ w["mlp.up_proj.weight"].T
         act = silu(g) if s["act"] == "silu" else gelu_tanh(g)
-        h = h + (act * u) @ w["mlp.down_proj.weight"].T
+        h = h + st(act * u) @ w["mlp.down_proj.weight"].T
         return h.astype(np.float32)
 
     def hidden(self, ids: np.ndarray) -> np.ndarray:

@@ -280,7 +280,7 @@ def test_tensor_core_attention_matches_warp_level_attention(mode):
 @pytest.mark.parametrize("preset,act_dtype", [("onejev-9b", "fp16"), ("onejev-9b", "bf16"), ("decider-2b", "fp16")])
 def test_fused_rmsnorm_matches_separate_rmsnorm(preset, act_dtype):
     """RMSNorm fused into the residual GEMMs (row statistics, 16-bit copy of
-    the residual) and into the consuming projections (gains folded into W, row
+    the residual times the gains) and into the consuming projections (row
     factor in the epilogue) against the standalone norm kernel: the same
     decisions, both near the oracle."""
     spec, batch = decoder_case(preset, 3, 6, seed=19, max_len=1200)
