@@ -337,12 +337,15 @@ __global__ void __launch_bounds__(AttnTcHeadConfig<HD, SPR>::THREADS, AttnTcHead
             for (int i = 0; i < KC; ++i) {
               const int kv = kv0 + i;
               if (kv >= seg_len || kv > causal_row) sr[i] = __float_as_uint(-INFINITY);
-              mx = fmaxf(mx, __uint_as_float(sr[i]));
             }
-          } else {
-#pragma unroll
-            for (int i = 0; i < KC; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
           }
+          // Eight independent max chains (the maximum is exact in any order).
+          float m8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(sr[i]);
+#pragma unroll
+          for (int i = 8; i < KC; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sr[i]));
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         }
         if constexpr (SPR == 2) {
           // The pair agrees on going on (a barrier must not wait for a warp
@@ -363,7 +366,8 @@ __global__ void __launch_bounds__(AttnTcHeadConfig<HD, SPR>::THREADS, AttnTcHead
         const bool warp_raise = __any_sync(0xffffffffu, raise);
         const float m_new = raise ? m_tile : m_run;
         const float alpha = raise ? fast_exp2(m_run - m_new) : 1.0f;
-        float rs = 0.0f;
+        // Row sum in four independent chains, added pairwise at the end.
+        float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int c = 0; c < KC / 32; ++c) {
           uint32_t pk[16];
@@ -371,11 +375,12 @@ __global__ void __launch_bounds__(AttnTcHeadConfig<HD, SPR>::THREADS, AttnTcHead
           for (int i = 0; i < 32; i += 2) {
             const float e0 = fast_exp2(__uint_as_float(sr[c * 32 + i]) * p.scale_log2 - m_new);
             const float e1 = fast_exp2(__uint_as_float(sr[c * 32 + i + 1]) * p.scale_log2 - m_new);
-            rs += e0 + e1;
+            rs4[(i >> 1) & 3] += e0 + e1;
             pk[i >> 1] = Elem<T>::pack2(e0, e1);
           }
           tmem_st16(s_tm + part * (KC / 2) + c * 16, pk);
         }
+        const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
         // A raised max rescales the O rows accumulated so far, once P(j - 1) V
         // has landed (P(j) V cannot start before this warp's p_full arrival).
         if (warp_raise && j > 0) {
