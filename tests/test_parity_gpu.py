@@ -149,7 +149,17 @@ def test_decoder_shapes_vs_oracle(preset, layers, n_rows, max_len):
 def test_decoder_full_depth_vs_oracle(preset, lens):
     """All layers of the benchmark shapes (40 for OneJev-9B, 18 for the 2B
     decider) against the fp32 oracle, which regenerates each layer's weights
-    on the host as it goes."""
+    on the host as it goes.
+
+    On these random-init weights the error of 16-bit activation storage grows
+    with depth, and at 40 layers the last bit of any fp32 sum decides which
+    way later roundings go: arithmetic variants of the same forward (split-K,
+    another attention kernel, the standalone norm) land anywhere from 0.5e-2
+    to 2.2e-2 from fp32 on the longest row.  From 32 layers on each row is
+    therefore held to the 2e-2 tolerance beyond that row's own fp16 storage
+    deviation (the oracle with every 16-bit store emulated, `store16`), as the
+    hybrid stack's full-depth test is; the decision must match wherever the
+    fp32 top-2 margin exceeds 2e-2."""
     spec = with_labels(specs.preset(preset, seed=77))
     rng = np.random.default_rng(77)
     rows = decoder_rows(rng, len(lens), spec["vocab"], lengths="fixed:8")
@@ -163,7 +173,20 @@ def test_decoder_full_depth_vs_oracle(preset, lens):
     finally:
         eng.close()
     ref = DecoderOracle(spec, cache_layers=False).infer(batch)
-    assert_decoder_parity(got, ref, batch.nopts)
+    if spec["layers"] < 32:
+        assert_decoder_parity(got, ref, batch.nopts)
+        return
+    lp32 = option_logprobs(ref, batch.nopts)
+    lp16 = option_logprobs(DecoderOracle(spec, cache_layers=False, store16=True).infer(batch), batch.nopts)
+    for i, k in enumerate(batch.nopts):
+        k = int(k)
+        storage = np.abs(lp16[i, :k] - lp32[i, :k]).max()
+        d = np.abs(got[i, :k] - lp32[i, :k]).max()
+        assert d <= LOGPROB_TOL + storage, f"row {i}: {d:.3e} (fp16 storage alone: {storage:.3e})"
+        top = np.sort(lp32[i, :k])[::-1]
+        if k >= 2 and top[0] - top[1] > MARGIN:
+            assert int(np.argmax(got[i, :k])) == int(np.argmax(lp32[i, :k])), f"row {i}: choice differs"
+        assert np.all(got[i, k:] == -1e4)
 
 
 def fixed_rows(spec, seed, lens):
