@@ -465,6 +465,9 @@ def main():
                     help="tcgen05 attention: CTAs loop over work items (on) or one CTA per item (off)")
     ap.add_argument("--l2-hints", default="off", choices=["on", "off"],
                     help="pair GEMM: L2 evict-last hints on A loads and evict-first on W loads")
+    ap.add_argument("--pdl", default="on", choices=["on", "off"],
+                    help="GEMM and attention kernels set up under the previous kernel's tail (programmatic "
+                         "dependent launch)")
     ap.add_argument("--attn-spr", type=int, default=1, choices=[1, 2],
                     help="tcgen05 attention: softmax threads per query row")
     ap.add_argument("--split-k", default="off", choices=["on", "off"],
@@ -524,7 +527,7 @@ def main():
                      gemm=args.gemm, raster_group=args.raster_group, gdn=args.gdn, act_dtype=args.act_dtype,
                      norm=args.norm, split_k=args.split_k == "on",
                      attention_persistent=args.attn_persistent == "on", attention_threads_per_row=args.attn_spr,
-                     l2_hints=args.l2_hints == "on")
+                     l2_hints=args.l2_hints == "on", pdl=args.pdl == "on")
     # Declared state-prefix lengths travel with the batch (host metadata, like real_len).
     shared = args.workload == "shared-prefix"
     width = eng.width if not encoder else max(b.k for b in batches)  # encoders: one logit per marker slot
@@ -766,7 +769,7 @@ def main():
                        "model": args.model,
                        "layers": spec["layers"], "attention": args.attention, "fork": args.fork, "gemm": args.gemm,
                        "norm": args.norm, "split_k": args.split_k, "attn_persistent": args.attn_persistent,
-                       "attn_threads_per_row": args.attn_spr, "l2_hints": args.l2_hints,
+                       "attn_threads_per_row": args.attn_spr, "l2_hints": args.l2_hints, "pdl": args.pdl,
                        "raster_group": args.raster_group or "default",
                        **({"gdn": args.gdn} if specs.is_hybrid(spec) else {}),
                        "decisions_per_step_per_gpu": args.batch, "mean_tokens_per_step": tokens_per_step,

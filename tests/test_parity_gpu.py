@@ -329,6 +329,31 @@ def test_fused_rmsnorm_matches_separate_rmsnorm(preset, act_dtype):
 
 
 @pytest.mark.parametrize("preset,lengths", [("onejev-9b", None), ("decider-2b", None), ("laya-xlmr", "lognormal-xlmr")])
+def test_programmatic_launch_is_bit_exact(preset, lengths):
+    """GEMM and attention kernels launched with programmatic stream
+    serialization (each sets up under the previous kernel's tail, then waits
+    for its results) against plain stream order: the same bits."""
+    if lengths is None:
+        spec, batch = decoder_case(preset, 3, 9, seed=37, max_len=1500)
+    else:
+        spec = specs.preset(preset, layers=3, seed=37)
+        rng = np.random.default_rng(37)
+        rows = encoder_rows(rng, 40, spec["vocab"], lengths=lengths, cls_id=0, sep_id=2, id_low=5,
+                            max_len=spec["max_pos"] - 2)
+        batch = collate(rows, Layout(pad_id=spec["pad_id"]))
+    got = []
+    for pdl in (True, False):
+        eng = B200Engine(spec, max_tokens=16384, max_rows=64, max_seq=4096, pdl=pdl)
+        try:
+            got.append(engine_logprobs(eng, batch))
+            got.append(engine_logprobs(eng, batch))  # a second call on the same handle
+        finally:
+            eng.close()
+    for g in got[1:]:
+        np.testing.assert_array_equal(got[0], g)
+
+
+@pytest.mark.parametrize("preset,lengths", [("onejev-9b", None), ("decider-2b", None), ("laya-xlmr", "lognormal-xlmr")])
 def test_persistent_attention_is_bit_exact(preset, lengths):
     """The tcgen05 attention with CTAs looping over work items (default) and
     with one CTA per item run the same arithmetic per item: the same bits."""

@@ -228,6 +228,10 @@ __global__ void __launch_bounds__(AttnTcHeadConfig<HD, SPR>::THREADS, AttnTcHead
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched with programmatic stream serialization: the set-up above ran
+  // under the previous kernel's tail; its results are needed from here on.
+  pdl_wait_prior();
+  pdl_trigger_next();
 
   // Key tiles are counted over all of this CTA's items (g): K / V stage and
   // S / P buffer g & 1, phase (g >> 1) & 1.  Items are counted by qi.

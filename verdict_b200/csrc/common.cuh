@@ -186,6 +186,15 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it in the stream is still
+// running.  It sets up its barriers and tensor memory, then waits here for
+// that kernel's results before it touches global memory; without such a
+// predecessor the wait returns at once.  Triggering lets the next kernel do
+// the same as soon as SMs free up.
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 or bf16 inputs per the
 // instruction descriptor, fp32 accumulate).
 __device__ __forceinline__ void umma_f16kind(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,

@@ -682,6 +682,11 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization, the set-up above ran
+  // under the previous kernel's tail.  Every role waits for that kernel's
+  // results before it touches global memory; the producer first loads the
+  // weight tiles of its first k-blocks, which do not depend on it.
+  pdl_trigger_next();
 
   const int num_m = (shape.M + BM - 1) / BM;
   const int num_n = shape.N / BN;
@@ -701,6 +706,21 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       tma_prefetch_desc(&tmB);
       tma_prefetch_desc(&tmC);
       if constexpr (EPI == kEpiResidualNorm) tma_prefetch_desc(&tmD);
+      // The first unit's first `pre` stages (all free: nothing has used them
+      // yet) get their W tiles now and their A rows after the wait; not on
+      // the failure-path test's stalled launches.
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < units && shape.stall_after == 0) {
+        int m, n, kb0, kb1;
+        tile_coords(blockIdx.x / splits, num_m, num_n, shape.group_m, m, n);
+        k_range(blockIdx.x, kb0, kb1);
+        pre = kb1 - kb0 < STAGES ? kb1 - kb0 : STAGES;
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], Cfg::STAGE_BYTES);
+          tma_load_2d(sB + i * Cfg::B_BYTES, &tmB, &full[i], (kb0 + i) * BK, n * BN);
+        }
+      }
+      pdl_wait_prior();
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
@@ -712,9 +732,10 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
           if (shape.stall_after > 0 && issued == shape.stall_after) goto producer_drain;
           ++issued;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, wait_ns)) goto producer_done;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          const bool w_loaded = u == static_cast<int>(blockIdx.x) && kb - kb0 < pre;
+          if (!w_loaded) mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * BK, m * BM);
-          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * BK, n * BN);
+          if (!w_loaded) tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * BK, n * BN);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -783,6 +804,7 @@ __global__ void __launch_bounds__(GemmConfig<BN>::THREADS, 1)
       }
     }
   } else {
+    pdl_wait_prior();
     // Epilogue warps 2..9: warp w drains TMEM lanes 32*(w%4).. (the quarter it
     // may access) and column half (w-2)/4 of the tile.
     const int lane_group = warp & 3;

@@ -215,6 +215,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
   cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization, the set-up above ran
+  // under the previous kernel's tail.  Every role waits for that kernel's
+  // results before it touches global memory; the producer first loads the
+  // weight tiles of its first k-blocks, which do not depend on it.
+  pdl_trigger_next();
 
   const int num_m = (shape.M + 2 * BM - 1) / (2 * BM);
   const int num_n = shape.N / BN;
@@ -229,6 +234,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       tma_prefetch_desc(&tmC);
       if constexpr (EPI == kEpiResidualNorm) tma_prefetch_desc(&tmD);
       const uint64_t pol_keep = l2_policy_evict_last(), pol_stream = l2_policy_evict_first();
+      // The first tile's first `pre` stages (all free: nothing has used them
+      // yet) get their W halves now and their A rows after the wait.
+      int pre = 0;
+      if (pair < tiles) {
+        int m, n;
+        tile_coords(pair, num_m, num_n, shape.group_m, m, n);
+        const int yb = n * BN + static_cast<int>(rank) * (BN / 2);
+        pre = kblocks < STAGES ? kblocks : STAGES;
+        for (int kb = 0; kb < pre; ++kb) {
+          if (leader) mbar_arrive_expect_tx(&full[kb], Cfg::PAIR_STAGE_BYTES);
+          const uint32_t bar = mapa_shared(smem_u32(&full[kb]), 0);
+          if (shape.l2_hints) tma_load_2d_pair_hint(sB + kb * Cfg::B_BYTES, &tmB, bar, kb * BK, yb, pol_stream);
+          else tma_load_2d_pair(sB + kb * Cfg::B_BYTES, &tmB, bar, kb * BK, yb);
+        }
+      }
+      pdl_wait_prior();
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = pair; tile < tiles; tile += pairs) {
@@ -238,17 +259,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
         const int yb = n * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, abort_flag, err, kErrTimeoutEmpty, shape.wait_ns)) goto producer_done;
-          if (leader) mbar_arrive_expect_tx(&full[stage], Cfg::PAIR_STAGE_BYTES);
+          const bool w_loaded = tile == pair && kb < pre;
+          if (leader && !w_loaded) mbar_arrive_expect_tx(&full[stage], Cfg::PAIR_STAGE_BYTES);
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
           if (shape.l2_hints) {
             // A rows are reused by every N tile of the raster group (long reuse
             // distance): keep them; W tiles are used by the group's M tiles at
             // about the same time and then not again for a while.
             tma_load_2d_pair_hint(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * BK, ya, pol_keep);
-            tma_load_2d_pair_hint(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb, pol_stream);
+            if (!w_loaded) tma_load_2d_pair_hint(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb, pol_stream);
           } else {
             tma_load_2d_pair(sA + stage * Cfg::A_BYTES, &tmA, bar, kb * BK, ya);
-            tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb);
+            if (!w_loaded) tma_load_2d_pair(sB + stage * Cfg::B_BYTES, &tmB, bar, kb * BK, yb);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -305,6 +327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2Config::THREADS
       }
     }
   } else {
+    pdl_wait_prior();
     // Epilogue warps 2..9 of this CTA's 128 accumulator rows (TMEM lane
     // quarter warp % 4, column half (warp - 2) / 4).
     const int lane_group = warp & 3;

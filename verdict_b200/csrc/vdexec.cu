@@ -636,6 +636,7 @@ struct Options {
   bool attn_persistent = true;  // one-head tcgen05 attention: CTAs loop over work items
   int attn_spr = 1;             // one-head tcgen05 attention: softmax threads per query row (1 or 2)
   bool l2_hints = false;        // pair GEMM: L2 eviction hints on its TMA loads
+  bool pdl = true;           // GEMMs and attention start their set-up under the previous kernel's tail
   uint64_t wait_ns = 0;      // limit of the GEMM kernels' barrier waits (0: the compiled 2 s)
   int debug_stall = 0;       // failure-path tests: the first one-CTA GEMM of a call stalls after this many k-blocks
 };
@@ -753,6 +754,29 @@ static cudaEvent_t prof_event(vd_handle* H) {
     H->prof_pool.push_back(e);
   }
   return H->prof_pool[H->prof_next++];
+}
+
+// The GEMM and attention kernels: launched with programmatic stream
+// serialization (option "pdl"), a kernel's CTAs may start on SMs the
+// previous kernel has left while it finishes; each waits for the previous
+// kernel's results (griddepcontrol.wait) before it touches global memory.
+template <class... KArgs, class... Args>
+static void launch_k(vd_handle* H, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+  if (!H->opt.pdl) {
+    kernel<<<grid, block, smem, H->stream>>>(std::forward<Args>(args)...);
+    return;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = H->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "kernel launch");
 }
 
 // Every forward kernel goes through here: counts launches and algorithmic FLOPs
@@ -1433,13 +1457,13 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
       stall_one_cta();
       launch(H, kind, flops, [&] {
         if (L.bn == 256) {
-          gemm_tcgen05_kernel<256, EPI, T><<<grid_s, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES,
-                                              H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
+          launch_k(H, gemm_tcgen05_kernel<256, EPI, T>, grid_s, GemmConfig<256>::THREADS,
+                   GemmConfig<256>::SMEM_BYTES, a, L.map, c, d, shape, ep, H->d_err);
         } else {
           if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
           else
-            gemm_tcgen05_kernel<128, EPI, T><<<grid_s, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
-                                                H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
+            launch_k(H, gemm_tcgen05_kernel<128, EPI, T>, grid_s, GemmConfig<128>::THREADS,
+                     GemmConfig<128>::SMEM_BYTES, a, L.map, c, d, shape, ep, H->d_err);
         }
       });
       return;
@@ -1461,8 +1485,8 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
         const int grid1 = static_cast<int>(std::min<int64_t>(t128, H->num_sms));
         stall_one_cta();
         launch(H, kind, flops, [&] {
-          gemm_tcgen05_kernel<128, EPI, T><<<grid1, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES,
-                                             H->stream>>>(a, L.map_half, c, d, shape, ep, H->d_err);
+          launch_k(H, gemm_tcgen05_kernel<128, EPI, T>, grid1, GemmConfig<128>::THREADS,
+                   GemmConfig<128>::SMEM_BYTES, a, L.map_half, c, d, shape, ep, H->d_err);
         });
         return;
       }
@@ -1470,21 +1494,21 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
     if (H->opt.raster_group <= 0) shape.group_m = Gemm2Config::GROUP_M;
     const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
     launch(H, kind, flops, [&] {
-      gemm2_tcgen05_kernel<EPI, T><<<grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, H->stream>>>(
-          a, L.map_half, c, d, shape, ep, H->d_err);
+      launch_k(H, gemm2_tcgen05_kernel<EPI, T>, grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, a, L.map_half,
+               c, d, shape, ep, H->d_err);
     });
     return;
   }
   stall_one_cta();
   launch(H, kind, flops, [&] {
     if (L.bn == 256) {
-      gemm_tcgen05_kernel<256, EPI, T>
-          <<<grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
+      launch_k(H, gemm_tcgen05_kernel<256, EPI, T>, grid, GemmConfig<256>::THREADS, GemmConfig<256>::SMEM_BYTES, a,
+               L.map, c, d, shape, ep, H->d_err);
     } else {
       if constexpr (EPI == kEpiGated) fail(VD_ESPEC, "gated GEMM needs 256-wide tiles");
       else
-        gemm_tcgen05_kernel<128, EPI, T>
-            <<<grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, H->stream>>>(a, L.map, c, d, shape, ep, H->d_err);
+        launch_k(H, gemm_tcgen05_kernel<128, EPI, T>, grid, GemmConfig<128>::THREADS, GemmConfig<128>::SMEM_BYTES, a,
+                 L.map, c, d, shape, ep, H->d_err);
     }
   });
 }
@@ -1518,8 +1542,8 @@ static int attn_head_grid(const vd_handle* H, int items, int ctas_per_sm) {
 template <int HD, class T, bool CAUSAL, int SPR>
 static void launch_attn_head(vd_handle* H, const AttnTcHeadParams& tp, int items) {
   using C = AttnTcHeadConfig<HD, SPR>;
-  attention_tc_head_kernel<HD, T, CAUSAL, SPR>
-      <<<attn_head_grid(H, items, C::MIN_CTAS), C::THREADS, C::SMEM_BYTES, H->stream>>>(H->map_qkv64, tp);
+  launch_k(H, attention_tc_head_kernel<HD, T, CAUSAL, SPR>, attn_head_grid(H, items, C::MIN_CTAS), C::THREADS,
+           C::SMEM_BYTES, H->map_qkv64, tp);
 }
 
 // gate_col0 >= 0: gated attention (the output is multiplied by the sigmoid of
@@ -2429,6 +2453,7 @@ extern "C" VD_API int vd_open(const char* model, int device, const char* opts_js
       H->opt.split_k = o.boolean_or("split_k", false);
       H->opt.attn_persistent = o.boolean_or("attention_persistent", true);
       H->opt.l2_hints = o.boolean_or("l2_hints", false);
+      H->opt.pdl = o.boolean_or("pdl", true);
       H->opt.attn_spr = static_cast<int>(o.integer_or("attention_threads_per_row", 1));
       if (H->opt.attn_spr != 1 && H->opt.attn_spr != 2) fail(VD_EINVAL, "attention_threads_per_row must be 1 or 2");
       const long long wait_us = o.integer_or("wait_limit_us", 0);

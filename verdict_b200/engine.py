@@ -76,7 +76,7 @@ class B200Engine(Engine):
                  prune_last_layer: bool = True, fork: bool = True, gemm: str = "2sm",
                  raster_group: int = 0, gdn: str = "chunk", norm: str = "fused", split_k: bool = False,
                  attention_persistent: bool = True, attention_threads_per_row: int = 1, l2_hints: bool = False,
-                 wait_limit_us: int = 0, debug_stall_gemm: int = 0):
+                 pdl: bool = True, wait_limit_us: int = 0, debug_stall_gemm: int = 0):
         """`spec`: a spec dict, or a directory holding `vdexec.json` (whose
         relative "checkpoint" path is taken from that directory).
         `norm` (decoders): "fused" folds each RMSNorm into the residual GEMM that
@@ -93,6 +93,9 @@ class B200Engine(Engine):
         kernel (1: four softmax warps; 2: eight, each with half a key tile).
         `l2_hints`: the pair GEMM's TMA loads ask L2 to keep A rows (evict
         last) and let W tiles go first (evict first).
+        `pdl`: the GEMM and attention kernels are launched with programmatic
+        stream serialization, so each sets up under the previous kernel's tail
+        and waits for its results before touching global memory.
         `wait_limit_us`: limit of the GEMM kernels' pipeline waits (0: 2 s);
         `debug_stall_gemm` (failure-path tests only): the first one-CTA GEMM of
         every call stops loading after that many k-blocks, so its wait runs out."""
@@ -113,7 +116,7 @@ class B200Engine(Engine):
                                gemm=gemm, raster_group=raster_group, gdn=gdn, norm=norm, split_k=split_k,
                                attention_persistent=attention_persistent,
                                attention_threads_per_row=attention_threads_per_row, l2_hints=l2_hints,
-                               wait_limit_us=wait_limit_us,
+                               pdl=pdl, wait_limit_us=wait_limit_us,
                                debug_stall_gemm=debug_stall_gemm))
         err = ctypes.create_string_buffer(1024)
         h = ctypes.c_void_p()
