@@ -1491,13 +1491,23 @@ static void gemm(vd_handle* H, int kind, const CUtensorMap& a, const Linear& L, 
         return;
       }
     }
-    if (H->opt.raster_group <= 0) shape.group_m = Gemm2Config::GROUP_M;
-    const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
-    launch(H, kind, flops, [&] {
-      launch_k(H, gemm2_tcgen05_kernel<EPI, T>, grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, a, L.map_half,
-               c, d, shape, ep, H->d_err);
-    });
-    return;
+    // One CTA per 128 x 256 tile does the same per-SM MMA work per round as a
+    // CTA of a pair tile, over half the rows, but runs a tile ~10 % slower
+    // (it loads all of W's tile instead of half).  Where that still takes
+    // fewer rounds (a last pair row mostly padding, or pair tiles a fraction
+    // of a round past a whole number: one decision's ~800 tokens, the last
+    // layer's slot rows) the one-CTA kernel runs it.  Same bits either way.
+    const int64_t rounds_pair = (pair_tiles + H->gemm2_pairs - 1) / H->gemm2_pairs;
+    const int64_t rounds_one = (static_cast<int64_t>(num_m) * (L.n / 256) + H->num_sms - 1) / H->num_sms;
+    if (10 * rounds_pair < 11 * rounds_one) {
+      if (H->opt.raster_group <= 0) shape.group_m = Gemm2Config::GROUP_M;
+      const int grid = 2 * std::min(pair_tiles, H->gemm2_pairs);
+      launch(H, kind, flops, [&] {
+        launch_k(H, gemm2_tcgen05_kernel<EPI, T>, grid, Gemm2Config::THREADS, Gemm2Config::SMEM_BYTES, a,
+                 L.map_half, c, d, shape, ep, H->d_err);
+      });
+      return;
+    }
   }
   stall_one_cta();
   launch(H, kind, flops, [&] {
